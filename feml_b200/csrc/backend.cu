@@ -1,0 +1,677 @@
+// The B200 backend behind the C ABI (include/feml_b200.h): an implementation
+// of feml-core's `Backend` contract (feml-core/src/backend.rs:86-122) for the
+// mul_mat / mul_mat_id path.
+//
+//  - One backend = one device + one non-blocking CUDA stream; all state sits
+//    behind a mutex, so it is safe to share between threads (Send + Sync).
+//  - Buffers are cudaMalloc'd, zero-initialised and addressed by opaque
+//    32-bit handles; every byte range is checked before any copy.
+//  - write/read are blocking (feml-cuda/src/backend.rs:96-141); fill and
+//    graph_compute are asynchronous until synchronize().
+//  - graph_compute allocates nothing: intermediates (Q8_0 activations, MoE
+//    routing tables) live in a device scratch arena sized whenever a Compute
+//    buffer is created (scratch >= compute buffer bytes covers every node whose
+//    activations live in that buffer).
+//  - Kernels record data-dependent failures (bad mul_mat_id ids, a wait that
+//    ran out) in a device status word that synchronize() reads and clears.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <new>
+
+#include "host_common.h"
+#include "kernels/common.cuh"
+#include "kernels/kernels.h"
+
+using fb::set_error;
+
+namespace fbk {
+
+int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        cache[dev] = v;
+    }
+    return cache[dev];
+}
+
+}  // namespace fbk
+
+namespace {
+
+constexpr uint64_t kPad = 256;  // slack after every allocation
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return set_error(FB_ERR_CUDA, "B200 backend error: %s: %s", what, cudaGetErrorString(e));
+}
+
+bool is_weight_dtype(int32_t d) { return d == FB_F32 || d == FB_Q8_0 || d == FB_Q4_0 || d == FB_Q4_K; }
+
+uint64_t align256(uint64_t v) { return (v + 255) / 256 * 256; }
+
+// ---------------------------------------------------------------------------
+// mul_mat / mul_mat_id dispatch on device pointers (shared by graph_compute
+// and the kernel-level entry points).
+// ---------------------------------------------------------------------------
+uint64_t mul_mat_ws(int32_t wtype, int64_t K, int64_t M, int64_t N) {
+    (void)M;
+    if (wtype == FB_F32) return 0;
+    if (fbk::gemv_supported(wtype, K, N) && fbk::gemv_fused_ok(K, N)) return 0;
+    return fbk::q8_planar_bytes(K, N);
+}
+
+int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
+               int64_t K, int64_t M, int64_t N, void *ws, uint64_t ws_bytes, int32_t *status, cudaStream_t s) {
+    if (K < 0 || M < 0 || N < 0) return set_error(FB_ERR_INVALID, "mul_mat: negative dimension");
+    if (M == 0 || N == 0) return FB_OK;
+    if (!w || !x || !y) return set_error(FB_ERR_INVALID, "mul_mat: null operand");
+    if (!is_weight_dtype(wtype)) return set_error(FB_ERR_UNSUPPORTED, "mul_mat: weight dtype %d not supported", wtype);
+    const fb::DTypeTraits *t = fb::dtype_traits(wtype);
+    if (K % t->block_size) return set_error(FB_ERR_SHAPE, "mul_mat: K %ld not a multiple of %ld", (long)K, (long)t->block_size);
+    if (wtype == FB_F32) return fbk::launch_gemm_f32(w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, s);
+    if (K == 0) return set_error(FB_ERR_SHAPE, "mul_mat: K == 0");
+
+    const uint64_t need = mul_mat_ws(wtype, K, M, N);
+    if (need > ws_bytes)
+        return set_error(FB_ERR_INVALID, "mul_mat: workspace of %lu bytes needed, %lu given", (unsigned long)need,
+                         (unsigned long)ws_bytes);
+    if (need == 0) return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, nullptr, status, s, false);
+
+    const fbk::Q8Planar xq = fbk::q8_planar_carve(ws, K, N);
+    int rc = fbk::launch_quantize_q8_planar(x, x_nb1, K, N, xq, s);
+    if (rc) return rc;
+    if (fbk::gemv_supported(wtype, K, N))
+        return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, &xq, status, s, true);
+    if (fbk::gemm_q_supported(wtype, K, w, w_nb1))
+        return fbk::launch_gemm_q(wtype, w, w_nb1, xq, K, M, N, y, y_nb1, nullptr, s);
+    // Shapes the GEMM cannot tile (K % 256 != 0, unaligned rows): the GEMV on
+    // groups of up to 4 columns of the already-quantized activations.
+    const int64_t nblk = K / 32;
+    for (int64_t n0 = 0; n0 < N; n0 += 4) {
+        const int64_t nc = std::min<int64_t>(4, N - n0);
+        fbk::Q8Planar sub{xq.qs + n0 * K, xq.d + n0 * nblk, xq.sum + n0 * nblk};
+        rc = fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, static_cast<uint8_t *>(y) + n0 * y_nb1, y_nb1, K, M, nc,
+                              &sub, status, s, false);
+        if (rc) return rc;
+    }
+    return FB_OK;
+}
+
+struct IdWorkspace {
+    int32_t *counts, *offsets, *tile_start, *rows;
+    void *xq;
+    uint64_t total;
+};
+
+IdWorkspace id_ws_layout(void *base, int32_t wtype, int64_t K, int64_t N, int64_t n_sel, int64_t E) {
+    IdWorkspace L{};
+    uint8_t *p = static_cast<uint8_t *>(base);
+    uint64_t off = 0;
+    auto take = [&](uint64_t bytes) {
+        uint8_t *r = p ? p + off : nullptr;
+        off += align256(bytes);
+        return r;
+    };
+    L.counts = reinterpret_cast<int32_t *>(take(4 * E));
+    L.offsets = reinterpret_cast<int32_t *>(take(4 * E));
+    L.tile_start = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
+    L.rows = reinterpret_cast<int32_t *>(take(4 * n_sel * N));
+    L.xq = wtype == FB_F32 ? nullptr : take(fbk::q8_planar_bytes(K, N));
+    L.total = off;
+    return L;
+}
+
+int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t E, const void *x,
+                  uint64_t x_nb1, const int32_t *ids, uint64_t ids_nb1, int64_t n_sel, void *dst, uint64_t dst_nb1,
+                  uint64_t dst_nb2, int64_t K, int64_t M, int64_t N, void *ws, uint64_t ws_bytes, int32_t *status,
+                  cudaStream_t s) {
+    if (K < 0 || M < 0 || N < 0 || n_sel < 1 || E < 1) return set_error(FB_ERR_INVALID, "mul_mat_id: bad dimensions");
+    if (M == 0 || N == 0) return FB_OK;
+    if (!w || !x || !ids || !dst) return set_error(FB_ERR_INVALID, "mul_mat_id: null operand");
+    if (!is_weight_dtype(wtype)) return set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: weight dtype %d not supported", wtype);
+    const fb::DTypeTraits *t = fb::dtype_traits(wtype);
+    if (K % t->block_size) return set_error(FB_ERR_SHAPE, "mul_mat_id: K not a block multiple");
+    const IdWorkspace need = id_ws_layout(nullptr, wtype, K, N, n_sel, E);
+    if (need.total > ws_bytes)
+        return set_error(FB_ERR_INVALID, "mul_mat_id: workspace of %lu bytes needed, %lu given",
+                         (unsigned long)need.total, (unsigned long)ws_bytes);
+    const IdWorkspace L = id_ws_layout(ws, wtype, K, N, n_sel, E);
+    const int block_n = wtype == FB_F32 ? fbk::gemm_f32_block_n() : fbk::gemm_q_block_n();
+    if (wtype != FB_F32 && !fbk::gemm_q_supported(wtype, K, w, w_nb1))
+        return set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: quantized experts need K %% 256 == 0 and 16-byte aligned rows");
+    int rc = fbk::launch_moe_route(ids, ids_nb1, n_sel, N, E, L.counts, L.offsets, L.rows, L.tile_start, block_n,
+                                   status, dst, dst_nb1, dst_nb2, M, s);
+    if (rc) return rc;
+    fbk::GroupMap g{};
+    g.counts = L.counts;
+    g.offsets = L.offsets;
+    g.rows = L.rows;
+    g.tile_start = L.tile_start;
+    g.n_groups = (int32_t)E;
+    g.n_selected = (int32_t)n_sel;
+    g.w_group_stride = w_nb2;
+    g.dst_nb1 = dst_nb1;
+    g.dst_nb2 = dst_nb2;
+    g.max_tiles = (int32_t)((n_sel * N + block_n - 1) / block_n + E);
+    if (wtype == FB_F32) return fbk::launch_gemm_f32_grouped(w, w_nb1, x, x_nb1, K, M, dst, g, s);
+    const fbk::Q8Planar xq = fbk::q8_planar_carve(L.xq, K, N);
+    rc = fbk::launch_quantize_q8_planar(x, x_nb1, K, N, xq, s);
+    if (rc) return rc;
+    return fbk::launch_gemm_q(wtype, w, w_nb1, xq, K, M, 0, dst, 0, &g, s);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Backend object
+// ---------------------------------------------------------------------------
+struct Buffer {
+    uint8_t *ptr;
+    uint64_t size;
+    int32_t usage;
+};
+
+struct fb_backend {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    std::map<uint32_t, Buffer> buffers;
+    uint32_t next_handle = 1;
+    void *scratch = nullptr;
+    uint64_t scratch_bytes = 0;
+    int32_t *status_dev = nullptr;
+    int32_t *status_host = nullptr;  // pinned
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int lookup(fb_backend *b, uint32_t h, const char *op, Buffer **out) {
+    auto it = b->buffers.find(h);
+    if (it == b->buffers.end()) return set_error(FB_ERR_INVALID, "%s: unknown buffer buf#%u", op, h);
+    *out = &it->second;
+    return FB_OK;
+}
+
+int check_range(const Buffer &buf, uint32_t h, uint64_t off, uint64_t n, const char *op) {
+    if (off > buf.size || n > buf.size - off)
+        return set_error(FB_ERR_INVALID, "%s: buf#%u overflow: offset %lu + %lu > buffer %lu", op, h,
+                         (unsigned long)off, (unsigned long)n, (unsigned long)buf.size);
+    return FB_OK;
+}
+
+int grow_scratch(fb_backend *b, uint64_t bytes) {
+    if (bytes <= b->scratch_bytes) return FB_OK;
+    bytes = align256(bytes);
+    cudaError_t e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "scratch sync");
+    if (b->scratch) cudaFree(b->scratch);
+    b->scratch = nullptr;
+    b->scratch_bytes = 0;
+    e = cudaMalloc(&b->scratch, bytes);
+    if (e != cudaSuccess) {
+        b->scratch = nullptr;
+        return cuda_fail(e, "scratch alloc");
+    }
+    b->scratch_bytes = bytes;
+    return FB_OK;
+}
+
+// A plan tensor resolved to device memory.
+struct DevTensor {
+    const fb_plan_tensor *t;
+    uint8_t *ptr;
+    uint32_t handle;
+    uint64_t nbytes;
+};
+
+int resolve(fb_backend *b, const fb_plan *plan, int64_t idx, DevTensor *out) {
+    if (idx < 0 || idx >= plan->n_tensors) return set_error(FB_ERR_INVALID, "graph_compute: tensor index %ld out of range", (long)idx);
+    const fb_plan_tensor &t = plan->tensors[idx];
+    if (t.buffer < 0 || t.buffer >= plan->n_buffers)
+        return set_error(FB_ERR_INVALID, "graph_compute: tensor %u has no buffer", t.id);
+    const uint32_t h = plan->buffers[t.buffer].handle;
+    Buffer *buf;
+    int rc = lookup(b, h, "graph_compute", &buf);
+    if (rc) return rc;
+    uint64_t nb = 0;
+    rc = fb_layout_nbytes(t.dtype, t.ne, t.nb, &nb);
+    if (rc) return rc;
+    rc = check_range(*buf, h, t.offset, nb, "graph_compute");
+    if (rc) return rc;
+    out->t = &t;
+    out->ptr = buf->ptr + t.offset;
+    out->handle = h;
+    out->nbytes = nb;
+    return FB_OK;
+}
+
+bool overlap(const DevTensor &a, const DevTensor &c) {
+    if (a.handle != c.handle) return false;
+    const uint64_t ao = a.t->offset, co = c.t->offset;
+    return ao < co + c.nbytes && co < ao + a.nbytes;
+}
+
+int compute_mul_mat(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
+    if (node.n_srcs != 2) return set_error(FB_ERR_INVALID, "mul_mat: expected 2 sources");
+    DevTensor A, B, C;
+    int rc;
+    if ((rc = resolve(b, plan, node.srcs[0], &A)) || (rc = resolve(b, plan, node.srcs[1], &B))) return rc;
+    if ((rc = resolve(b, plan, &node - plan->tensors, &C))) return rc;
+    if (overlap(A, C) || overlap(B, C)) return set_error(FB_ERR_INVALID, "B200: mul_mat dst aliases a source");
+    const fb_plan_tensor &a = *A.t, &x = *B.t, &y = *C.t;
+    if (!is_weight_dtype(a.dtype) || x.dtype != FB_F32 || y.dtype != FB_F32)
+        return set_error(FB_ERR_UNSUPPORTED, "B200: mul_mat dtypes not supported");
+    const int64_t K = a.ne[0], M = a.ne[1], N = x.ne[1];
+    if (x.ne[0] != K || y.ne[0] != M || y.ne[1] != N)
+        return set_error(FB_ERR_SHAPE, "shape error: mul_mat: dst %ldx%ld but expected %ldx%ld", (long)y.ne[0],
+                         (long)y.ne[1], (long)M, (long)N);
+    if (a.ne[2] != 1 || a.ne[3] != 1 || x.ne[2] != 1 || x.ne[3] != 1 || y.ne[2] != 1 || y.ne[3] != 1)
+        return set_error(FB_ERR_SHAPE, "shape error: mul_mat: rank > 2 not supported yet");
+    if (a.nb[0] != (uint64_t)fb::dtype_traits(a.dtype)->type_size || x.nb[0] != 4 || y.nb[0] != 4)
+        return set_error(FB_ERR_UNSUPPORTED, "B200: mul_mat needs contiguous rows");
+    return do_mul_mat(a.dtype, A.ptr, a.nb[1], B.ptr, x.nb[1], C.ptr, y.nb[1], K, M, N, b->scratch, b->scratch_bytes,
+                      b->status_dev, b->stream);
+}
+
+int compute_mul_mat_id(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
+    if (node.n_srcs != 3) return set_error(FB_ERR_INVALID, "mul_mat_id: expected 3 sources");
+    DevTensor W, X, I, D;
+    int rc;
+    if ((rc = resolve(b, plan, node.srcs[0], &W)) || (rc = resolve(b, plan, node.srcs[1], &X)) ||
+        (rc = resolve(b, plan, node.srcs[2], &I)))
+        return rc;
+    if ((rc = resolve(b, plan, &node - plan->tensors, &D))) return rc;
+    if (overlap(W, D) || overlap(X, D) || overlap(I, D))
+        return set_error(FB_ERR_INVALID, "B200: mul_mat_id dst aliases a source");
+    const fb_plan_tensor &w = *W.t, &x = *X.t, &ids = *I.t, &d = *D.t;
+    if (!is_weight_dtype(w.dtype) || x.dtype != FB_F32 || ids.dtype != FB_I32 || d.dtype != FB_F32)
+        return set_error(FB_ERR_UNSUPPORTED, "B200: mul_mat_id dtypes not supported");
+    const int64_t K = w.ne[0], M = w.ne[1], E = w.ne[2], N = x.ne[1], n_sel = ids.ne[0];
+    if (x.ne[0] != K || ids.ne[1] != N || d.ne[0] != M || d.ne[1] != n_sel || d.ne[2] != N || w.ne[3] != 1)
+        return set_error(FB_ERR_SHAPE, "shape error: mul_mat_id: inconsistent shapes");
+    if (w.nb[0] != (uint64_t)fb::dtype_traits(w.dtype)->type_size || x.nb[0] != 4 || ids.nb[0] != 4 || d.nb[0] != 4)
+        return set_error(FB_ERR_UNSUPPORTED, "B200: mul_mat_id needs contiguous rows");
+    return do_mul_mat_id(w.dtype, W.ptr, w.nb[1], w.nb[2], E, X.ptr, x.nb[1], reinterpret_cast<int32_t *>(I.ptr),
+                         ids.nb[1], n_sel, D.ptr, d.nb[1], d.nb[2], K, M, N, b->scratch, b->scratch_bytes,
+                         b->status_dev, b->stream);
+}
+
+// vtable adapters
+const char *vt_name(void *) { return "B200"; }
+int vt_create(void *c, uint64_t size, int32_t usage, uint32_t *h) {
+    return feml_b200_create_buffer(static_cast<fb_backend *>(c), size, usage, h);
+}
+int vt_release(void *c, uint32_t h) { return feml_b200_release_buffer(static_cast<fb_backend *>(c), h); }
+int vt_write(void *c, uint32_t h, uint64_t o, const void *s, uint64_t n) {
+    return feml_b200_write(static_cast<fb_backend *>(c), h, o, s, n);
+}
+int vt_read(void *c, uint32_t h, uint64_t o, void *d, uint64_t n) {
+    return feml_b200_read(static_cast<fb_backend *>(c), h, o, d, n);
+}
+int vt_fill(void *c, uint32_t h, uint64_t o, uint8_t v, uint64_t n) {
+    return feml_b200_fill(static_cast<fb_backend *>(c), h, o, v, n);
+}
+int vt_sync(void *c) { return feml_b200_synchronize(static_cast<fb_backend *>(c)); }
+int vt_compute(void *c, const fb_plan *p) { return feml_b200_graph_compute(static_cast<fb_backend *>(c), p); }
+int vt_supports(void *c, int32_t op, const int32_t *d, int32_t n) {
+    return feml_b200_supports_op(static_cast<fb_backend *>(c), op, d, n);
+}
+
+bool is_sm100(int dev) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return false;
+    return prop.major == 10 && prop.minor == 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int feml_b200_device_count(int32_t *count) {
+    if (!count) return set_error(FB_ERR_INVALID, "device_count: null out");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();  // no driver / no device: an empty registrar, not an error
+        n = 0;
+    }
+    int c = 0;
+    for (int d = 0; d < n; d++)
+        if (is_sm100(d)) c++;
+    *count = c;
+    return FB_OK;
+}
+
+int feml_b200_registrar_score(uint32_t *score) {
+    int32_t n = 0;
+    feml_b200_device_count(&n);
+    if (score) *score = n > 0 ? 2000u : 0u;
+    return FB_OK;
+}
+
+int feml_b200_device_info(int32_t device, fb_device_info *info) {
+    if (!info) return set_error(FB_ERR_INVALID, "device_info: null out");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return set_error(FB_ERR_NO_DEVICE, "B200: device %d not found", device);
+    }
+    cudaDeviceProp prop;
+    cudaError_t e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_fail(e, "device properties");
+    memset(info, 0, sizeof(*info));
+    snprintf(info->name, sizeof(info->name), "%s", prop.name);
+    {
+        DeviceGuard g(device);
+        size_t fr = 0, tot = 0;
+        if (cudaMemGetInfo(&fr, &tot) == cudaSuccess) {
+            info->memory_free = fr;
+            info->memory_total = tot;
+        }
+    }
+    info->cc_major = prop.major;
+    info->cc_minor = prop.minor;
+    info->sm_count = prop.multiProcessorCount;
+    info->device_type = 1;
+    info->async_compute = 1;
+    info->host_buffer = 0;
+    info->events = 1;
+    return FB_OK;
+}
+
+int feml_b200_open(int32_t device, fb_backend **out) {
+    if (!out) return set_error(FB_ERR_INVALID, "open: null out");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return set_error(FB_ERR_NO_DEVICE, "B200: device %d not found", device);
+    }
+    if (!is_sm100(device)) return set_error(FB_ERR_NO_DEVICE, "B200: device %d is not an sm_100 GPU", device);
+    fb_backend *b = new (std::nothrow) fb_backend();
+    if (!b) return set_error(FB_ERR_INVALID, "open: out of host memory");
+    b->device = device;
+    DeviceGuard g(device);
+    cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&b->status_dev, 256);
+    if (e == cudaSuccess) e = cudaMemset(b->status_dev, 0, 256);
+    if (e == cudaSuccess) e = cudaMallocHost(&b->status_host, 256);
+    if (e != cudaSuccess) {
+        int rc = cuda_fail(e, "open");
+        feml_b200_close(b);
+        return rc;
+    }
+    fbk::sm_count();
+    *out = b;
+    return FB_OK;
+}
+
+int feml_b200_close(fb_backend *b) {
+    if (!b) return FB_OK;
+    {
+        DeviceGuard g(b->device);
+        if (b->stream) cudaStreamSynchronize(b->stream);
+        for (auto &kv : b->buffers) cudaFree(kv.second.ptr);
+        if (b->scratch) cudaFree(b->scratch);
+        if (b->status_dev) cudaFree(b->status_dev);
+        if (b->status_host) cudaFreeHost(b->status_host);
+        if (b->stream) cudaStreamDestroy(b->stream);
+    }
+    delete b;
+    return FB_OK;
+}
+
+const char *feml_b200_name(fb_backend *) { return "B200"; }
+
+int feml_b200_create_buffer(fb_backend *b, uint64_t size, int32_t usage, uint32_t *handle) {
+    if (!b || !handle) return set_error(FB_ERR_INVALID, "create_buffer: null argument");
+    if (usage != FB_USAGE_WEIGHTS && usage != FB_USAGE_COMPUTE)
+        return set_error(FB_ERR_INVALID, "create_buffer: bad usage %d", usage);
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    if (usage == FB_USAGE_COMPUTE) {
+        // intermediates of any node whose activations live in this buffer fit
+        // in its size plus a fixed margin (256-byte padding of each part)
+        int rc = grow_scratch(b, size + (1u << 20));
+        if (rc) return rc;
+    }
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, size + kPad);
+    if (e != cudaSuccess) return cuda_fail(e, "create_buffer");
+    e = cudaMemsetAsync(p, 0, size + kPad, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "create_buffer zero-fill");
+    }
+    const uint32_t h = b->next_handle++;
+    b->buffers[h] = Buffer{static_cast<uint8_t *>(p), size, usage};
+    *handle = h;
+    return FB_OK;
+}
+
+int feml_b200_release_buffer(fb_backend *b, uint32_t handle) {
+    if (!b) return set_error(FB_ERR_INVALID, "release_buffer: null backend");
+    std::lock_guard<std::mutex> lk(b->mu);
+    Buffer *buf;
+    int rc = lookup(b, handle, "release_buffer", &buf);
+    if (rc) return rc;
+    DeviceGuard g(b->device);
+    cudaStreamSynchronize(b->stream);  // queued work may still read it
+    cudaFree(buf->ptr);
+    b->buffers.erase(handle);
+    return FB_OK;
+}
+
+int feml_b200_write(fb_backend *b, uint32_t h, uint64_t off, const void *src, uint64_t n) {
+    if (!b || (!src && n)) return set_error(FB_ERR_INVALID, "write: null argument");
+    std::lock_guard<std::mutex> lk(b->mu);
+    Buffer *buf;
+    int rc = lookup(b, h, "write", &buf);
+    if (rc || (rc = check_range(*buf, h, off, n, "write"))) return rc;
+    if (n == 0) return FB_OK;
+    DeviceGuard g(b->device);
+    cudaError_t e = cudaMemcpyAsync(buf->ptr + off, src, n, cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    return e == cudaSuccess ? FB_OK : cuda_fail(e, "write");
+}
+
+int feml_b200_read(fb_backend *b, uint32_t h, uint64_t off, void *dst, uint64_t n) {
+    if (!b || (!dst && n)) return set_error(FB_ERR_INVALID, "read: null argument");
+    std::lock_guard<std::mutex> lk(b->mu);
+    Buffer *buf;
+    int rc = lookup(b, h, "read", &buf);
+    if (rc || (rc = check_range(*buf, h, off, n, "read"))) return rc;
+    if (n == 0) return FB_OK;
+    DeviceGuard g(b->device);
+    cudaError_t e = cudaMemcpyAsync(dst, buf->ptr + off, n, cudaMemcpyDeviceToHost, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    return e == cudaSuccess ? FB_OK : cuda_fail(e, "read");
+}
+
+int feml_b200_fill(fb_backend *b, uint32_t h, uint64_t off, uint8_t value, uint64_t n) {
+    if (!b) return set_error(FB_ERR_INVALID, "fill: null backend");
+    std::lock_guard<std::mutex> lk(b->mu);
+    Buffer *buf;
+    int rc = lookup(b, h, "fill", &buf);
+    if (rc || (rc = check_range(*buf, h, off, n, "fill"))) return rc;
+    if (n == 0) return FB_OK;
+    DeviceGuard g(b->device);
+    cudaError_t e = cudaMemsetAsync(buf->ptr + off, value, n, b->stream);
+    return e == cudaSuccess ? FB_OK : cuda_fail(e, "fill");
+}
+
+int feml_b200_synchronize(fb_backend *b) {
+    if (!b) return set_error(FB_ERR_INVALID, "synchronize: null backend");
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    cudaError_t e = cudaMemcpyAsync(b->status_host, b->status_dev, 4, cudaMemcpyDeviceToHost, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+    const int32_t st = *b->status_host;
+    if (st != 0) {
+        cudaMemsetAsync(b->status_dev, 0, 4, b->stream);
+        cudaStreamSynchronize(b->stream);
+        if (st & fbk::STATUS_BAD_ID)
+            return set_error(FB_ERR_DEVICE, "B200 backend error: mul_mat_id: expert id out of range (slots zeroed)");
+        if (st & fbk::STATUS_TIMEOUT)
+            return set_error(FB_ERR_DEVICE, "B200 backend error: a kernel wait timed out (results invalid)");
+        return set_error(FB_ERR_DEVICE, "B200 backend error: kernel status 0x%x", (unsigned)st);
+    }
+    return FB_OK;
+}
+
+int feml_b200_supports_op(fb_backend *, int32_t op, const int32_t *dt, int32_t n) {
+    switch (op) {
+    case FB_OP_VIEW:
+        return 1;  // zero-copy: nothing to execute
+    case FB_OP_MUL_MAT:
+        return n == 2 && dt && is_weight_dtype(dt[0]) && dt[1] == FB_F32;
+    case FB_OP_MUL_MAT_ID:
+        return n == 3 && dt && is_weight_dtype(dt[0]) && dt[1] == FB_F32 && dt[2] == FB_I32;
+    default:
+        return 0;
+    }
+}
+
+int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
+    if (!b || !plan) return set_error(FB_ERR_INVALID, "graph_compute: null argument");
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    for (int64_t i = 0; i < plan->n_nodes; i++) {
+        const int64_t ti = plan->nodes[i];
+        if (ti < 0 || ti >= plan->n_tensors) return set_error(FB_ERR_INVALID, "graph_compute: bad node index");
+        const fb_plan_tensor &node = plan->tensors[ti];
+        int rc;
+        switch (node.op) {
+        case FB_OP_VIEW:
+            rc = FB_OK;
+            break;
+        case FB_OP_MUL_MAT:
+            rc = compute_mul_mat(b, plan, node);
+            break;
+        case FB_OP_MUL_MAT_ID:
+            rc = compute_mul_mat_id(b, plan, node);
+            break;
+        default:
+            rc = set_error(FB_ERR_UNSUPPORTED, "B200: op %s not implemented", fb::op_name(node.op));
+        }
+        if (rc) return rc;
+    }
+    return FB_OK;
+}
+
+int feml_b200_backend_vtable(fb_backend *b, fb_backend_vtable *vt) {
+    if (!b || !vt) return set_error(FB_ERR_INVALID, "backend_vtable: null argument");
+    vt->ctx = b;
+    vt->name = vt_name;
+    vt->create_buffer = vt_create;
+    vt->release_buffer = vt_release;
+    vt->write = vt_write;
+    vt->read = vt_read;
+    vt->fill = vt_fill;
+    vt->synchronize = vt_sync;
+    vt->graph_compute = vt_compute;
+    vt->supports_op = vt_supports;
+    return FB_OK;
+}
+
+int feml_b200_buffer_device_ptr(fb_backend *b, uint32_t h, void **ptr, uint64_t *size) {
+    if (!b || !ptr) return set_error(FB_ERR_INVALID, "buffer_device_ptr: null argument");
+    std::lock_guard<std::mutex> lk(b->mu);
+    Buffer *buf;
+    int rc = lookup(b, h, "buffer_device_ptr", &buf);
+    if (rc) return rc;
+    *ptr = buf->ptr;
+    if (size) *size = buf->size;
+    return FB_OK;
+}
+
+int feml_b200_stream(fb_backend *b, void **stream) {
+    if (!b || !stream) return set_error(FB_ERR_INVALID, "stream: null argument");
+    *stream = b->stream;
+    return FB_OK;
+}
+
+int feml_b200_scratch_bytes(fb_backend *b, uint64_t *bytes) {
+    if (!b || !bytes) return set_error(FB_ERR_INVALID, "scratch_bytes: null argument");
+    std::lock_guard<std::mutex> lk(b->mu);
+    *bytes = b->scratch_bytes;
+    return FB_OK;
+}
+
+int feml_b200_reserve_scratch(fb_backend *b, uint64_t bytes) {
+    if (!b) return set_error(FB_ERR_INVALID, "reserve_scratch: null backend");
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    return grow_scratch(b, bytes);
+}
+
+// ---- kernel-level entry points --------------------------------------------
+int feml_b200_quantize(int32_t dtype, const void *x, uint64_t x_row_stride, void *y, int64_t rows, int64_t k,
+                       void *stream) {
+    return fbk::launch_quantize_rows(dtype, x, x_row_stride, y, rows, k, static_cast<cudaStream_t>(stream));
+}
+
+int feml_b200_mul_mat_workspace(int32_t wtype, int64_t K, int64_t M, int64_t N, uint64_t *bytes) {
+    if (!bytes) return set_error(FB_ERR_INVALID, "mul_mat_workspace: null out");
+    *bytes = mul_mat_ws(wtype, K, M, N);
+    return FB_OK;
+}
+
+int feml_b200_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *dst,
+                      uint64_t dst_nb1, int64_t K, int64_t M, int64_t N, void *workspace, uint64_t workspace_bytes,
+                      void *stream) {
+    return do_mul_mat(wtype, w, w_nb1, x, x_nb1, dst, dst_nb1, K, M, N, workspace, workspace_bytes, nullptr,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int feml_b200_mul_mat_id_workspace(int32_t wtype, int64_t K, int64_t M, int64_t N, int64_t n_selected,
+                                   int64_t n_experts, uint64_t *bytes) {
+    (void)M;
+    if (!bytes) return set_error(FB_ERR_INVALID, "mul_mat_id_workspace: null out");
+    *bytes = id_ws_layout(nullptr, wtype, K, N, n_selected, n_experts).total;
+    return FB_OK;
+}
+
+int feml_b200_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,
+                         const void *x, uint64_t x_nb1, const int32_t *ids, uint64_t ids_nb1, int64_t n_selected,
+                         void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t K, int64_t M, int64_t N,
+                         void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream) {
+    return do_mul_mat_id(wtype, w, w_nb1, w_nb2, n_experts, x, x_nb1, ids, ids_nb1, n_selected, dst, dst_nb1, dst_nb2,
+                         K, M, N, workspace, workspace_bytes, status, static_cast<cudaStream_t>(stream));
+}
+
+int feml_b200_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
+                        int32_t *counts, int32_t *offsets, int32_t *rows, int32_t *status, void *stream) {
+    if (!ids || !counts || !offsets || !rows) return set_error(FB_ERR_INVALID, "moe_route: null argument");
+    return fbk::launch_moe_route(ids, ids_nb1, n_selected, N, n_experts, counts, offsets, rows, nullptr, 64, status,
+                                 nullptr, 0, 0, 0,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+int feml_b200_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *xq, int64_t K, int64_t M,
+                         int64_t N, int32_t *out, void *stream) {
+    if (!w || !xq || !out) return set_error(FB_ERR_INVALID, "block_dots: null argument");
+    return fbk::launch_block_dots(wtype, w, w_nb1, xq, K, M, N, out, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,80 @@
+// Host-side launch interface of the sm_100a kernels (one .cu per family).
+// Every launcher validates its arguments, enqueues on `stream` and returns an
+// FB_* status (recording the message through fb::set_error on failure).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace fbk {
+
+// Planar Q8_0 activations: the device-internal form the quantized kernels
+// read. Column n of an activation matrix [K, N] becomes qs[n*K .. n*K+K)
+// (int8), d[n*(K/32) + b] (the f16-rounded block scale as f32) and
+// sum[n*(K/32) + b] (sum of the block's 32 integers).
+struct Q8Planar {
+    int8_t *qs;
+    float *d;
+    int32_t *sum;
+};
+
+// Bytes of a planar Q8_0 buffer for [K, N] activations (each part padded to
+// 256 bytes).
+uint64_t q8_planar_bytes(int64_t K, int64_t N);
+Q8Planar q8_planar_carve(void *base, int64_t K, int64_t N);
+
+// quantize.cu
+int launch_quantize_rows(int32_t dtype, const void *x, uint64_t x_row_stride, void *y, int64_t rows, int64_t k,
+                         cudaStream_t s);
+// quantize_row_q8_0 into planar form; columns of x at x + n*x_nb1.
+int launch_quantize_q8_planar(const void *x, uint64_t x_nb1, int64_t K, int64_t N, Q8Planar out, cudaStream_t s);
+
+// gemv.cu: dequant-fused GEMV for small N (1..8). When `xq` is non-null the
+// activations were quantized by a preceding kernel (read after a
+// programmatic-dependent-launch wait); otherwise each CTA quantizes them
+// itself (fused path, no workspace).
+bool gemv_supported(int32_t wtype, int64_t K, int64_t N);
+bool gemv_fused_ok(int64_t K, int64_t N);
+int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y,
+                uint64_t y_nb1, int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status,
+                cudaStream_t s, bool pdl);
+
+// gemm_f32.cu: F32 mul_mat on SIMT FP32 (any N).
+int launch_gemm_f32(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
+                    int64_t K, int64_t M, int64_t N, cudaStream_t s);
+
+// gemm_q.cu: quantized mul_mat for large N on Q8Planar activations. The
+// optional gather maps (MoE) select activation columns and output columns.
+struct GroupMap {
+    const int32_t *counts;   // [n_groups] columns per group (device)
+    const int32_t *offsets;  // [n_groups] exclusive prefix (device)
+    const int32_t *rows;     // [n_slots] slot ids in group order (device)
+    const int32_t *tile_start;  // [n_groups + 1] prefix of ceil(count/BN) (device)
+    int32_t n_groups;
+    int32_t n_selected;
+    uint64_t w_group_stride;   // bytes between experts' weights
+    uint64_t dst_nb1, dst_nb2; // dst column (s, t) at dst + s*nb1 + t*nb2
+    int32_t max_tiles;         // upper bound of total column tiles
+};
+int launch_gemm_f32_grouped(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, int64_t K, int64_t M,
+                            void *dst, const GroupMap &g, cudaStream_t s);
+int gemm_f32_block_n();
+bool gemm_q_supported(int32_t wtype, int64_t K, const void *w, uint64_t w_nb1);
+int launch_gemm_q(int32_t wtype, const void *w, uint64_t w_nb1, const Q8Planar &xq, int64_t K, int64_t M, int64_t N,
+                  void *y, uint64_t y_nb1, const GroupMap *groups, cudaStream_t s);
+int gemm_q_block_n();
+
+// Per-block int32 sums (bit-exactness probe); xq in ggml Q8_0 layout.
+int launch_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *xq, int64_t K, int64_t M, int64_t N,
+                      int32_t *out, cudaStream_t s);
+
+// moe.cu: routing tables + column-tile prefix for gemm_q's grouped mode.
+// When dst is non-null, output columns of slots with an invalid id are
+// zeroed (and STATUS_BAD_ID is raised).
+int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
+                     int32_t *counts, int32_t *offsets, int32_t *rows, int32_t *tile_start, int32_t block_n,
+                     int32_t *status, void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t M, cudaStream_t s);
+
+int sm_count();
+
+}  // namespace fbk

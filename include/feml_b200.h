@@ -1,0 +1,313 @@
+/*
+ * feml_b200.h -- C ABI of libfeml_b200.so, a B200 (sm_100a) backend for
+ * feml's mul_mat / mul_mat_id path.
+ *
+ * Conventions
+ *  - Every call returns int status: FB_OK (0) or an FB_ERR_* code; the
+ *    message of the last failure on the calling thread is returned by
+ *    feml_b200_last_error(). No C++ exception or abort crosses this boundary
+ *    (the reference's zero-panic contract, feml-core/src/backend.rs:80-122).
+ *  - Enum values are the discriminants of the reference enums: DType
+ *    (feml-core/src/dtype.rs:14-35), Op (feml-core/src/op.rs:12-43),
+ *    BufferUsage (feml-core/src/backend.rs:52-57).
+ *  - Tensor layout is ggml's: ne[] element counts, nb[] byte strides,
+ *    nb[0] = type_size, nb[1] = row bytes (feml-core/src/layout.rs:32-48).
+ *  - "stream" arguments are cudaStream_t passed as void* (NULL = the legacy
+ *    default stream).
+ */
+#ifndef FEML_B200_H
+#define FEML_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* every declaration below is exported even when the library is built with
+ * -fvisibility=hidden */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define FB_OK 0
+#define FB_ERR_INVALID 1     /* bad argument, unknown handle, range outside a buffer */
+#define FB_ERR_UNSUPPORTED 2 /* op / dtype / shape not supported by this backend */
+#define FB_ERR_SHAPE 3       /* shape or layout mismatch (reference ErrorKind::Shape) */
+#define FB_ERR_CUDA 4        /* CUDA runtime error */
+#define FB_ERR_DEVICE 5      /* error reported by a kernel (e.g. mul_mat_id id out of range) */
+#define FB_ERR_NO_DEVICE 6   /* no usable sm_100 device */
+
+/* ---- enums (reference discriminants) ----------------------------------- */
+enum fb_dtype {
+    FB_I8 = 0, FB_I16, FB_I32, FB_I64, FB_F16, FB_F32, FB_F64,
+    FB_Q4_0, FB_Q4_1, FB_Q5_0, FB_Q5_1, FB_Q8_0, FB_Q8_1,
+    FB_Q2_K, FB_Q3_K, FB_Q4_K, FB_Q5_K, FB_Q6_K, FB_Q8_K,
+    FB_DTYPE_COUNT
+};
+
+enum fb_op {
+    FB_OP_NONE = 0, FB_OP_VIEW, FB_OP_MUL, FB_OP_ADD, FB_OP_MUL_MAT, FB_OP_MUL_MAT_ID,
+    FB_OP_RMS_NORM, FB_OP_SOFTMAX, FB_OP_ROPE, FB_OP_SILU, FB_OP_GET_ROWS, FB_OP_CONCAT,
+    FB_OP_COPY, FB_OP_DIAG_MASK_INF, FB_OP_SCALE
+};
+
+enum fb_usage { FB_USAGE_WEIGHTS = 0, FB_USAGE_COMPUTE = 1 };
+
+/* TensorFlags bits, feml-core/src/tensor.rs:48-68 */
+#define FB_FLAG_INPUT 1u
+#define FB_FLAG_OUTPUT 2u
+#define FB_FLAG_WEIGHT 4u
+
+/* ---- plan mirror: repr(C) image of feml_core::plan::GraphPlan ----------
+ * (feml-core/src/plan.rs:15-45). A Rust caller fills these from its
+ * GraphPlan; op_params carries the inline Op payload (MulMatId:
+ * [0] = n_experts, [1] = n_selected). */
+#define FB_MAX_SRC 4
+typedef struct {
+    uint32_t id;
+    int32_t op;
+    uint32_t op_params[2];
+    int32_t n_srcs;
+    int32_t srcs[FB_MAX_SRC]; /* indices into fb_plan.tensors */
+    int32_t buffer;           /* index into fb_plan.buffers */
+    uint64_t offset;          /* byte offset within the buffer */
+    int32_t dtype;
+    uint32_t flags;
+    int64_t ne[4];
+    uint64_t nb[4];
+} fb_plan_tensor;
+
+typedef struct {
+    uint32_t handle;
+    uint64_t size;
+    int32_t usage;
+} fb_plan_buffer;
+
+typedef struct {
+    uint64_t uid;
+    const fb_plan_tensor *tensors;
+    int64_t n_tensors;
+    const int64_t *nodes; /* indices into tensors, execution order */
+    int64_t n_nodes;
+    const fb_plan_buffer *buffers;
+    int64_t n_buffers;
+} fb_plan;
+
+/* ---- generic backend vtable: C image of `&dyn Backend` -----------------
+ * (feml-core/src/backend.rs:86-122). GraphBuilder::compile below drives any
+ * backend through this table; feml_b200_backend_vtable() fills one for the
+ * B200 backend. */
+typedef struct {
+    void *ctx;
+    const char *(*name)(void *ctx);
+    int (*create_buffer)(void *ctx, uint64_t size, int32_t usage, uint32_t *handle);
+    int (*release_buffer)(void *ctx, uint32_t handle);
+    int (*write)(void *ctx, uint32_t handle, uint64_t offset, const void *src, uint64_t n);
+    int (*read)(void *ctx, uint32_t handle, uint64_t offset, void *dst, uint64_t n);
+    int (*fill)(void *ctx, uint32_t handle, uint64_t offset, uint8_t value, uint64_t n);
+    int (*synchronize)(void *ctx);
+    int (*graph_compute)(void *ctx, const fb_plan *plan);
+    int (*supports_op)(void *ctx, int32_t op, const int32_t *src_dtypes, int32_t n);
+} fb_backend_vtable;
+
+const char *feml_b200_last_error(void);
+const char *feml_b200_version(void);
+
+/* ======================================================================== */
+/* 1. Backend (the drop-in boundary).                                       */
+/* ======================================================================== */
+typedef struct fb_backend fb_backend;
+
+typedef struct {
+    char name[256];
+    uint64_t memory_total;
+    uint64_t memory_free;
+    int32_t cc_major, cc_minor;
+    int32_t sm_count;
+    int32_t device_type; /* feml-core DeviceType: 1 = Gpu */
+    int32_t async_compute, host_buffer, events;
+} fb_device_info;
+
+/* BackendRegistrar::device_count / score (feml-core/src/backend.rs:157-165;
+ * CUDA registrar scores 1000, feml-cuda/src/device.rs:118-120; this backend
+ * reports 2000 when an sm_100 device is present, else 0). */
+int feml_b200_device_count(int32_t *count);
+int feml_b200_registrar_score(uint32_t *score);
+/* BackendDevice::info (feml-core/src/backend.rs:130-131). */
+int feml_b200_device_info(int32_t device, fb_device_info *info);
+
+/* BackendDevice::init_backend (feml-core/src/backend.rs:133-134): one
+ * backend = one device + one CUDA stream. */
+int feml_b200_open(int32_t device, fb_backend **out);
+int feml_b200_close(fb_backend *b);
+/* Backend::name -> "B200". */
+const char *feml_b200_name(fb_backend *b);
+/* Backend::create_buffer, zero-initialised (backend.rs:90-92). */
+int feml_b200_create_buffer(fb_backend *b, uint64_t size, int32_t usage, uint32_t *handle);
+/* Backend::release_buffer (backend.rs:94-95). */
+int feml_b200_release_buffer(fb_backend *b, uint32_t handle);
+/* Backend::write / read: blocking; the byte range must lie inside the
+ * buffer or FB_ERR_INVALID is returned and nothing is written
+ * (backend.rs:97-103). */
+int feml_b200_write(fb_backend *b, uint32_t handle, uint64_t offset, const void *src, uint64_t n);
+int feml_b200_read(fb_backend *b, uint32_t handle, uint64_t offset, void *dst, uint64_t n);
+/* Backend::fill (backend.rs:105-106), asynchronous like the reference CUDA
+ * fill kernel (feml-cuda/src/kernels.cu:124-133). */
+int feml_b200_fill(fb_backend *b, uint32_t handle, uint64_t offset, uint8_t value, uint64_t n);
+/* Backend::synchronize (backend.rs:108-109). Also reports, once, any error
+ * a kernel recorded since the last call (FB_ERR_DEVICE). */
+int feml_b200_synchronize(fb_backend *b);
+/* Backend::supports_op (backend.rs:117-121): 1 = supported, 0 = not.
+ * MulMat: src0 in {F32, Q8_0, Q4_0, Q4_K}, src1 = F32.
+ * MulMatId: src0 in the same set, src1 = F32, src2 = I32. */
+int feml_b200_supports_op(fb_backend *b, int32_t op, const int32_t *src_dtypes, int32_t n);
+/* Backend::graph_compute (backend.rs:111-114): enqueues every node on the
+ * backend stream and returns; no allocation, no host synchronisation. */
+int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan);
+/* Fill a vtable bound to `b` (for compile() and other generic callers). */
+int feml_b200_backend_vtable(fb_backend *b, fb_backend_vtable *vt);
+
+/* Interop: device address of a buffer and the backend's CUDA stream. */
+int feml_b200_buffer_device_ptr(fb_backend *b, uint32_t handle, void **ptr, uint64_t *size);
+int feml_b200_stream(fb_backend *b, void **stream);
+/* Bytes of device scratch the backend holds for mul_mat/mul_mat_id
+ * intermediates (grown when a Compute buffer is created, never inside
+ * graph_compute). */
+int feml_b200_scratch_bytes(fb_backend *b, uint64_t *bytes);
+int feml_b200_reserve_scratch(fb_backend *b, uint64_t bytes);
+
+/* ======================================================================== */
+/* 2. Graph builder / planner mirror (C++ restatement of feml-core's        */
+/*    GraphBuilder -> compile -> GraphPlan, feml-core/src/graph.rs,         */
+/*    planner.rs, plan.rs), used by C/C++/Python callers without Rust.      */
+/* ======================================================================== */
+typedef struct fb_graph fb_graph;
+typedef struct fb_compiled_plan fb_compiled_plan;
+
+int fb_graph_new(fb_graph **out);
+void fb_graph_free(fb_graph *g);
+/* GraphBuilder::input / weight (graph.rs:67-87). */
+int fb_graph_input(fb_graph *g, const char *name, int32_t dtype, const int64_t *dims, int32_t rank, uint32_t *id);
+int fb_graph_weight(fb_graph *g, const char *name, int32_t dtype, const int64_t *dims, int32_t rank, uint32_t *id);
+/* GraphBuilder::view (graph.rs:89-108). */
+int fb_graph_view(fb_graph *g, uint32_t src, uint64_t offset, const int64_t *dims, int32_t rank, uint32_t *id);
+/* GraphBuilder::mul / add (graph.rs:110-120); built for planner parity,
+ * not executed by this backend (supports_op = 0). */
+int fb_graph_mul(fb_graph *g, uint32_t a, uint32_t b, uint32_t *id);
+int fb_graph_add(fb_graph *g, uint32_t a, uint32_t b, uint32_t *id);
+int fb_graph_silu(fb_graph *g, uint32_t x, uint32_t *id);
+int fb_graph_copy(fb_graph *g, uint32_t x, uint32_t *id);
+/* GraphBuilder::mul_mat (graph.rs:122-138), relaxed: src0 in {F32, Q8_0,
+ * Q4_0, Q4_K}, src1 F32, output F32 [ne1(a), ne1(b)], ne0(a) % block == 0. */
+int fb_graph_mul_mat(fb_graph *g, uint32_t a, uint32_t b, uint32_t *id);
+/* GraphBuilder::mul_mat_id (graph.rs:215-250), ggml semantics: weights
+ * [K, M, E], x [K, N], ids I32 [n_selected, N], output F32
+ * [M, n_selected, N]; out[:, s, t] = W[:, :, ids[s, t]]^T x[:, t]. */
+int fb_graph_mul_mat_id(fb_graph *g, uint32_t w, uint32_t x, uint32_t ids, uint32_t n_selected, uint32_t *id);
+/* GraphBuilder::mark_output (graph.rs:57-65). */
+int fb_graph_mark_output(fb_graph *g, uint32_t id);
+/* Tensor metadata: dtype, ne[4], nb[4], flags, op. */
+int fb_graph_tensor_info(fb_graph *g, uint32_t id, int32_t *dtype, int64_t *ne, uint64_t *nb, uint32_t *flags, int32_t *op);
+/* GraphBuilder::compile (graph.rs:349-442) against any backend vtable. */
+int fb_graph_compile(fb_graph *g, const fb_backend_vtable *backend, fb_compiled_plan **out);
+
+const fb_plan *fb_plan_get(fb_compiled_plan *p);
+/* GraphPlan::find (plan.rs:54-56): index into tensors, or -1. */
+int64_t fb_plan_find(fb_compiled_plan *p, uint32_t id);
+/* GraphPlan::write_tensor / read_tensor (plan.rs:77-115): n must equal the
+ * tensor's nbytes. */
+int fb_plan_write_tensor(fb_compiled_plan *p, const fb_backend_vtable *backend, uint32_t id, const void *src, uint64_t n);
+int fb_plan_read_tensor(fb_compiled_plan *p, const fb_backend_vtable *backend, uint32_t id, void *dst, uint64_t n);
+/* GraphPlan::release (plan.rs:68-73). */
+int fb_plan_release(fb_compiled_plan *p, const fb_backend_vtable *backend);
+void fb_plan_free(fb_compiled_plan *p);
+
+/* Planner-only entry (feml-core/src/planner.rs:156-261) for planner parity
+ * tests: tensors described by (id, dtype, ne, flags, op, srcs, view_src,
+ * view_offset); `order` indexes them; out receives per-tensor (kind, offset),
+ * kind 0 = Weights, 1 = Compute. */
+typedef struct {
+    uint32_t id;
+    int32_t dtype;
+    int64_t ne[4];
+    int32_t rank;
+    uint32_t flags;
+    int32_t op;
+    int32_t n_srcs;
+    uint32_t srcs[FB_MAX_SRC]; /* tensor ids */
+    uint32_t view_src;         /* 0 = not a view */
+    uint64_t view_offset;
+} fb_planner_tensor;
+
+int fb_planner_plan(const fb_planner_tensor *tensors, int64_t n, const int64_t *order, int64_t n_order,
+                    int32_t *kinds, uint64_t *offsets, uint64_t *weights_size, uint64_t *compute_size);
+
+/* Layout helpers (layout.rs:32-60, dtype.rs:105-116). */
+int fb_layout_new(int32_t dtype, const int64_t *dims, int32_t rank, uint64_t *nb);
+int fb_layout_nbytes(int32_t dtype, const int64_t *ne, const uint64_t *nb, uint64_t *nbytes);
+int fb_dtype_traits(int32_t dtype, int64_t *block_size, int64_t *type_size, int32_t *quantized);
+
+/* ======================================================================== */
+/* 3. Kernel-level entry points on device pointers (what graph_compute     */
+/*    launches). All asynchronous on `stream`.                              */
+/* ======================================================================== */
+
+/* Quantize `rows` rows of `k` f32 (row r at x + r*x_row_stride bytes) into
+ * ggml blocks of `dtype` (FB_Q8_0, FB_Q4_0, FB_Q4_K), row r at
+ * y + r*row_size(dtype, k). FB_Q8_0 on activations is quantize_row_q8_0:
+ * d = f16(amax/127), q = round-half-away(x * (1/d)). The Q4_K scheme is this
+ * library's deterministic single-pass quantizer. */
+int feml_b200_quantize(int32_t dtype, const void *x, uint64_t x_row_stride, void *y, int64_t rows, int64_t k,
+                       void *stream);
+
+/* Workspace bytes feml_b200_mul_mat needs for this shape (0 when the
+ * activation quantisation is fused into the kernel). */
+int feml_b200_mul_mat_workspace(int32_t wtype, int64_t K, int64_t M, int64_t N, uint64_t *bytes);
+
+/* mul_mat, ggml semantics (feml-cpu/src/ops/mul_mat.rs:14-58):
+ *   dst[m*4 + n*dst_nb1] = sum_k W[k, m] * X[k, n]
+ * W: wtype blocks, row m at w + m*w_nb1; X: f32, column n at x + n*x_nb1;
+ * quantized weights are multiplied against the Q8_0-quantized activations
+ * with int32 per-block sums. dst must not overlap w or x. */
+int feml_b200_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *dst,
+                      uint64_t dst_nb1, int64_t K, int64_t M, int64_t N, void *workspace, uint64_t workspace_bytes,
+                      void *stream);
+
+int feml_b200_mul_mat_id_workspace(int32_t wtype, int64_t K, int64_t M, int64_t N, int64_t n_selected,
+                                   int64_t n_experts, uint64_t *bytes);
+
+/* mul_mat_id, ggml semantics: expert e's weight rows at w + e*w_nb2 + m*w_nb1;
+ * x column t at x + t*x_nb1; ids[s + t*ids_nb1/4] selects the expert of slot
+ * (s, t); dst column (s, t) at dst + s*dst_nb1 + t*dst_nb2. Slots with an id
+ * outside [0, n_experts) produce zeros and set bit 1 of *status (device
+ * int32, may be NULL). */
+int feml_b200_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,
+                         const void *x, uint64_t x_nb1, const int32_t *ids, uint64_t ids_nb1, int64_t n_selected,
+                         void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t K, int64_t M, int64_t N,
+                         void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream);
+
+/* mul_mat_id routing tables: counts[e], offsets[e] (exclusive prefix sum)
+ * and rows[offsets[e] + r] = r-th slot index i = s + t*n_selected routed to
+ * e, ascending. Bad ids are skipped and flagged in *status. */
+int feml_b200_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
+                        int32_t *counts, int32_t *offsets, int32_t *rows, int32_t *status, void *stream);
+
+/* Per-block int32 sums used by the quantized kernels (for bit-exact
+ * checking): out[(m*N + n)*(K/32) + b] = sum over 32-block b of weight
+ * integer * activation q8 integer; xq = Q8_0 activations, column n at
+ * xq + n*row_size(Q8_0, K). Weight integers: Q8_0 q, Q4_0 nibble-8, Q4_K
+ * nibble. */
+int feml_b200_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *xq, int64_t K, int64_t M,
+                         int64_t N, int32_t *out, void *stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FEML_B200_H */

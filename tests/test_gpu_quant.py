@@ -1,0 +1,151 @@
+"""GPU parity for the quantized mul_mat path.
+
+Bit-exact: the device quantizers (quantize_row_q8_0 on activations, the
+Q8_0/Q4_0/Q4_K weight quantizers) and the per-block int32 sums.
+Within tolerance (|got - want| <= 1e-3 + 1e-4*|want|): mul_mat outputs
+against the oracle's F32 mul_mat on the identically dequantized weights and
+dequantized Q8_0 activations (the reference has no quant kernel, so its F32
+mul_mat on dequantized operands is the parity target)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from feml_b200 import DType
+from feml_b200 import ops
+from oracle import oracle as O
+from tests.conftest import tol_ok
+from tests.gpu_helpers import run_mul_mat, weights
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+QT = {DType.Q8_0: O.DT_Q8_0, DType.Q4_0: O.DT_Q4_0, DType.Q4_K: O.DT_Q4_K}
+
+
+def _inputs(seed, rows, k):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, k)).astype(np.float32)
+    x[0, :32] = 0.0                       # zero block
+    x[0, 32:64] = -0.0
+    x[1 % rows, :32] = np.arange(32, dtype=np.float32) - 15.5   # exact .5 products
+    if rows > 2:
+        x[2, :32] = 7.0                   # constant block
+        x[2, 64:96] = np.where(np.arange(32) % 2 == 0, 3.0, -3.0)
+    return x
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0, DType.Q4_K])
+def test_device_quantizer_bit_exact_golden(b200, dt):
+    gv = np.load(os.path.join(GOLD, "quant_vectors.npz"))
+    x = torch.from_numpy(gv["x"]).cuda()
+    got = ops.quantize(dt, x).cpu().numpy()
+    assert np.array_equal(got, gv[dt.name.lower()])
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0, DType.Q4_K])
+@pytest.mark.parametrize("rows,k,scale", [(7, 256, 1.0), (64, 4096, 0.02), (3, 14336, 3.0), (33, 768, 1e-3)])
+def test_device_quantizer_bit_exact_random(b200, dt, rows, k, scale):
+    x = _inputs(rows * 1000 + k, rows, k) * np.float32(scale)
+    got = ops.quantize(dt, torch.from_numpy(x).cuda()).cpu().numpy()
+    want = O.quantize(QT[dt], x)
+    assert np.array_equal(got, want)
+
+
+def test_quantize_row_q8_0_activations_bit_exact(b200):
+    # the activation quantizer at the decode shape, with a strided source
+    x = _inputs(5, 16, 4096)
+    xt = torch.from_numpy(np.pad(x, ((0, 0), (0, 64)))).cuda()[:, :4096]
+    got = ops.quantize(DType.Q8_0, xt).cpu().numpy()
+    assert np.array_equal(got, O.quantize(O.DT_Q8_0, x))
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0, DType.Q4_K])
+@pytest.mark.parametrize("K,M,N", [(256, 5, 1), (1024, 33, 3), (4096, 64, 2)])
+def test_block_dots_bit_exact(b200, dt, K, M, N):
+    rng = np.random.default_rng(K + M + N)
+    w = weights(rng, M, K, std=0.5)
+    x = _inputs(K, N, K)
+    wq = O.quantize(QT[dt], w)
+    xq = O.quantize(O.DT_Q8_0, x)
+    want, _ = O.block_dots(QT[dt], wq, xq, M, K, N)
+    got = ops.block_dots(dt, torch.from_numpy(wq).cuda(), torch.from_numpy(xq).cuda(), K).cpu().numpy()
+    assert np.array_equal(got, want)
+
+
+SHAPES = [
+    (256, 7, 1), (512, 33, 2), (1024, 130, 3), (4096, 256, 4),     # decode GEMV, fused quantization
+    (8192, 40, 4),                                                  # GEMV with a pre-quantized activation buffer
+    (512, 100, 5), (1024, 64, 8), (256, 300, 16), (2048, 200, 64),  # GEMM path
+    (768, 150, 33), (256, 1, 100), (4096, 257, 128),
+]
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0, DType.Q4_K])
+@pytest.mark.parametrize("K,M,N", SHAPES)
+def test_mul_mat_quant_matches_oracle(b200, dt, K, M, N):
+    rng = np.random.default_rng(K * 7 + M * 3 + N)
+    w = weights(rng, M, K)
+    x = _inputs(K + N, N, K)
+    wq = O.quantize(QT[dt], w)
+    got = run_mul_mat(b200, dt, wq, x, K, M)
+    want = O.mul_mat_quant_ref(QT[dt], wq, x, K)
+    ok, err = tol_ok(got, want)
+    assert ok, f"max abs err {err}"
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0])
+@pytest.mark.parametrize("K,M,N", [(96, 40, 1), (160, 9, 6), (32, 3, 2), (288, 70, 12)])
+def test_mul_mat_ragged_k(b200, dt, K, M, N):
+    # K not a multiple of 256: row bytes not 16-aligned, TMA interior + plain edges
+    rng = np.random.default_rng(K + N)
+    w = weights(rng, M, K, std=1.0)
+    x = _inputs(K, N, K)
+    wq = O.quantize(QT[dt], w)
+    got = run_mul_mat(b200, dt, wq, x, K, M)
+    ok, err = tol_ok(got, O.mul_mat_quant_ref(QT[dt], wq, x, K))
+    assert ok, err
+
+
+@pytest.mark.parametrize("K,M,N", [(16, 8, 32), (4096, 64, 32), (100, 37, 5), (1000, 129, 1), (64, 3, 70)])
+def test_mul_mat_f32_matches_oracle(b200, K, M, N):
+    rng = np.random.default_rng(K + M + N)
+    w = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    x = rng.uniform(-1, 1, (N, K)).astype(np.float32)
+    got = run_mul_mat(b200, DType.F32, w, x, K, M)
+    ok, err = tol_ok(got, O.mul_mat_f32(w, x))
+    assert ok, err
+
+
+def test_kernel_level_entry_matches_graph_path(b200):
+    rng = np.random.default_rng(3)
+    K, M, N = 4096, 300, 6
+    w = weights(rng, M, K)
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    wq = O.quantize(O.DT_Q4_0, w)
+    via_graph = run_mul_mat(b200, DType.Q4_0, wq, x, K, M)
+    via_ops = ops.mul_mat(DType.Q4_0, torch.from_numpy(wq).cuda(), torch.from_numpy(x).cuda(), K)
+    torch.cuda.synchronize()
+    assert np.array_equal(via_ops.cpu().numpy(), via_graph)
+
+
+def test_scaling_by_power_of_two_is_exact(b200):
+    # size-independent property: x -> 4x scales every Q8_0 scale by 4 exactly
+    # and leaves the integers unchanged, so y scales exactly
+    rng = np.random.default_rng(9)
+    K, M, N = 4096, 512, 40
+    wq = O.quantize(O.DT_Q8_0, weights(rng, M, K))
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    y1 = run_mul_mat(b200, DType.Q8_0, wq, x, K, M)
+    y4 = run_mul_mat(b200, DType.Q8_0, wq, x * np.float32(4), K, M)
+    assert np.array_equal(y4, y1 * np.float32(4))
+
+
+def test_repeated_calls_are_deterministic(b200):
+    rng = np.random.default_rng(21)
+    K, M, N = 2048, 1000, 64
+    wq = O.quantize(O.DT_Q4_K, weights(rng, M, K))
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    a = run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
+    b = run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
+    assert np.array_equal(a, b)
