@@ -73,18 +73,29 @@ __device__ __forceinline__ int warp_sum_i(int v) {
     return v;
 }
 
-// quantize_row_q8_0 for one 32-element block held one element per lane:
-// d = amax / 127 (IEEE division), id = 1/d (IEEE reciprocal, 0 when d == 0),
-// q = roundf(x * id) (half away from zero). Returns q for this lane; the
-// f16 bits of d and the block's integer sum come back through the refs.
-__device__ __forceinline__ int quantize_q8_0_lane(float v, uint16_t &d_bits, int &qsum) {
-    const float amax = warp_max(fabsf(v));
+// quantize_row_q8_0 for one 32-element block spread over 8 consecutive lanes
+// (group aligned to 8) holding 4 elements each:
+//   d = amax / 127 (IEEE division), id = 1/d (IEEE reciprocal, 0 when d == 0),
+//   q = roundf(x * id) (half away from zero).
+// Returns the lane's 4 values packed little-endian; the f16 bits of d and the
+// block's integer sum come back through the refs. All 32 lanes must call it.
+__device__ __forceinline__ uint32_t quantize_q8_0_quad(float4 v, uint16_t &d_bits, int &qsum) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
-    const int q = (int)roundf(__fmul_rn(v, id));
+    const int q0 = (int)roundf(__fmul_rn(v.x, id));
+    const int q1 = (int)roundf(__fmul_rn(v.y, id));
+    const int q2 = (int)roundf(__fmul_rn(v.z, id));
+    const int q3 = (int)roundf(__fmul_rn(v.w, id));
+    int s = q0 + q1 + q2 + q3;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     d_bits = __half_as_ushort(__float2half_rn(d));
-    qsum = warp_sum_i(q);
-    return q;
+    qsum = s;
+    return (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+           ((uint32_t)(q3 & 0xff) << 24);
 }
 
 // ---------------------------------------------------------------------------

@@ -1,10 +1,17 @@
-// F32 mul_mat (feml-cpu/src/ops/mul_mat.rs:14-58 semantics):
-//   y[n][m] = sum_k W[m][k] * X[n][k]   (both operands K-contiguous)
-// SIMT FP32 with FMA. Each CTA owns a 32x32 output tile; its 16 warps form
-// four K-slices that each accumulate a partial tile, then the partials are
-// added in slice order in shared memory, so the result does not depend on
-// scheduling. Optional column grouping (mul_mat_id with F32 experts) reuses
-// the routing tables of the quantized path.
+// F32 mul_mat with the reference's rounding, bit for bit
+// (feml-cpu/src/ops/mul_mat.rs:36-57, and feml-cuda's kernel_mul_mat built
+// with fmad=false, feml-cuda/src/backend.rs:42-49):
+//   acc = 0; for k in 0..K: acc = acc + round(a[k, m] * b[k, n])
+// Every output is one sequential chain in k with the product and the sum
+// rounded separately (__fmul_rn / __fadd_rn: no contraction, no reordering),
+// so results equal the reference CPU backend exactly.
+//
+// Tiling: a CTA owns a 32x32 output tile; each of its 128 threads owns a
+// 4 (rows) x 2 (columns) micro-tile, i.e. 8 independent chains (the ILP that
+// hides the add latency). K is walked in 32-wide slabs staged through a
+// two-stage cp.async ring; the weight slab is stored k-major so a thread
+// reads its 4 rows with one 16-byte load. Optional column grouping
+// (mul_mat_id with F32 experts) reuses the routing tables.
 #include <cuda_runtime.h>
 
 #include "../host_common.h"
@@ -16,8 +23,9 @@ namespace fbk {
 namespace {
 
 constexpr int BM = 32, BN = 32, BK = 32;
-constexpr int SLICES = 4, SLICE_THREADS = 128;
-constexpr int THREADS = SLICES * SLICE_THREADS;
+constexpr int THREADS = 128;
+constexpr int AS = BM + 4;  // k-major row strides (floats)
+constexpr int BS = BN + 4;
 
 struct F32Params {
     const uint8_t *w;
@@ -31,128 +39,137 @@ struct F32Params {
     bool grouped;
 };
 
-__global__ void __launch_bounds__(THREADS) gemm_f32_kernel(const F32Params p) {
-    // operand tiles during the K loop; the same bytes hold the partial tiles
-    // for the final reduction
-    constexpr int kTileFloats = SLICES * BK * (BM + 4) + SLICES * BK * (BN + 4);
-    constexpr int kRedFloats = SLICES * BN * (BM + 1);
-    __shared__ __align__(16) float buf[kTileFloats > kRedFloats ? kTileFloats : kRedFloats];
-    auto As = reinterpret_cast<float(*)[BK][BM + 4]>(buf);
-    auto Bs = reinterpret_cast<float(*)[BK][BN + 4]>(buf + SLICES * BK * (BM + 4));
-    auto Red = reinterpret_cast<float(*)[BN][BM + 1]>(buf);
-    __shared__ int col_src[BN];     // activation column per tile column (-1 = none)
-    __shared__ uint64_t col_dst[BN];  // output byte offset per tile column
+__device__ __forceinline__ void cp_async4(float *smem_dst, const float *gsrc, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+                 "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
-    const int slice = threadIdx.x / SLICE_THREADS;
-    const int t = threadIdx.x % SLICE_THREADS;
+__global__ void __launch_bounds__(THREADS) gemm_f32_exact_kernel(const F32Params p) {
+    __shared__ __align__(16) float As[2][BK][AS];
+    __shared__ __align__(16) float Bs[2][BK][BS];
+    __shared__ int col_src[BN];
+    __shared__ uint64_t col_dst[BN];
+
+    const int tid = threadIdx.x;
     const int m0 = blockIdx.x * BM;
-
     const uint8_t *w = p.w;
-    if (threadIdx.x < BN) {
-        const int c = threadIdx.x;
+    int e = 0;
+    if (p.grouped) {
+        while (e < p.g.n_groups && p.g.tile_start[e + 1] <= (int)blockIdx.y) e++;
+        if (e >= p.g.n_groups) return;  // uniform across the CTA
+        w += (uint64_t)e * p.g.w_group_stride;
+    }
+    if (tid < BN) {
         int src = -1;
         uint64_t dst = 0;
         if (!p.grouped) {
-            const int n = blockIdx.y * BN + c;
+            const int n = blockIdx.y * BN + tid;
             if (n < p.N) {
                 src = n;
                 dst = (uint64_t)n * p.y_nb1;
             }
         } else {
-            const int tile = blockIdx.y;
-            int e = 0;
-            while (e < p.g.n_groups && p.g.tile_start[e + 1] <= tile) e++;
-            if (e < p.g.n_groups) {
-                const int j = (tile - p.g.tile_start[e]) * BN + c;
-                if (j < p.g.counts[e]) {
-                    const int slot = p.g.rows[p.g.offsets[e] + j];
-                    const int tok = slot / p.g.n_selected, s = slot % p.g.n_selected;
-                    src = tok;
-                    dst = (uint64_t)s * p.g.dst_nb1 + (uint64_t)tok * p.g.dst_nb2;
-                }
+            const int j = ((int)blockIdx.y - p.g.tile_start[e]) * BN + tid;
+            if (j < p.g.counts[e]) {
+                const int slot = p.g.rows[p.g.offsets[e] + j];
+                const int tok = slot / p.g.n_selected, s = slot % p.g.n_selected;
+                src = tok;
+                dst = (uint64_t)s * p.g.dst_nb1 + (uint64_t)tok * p.g.dst_nb2;
             }
         }
-        col_src[c] = src;
-        col_dst[c] = dst;
-    }
-    if (p.grouped) {
-        const int tile = blockIdx.y;
-        int e = 0;
-        while (e < p.g.n_groups && p.g.tile_start[e + 1] <= tile) e++;
-        if (e >= p.g.n_groups) return;  // uniform across the CTA
-        w += (uint64_t)e * p.g.w_group_stride;
+        col_src[tid] = src;
+        col_dst[tid] = dst;
     }
     __syncthreads();
 
-    // this slice's K range
-    const int kper = (p.K + SLICES - 1) / SLICES;
-    const int kb = slice * kper;
-    const int ke = min(p.K, kb + kper);
-    const int trips = (kper + BK - 1) / BK;
-
-    const int tm = (t % 8) * 4;   // 4 rows
-    const int tn = (t / 8) * 2;   // 2 cols
-    float acc[4][2] = {};
-
-    for (int it = 0; it < trips; it++) {
-        const int k0 = kb + it * BK;
-        // load A: BM rows x BK k, lane -> k (coalesced)
-        for (int i = t; i < BM * BK; i += SLICE_THREADS) {
-            const int kk = i % BK, mm = i / BK;
-            const int m = m0 + mm, k = k0 + kk;
-            float v = 0.0f;
-            if (m < p.M && k < ke) v = reinterpret_cast<const float *>(w + (uint64_t)m * p.w_nb1)[k];
-            As[slice][kk][mm] = v;
+    // per-thread load coordinates: element i = tid + 128*j of a 32x32 slab,
+    // k = i % 32 (coalesced along k), row/col = i / 32
+    auto load = [&](int st, int k0) {
+#pragma unroll
+        for (int j = 0; j < (BM * BK) / THREADS; j++) {
+            const int i = tid + THREADS * j;
+            const int kk = i % BK, r = i / BK;
+            const int k = k0 + kk, m = m0 + r;
+            const bool ok = k < p.K && m < p.M;
+            const float *src = ok ? reinterpret_cast<const float *>(w + (uint64_t)m * p.w_nb1) + k
+                                  : reinterpret_cast<const float *>(w);
+            cp_async4(&As[st][kk][r], src, ok);
         }
-        for (int i = t; i < BN * BK; i += SLICE_THREADS) {
-            const int kk = i % BK, nn = i / BK;
-            const int src = col_src[nn], k = k0 + kk;
-            float v = 0.0f;
-            if (src >= 0 && k < ke) v = reinterpret_cast<const float *>(p.x + (uint64_t)src * p.x_nb1)[k];
-            Bs[slice][kk][nn] = v;
+#pragma unroll
+        for (int j = 0; j < (BN * BK) / THREADS; j++) {
+            const int i = tid + THREADS * j;
+            const int kk = i % BK, c = i / BK;
+            const int k = k0 + kk, s = col_src[c];
+            const bool ok = k < p.K && s >= 0;
+            const float *src = ok ? reinterpret_cast<const float *>(p.x + (uint64_t)s * p.x_nb1) + k
+                                  : reinterpret_cast<const float *>(p.x);
+            cp_async4(&Bs[st][kk][c], src, ok);
+        }
+    };
+
+    const int tm = (tid % 8) * 4;  // rows tm..tm+3
+    const int tn = (tid / 8) * 2;  // cols tn, tn+1
+    float acc[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = 0.0f;
+
+    const int nslab = (p.K + BK - 1) / BK;
+    load(0, 0);
+    cp_commit();
+    for (int sl = 0; sl < nslab; sl++) {
+        const int st = sl & 1;
+        if (sl + 1 < nslab) {
+            load(st ^ 1, (sl + 1) * BK);
+            cp_commit();
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
         }
         __syncthreads();
+        const int kn = min(BK, p.K - sl * BK);  // zero-filled tail must not add (-0 + 0 != -0)
 #pragma unroll 8
-        for (int kk = 0; kk < BK; kk++) {
-            const float4 a = *reinterpret_cast<const float4 *>(&As[slice][kk][tm]);
-            const float2 b = *reinterpret_cast<const float2 *>(&Bs[slice][kk][tn]);
-            acc[0][0] = fmaf(a.x, b.x, acc[0][0]);
-            acc[1][0] = fmaf(a.y, b.x, acc[1][0]);
-            acc[2][0] = fmaf(a.z, b.x, acc[2][0]);
-            acc[3][0] = fmaf(a.w, b.x, acc[3][0]);
-            acc[0][1] = fmaf(a.x, b.y, acc[0][1]);
-            acc[1][1] = fmaf(a.y, b.y, acc[1][1]);
-            acc[2][1] = fmaf(a.z, b.y, acc[2][1]);
-            acc[3][1] = fmaf(a.w, b.y, acc[3][1]);
+        for (int kk = 0; kk < kn; kk++) {
+            const float4 a = *reinterpret_cast<const float4 *>(&As[st][kk][tm]);
+            const float2 b = *reinterpret_cast<const float2 *>(&Bs[st][kk][tn]);
+            acc[0][0] = __fadd_rn(acc[0][0], __fmul_rn(a.x, b.x));
+            acc[1][0] = __fadd_rn(acc[1][0], __fmul_rn(a.y, b.x));
+            acc[2][0] = __fadd_rn(acc[2][0], __fmul_rn(a.z, b.x));
+            acc[3][0] = __fadd_rn(acc[3][0], __fmul_rn(a.w, b.x));
+            acc[0][1] = __fadd_rn(acc[0][1], __fmul_rn(a.x, b.y));
+            acc[1][1] = __fadd_rn(acc[1][1], __fmul_rn(a.y, b.y));
+            acc[2][1] = __fadd_rn(acc[2][1], __fmul_rn(a.z, b.y));
+            acc[3][1] = __fadd_rn(acc[3][1], __fmul_rn(a.w, b.y));
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int j = 0; j < 2; j++) {
+        const int c = tn + j;
+        if (col_src[c] < 0) continue;
+        float *yc = reinterpret_cast<float *>(p.y + col_dst[c]);
 #pragma unroll
-        for (int j = 0; j < 2; j++) Red[slice][tn + j][tm + i] = acc[i][j];
-    __syncthreads();
-    for (int i = threadIdx.x; i < BM * BN; i += THREADS) {
-        const int mm = i % BM, nn = i / BM;
-        const int m = m0 + mm;
-        if (m >= p.M || col_src[nn] < 0) continue;
-        float v = Red[0][nn][mm];
-#pragma unroll
-        for (int s = 1; s < SLICES; s++) v += Red[s][nn][mm];
-        reinterpret_cast<float *>(p.y + col_dst[nn])[m] = v;
+        for (int i = 0; i < 4; i++)
+            if (m0 + tm + i < p.M) yc[m0 + tm + i] = acc[i][j];
     }
 }
 
-}  // namespace
-
-static int launch_f32(const F32Params &p, int tiles_n, cudaStream_t s) {
+int launch_f32(const F32Params &p, int tiles_n, cudaStream_t s) {
     if (p.M == 0 || tiles_n == 0) return FB_OK;
+    if (tiles_n > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "mul_mat f32: too many column tiles");
     dim3 grid((p.M + BM - 1) / BM, tiles_n);
-    gemm_f32_kernel<<<grid, THREADS, 0, s>>>(p);
+    gemm_f32_exact_kernel<<<grid, THREADS, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_f32 launch: %s", cudaGetErrorString(e));
     return FB_OK;
 }
+
+}  // namespace
 
 int launch_gemm_f32(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1, int64_t K,
                     int64_t M, int64_t N, cudaStream_t s) {

@@ -164,18 +164,43 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         for (; issued < min(p.nstage, n_items); issued++) issue(issued);
     issued = __shfl_sync(0xffffffffu, issued, 0);
 
-    // Activations -> Q8_0 in shared memory (overlaps the weight stream).
+    // Activations -> Q8_0 in shared memory (overlaps the weight stream). Every
+    // thread issues all its float4 loads first (one L2 round trip in total),
+    // then 8-lane groups quantize one 32-element block each.
     if (p.xq.qs == nullptr) {
-        for (int t = warp; t < NC * nblk; t += kGemvWarps) {
-            const int n = t / nblk, b = t % nblk;
-            const float v = reinterpret_cast<const float *>(p.x + (uint64_t)n * p.x_nb1)[b * QK + lane];
-            uint16_t dbits;
-            int qsum;
-            const int q = quantize_q8_0_lane(v, dbits, qsum);
-            sq[n * K + b * QK + lane] = (int8_t)q;
-            if (lane == 0) {
-                sd[n * nblk + b] = f16_bits_to_f32(dbits);
-                ss[n * nblk + b] = qsum;
+        constexpr int kBatch = 8;  // float4 loads in flight per thread
+        const int nq = NC * K / 4;  // float4 quads; a block is 8 consecutive quads
+        for (int base = 0; base < nq; base += kGemvThreads * kBatch) {  // uniform trip count
+            const int q0 = base + (int)threadIdx.x;
+            float4 v[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch; j++) {
+                const int q = q0 + j * kGemvThreads;
+                if (q < nq) {
+                    const int n = q / (K / 4), e = (q % (K / 4)) * 4;
+                    const float *xr = reinterpret_cast<const float *>(p.x + (uint64_t)n * p.x_nb1);
+                    v[j] = make_float4(xr[e], xr[e + 1], xr[e + 2], xr[e + 3]);
+                } else {
+                    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kBatch; j++) {
+                // every lane takes part in the group shuffles (padding quads are
+                // zeros); nq is a multiple of 8, so a group is valid or not as a whole
+                const int q = q0 + j * kGemvThreads;
+                uint16_t dbits;
+                int qsum;
+                const uint32_t packed = quantize_q8_0_quad(v[j], dbits, qsum);
+                if (q < nq) {
+                    const int n = q / (K / 4), e = (q % (K / 4)) * 4;
+                    *reinterpret_cast<uint32_t *>(sq + n * K + e) = packed;
+                    if ((threadIdx.x & 7u) == 0) {
+                        const int b = e / QK;
+                        sd[n * nblk + b] = f16_bits_to_f32(dbits);
+                        ss[n * nblk + b] = qsum;
+                    }
+                }
             }
         }
     } else {

@@ -4,6 +4,8 @@
 // _rn intrinsics, so the bytes equal the CPU restatement's bit for bit.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "../host_common.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -14,39 +16,62 @@ namespace {
 
 constexpr int kWarps = 8;
 
-// Q8_0: one warp per 32-element block; lane j owns element j.
-__global__ void __launch_bounds__(kWarps * 32) quantize_q8_0_kernel(const uint8_t *__restrict__ x, uint64_t x_stride,
-                                                                     uint8_t *__restrict__ y, int64_t rows,
-                                                                     int64_t nblk) {
-    const int lane = threadIdx.x & 31;
-    const int64_t total = rows * nblk;
-    for (int64_t i = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); i < total; i += (int64_t)gridDim.x * kWarps) {
-        const int64_t r = i / nblk, b = i % nblk;
-        const float v = reinterpret_cast<const float *>(x + r * x_stride)[b * QK + lane];
+// Q8_0 in ggml layout: the same 8-lanes-per-block routine as the planar and
+// in-GEMV activation quantizers (one implementation of quantize_row_q8_0).
+__global__ void __launch_bounds__(256) quantize_q8_0_kernel(const uint8_t *__restrict__ x, uint64_t x_stride,
+                                                            uint8_t *__restrict__ y, int64_t rows, int64_t k) {
+    const int64_t qpr = k / 4;
+    const int64_t nq = rows * qpr;  // a multiple of 8
+    for (int64_t base = (int64_t)blockIdx.x * 256; base < nq; base += (int64_t)gridDim.x * 256) {
+        const int64_t q = base + threadIdx.x;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        int64_t r = 0, e = 0;
+        if (q < nq) {
+            r = q / qpr;
+            e = (q % qpr) * 4;
+            const float *xr = reinterpret_cast<const float *>(x + r * x_stride);
+            v = make_float4(xr[e], xr[e + 1], xr[e + 2], xr[e + 3]);
+        }
         uint16_t dbits;
         int qsum;
-        const int q = quantize_q8_0_lane(v, dbits, qsum);
-        uint8_t *yb = y + (r * nblk + b) * Q8_0_BYTES;
-        yb[2 + lane] = (uint8_t)(int8_t)q;
-        if (lane == 0) *reinterpret_cast<uint16_t *>(yb) = dbits;
+        const uint32_t packed = quantize_q8_0_quad(v, dbits, qsum);
+        if (q < nq) {
+            uint8_t *yb = y + (r * (k / QK) + e / QK) * Q8_0_BYTES;
+            const int o = (int)(e % QK);
+            // 2-byte-aligned destination: two 16-bit stores
+            *reinterpret_cast<uint16_t *>(yb + 2 + o) = (uint16_t)(packed & 0xffffu);
+            *reinterpret_cast<uint16_t *>(yb + 4 + o) = (uint16_t)(packed >> 16);
+            if ((threadIdx.x & 7u) == 0) *reinterpret_cast<uint16_t *>(yb) = dbits;
+        }
     }
 }
 
-__global__ void __launch_bounds__(kWarps * 32) quantize_q8_planar_kernel(const uint8_t *__restrict__ x, uint64_t x_nb1,
-                                                                          int64_t K, int64_t N, Q8Planar out) {
-    const int lane = threadIdx.x & 31;
+// Planar activations: one float4 quad per thread per pass, 8 lanes per block,
+// so every thread has its load in flight at once.
+__global__ void __launch_bounds__(256) quantize_q8_planar_kernel(const uint8_t *__restrict__ x, uint64_t x_nb1,
+                                                                 int64_t K, int64_t N, Q8Planar out) {
     const int64_t nblk = K / QK;
-    const int64_t total = N * nblk;
-    for (int64_t i = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); i < total; i += (int64_t)gridDim.x * kWarps) {
-        const int64_t n = i / nblk, b = i % nblk;
-        const float v = reinterpret_cast<const float *>(x + n * x_nb1)[b * QK + lane];
+    const int64_t qpr = K / 4;       // quads per column
+    const int64_t nq = N * qpr;      // a multiple of 8: groups never straddle the end
+    for (int64_t base = (int64_t)blockIdx.x * 256; base < nq; base += (int64_t)gridDim.x * 256) {
+        const int64_t q = base + threadIdx.x;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        int64_t n = 0, e = 0;
+        if (q < nq) {
+            n = q / qpr;
+            e = (q % qpr) * 4;
+            const float *xr = reinterpret_cast<const float *>(x + n * x_nb1);
+            v = make_float4(xr[e], xr[e + 1], xr[e + 2], xr[e + 3]);
+        }
         uint16_t dbits;
         int qsum;
-        const int q = quantize_q8_0_lane(v, dbits, qsum);
-        out.qs[n * K + b * QK + lane] = (int8_t)q;
-        if (lane == 0) {
-            out.d[n * nblk + b] = f16_bits_to_f32(dbits);
-            out.sum[n * nblk + b] = qsum;
+        const uint32_t packed = quantize_q8_0_quad(v, dbits, qsum);  // all lanes take part
+        if (q < nq) {
+            *reinterpret_cast<uint32_t *>(out.qs + n * K + e) = packed;
+            if ((threadIdx.x & 7u) == 0) {
+                out.d[n * nblk + e / QK] = f16_bits_to_f32(dbits);
+                out.sum[n * nblk + e / QK] = qsum;
+            }
         }
     }
     // Let a dependent (programmatic) launch start its prologue.
@@ -218,9 +243,10 @@ int launch_quantize_rows(int32_t dtype, const void *x, uint64_t x_row_stride, vo
         if (k % QK) return fb::set_error(FB_ERR_SHAPE, "quantize: k %ld is not a multiple of 32", (long)k);
         if (reinterpret_cast<uintptr_t>(y) & 1) return fb::set_error(FB_ERR_INVALID, "quantize: y must be 2-byte aligned");
         const int64_t nblk = k / QK;
-        if (dtype == WT_Q8_0)
-            quantize_q8_0_kernel<<<grid_for(rows * nblk), kWarps * 32, 0, s>>>(xb, x_row_stride, yb, rows, nblk);
-        else
+        if (dtype == WT_Q8_0) {
+            const int grid = (int)std::min<int64_t>((rows * k / 4 + 255) / 256, (int64_t)sm_count() * 16);
+            quantize_q8_0_kernel<<<grid, 256, 0, s>>>(xb, x_row_stride, yb, rows, k);
+        } else
             quantize_q4_0_kernel<<<grid_for(rows * nblk), kWarps * 32, 0, s>>>(xb, x_row_stride, yb, rows, nblk);
         break;
     }
@@ -249,8 +275,9 @@ int launch_quantize_q8_planar(const void *x, uint64_t x_nb1, int64_t K, int64_t 
     if (N == 0 || K == 0) return FB_OK;
     if ((reinterpret_cast<uintptr_t>(x) & 3) || (x_nb1 & 3))
         return fb::set_error(FB_ERR_INVALID, "quantize_q8_0: activations must be 4-byte aligned");
-    quantize_q8_planar_kernel<<<grid_for(N * (K / QK)), kWarps * 32, 0, s>>>(static_cast<const uint8_t *>(x), x_nb1,
-                                                                              K, N, out);
+    const int64_t nq = N * K / 4;
+    const int grid = (int)std::min<int64_t>((nq + 255) / 256, (int64_t)sm_count() * 16);
+    quantize_q8_planar_kernel<<<grid, 256, 0, s>>>(static_cast<const uint8_t *>(x), x_nb1, K, N, out);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "quantize_q8_0 launch: %s", cudaGetErrorString(e));
     return FB_OK;
