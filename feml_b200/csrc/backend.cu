@@ -82,7 +82,7 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
     if (need > ws_bytes)
         return set_error(FB_ERR_INVALID, "mul_mat: workspace of %lu bytes needed, %lu given", (unsigned long)need,
                          (unsigned long)ws_bytes);
-    if (need == 0) return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, nullptr, status, s, false);
+    if (need == 0) return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, nullptr, status, s, true);
 
     const fbk::Q8Planar xq = fbk::q8_planar_carve(ws, K, N);
     int rc = fbk::launch_quantize_q8_planar(x, x_nb1, K, N, xq, s);

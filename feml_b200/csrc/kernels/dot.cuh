@@ -1,89 +1,217 @@
-// Per-unit integer dot products of ggml weight blocks against Q8_0
-// activations (dp4a). A "unit" is 32 weight elements: one Q8_0 / Q4_0 block
-// or one Q4_K sub-block. The same routines feed the decode GEMV and the
-// block-sum probe used for bit-exact checking.
+// Integer dot products of ggml weight blocks against Q8_0 activations
+// (dp4a), shared by the decode GEMV and the block-sum probe used for
+// bit-exact checking.
+//
+// Work is done in 64-element pairs so that every shared-memory load is
+// aligned:
+//  - Q8_0 / Q4_0: two consecutive 32-element blocks (68 / 36 bytes, 4-byte
+//    aligned when the row is). The odd block's integers are word aligned; the
+//    even block's start 2 bytes into a word, so they are multiplied against a
+//    copy of the activations shifted by 2 bytes with zeros at both ends (the
+//    zero lanes cancel the f16 scale bytes that share those words).
+//  - Q4_K: the two sub-blocks 2g, 2g+1 of a super-block, which share 32
+//    nibble bytes (low nibbles: sub-block 2g, high: 2g+1). High nibbles are
+//    used in place, as 16*h bytes in an unsigned x signed dp4a, and the sum is
+//    divided by 16 (exact: every term is a multiple of 16).
 #pragma once
 
 #include "common.cuh"
 
 namespace fbk {
 
-// Weight integers of one unit packed 4 per 32-bit word (dp4a operands) plus
-// its float scale terms.
-struct Unit {
-    uint32_t q[8];
-    float s0;  // Q8_0/Q4_0: d; Q4_K: d*sc
-    float s1;  // Q4_K: dmin*m (unused otherwise)
-};
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    return __dp4a((int)a, (int)b, c);
+}
+// unsigned bytes of a times signed bytes of b
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 
-template <int WT>
-__device__ __forceinline__ int unit_stride_bytes();
-template <>
-__device__ __forceinline__ int unit_stride_bytes<WT_Q8_0>() { return Q8_0_BYTES; }
-template <>
-__device__ __forceinline__ int unit_stride_bytes<WT_Q4_0>() { return Q4_0_BYTES; }
+// Shifted activation words of one even block, as the pair kernels read them
+// (12 words, 16-byte aligned):
+//   Q8_0: words 0..8  = bytes [0, 0, x0 .. x31, 0, 0]
+//   Q4_0: words 0..4  = bytes [0, 0, x0 .. x15, 0, 0]
+//         words 5..9  = bytes [0, 0, x16 .. x31, 0, 0]
+constexpr int kShiftWords = 12;
 
-// `row` points at the first byte of a weight row (2-byte aligned); u is the
-// unit index within the row.
+// Builds the shifted words from the block's 8 packed activation words.
 template <int WT>
-__device__ __forceinline__ void load_unit(const uint8_t *row, int u, Unit &U) {
+__device__ __forceinline__ void make_shifted(const uint32_t (&w)[8], uint32_t (&s)[kShiftWords]) {
+#pragma unroll
+    for (int i = 0; i < kShiftWords; i++) s[i] = 0;
     if constexpr (WT == WT_Q8_0) {
-        const uint8_t *blk = row + Q8_0_BYTES * u;
-        U.s0 = f16_bits_to_f32(ld_u16(blk));
-        U.s1 = 0.0f;
-        ld_words_a2<8>(blk + 2, U.q);
-    } else if constexpr (WT == WT_Q4_0) {
-        const uint8_t *blk = row + Q4_0_BYTES * u;
-        U.s0 = f16_bits_to_f32(ld_u16(blk));
-        U.s1 = 0.0f;
-        uint32_t w[4];
-        ld_words_a2<4>(blk + 2, w);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            U.q[i] = w[i] & 0x0f0f0f0fu;            // elements 4i..4i+3 (low nibbles)
-            U.q[4 + i] = (w[i] >> 4) & 0x0f0f0f0fu;  // elements 16+4i.. (high nibbles)
+        for (int k = 0; k <= 8; k++) s[k] = __funnelshift_r(k > 0 ? w[k - 1] : 0u, k < 8 ? w[k] : 0u, 16);
+    } else {
+#pragma unroll
+        for (int k = 0; k <= 4; k++) {
+            s[k] = __funnelshift_r(k > 0 ? w[k - 1] : 0u, k < 4 ? w[k] : 0u, 16);
+            s[5 + k] = __funnelshift_r(k > 0 ? w[3 + k] : 0u, k < 4 ? w[4 + k] : 0u, 16);
         }
-    } else {  // Q4_K: sub-block j of super-block u/8
-        const int j = u & 7;
-        const uint8_t *sb = row + Q4_K_BYTES * (u >> 3);
-        const float d = f16_bits_to_f32(ld_u16(sb));
-        const float dmin = f16_bits_to_f32(ld_u16(sb + 2));
-        int sc, m;
-        q4k_scale_min(j, sb + 4, sc, m);
-        U.s0 = d * (float)sc;
-        U.s1 = dmin * (float)m;
-        uint32_t w[8];
-        ld_words_a2<8>(sb + 16 + 32 * (j >> 1), w);
-        const uint32_t sh = 4u * (uint32_t)(j & 1);
-#pragma unroll
-        for (int i = 0; i < 8; i++) U.q[i] = (w[i] >> sh) & 0x0f0f0f0fu;
     }
 }
 
-// Integer block sum: Q8_0 sum q_w*q_x; Q4_0 sum (nibble-8)*q_x; Q4_K sum nibble*q_x.
+// Block-pair integer sums. `wp` is the pair's first byte (4-byte aligned);
+// `xe` the even block's shifted words, `xo` the odd block's 8 words; xsum_*
+// the activation block sums (Q4_0 offset). Returns sums s0 (even block),
+// s1 (odd block) and the blocks' f16 scales as f32.
 template <int WT>
-__device__ __forceinline__ int unit_sumi(const Unit &U, const int4 x0, const int4 x1, int xsum) {
+__device__ __forceinline__ void pair_dot(const uint32_t *wp, const uint32_t *xe, const uint32_t *xo, int xsum0,
+                                         int xsum1, int &s0, int &s1, float &d0, float &d1) {
+    if constexpr (WT == WT_Q8_0) {
+        uint32_t w[17];
+#pragma unroll
+        for (int i = 0; i < 17; i++) w[i] = wp[i];
+        const uint4 e0 = *reinterpret_cast<const uint4 *>(xe);
+        const uint4 e1 = *reinterpret_cast<const uint4 *>(xe + 4);
+        const uint32_t e8 = xe[8];
+        const uint4 o0 = *reinterpret_cast<const uint4 *>(xo);
+        const uint4 o1 = *reinterpret_cast<const uint4 *>(xo + 4);
+        // four independent chains (even lo/hi, odd lo/hi) for ILP
+        int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+        a0 = dp4a_ss(w[0], e0.x, a0);
+        a1 = dp4a_ss(w[1], e0.y, a1);
+        b0 = dp4a_ss(w[9], o0.x, b0);
+        b1 = dp4a_ss(w[10], o0.y, b1);
+        a0 = dp4a_ss(w[2], e0.z, a0);
+        a1 = dp4a_ss(w[3], e0.w, a1);
+        b0 = dp4a_ss(w[11], o0.z, b0);
+        b1 = dp4a_ss(w[12], o0.w, b1);
+        a0 = dp4a_ss(w[4], e1.x, a0);
+        a1 = dp4a_ss(w[5], e1.y, a1);
+        b0 = dp4a_ss(w[13], o1.x, b0);
+        b1 = dp4a_ss(w[14], o1.y, b1);
+        a0 = dp4a_ss(w[6], e1.z, a0);
+        a1 = dp4a_ss(w[7], e1.w, a1);
+        b0 = dp4a_ss(w[15], o1.z, b0);
+        b1 = dp4a_ss(w[16], o1.w, b1);
+        a0 = dp4a_ss(w[8], e8, a0);
+        const int a = a0 + a1, b = b0 + b1;
+        s0 = a;
+        s1 = b;
+        d0 = f16_bits_to_f32((uint16_t)(w[0] & 0xffffu));
+        d1 = f16_bits_to_f32((uint16_t)(w[8] >> 16));
+    } else {  // Q4_0: 36 bytes
+        uint32_t w[9];
+#pragma unroll
+        for (int i = 0; i < 9; i++) w[i] = wp[i];
+        const uint4 e0 = *reinterpret_cast<const uint4 *>(xe);
+        const uint4 e1 = *reinterpret_cast<const uint4 *>(xe + 4);
+        const uint2 e2 = *reinterpret_cast<const uint2 *>(xe + 8);
+        const uint4 o0 = *reinterpret_cast<const uint4 *>(xo);
+        const uint4 o1 = *reinterpret_cast<const uint4 *>(xo + 4);
+        const uint32_t lo = 0x0f0f0f0fu, hi = 0xf0f0f0f0u;
+        // even block: low nibbles vs shifted x0..15 (words 0..4), high vs x16..31 (words 5..9)
+        int el = 0, eh = 0;
+        el = dp4a_ss(w[0] & lo, e0.x, el);
+        el = dp4a_ss(w[1] & lo, e0.y, el);
+        el = dp4a_ss(w[2] & lo, e0.z, el);
+        el = dp4a_ss(w[3] & lo, e0.w, el);
+        el = dp4a_ss(w[4] & lo, e1.x, el);
+        eh = dp4a_us(w[0] & hi, e1.y, eh);
+        eh = dp4a_us(w[1] & hi, e1.z, eh);
+        eh = dp4a_us(w[2] & hi, e1.w, eh);
+        eh = dp4a_us(w[3] & hi, e2.x, eh);
+        eh = dp4a_us(w[4] & hi, e2.y, eh);
+        // odd block: words 5..8
+        int ol = 0, oh = 0;
+        ol = dp4a_ss(w[5] & lo, o0.x, ol);
+        ol = dp4a_ss(w[6] & lo, o0.y, ol);
+        ol = dp4a_ss(w[7] & lo, o0.z, ol);
+        ol = dp4a_ss(w[8] & lo, o0.w, ol);
+        oh = dp4a_us(w[5] & hi, o1.x, oh);
+        oh = dp4a_us(w[6] & hi, o1.y, oh);
+        oh = dp4a_us(w[7] & hi, o1.z, oh);
+        oh = dp4a_us(w[8] & hi, o1.w, oh);
+        s0 = el + (eh >> 4) - 8 * xsum0;
+        s1 = ol + (oh >> 4) - 8 * xsum1;
+        d0 = f16_bits_to_f32((uint16_t)(w[0] & 0xffffu));
+        d1 = f16_bits_to_f32((uint16_t)(w[4] >> 16));
+    }
+}
+
+// One even block with no odd partner (odd block count): Q8_0 / Q4_0 sums
+// against the shifted activations (the bytes after the block meet the zero
+// padding).
+template <int WT>
+__device__ __forceinline__ int single_even_dot(const uint32_t *wp, const uint32_t *xe, int xsum, float &d) {
     int s = 0;
-    s = __dp4a((int)U.q[0], x0.x, s);
-    s = __dp4a((int)U.q[1], x0.y, s);
-    s = __dp4a((int)U.q[2], x0.z, s);
-    s = __dp4a((int)U.q[3], x0.w, s);
-    s = __dp4a((int)U.q[4], x1.x, s);
-    s = __dp4a((int)U.q[5], x1.y, s);
-    s = __dp4a((int)U.q[6], x1.z, s);
-    s = __dp4a((int)U.q[7], x1.w, s);
-    if constexpr (WT == WT_Q4_0) s -= 8 * xsum;
+    if constexpr (WT == WT_Q8_0) {
+#pragma unroll
+        for (int i = 0; i < 9; i++) s = dp4a_ss(wp[i], xe[i], s);
+    } else {
+        int l = 0, h = 0;
+#pragma unroll
+        for (int i = 0; i < 5; i++) {
+            l = dp4a_ss(wp[i] & 0x0f0f0f0fu, xe[i], l);
+            h = dp4a_us(wp[i] & 0xf0f0f0f0u, xe[5 + i], h);
+        }
+        s = l + (h >> 4) - 8 * xsum;
+    }
+    d = f16_bits_to_f32((uint16_t)(wp[0] & 0xffffu));
     return s;
 }
 
-// Contribution of one unit to y: Q8_0/Q4_0 d_w*d_x*sumi;
-// Q4_K d_x*(d*sc*sumi - dmin*m*xsum).
-template <int WT>
-__device__ __forceinline__ float unit_scale(const Unit &U, int sumi, float dx, int xsum) {
-    if constexpr (WT == WT_Q4_K)
-        return dx * (U.s0 * (float)sumi - U.s1 * (float)xsum);
-    else
-        return (U.s0 * dx) * (float)sumi;
+// Q4_K sub-block pair g (0..3) of the super-block at `sb` (16-byte aligned):
+// integer sums s0 (sub-block 2g, low nibbles), s1 (sub-block 2g+1, high
+// nibbles) and the scale terms d*sc, dmin*m of both.
+__device__ __forceinline__ void q4k_pair_dot(const uint8_t *sb, int g, const uint32_t *xa, const uint32_t *xb,
+                                             int &s0, int &s1, float &dsc0, float &dmm0, float &dsc1, float &dmm1) {
+    const uint4 h = *reinterpret_cast<const uint4 *>(sb);
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(sb + 16 + 32 * g);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(sb + 32 + 32 * g);
+    const uint4 a0 = *reinterpret_cast<const uint4 *>(xa);
+    const uint4 a1 = *reinterpret_cast<const uint4 *>(xa + 4);
+    const uint4 b0 = *reinterpret_cast<const uint4 *>(xb);
+    const uint4 b1 = *reinterpret_cast<const uint4 *>(xb + 4);
+    const uint32_t lo = 0x0f0f0f0fu, hi = 0xf0f0f0f0u;
+    int l0 = 0, l1 = 0, u0 = 0, u1 = 0;  // independent chains for ILP
+    l0 = dp4a_ss(q0.x & lo, a0.x, l0);
+    l1 = dp4a_ss(q0.y & lo, a0.y, l1);
+    u0 = dp4a_us(q0.x & hi, b0.x, u0);
+    u1 = dp4a_us(q0.y & hi, b0.y, u1);
+    l0 = dp4a_ss(q0.z & lo, a0.z, l0);
+    l1 = dp4a_ss(q0.w & lo, a0.w, l1);
+    u0 = dp4a_us(q0.z & hi, b0.z, u0);
+    u1 = dp4a_us(q0.w & hi, b0.w, u1);
+    l0 = dp4a_ss(q1.x & lo, a1.x, l0);
+    l1 = dp4a_ss(q1.y & lo, a1.y, l1);
+    u0 = dp4a_us(q1.x & hi, b1.x, u0);
+    u1 = dp4a_us(q1.y & hi, b1.y, u1);
+    l0 = dp4a_ss(q1.z & lo, a1.z, l0);
+    l1 = dp4a_ss(q1.w & lo, a1.w, l1);
+    u0 = dp4a_us(q1.z & hi, b1.z, u0);
+    u1 = dp4a_us(q1.w & hi, b1.w, u1);
+    const int l = l0 + l1, u = u0 + u1;
+    s0 = l;
+    s1 = u >> 4;
+    // 6-bit (scale, min) pairs j0 = 2g, j1 = 2g+1 (public ggml get_scale_min_k4
+    // layout) from scale bytes 0..11 = words h.y, h.z, h.w
+    auto byte = [&](int j) -> int {
+        const uint32_t w = (j >> 2) == 0 ? h.y : ((j >> 2) == 1 ? h.z : h.w);
+        return (int)((w >> (8 * (j & 3))) & 0xffu);
+    };
+    int sc0, m0, sc1, m1;
+    const int j0 = 2 * g, j1 = 2 * g + 1;
+    if (g < 2) {
+        sc0 = byte(j0) & 63;
+        m0 = byte(j0 + 4) & 63;
+        sc1 = byte(j1) & 63;
+        m1 = byte(j1 + 4) & 63;
+    } else {
+        sc0 = (byte(j0 + 4) & 0x0f) | ((byte(j0 - 4) >> 6) << 4);
+        m0 = (byte(j0 + 4) >> 4) | ((byte(j0) >> 6) << 4);
+        sc1 = (byte(j1 + 4) & 0x0f) | ((byte(j1 - 4) >> 6) << 4);
+        m1 = (byte(j1 + 4) >> 4) | ((byte(j1) >> 6) << 4);
+    }
+    const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
+    const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+    dsc0 = d * (float)sc0;
+    dmm0 = dmin * (float)m0;
+    dsc1 = d * (float)sc1;
+    dmm1 = dmin * (float)m1;
 }
 
 }  // namespace fbk

@@ -331,44 +331,60 @@ int launch_wt(const GemmQParams &p, int tiles_n, cudaStream_t s) {
     return launch_bm<WT, 32>(p, tiles_n, s);
 }
 
-// One thread per (m, n, block): the same unit loaders as the decode GEMV,
-// reading ggml bytes from global memory with byte-exact bounds.
+// One thread per (m, n, 64-element pair): the pair routines of the decode
+// GEMV, on copies of the pair's bytes in an aligned local buffer (so nothing
+// is read past the tensors' ends).
 template <int WT>
 __global__ void block_dots_kernel(const uint8_t *w, uint64_t w_nb1, const uint8_t *xq, int K, int M, int N,
                                   int32_t *out) {
-    const int nblk = K / QK;
-    const int64_t total = (int64_t)M * N * nblk;
+    const int nblk = K / QK, npair = (nblk + 1) / 2;
+    const int64_t total = (int64_t)M * N * npair;
     const uint64_t xrow = (uint64_t)nblk * Q8_0_BYTES;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int b = (int)(i % nblk);
-        const int64_t mn = i / nblk;
+        const int pr = (int)(i % npair);
+        const int64_t mn = i / npair;
         const int n = (int)(mn % N), m = (int)(mn / N);
-        // activation block: copy to an aligned local array (no over-read)
-        const uint8_t *xb = xq + (uint64_t)n * xrow + (uint64_t)b * Q8_0_BYTES + 2;
-        int8_t xl[32];
-        int xsum = 0;
-#pragma unroll
-        for (int l = 0; l < 32; l++) {
-            xl[l] = (int8_t)xb[l];
-            xsum += xl[l];
+        const int b0 = 2 * pr;
+        const bool single = b0 + 1 >= nblk;
+        // activation blocks b0, b0+1 as packed words, their sums, the shifted form
+        uint32_t xw[2][8];
+        int xs[2] = {0, 0};
+        for (int k = 0; k < 2; k++) {
+            const int b = b0 + k;
+            for (int l = 0; l < 8; l++) xw[k][l] = 0;
+            if (b >= nblk) continue;
+            const uint8_t *xb = xq + (uint64_t)n * xrow + (uint64_t)b * Q8_0_BYTES + 2;
+            for (int l = 0; l < 32; l++) {
+                xw[k][l / 4] |= (uint32_t)xb[l] << (8 * (l % 4));
+                xs[k] += (int8_t)xb[l];
+            }
         }
-        const int4 *xv = reinterpret_cast<const int4 *>(xl);
-        // weight unit: copy its bytes to a local aligned buffer first
         const uint8_t *row = w + (uint64_t)m * w_nb1;
-        Unit U;
+        int s0 = 0, s1 = 0;
         if constexpr (WT == WT_Q4_K) {
-            __align__(16) uint8_t sbuf[Q4_K_BYTES + 4];
-            const uint8_t *sbp = row + (uint64_t)(b >> 3) * Q4_K_BYTES;
+            __align__(16) uint8_t sbuf[Q4_K_BYTES];
+            const uint8_t *sbp = row + (uint64_t)(b0 / 8) * Q4_K_BYTES;
             for (int l = 0; l < Q4_K_BYTES; l++) sbuf[l] = sbp[l];
-            load_unit<WT>(sbuf, b & 7, U);
+            float a, b, c, d;
+            q4k_pair_dot(sbuf, (b0 % 8) / 2, xw[0], xw[1], s0, s1, a, b, c, d);
         } else {
             constexpr int UBY = WT == WT_Q8_0 ? Q8_0_BYTES : Q4_0_BYTES;
-            __align__(16) uint8_t ubuf[UBY + 6];
-            const uint8_t *up = row + (uint64_t)b * UBY;
-            for (int l = 0; l < UBY; l++) ubuf[l] = up[l];
-            load_unit<WT>(ubuf, 0, U);
+            __align__(16) uint32_t wbuf[(2 * UBY + 4 + 3) / 4];
+            uint8_t *wb8 = reinterpret_cast<uint8_t *>(wbuf);
+            const uint8_t *up = row + (uint64_t)b0 * UBY;
+            const int nb = single ? UBY : 2 * UBY;
+            for (int l = 0; l < (int)sizeof(wbuf); l++) wb8[l] = l < nb ? up[l] : 0;
+            uint32_t sh[kShiftWords];
+            make_shifted<WT>(xw[0], sh);
+            float d0, d1;
+            if (single)
+                s0 = single_even_dot<WT>(wbuf, sh, xs[0], d0);
+            else
+                pair_dot<WT>(wbuf, sh, xw[1], xs[0], xs[1], s0, s1, d0, d1);
         }
-        out[i] = unit_sumi<WT>(U, xv[0], xv[1], xsum);
+        int32_t *o = out + ((int64_t)m * N + n) * nblk + b0;
+        o[0] = s0;
+        if (!single) o[1] = s1;
     }
 }
 
@@ -421,7 +437,7 @@ int launch_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *
                       int32_t *out, cudaStream_t s) {
     if (K % (wtype == WT_Q4_K ? QKK : QK)) return fb::set_error(FB_ERR_SHAPE, "block_dots: K not a block multiple");
     if (M * N * (K / QK) == 0) return FB_OK;
-    const int64_t total = M * N * (K / QK);
+    const int64_t total = M * N * ((K / QK + 1) / 2);
     const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 32);
     const auto *wb = static_cast<const uint8_t *>(w);
     const auto *xb = static_cast<const uint8_t *>(xq);

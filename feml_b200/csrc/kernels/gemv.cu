@@ -4,22 +4,24 @@
 // matching Q8_0 activation block (dp4a), scale = d_w * d_x (Q8_0, Q4_0) or
 // d_x * (d*sc, dmin*m terms) for Q4_K sub-blocks.
 //
-// B200 mapping. The kernel is HBM-bound (weights are read once), so it is
-// built to keep as many weight bytes in flight as possible:
-//  - one CTA per SM, each owning a contiguous range of weight rows;
-//  - every warp owns its rows and a private ring of shared-memory stages;
-//    lane 0 streams row chunks with cp.async.bulk (TMA, evict-first L2 policy)
-//    completing on per-stage mbarriers, and re-arms a stage as soon as the
-//    warp has consumed it, so a warp has `nstage` chunks in flight at once;
-//  - activations are quantized to Q8_0 into shared memory by the CTA itself
-//    while the first weight chunks are in flight (no workspace), or read from
-//    a planar buffer written by a preceding quantize kernel launched with
-//    programmatic dependent launch, so the weight stream starts before the
-//    activation quantizer finishes;
-//  - ggml blocks keep their 2-byte alignment in shared memory; 32-bit words
-//    are assembled with funnel shifts. Row chunks whose global address is not
-//    16-byte aligned are copied in their aligned interior by TMA and their
-//    ragged head/tail bytes by plain loads.
+// B200 mapping. The kernel is HBM-bound (weights are read once):
+//  - one CTA per SM with at most ~100 KB of shared memory, so the CTA of the
+//    next launch fits beside it; launches are chained with programmatic
+//    dependent launch (PDL): a CTA streams its weights before waiting for the
+//    preceding grid, so the weight stream of launch i+1 overlaps launch i;
+//    activations are read and outputs written only after that wait;
+//  - every warp owns a contiguous share of the CTA's rows and a private ring of
+//    shared-memory stages; lane 0 streams row chunks with cp.async.bulk (TMA,
+//    L2 evict-first) completing on per-stage mbarriers (bounded waits) and
+//    re-arms a stage as soon as the warp has consumed it;
+//  - activations are quantized to Q8_0 into shared memory by the CTA (one
+//    thread per 32-element block), or copied from a planar buffer written by a
+//    preceding quantize kernel (large N*K);
+//  - the dot products run on 64-element pairs with aligned shared-memory loads
+//    (kernels/dot.cuh);
+//  - rows whose bytes are not 4-byte (Q4_K: 16-byte) aligned are copied into
+//    the stage with plain loads instead of TMA; rows that are aligned but not
+//    16-byte aligned get their ragged head/tail bytes by plain loads.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -37,21 +39,26 @@ constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kMaxCols = 4;
 constexpr int kSmemLimit = 227 * 1024;
-constexpr int kFusedMaxElems = 16384;  // N*K up to which each CTA quantizes x itself
+constexpr int kFusedMaxElems = 16384;            // N*K up to which each CTA quantizes x itself
+constexpr uint32_t kCoResidentCta = 100 * 1024;  // per-CTA smem that leaves room for the next launch
+constexpr uint32_t kCoResidentActs = 40 * 1024;  // activation bytes up to which that budget is used
 
 template <int WT>
 struct Fmt;
 template <>
 struct Fmt<WT_Q8_0> {
     static constexpr int kUnitBytes = Q8_0_BYTES;  // one 32-element block
+    static constexpr bool kShifted = true;
 };
 template <>
 struct Fmt<WT_Q4_0> {
     static constexpr int kUnitBytes = Q4_0_BYTES;
+    static constexpr bool kShifted = true;
 };
 template <>
 struct Fmt<WT_Q4_K> {
     static constexpr int kUnitBytes = Q4_K_BYTES / 8;  // one 32-element sub-block
+    static constexpr bool kShifted = false;
 };
 
 struct GemvParams {
@@ -67,40 +74,105 @@ struct GemvParams {
     int chunk_units;  // 32-element units per chunk (multiple of 8)
     int nstage;       // ring stages per warp
     uint32_t stage_bytes;
-    Q8Planar xq;  // xq.qs == nullptr: quantize in-kernel
+    Q8Planar xq;      // xq.qs == nullptr: quantize in-kernel
     int32_t *status;
+    bool x_vec16;     // activation columns are 16-byte aligned
+    bool copy_rows;   // rows not aligned for the pair loads: plain copies
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t v) { return (v + 15u) & ~15u; }
 
 struct SmemLayout {
-    uint32_t bars, qs, d, sum, ring, total;
+    uint32_t bars, qs, sx2, d, sum, ring, total;
 };
 
-__host__ __device__ inline SmemLayout smem_layout(int K, int ncols, int nstage, uint32_t stage_bytes) {
+__host__ __device__ inline SmemLayout smem_layout(int K, int ncols, bool shifted, int nstage, uint32_t stage_bytes) {
     SmemLayout L;
     const uint32_t nblk = (uint32_t)K / QK;
     L.bars = 0;
     L.qs = align16(kGemvWarps * nstage * 8);
-    L.d = L.qs + align16((uint32_t)ncols * K);
-    L.sum = L.d + align16(ncols * nblk * 4);
-    L.ring = (L.sum + align16(ncols * nblk * 4) + 127u) & ~127u;
+    L.sx2 = L.qs + align16((uint32_t)ncols * K);
+    const uint32_t nbp = (nblk + 1) & ~1u;  // per-column stride of d/sum, even so pairs load as float2/int2
+    L.d = L.sx2 + (shifted ? (uint32_t)ncols * ((nblk + 1) / 2) * kShiftWords * 4 : 0u);
+    L.sum = L.d + align16(ncols * nbp * 4);
+    L.ring = (L.sum + align16(ncols * nbp * 4) + 127u) & ~127u;
     L.total = L.ring + (uint32_t)kGemvWarps * nstage * stage_bytes;
     return L;
 }
 
-// One 32-element unit against NC activation columns, accumulated into acc[n].
-template <int WT, int NC>
-__device__ __forceinline__ void dot_unit(const uint8_t *p0, int u, int b, const int8_t *sq, const float *sd,
-                                         const int32_t *ss, int K, int nblk, float (&acc)[kMaxCols]) {
-    Unit U;
-    load_unit<WT>(p0, u, U);
+// Quantize one 32-element activation block with 4 lanes (an aligned lane
+// group), 8 elements per lane: the same operations as quantize_q8_0_quad
+// (d = amax/127, id = 1/d, q = roundf(x*id)). Writes the block's packed
+// integers, f16-rounded scale and integer sum, and for even blocks of Q8_0 /
+// Q4_0 the shifted copy read by the pair kernels. All 32 lanes of the warp
+// must call it (`valid` false for padding groups).
+template <int WT>
+__device__ __forceinline__ void quantize_block_quarter(const float *xb, bool vec, bool valid, bool even, int8_t *sq_blk,
+                                                       uint32_t *sx2_blk, float *sd_b, int32_t *ss_b) {
+    const int t = threadIdx.x & 3;  // quarter of the block
+    float v[8];
+    if (valid) {
+        const float *xe = xb + 8 * t;
+        if (vec) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(xe));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(xe) + 1);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
 #pragma unroll
-    for (int n = 0; n < NC; n++) {
-        const int4 *xv = reinterpret_cast<const int4 *>(sq + n * K + b * QK);
-        const int xsum = ss[n * nblk + b];
-        const int s = unit_sumi<WT>(U, xv[0], xv[1], xsum);
-        acc[n] += unit_scale<WT>(U, s, sd[n * nblk + b], xsum);
+            for (int i = 0; i < 8; i++) v[i] = __ldg(xe + i);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = 0.0f;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    uint32_t w[2];
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int q0 = (int)roundf(__fmul_rn(v[4 * k], id));
+        const int q1 = (int)roundf(__fmul_rn(v[4 * k + 1], id));
+        const int q2 = (int)roundf(__fmul_rn(v[4 * k + 2], id));
+        const int q3 = (int)roundf(__fmul_rn(v[4 * k + 3], id));
+        s += q0 + q1 + q2 + q3;
+        w[k] = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+               ((uint32_t)(q3 & 0xff) << 24);
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    // the word just before this lane's pair (lane t-1's second word)
+    const uint32_t prev = __shfl_up_sync(0xffffffffu, w[1], 1);
+    if (!valid) return;
+    reinterpret_cast<uint2 *>(sq_blk)[t] = make_uint2(w[0], w[1]);
+    if (t == 0) {
+        *sd_b = f16_bits_to_f32(__half_as_ushort(__float2half_rn(d)));
+        *ss_b = s;
+    }
+    if constexpr (WT != WT_Q4_K) {
+        if (even) {
+            // byte stream shifted by 2 with zeros at the ends (see make_shifted)
+            if constexpr (WT == WT_Q8_0) {
+                const uint32_t pw = t == 0 ? 0u : prev;
+                sx2_blk[2 * t] = __funnelshift_r(pw, w[0], 16);
+                sx2_blk[2 * t + 1] = __funnelshift_r(w[0], w[1], 16);
+                if (t == 3) sx2_blk[8] = w[1] >> 16;
+            } else {
+                // low nibble half: words 0..3 -> shifted words 0..4; high half: 4..7 -> 5..9
+                const uint32_t pw = (t == 0 || t == 2) ? 0u : prev;
+                const int o = t < 2 ? 2 * t : 5 + 2 * (t - 2);
+                sx2_blk[o] = __funnelshift_r(pw, w[0], 16);
+                sx2_blk[o + 1] = __funnelshift_r(w[0], w[1], 16);
+                if (t == 1) sx2_blk[4] = w[1] >> 16;
+                if (t == 3) sx2_blk[9] = w[1] >> 16;
+            }
+        }
     }
 }
 
@@ -108,29 +180,31 @@ template <int WT, int NC>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int UB = Fmt<WT>::kUnitBytes;
+    constexpr bool SH = Fmt<WT>::kShifted;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int K = p.K, nblk = K / QK;
-    const SmemLayout L = smem_layout(K, NC, p.nstage, p.stage_bytes);
+    const int K = p.K, nblk = K / QK, npair_blk = (nblk + 1) / 2, nbp = 2 * npair_blk;
+    const SmemLayout L = smem_layout(K, NC, SH, p.nstage, p.stage_bytes);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * p.nstage;
     int8_t *sq = reinterpret_cast<int8_t *>(smem + L.qs);
+    uint32_t *sx2 = reinterpret_cast<uint32_t *>(smem + L.sx2);
     float *sd = reinterpret_cast<float *>(smem + L.d);
     int32_t *ss = reinterpret_cast<int32_t *>(smem + L.sum);
     uint8_t *ring = smem + L.ring + (uint32_t)warp * p.nstage * p.stage_bytes;
 
+    // rows of this CTA, then a contiguous share per warp
     const int r_begin = (int)((int64_t)blockIdx.x * p.M / gridDim.x);
     const int r_end = (int)((int64_t)(blockIdx.x + 1) * p.M / gridDim.x);
     const int cta_rows = r_end - r_begin;
-    const int my_rows = cta_rows > warp ? (cta_rows - warp + kGemvWarps - 1) / kGemvWarps : 0;
-    const int n_items = my_rows * p.nchunks;
+    const int w_begin = r_begin + cta_rows * warp / kGemvWarps;
+    const int w_end = r_begin + cta_rows * (warp + 1) / kGemvWarps;
+    const int n_items = (w_end - w_begin) * p.nchunks;
     const uint32_t chunk_bytes = (uint32_t)p.chunk_units * UB;
-    const uint32_t row_units = (uint32_t)nblk;
 
-    // Item i of this warp = (row, chunk); its global byte range.
     auto item_range = [&](int i, uintptr_t &start, uint32_t &len, int &row, int &c) {
-        row = r_begin + warp + (i / p.nchunks) * kGemvWarps;
+        row = w_begin + i / p.nchunks;
         c = i % p.nchunks;
         const uint32_t u0 = (uint32_t)c * p.chunk_units;
-        const uint32_t nu = min((uint32_t)p.chunk_units, row_units - u0);
+        const uint32_t nu = min((uint32_t)p.chunk_units, (uint32_t)nblk - u0);
         start = reinterpret_cast<uintptr_t>(p.w + (uint64_t)row * p.w_nb1 + (uint64_t)c * chunk_bytes);
         len = nu * UB;
     };
@@ -141,12 +215,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         uint32_t len;
         int row, c;
         item_range(i, start, len, row, c);
+        uint64_t *bar = &bars[i % p.nstage];
         const uintptr_t base = start & ~uintptr_t(15);
         const uintptr_t a = (start + 15) & ~uintptr_t(15);
         const uintptr_t e = (start + len) & ~uintptr_t(15);
-        uint64_t *bar = &bars[i % p.nstage];
-        uint8_t *dst = ring + (uint32_t)(i % p.nstage) * p.stage_bytes;
-        if (e > a) {
+        if (!p.copy_rows && e > a) {
+            uint8_t *dst = ring + (uint32_t)(i % p.nstage) * p.stage_bytes;
             mbar_arrive_expect_tx(bar, (uint32_t)(e - a));
             bulk_g2s_evict_first(dst + (a - base), reinterpret_cast<const void *>(a), (uint32_t)(e - a), bar, policy);
         } else {
@@ -159,58 +233,65 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         fence_barrier_init();
     }
     __syncwarp();
+    // Weight prefetch: every ring stage is issued before the dependency wait
+    // (weights are never written by the kernels this one waits for).
     int issued = 0;
-    if (lane == 0)
+    if (lane == 0) {
         for (; issued < min(p.nstage, n_items); issued++) issue(issued);
+        // rows beyond the ring go to L2 now, so the refills after the wait hit L2
+        if (!p.copy_rows)
+            for (int i = issued; i < n_items; i++) {
+                uintptr_t start;
+                uint32_t len;
+                int row, c;
+                item_range(i, start, len, row, c);
+                const uintptr_t a = (start + 15) & ~uintptr_t(15), e = (start + len) & ~uintptr_t(15);
+                if (e > a) bulk_prefetch_l2(reinterpret_cast<const void *>(a), (uint32_t)(e - a));
+            }
+    }
     issued = __shfl_sync(0xffffffffu, issued, 0);
 
-    // Activations -> Q8_0 in shared memory (overlaps the weight stream). Every
-    // thread issues all its float4 loads first (one L2 round trip in total),
-    // then 8-lane groups quantize one 32-element block each.
+    grid_launch_dependents();
+    grid_dependency_wait();
+
+    // Activations -> Q8_0 in shared memory.
     if (p.xq.qs == nullptr) {
-        constexpr int kBatch = 8;  // float4 loads in flight per thread
-        const int nq = NC * K / 4;  // float4 quads; a block is 8 consecutive quads
-        for (int base = 0; base < nq; base += kGemvThreads * kBatch) {  // uniform trip count
-            const int q0 = base + (int)threadIdx.x;
-            float4 v[kBatch];
-#pragma unroll
-            for (int j = 0; j < kBatch; j++) {
-                const int q = q0 + j * kGemvThreads;
-                if (q < nq) {
-                    const int n = q / (K / 4), e = (q % (K / 4)) * 4;
-                    const float *xr = reinterpret_cast<const float *>(p.x + (uint64_t)n * p.x_nb1);
-                    v[j] = make_float4(xr[e], xr[e + 1], xr[e + 2], xr[e + 3]);
-                } else {
-                    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < kBatch; j++) {
-                // every lane takes part in the group shuffles (padding quads are
-                // zeros); nq is a multiple of 8, so a group is valid or not as a whole
-                const int q = q0 + j * kGemvThreads;
-                uint16_t dbits;
-                int qsum;
-                const uint32_t packed = quantize_q8_0_quad(v[j], dbits, qsum);
-                if (q < nq) {
-                    const int n = q / (K / 4), e = (q % (K / 4)) * 4;
-                    *reinterpret_cast<uint32_t *>(sq + n * K + e) = packed;
-                    if ((threadIdx.x & 7u) == 0) {
-                        const int b = e / QK;
-                        sd[n * nblk + b] = f16_bits_to_f32(dbits);
-                        ss[n * nblk + b] = qsum;
-                    }
-                }
-            }
+        constexpr int kGroups = kGemvThreads / 4;  // 4 lanes per block
+#pragma unroll 2
+        for (int base = 0; base < NC * nblk; base += kGroups) {  // uniform trip count
+            const int t = base + (int)(threadIdx.x >> 2);
+            const bool valid = t < NC * nblk;
+            const int n = !valid ? 0 : (NC == 1 ? 0 : t / nblk);
+            const int b = !valid ? 0 : t - n * nblk;
+            const float *xb = reinterpret_cast<const float *>(p.x + (uint64_t)n * p.x_nb1) + b * QK;
+            quantize_block_quarter<WT>(xb, p.x_vec16, valid, SH && !(b & 1), sq + n * K + b * QK,
+                                       sx2 + (n * npair_blk + b / 2) * kShiftWords, sd + n * nbp + b,
+                                       ss + n * nbp + b);
         }
     } else {
-        grid_dependency_wait();
         const int4 *src = reinterpret_cast<const int4 *>(p.xq.qs);
         int4 *dst = reinterpret_cast<int4 *>(sq);
         for (int t = threadIdx.x; t < NC * K / 16; t += kGemvThreads) dst[t] = src[t];
         for (int t = threadIdx.x; t < NC * nblk; t += kGemvThreads) {
-            sd[t] = p.xq.d[t];
-            ss[t] = p.xq.sum[t];
+            const int n = NC == 1 ? 0 : t / nblk;
+            sd[t + n * (nbp - nblk)] = p.xq.d[t];
+            ss[t + n * (nbp - nblk)] = p.xq.sum[t];
+        }
+        if constexpr (SH) {
+            __syncthreads();
+            for (int t = threadIdx.x; t < NC * npair_blk; t += kGemvThreads) {
+                const int n = NC == 1 ? 0 : t / npair_blk;
+                const int b = 2 * (t - n * npair_blk);
+                const uint4 *q = reinterpret_cast<const uint4 *>(sq + n * K + b * QK);
+                const uint4 q0 = q[0], q1 = q[1];
+                const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                uint32_t sh[kShiftWords];
+                make_shifted<WT>(w, sh);
+                uint4 *o = reinterpret_cast<uint4 *>(sx2 + t * kShiftWords);
+                o[0] = make_uint4(sh[0], sh[1], sh[2], sh[3]);
+                o[1] = make_uint4(sh[4], sh[5], sh[6], sh[7]);
+                o[2] = make_uint4(sh[8], sh[9], sh[10], sh[11]);
+            }
         }
     }
     __syncthreads();
@@ -235,23 +316,79 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         int row, c;
         item_range(i, start, len, row, c);
         uint8_t *buf = ring + (uint32_t)stage * p.stage_bytes;
-        const uintptr_t base = start & ~uintptr_t(15);
-        const uintptr_t a = (start + 15) & ~uintptr_t(15);
-        const uintptr_t e = (start + len) & ~uintptr_t(15);
-        if (a != start || e != start + len) {  // ragged edges: plain byte loads
-            const uint8_t *g = reinterpret_cast<const uint8_t *>(base);
-            if (e > a) {
-                for (uintptr_t t = start + lane; t < a; t += 32) buf[t - base] = g[t - base];
-                for (uintptr_t t = e + lane; t < start + len; t += 32) buf[t - base] = g[t - base];
-            } else {
-                for (uintptr_t t = start + lane; t < start + len; t += 32) buf[t - base] = g[t - base];
-            }
+        const uint8_t *p0;
+        if (p.copy_rows) {  // 2-byte-aligned rows: plain copy to the aligned stage start
+            const uint16_t *g = reinterpret_cast<const uint16_t *>(start);
+            uint16_t *d = reinterpret_cast<uint16_t *>(buf);
+            for (uint32_t t = lane; t < len / 2; t += 32) d[t] = g[t];
             __syncwarp();
+            p0 = buf;
+        } else {
+            const uintptr_t base = start & ~uintptr_t(15);
+            const uintptr_t a = (start + 15) & ~uintptr_t(15);
+            const uintptr_t e = (start + len) & ~uintptr_t(15);
+            if (a != start || e != start + len) {  // ragged edges: plain byte loads
+                const uint8_t *g = reinterpret_cast<const uint8_t *>(base);
+                if (e > a) {
+                    for (uintptr_t t = start + lane; t < a; t += 32) buf[t - base] = g[t - base];
+                    for (uintptr_t t = e + lane; t < start + len; t += 32) buf[t - base] = g[t - base];
+                } else {
+                    for (uintptr_t t = start + lane; t < start + len; t += 32) buf[t - base] = g[t - base];
+                }
+                __syncwarp();
+            }
+            p0 = buf + (start - base);
         }
-        const uint8_t *p0 = buf + (start - base);
         const int u0 = c * p.chunk_units;
         const int nu = (int)(len / UB);
-        for (int u = lane; u < nu; u += 32) dot_unit<WT, NC>(p0, u, u0 + u, sq, sd, ss, K, nblk, acc);
+        const int np = nu / 2;  // pairs in this chunk
+        if constexpr (WT == WT_Q4_K) {
+#pragma unroll 2
+            for (int pr = lane; pr < np; pr += 32) {
+                const int b0 = u0 + 2 * pr;  // sub-block index within the row
+                const uint8_t *sb = p0 + Q4_K_BYTES * (pr >> 2);
+                const int g = pr & 3;
+#pragma unroll
+                for (int n = 0; n < NC; n++) {
+                    const uint32_t *xa = reinterpret_cast<const uint32_t *>(sq + n * K + b0 * QK);
+                    int s0, s1;
+                    float dsc0, dmm0, dsc1, dmm1;
+                    q4k_pair_dot(sb, g, xa, xa + 8, s0, s1, dsc0, dmm0, dsc1, dmm1);
+                    const float2 dx = *reinterpret_cast<const float2 *>(sd + n * nbp + b0);
+                    const int2 xs = *reinterpret_cast<const int2 *>(ss + n * nbp + b0);
+                    acc[n] += dx.x * (dsc0 * (float)s0 - dmm0 * (float)xs.x) +
+                              dx.y * (dsc1 * (float)s1 - dmm1 * (float)xs.y);
+                }
+            }
+        } else {
+#pragma unroll 2
+            for (int pr = lane; pr < np; pr += 32) {
+                const int b0 = u0 + 2 * pr;  // even block index within the row
+                const uint32_t *wp = reinterpret_cast<const uint32_t *>(p0 + 2 * UB * pr);
+#pragma unroll
+                for (int n = 0; n < NC; n++) {
+                    const uint32_t *xe = sx2 + (n * npair_blk + b0 / 2) * kShiftWords;
+                    const uint32_t *xo = reinterpret_cast<const uint32_t *>(sq + n * K + (b0 + 1) * QK);
+                    const int2 xs = *reinterpret_cast<const int2 *>(ss + n * nbp + b0);
+                    int s0, s1;
+                    float d0, d1;
+                    pair_dot<WT>(wp, xe, xo, xs.x, xs.y, s0, s1, d0, d1);
+                    const float2 dx = *reinterpret_cast<const float2 *>(sd + n * nbp + b0);
+                    acc[n] += (d0 * dx.x) * (float)s0 + (d1 * dx.y) * (float)s1;
+                }
+            }
+            if ((nu & 1) && lane == (np & 31)) {  // trailing unpaired block of an odd-length row
+                const int b0 = u0 + 2 * np;
+                const uint32_t *wp = reinterpret_cast<const uint32_t *>(p0 + 2 * UB * np);
+#pragma unroll
+                for (int n = 0; n < NC; n++) {
+                    const uint32_t *xe = sx2 + (n * npair_blk + b0 / 2) * kShiftWords;
+                    float d0;
+                    const int s0 = single_even_dot<WT>(wp, xe, ss[n * nbp + b0], d0);
+                    acc[n] += (d0 * sd[n * nbp + b0]) * (float)s0;
+                }
+            }
+        }
         __syncwarp();
         if (lane == 0 && issued < n_items) {
             fence_proxy_async_smem();
@@ -272,14 +409,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
 template <int WT, int NC>
 int launch_typed(const GemvParams &p, int grid, uint32_t smem, cudaStream_t s, bool pdl) {
     auto kern = gemv_kernel<WT, NC>;
-    static int smem_set[64] = {0};  // per device: largest dynamic smem size already granted
+    static bool smem_set[64] = {false};  // per device: the dynamic smem limit was raised
     int dev = 0;
     cudaGetDevice(&dev);
     cudaError_t e = cudaSuccess;
-    if (dev < 0 || dev >= 64 || smem_set[dev] < (int)smem) {
+    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) smem_set[dev] = kSmemLimit;
+        if (dev >= 0 && dev < 64) smem_set[dev] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -306,15 +443,19 @@ int launch_cols(int ncols, const GemvParams &p, int grid, uint32_t smem, cudaStr
     }
 }
 
+bool shifted_of(int32_t wtype) { return wtype != WT_Q4_K; }
+uint32_t unit_bytes_of(int32_t wtype) {
+    return wtype == WT_Q8_0 ? Q8_0_BYTES : (wtype == WT_Q4_0 ? Q4_0_BYTES : Q4_K_BYTES / 8);
+}
+
 }  // namespace
 
 bool gemv_supported(int32_t wtype, int64_t K, int64_t N) {
     if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K) return false;
     if (N < 1 || N > kMaxCols) return false;
     if (K % (wtype == WT_Q4_K ? QKK : QK)) return false;
-    // activations + at least two minimal stages per warp must fit
-    const uint32_t ub = wtype == WT_Q8_0 ? Q8_0_BYTES : Q4_0_BYTES;
-    const SmemLayout L = smem_layout((int)K, (int)N, 2, align16(8 * ub + 32));
+    // activations + two minimal stages per warp must fit
+    const SmemLayout L = smem_layout((int)K, (int)N, shifted_of(wtype), 2, align16(8 * unit_bytes_of(wtype) + 32));
     return K <= (1 << 20) && L.total <= (uint32_t)kSmemLimit;
 }
 
@@ -333,27 +474,29 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     if (M > INT32_MAX) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: M too large");
 
     const int nunits = (int)(K / QK);
-    const uint32_t ub = wtype == WT_Q8_0 ? Q8_0_BYTES : (wtype == WT_Q4_0 ? Q4_0_BYTES : Q4_K_BYTES / 8);
+    const uint32_t ub = unit_bytes_of(wtype);
+    const bool sh = shifted_of(wtype);
     const int sms = sm_count();
-    int grid = (int)std::min<int64_t>(sms, (M + kGemvWarps - 1) / kGemvWarps);
-    grid = std::max(grid, 1);
+    const int grid = std::max<int>(1, (int)std::min<int64_t>(sms, (M + 1) / 2));
 
-    // Ring sizing: a few stages per warp, chunks as large as the budget allows.
-    const SmemLayout base = smem_layout((int)K, (int)N, 4, 0);
-    const uint32_t budget = (uint32_t)kSmemLimit - base.total - 256;
-    int units_fit = (int)((budget / (kGemvWarps * 4) - 32) / ub);
-    units_fit = std::max(8, units_fit / 8 * 8);
-    int chunk_units = std::min(units_fit, (nunits + 7) / 8 * 8);
-    chunk_units = std::min(chunk_units, 512);  // keep chunks at most ~17 KB
+    // Shared-memory budget: small activations leave room for the next
+    // launch's CTA on the same SM; otherwise one large CTA.
+    const SmemLayout base = smem_layout((int)K, (int)N, sh, 4, 0);
+    const uint32_t cta_limit = base.total <= kCoResidentActs ? kCoResidentCta : (uint32_t)kSmemLimit;
+    const uint32_t per_warp = (cta_limit - base.total - 256) / kGemvWarps;
+    // chunks as large as two stages per warp allow (whole rows when they fit)
+    int chunk_units = (int)((per_warp / 2 - 32) / ub) / 8 * 8;
+    chunk_units = std::max(8, std::min({chunk_units, (nunits + 7) / 8 * 8, 512}));
     const int nchunks0 = (nunits + chunk_units - 1) / chunk_units;
     chunk_units = ((nunits + nchunks0 - 1) / nchunks0 + 7) / 8 * 8;  // balance the chunks of a row
     const int nchunks = (nunits + chunk_units - 1) / chunk_units;
     const uint32_t stage_bytes = align16((uint32_t)chunk_units * ub + 32);
     int nstage = 4;
-    while (nstage > 2 && smem_layout((int)K, (int)N, nstage, stage_bytes).total > (uint32_t)kSmemLimit) nstage--;
-    const SmemLayout L = smem_layout((int)K, (int)N, nstage, stage_bytes);
+    while (nstage > 2 && smem_layout((int)K, (int)N, sh, nstage, stage_bytes).total > cta_limit) nstage--;
+    const SmemLayout L = smem_layout((int)K, (int)N, sh, nstage, stage_bytes);
     if (L.total > (uint32_t)kSmemLimit) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: shared memory budget exceeded");
 
+    const int align = wtype == WT_Q4_K ? 16 : 4;
     GemvParams p;
     p.w = static_cast<const uint8_t *>(w);
     p.w_nb1 = w_nb1;
@@ -369,11 +512,12 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     p.stage_bytes = stage_bytes;
     p.xq = xq ? *xq : Q8Planar{nullptr, nullptr, nullptr};
     p.status = status;
-    const bool use_pdl = pdl && xq != nullptr;
+    p.x_vec16 = ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0;
+    p.copy_rows = ((reinterpret_cast<uintptr_t>(w) | w_nb1) % align) != 0;
     switch (wtype) {
-    case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, p, grid, L.total, s, use_pdl);
-    case WT_Q4_0: return launch_cols<WT_Q4_0>((int)N, p, grid, L.total, s, use_pdl);
-    default: return launch_cols<WT_Q4_K>((int)N, p, grid, L.total, s, use_pdl);
+    case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, p, grid, L.total, s, pdl);
+    case WT_Q4_0: return launch_cols<WT_Q4_0>((int)N, p, grid, L.total, s, pdl);
+    default: return launch_cols<WT_Q4_K>((int)N, p, grid, L.total, s, pdl);
     }
 }
 
