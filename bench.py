@@ -18,9 +18,12 @@ the hot path, for measurement.
 oracle/, on all host threads; the Rust reference cannot be built here) on
 the same workload; under torchrun only rank 0 runs it.
 
-Multi-GPU (torchrun, --gpus N): every rank runs its own replica of the
-workload on its own GPU (independent decode streams, weak scaling); the only
-collectives are the timing barrier and the max-over-ranks reduction.
+Multi-GPU (torchrun, --gpus N): by default every rank runs its own replica
+of the workload on its own GPU (independent decode streams, weak scaling);
+the only collectives are the timing barrier and the max-over-ranks
+reduction. --shard rows (c4) / --shard experts (c5) split one workload
+across the ranks instead (strong scaling, feml_b200.shard), with the NCCL
+all-gather / all-reduce that reassembles the output inside every step.
 """
 import argparse
 import json
@@ -464,6 +467,144 @@ def run_e2e(args, cfg, N, dt, wts, copies, ids_np, local):
 
 
 # ---------------------------------------------------------------------------
+def run_sharded(args, cfg, N):
+    """Strong scaling of one workload split across the ranks: --shard rows
+    (weight rows, all-gather of the output slices) or --shard experts
+    (experts e % world, sum all-reduce of the slot outputs). A step is the
+    local kernels plus the collective that leaves the full output on every
+    rank; the step sequence (NCCL calls included) is replayed as a CUDA graph."""
+    import torch
+    import torch.distributed as dist
+    from feml_b200 import DType, ops
+    from feml_b200.shard import ExpertShardedMulMatId, RowShardedMulMat, local_experts, row_range
+
+    ws, rank, local = dist_setup()
+    if ws == 1 and not dist.is_initialized():
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29500 + (os.getpid() % 1000)))
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dt = DType[cfg["wtype"]]
+    K, M = cfg["K"], cfg["M"]
+    wbytes_total, alg_total, ops_total = step_units(cfg, N)
+    rb = dt.row_size(K)
+    g = torch.Generator(device="cuda").manual_seed(cfg["seed"] * 1000)
+    is_moe = args.shard == "experts"
+    if is_moe:
+        E, n_sel = cfg["E"], cfg["n_sel"]
+        n_loc = local_experts(E, rank, ws)
+        local_w = torch.empty((max(n_loc, 1), M, rb), dtype=torch.uint8, device="cuda")
+        for e in range(E):  # every rank draws all experts from one seed and keeps its own
+            wf = torch.randn((M, K), generator=g, device="cuda") * 0.02
+            if e % ws == rank:
+                local_w[e // ws] = ops.quantize(dt, wf)
+            del wf
+        local_w = local_w[:n_loc]
+        local_bytes = n_loc * M * rb
+    else:
+        lo, hi, R = row_range(M, rank, ws)
+        wf = torch.randn((M, K), generator=g, device="cuda") * 0.02
+        local_w = ops.quantize(dt, wf[lo:hi].contiguous())
+        del wf
+        local_bytes = (hi - lo) * rb
+    copies = max(1, math.ceil(2.5 * L2_BYTES / max(local_bytes, 1)))
+    wts = [local_w.clone() for _ in range(copies)]
+    gx = torch.Generator(device="cuda").manual_seed(cfg["seed"] * 1000 + 500)
+    x = torch.randn((N, K), generator=gx, device="cuda")
+    if is_moe:
+        ids_np = make_ids(cfg, 0, N)
+        ids = torch.from_numpy(ids_np).cuda()
+        mods = [ExpertShardedMulMatId(dt, w, K, E, local=True) for w in wts]
+
+        def step(i):
+            return mods[i % copies](x, ids)
+    else:
+        mods = [RowShardedMulMat(dt, w, K, M, local=True) for w in wts]
+
+        def step(i):
+            return mods[i % copies](x)
+
+    chunk = max(1, min(args.steps, max(copies, 16), 256))
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for i in range(chunk):
+            step(i)
+    torch.cuda.synchronize()
+    reps = max(1, args.steps // chunk)
+    steps = reps * chunk
+    for _ in range(max(1, max(args.warmup, 3) // chunk + 1)):
+        gr.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(stream)
+    for _ in range(reps):
+        gr.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.time()
+    barrier()
+    ms_max = reduce_max(e0.elapsed_time(e1))
+    time.sleep(0.25)
+    sampler.stop()
+    sec_step = ms_max / 1e3 / steps
+    value, unit = metric_value(cfg, N, sec_step)  # the whole job's work per step
+    # e2e: x from pinned host memory, the sharded op, y to pinned host memory
+    x_host = torch.randn((N, K), dtype=torch.float32).pin_memory()
+    y_elems = N * M * (cfg["n_sel"] if is_moe else 1)
+    y_host = torch.empty(y_elems, dtype=torch.float32).pin_memory()
+    e2e_steps = min(steps, args.e2e_steps)
+    for i in range(5):
+        x.copy_(x_host, non_blocking=True)
+        y_host.copy_(step(i).reshape(-1), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    tt = time.perf_counter()
+    for i in range(e2e_steps):
+        x.copy_(x_host, non_blocking=True)
+        y_host.copy_(step(i).reshape(-1), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e_s = reduce_max(time.perf_counter() - tt) / e2e_steps
+    e2e_v, _ = metric_value(cfg, N, e2e_s)
+    peaks = load_peaks()
+    n_k = 3 if is_moe else 1 + (1 if ops.mul_mat_workspace(dt, K, M, N) else 0)
+    result = {
+        "metric": f"mul_mat {'mul_mat_id expert-sharded' if is_moe else 'row-sharded'} weight-GB/s "
+                  f"({args.config}: {cfg['workload']})",
+        "value": value, "unit": unit, "n_gpus": ws, "steps": steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 dot / f32 scale", "data": "synthetic (seeded torch.randn weights quantized on device)",
+        "config": {"workload": cfg["workload"], "config": args.config, "K": K, "M": M, "N": N,
+                   "weights_dtype": cfg["wtype"], "experts": cfg.get("E"), "n_selected": cfg.get("n_sel"),
+                   "parallelism": f"{'expert' if is_moe else 'row'}-sharded x{ws} + NCCL "
+                                  f"{'all_reduce' if is_moe else 'all_gather'}",
+                   "l2": f"{copies} rotating local weight copies ({copies * local_bytes / 2**20:.0f} MiB per rank)"},
+        "roofline": {"bound": "hbm", "achieved": alg_total / sec_step / 1e9, "peak": peaks["hbm_gbs"] * ws,
+                     "unit": "GB/s", "frac": alg_total / sec_step / 1e9 / (peaks["hbm_gbs"] * ws), "traffic": None,
+                     "peak_note": f"{ws} x HBM copy bandwidth ({peaks['source']}); step includes the collective"},
+        "e2e": {"value": e2e_v, "unit": unit, "h2d_bytes_per_step": N * K * 4, "d2h_bytes_per_step": y_elems * 4,
+                "steps": e2e_steps, "path": "feml_b200.shard wrapper, pinned host x -> device -> pinned host y"},
+        "gpu_launches": steps * n_k,
+        "clocks": sampler.summary(t0, t1),
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    del gr
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
 def cpu_baseline(cfg, N, wq_dev, budget_s=10.0, threads=None):
     """The reference's CPU mul_mat (oracle/, the C restatement of
     feml-cpu/src/ops/mul_mat.rs:36-57) on a bounded sample of the workload.
@@ -573,11 +714,18 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5000)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", default="none", choices=["none", "rows", "experts"],
+                    help="strong-scaling split of one workload across the ranks (c4: rows, c5: experts)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     N = args.n if args.n is not None else cfg["N"]
     if args.impl == "reference":
         run_reference(args, cfg, N)
+        return
+    if args.shard != "none":
+        if (args.shard == "experts") != ("E" in cfg) or cfg["wtype"] == "F32":
+            ap.error("--shard rows needs a quantized mul_mat config (c2, c3, c4); --shard experts needs c5")
+        run_sharded(args, cfg, N)
         return
     run_b200(args, cfg, N)
 

@@ -128,38 +128,45 @@ IdWorkspace id_ws_layout(void *base, int32_t wtype, int64_t K, int64_t N, int64_
     return L;
 }
 
-int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t E, const void *x,
-                  uint64_t x_nb1, const int32_t *ids, uint64_t ids_nb1, int64_t n_sel, void *dst, uint64_t dst_nb1,
-                  uint64_t dst_nb2, int64_t K, int64_t M, int64_t N, void *ws, uint64_t ws_bytes, int32_t *status,
-                  cudaStream_t s) {
+// Expert-sharded form: `w` holds this shard's experts (local expert j = global
+// expert shard + j*n_shards, j-th at w + j*w_nb2); slots routed to other
+// shards are left untouched. shard = 0, n_shards = 1 is plain mul_mat_id.
+int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t E, int64_t shard,
+                  int64_t n_shards, const void *x, uint64_t x_nb1, const int32_t *ids, uint64_t ids_nb1,
+                  int64_t n_sel, void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t K, int64_t M, int64_t N,
+                  void *ws, uint64_t ws_bytes, int32_t *status, cudaStream_t s) {
     if (K < 0 || M < 0 || N < 0 || n_sel < 1 || E < 1) return set_error(FB_ERR_INVALID, "mul_mat_id: bad dimensions");
+    if (n_shards < 1 || shard < 0 || shard >= n_shards) return set_error(FB_ERR_INVALID, "mul_mat_id: bad shard");
     if (M == 0 || N == 0) return FB_OK;
-    if (!w || !x || !ids || !dst) return set_error(FB_ERR_INVALID, "mul_mat_id: null operand");
+    const int64_t n_local = fbk::local_experts(E, shard, n_shards);
+    // a shard that owns no expert still routes (invalid ids are zeroed and reported)
+    if ((!w && n_local > 0) || !x || !ids || !dst) return set_error(FB_ERR_INVALID, "mul_mat_id: null operand");
     if (!is_weight_dtype(wtype)) return set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: weight dtype %d not supported", wtype);
     const fb::DTypeTraits *t = fb::dtype_traits(wtype);
     if (K % t->block_size) return set_error(FB_ERR_SHAPE, "mul_mat_id: K not a block multiple");
-    const IdWorkspace need = id_ws_layout(nullptr, wtype, K, N, n_sel, E);
+    const IdWorkspace need = id_ws_layout(nullptr, wtype, K, N, n_sel, n_local);
     if (need.total > ws_bytes)
         return set_error(FB_ERR_INVALID, "mul_mat_id: workspace of %lu bytes needed, %lu given",
                          (unsigned long)need.total, (unsigned long)ws_bytes);
-    const IdWorkspace L = id_ws_layout(ws, wtype, K, N, n_sel, E);
+    const IdWorkspace L = id_ws_layout(ws, wtype, K, N, n_sel, n_local);
     const int block_n = wtype == FB_F32 ? fbk::gemm_f32_block_n() : fbk::gemm_q_block_n();
     if (wtype != FB_F32 && !fbk::gemm_q_supported(wtype, K, w, w_nb1))
         return set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: quantized experts need K %% 256 == 0 and 16-byte aligned rows");
-    int rc = fbk::launch_moe_route(ids, ids_nb1, n_sel, N, E, L.counts, L.offsets, L.rows, L.tile_start, block_n,
-                                   status, dst, dst_nb1, dst_nb2, M, s);
+    int rc = fbk::launch_moe_route(ids, ids_nb1, n_sel, N, E, shard, n_shards, L.counts, L.offsets, L.rows,
+                                   L.tile_start, block_n, status, dst, dst_nb1, dst_nb2, M, s);
     if (rc) return rc;
     fbk::GroupMap g{};
     g.counts = L.counts;
     g.offsets = L.offsets;
     g.rows = L.rows;
     g.tile_start = L.tile_start;
-    g.n_groups = (int32_t)E;
+    g.n_groups = (int32_t)n_local;
     g.n_selected = (int32_t)n_sel;
     g.w_group_stride = w_nb2;
     g.dst_nb1 = dst_nb1;
     g.dst_nb2 = dst_nb2;
-    g.max_tiles = (int32_t)((n_sel * N + block_n - 1) / block_n + E);
+    g.max_tiles = (int32_t)((n_sel * N + block_n - 1) / block_n + n_local);
+    if (n_local == 0) return FB_OK;
     if (wtype == FB_F32) return fbk::launch_gemm_f32_grouped(w, w_nb1, x, x_nb1, K, M, dst, g, s);
     const fbk::Q8Planar xq = fbk::q8_planar_carve(L.xq, K, N);
     rc = fbk::launch_quantize_q8_planar(x, x_nb1, K, N, xq, s);
@@ -310,7 +317,7 @@ int compute_mul_mat_id(fb_backend *b, const fb_plan *plan, const fb_plan_tensor 
         return set_error(FB_ERR_SHAPE, "shape error: mul_mat_id: inconsistent shapes");
     if (w.nb[0] != (uint64_t)fb::dtype_traits(w.dtype)->type_size || x.nb[0] != 4 || ids.nb[0] != 4 || d.nb[0] != 4)
         return set_error(FB_ERR_UNSUPPORTED, "B200: mul_mat_id needs contiguous rows");
-    return do_mul_mat_id(w.dtype, W.ptr, w.nb[1], w.nb[2], E, X.ptr, x.nb[1], reinterpret_cast<int32_t *>(I.ptr),
+    return do_mul_mat_id(w.dtype, W.ptr, w.nb[1], w.nb[2], E, 0, 1, X.ptr, x.nb[1], reinterpret_cast<int32_t *>(I.ptr),
                          ids.nb[1], n_sel, D.ptr, d.nb[1], d.nb[2], K, M, N, b->scratch, b->scratch_bytes,
                          b->status_dev, b->stream);
 }
@@ -656,15 +663,25 @@ int feml_b200_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t 
                          const void *x, uint64_t x_nb1, const int32_t *ids, uint64_t ids_nb1, int64_t n_selected,
                          void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t K, int64_t M, int64_t N,
                          void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream) {
-    return do_mul_mat_id(wtype, w, w_nb1, w_nb2, n_experts, x, x_nb1, ids, ids_nb1, n_selected, dst, dst_nb1, dst_nb2,
-                         K, M, N, workspace, workspace_bytes, status, static_cast<cudaStream_t>(stream));
+    return do_mul_mat_id(wtype, w, w_nb1, w_nb2, n_experts, 0, 1, x, x_nb1, ids, ids_nb1, n_selected, dst, dst_nb1,
+                         dst_nb2, K, M, N, workspace, workspace_bytes, status, static_cast<cudaStream_t>(stream));
+}
+
+int feml_b200_mul_mat_id_shard(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,
+                               int64_t shard, int64_t n_shards, const void *x, uint64_t x_nb1, const int32_t *ids,
+                               uint64_t ids_nb1, int64_t n_selected, void *dst, uint64_t dst_nb1, uint64_t dst_nb2,
+                               int64_t K, int64_t M, int64_t N, void *workspace, uint64_t workspace_bytes,
+                               int32_t *status, void *stream) {
+    return do_mul_mat_id(wtype, w_local, w_nb1, w_nb2, n_experts, shard, n_shards, x, x_nb1, ids, ids_nb1, n_selected,
+                         dst, dst_nb1, dst_nb2, K, M, N, workspace, workspace_bytes, status,
+                         static_cast<cudaStream_t>(stream));
 }
 
 int feml_b200_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
                         int32_t *counts, int32_t *offsets, int32_t *rows, int32_t *status, void *stream) {
     if (!ids || !counts || !offsets || !rows) return set_error(FB_ERR_INVALID, "moe_route: null argument");
-    return fbk::launch_moe_route(ids, ids_nb1, n_selected, N, n_experts, counts, offsets, rows, nullptr, 64, status,
-                                 nullptr, 0, 0, 0,
+    return fbk::launch_moe_route(ids, ids_nb1, n_selected, N, n_experts, 0, 1, counts, offsets, rows, nullptr, 64,
+                                 status, nullptr, 0, 0, 0,
                                  static_cast<cudaStream_t>(stream));
 }
 

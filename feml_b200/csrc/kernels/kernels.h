@@ -71,9 +71,15 @@ int launch_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *
 // moe.cu: routing tables + column-tile prefix for gemm_q's grouped mode.
 // When dst is non-null, output columns of slots with an invalid id are
 // zeroed (and STATUS_BAD_ID is raised).
+// Expert sharding: expert e belongs to shard e % n_shards as local expert
+// e / n_shards; other shards' slots are skipped (no write).
+inline int64_t local_experts(int64_t n_experts, int64_t shard, int64_t n_shards) {
+    return n_experts > shard ? (n_experts - shard + n_shards - 1) / n_shards : 0;
+}
 int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
-                     int32_t *counts, int32_t *offsets, int32_t *rows, int32_t *tile_start, int32_t block_n,
-                     int32_t *status, void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t M, cudaStream_t s);
+                     int64_t shard, int64_t n_shards, int32_t *counts, int32_t *offsets, int32_t *rows,
+                     int32_t *tile_start, int32_t block_n, int32_t *status, void *dst, uint64_t dst_nb1,
+                     uint64_t dst_nb2, int64_t M, cudaStream_t s);
 
 int sm_count();
 

@@ -1,7 +1,10 @@
 // mul_mat_id front end: routing tables for the grouped GEMMs.
 //
 // Slot i = s + t*n_selected (ggml ids [n_selected, N]) selects expert
-// ids[s, t]. The tables list, per expert, its slots in ascending order:
+// ids[s, t]. With expert sharding, expert e belongs to shard e % n_shards
+// and is local expert e / n_shards there; slots of other shards are skipped
+// (their owner computes them), ids outside [0, E) are invalid. The tables
+// list, per local expert, its slots in ascending order:
 //   counts[e], offsets[e] (exclusive prefix), rows[offsets[e] + r],
 //   tile_start[e] = sum_{e' < e} ceil(counts[e'] / block_n)   (e = 0..E)
 // One CTA builds them: slots are processed in 1024-slot chunks; within a
@@ -23,7 +26,8 @@ constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kMaxExperts = 256;
 
 __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t *__restrict__ ids, uint64_t ids_stride,
-                                                                   int n_sel, int N, int E, int32_t *counts,
+                                                                   int n_sel, int N, int E, int shard, int n_shards,
+                                                                   int n_local, int32_t *counts,
                                                                    int32_t *offsets, int32_t *rows,
                                                                    int32_t *tile_start, int block_n, int32_t *status,
                                                                    uint8_t *dst, uint64_t dst_nb1, uint64_t dst_nb2,
@@ -34,17 +38,22 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
     __shared__ int wcnt[kRouteWarps][kMaxExperts];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_slots = n_sel * N;
-    for (int e = tid; e < E; e += kRouteThreads) {
+    // local expert of a slot: -1 = another shard's, -2 = invalid id
+    auto local_of = [&](int e) -> int {
+        if (e < 0 || e >= E) return -2;
+        return (e % n_shards) == shard ? e / n_shards : -1;
+    };
+    for (int e = tid; e < n_local; e += kRouteThreads) {
         cnt[e] = 0;
         base[e] = 0;
     }
     __syncthreads();
     int bad = 0;
     for (int i = tid; i < n_slots; i += kRouteThreads) {
-        const int e = ids[(uint64_t)(i / n_sel) * ids_stride + (i % n_sel)];
-        if (e >= 0 && e < E)
-            atomicAdd(&cnt[e], 1);
-        else
+        const int le = local_of(ids[(uint64_t)(i / n_sel) * ids_stride + (i % n_sel)]);
+        if (le >= 0)
+            atomicAdd(&cnt[le], 1);
+        else if (le == -2)
             bad = 1;
     }
     const int any_bad = __syncthreads_or(bad);
@@ -53,14 +62,14 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
         for (int i = 0; i < n_slots; i++) {
             const int t = i / n_sel, s = i % n_sel;
             const int e = ids[(uint64_t)t * ids_stride + s];
-            if (e >= 0 && e < E) continue;
+            if (local_of(e) != -2) continue;
             float *col = reinterpret_cast<float *>(dst + (uint64_t)s * dst_nb1 + (uint64_t)t * dst_nb2);
             for (int m = tid; m < M; m += kRouteThreads) col[m] = 0.0f;
         }
     }
     if (tid == 0) {
         int run = 0, tiles = 0;
-        for (int e = 0; e < E; e++) {
+        for (int e = 0; e < n_local; e++) {
             off[e] = run;
             counts[e] = cnt[e];
             offsets[e] = run;
@@ -68,24 +77,24 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
             run += cnt[e];
             tiles += (cnt[e] + block_n - 1) / block_n;
         }
-        if (tile_start) tile_start[E] = tiles;
+        if (tile_start) tile_start[n_local] = tiles;
     }
     __syncthreads();
     for (int c0 = 0; c0 < n_slots; c0 += kRouteThreads) {
-        for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) wcnt[i / E][i % E] = 0;
+        for (int i = tid; i < kRouteWarps * n_local; i += kRouteThreads) wcnt[i / n_local][i % n_local] = 0;
         __syncthreads();
         const int i = c0 + tid;
         int e = -1;
         if (i < n_slots) {
-            e = ids[(uint64_t)(i / n_sel) * ids_stride + (i % n_sel)];
-            if (e < 0 || e >= E) e = -1;
+            e = local_of(ids[(uint64_t)(i / n_sel) * ids_stride + (i % n_sel)]);
+            if (e < 0) e = -1;
         }
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(peers & ((1u << lane) - 1u));
         if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(peers);
         __syncthreads();
         // exclusive prefix over warps, per expert; advance the expert base
-        for (int x = tid; x < E; x += kRouteThreads) {
+        for (int x = tid; x < n_local; x += kRouteThreads) {
             int run = base[x];
             for (int w = 0; w < kRouteWarps; w++) {
                 const int v = wcnt[w][x];
@@ -103,15 +112,20 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
 }  // namespace
 
 int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
-                     int32_t *counts, int32_t *offsets, int32_t *rows, int32_t *tile_start, int32_t block_n,
-                     int32_t *status, void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t M, cudaStream_t s) {
+                     int64_t shard, int64_t n_shards, int32_t *counts, int32_t *offsets, int32_t *rows,
+                     int32_t *tile_start, int32_t block_n, int32_t *status, void *dst, uint64_t dst_nb1,
+                     uint64_t dst_nb2, int64_t M, cudaStream_t s) {
     if (n_experts < 1 || n_experts > kMaxExperts)
         return fb::set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: n_experts %ld not in [1, %d]", (long)n_experts, kMaxExperts);
+    if (n_shards < 1 || shard < 0 || shard >= n_shards)
+        return fb::set_error(FB_ERR_INVALID, "mul_mat_id: shard %ld of %ld", (long)shard, (long)n_shards);
+    const int64_t n_local = local_experts(n_experts, shard, n_shards);
     if (n_selected < 1 || N < 0 || n_selected * N > INT32_MAX / 2)
         return fb::set_error(FB_ERR_INVALID, "mul_mat_id: bad slot count");
     if (ids_nb1 % 4 || (reinterpret_cast<uintptr_t>(ids) & 3))
         return fb::set_error(FB_ERR_INVALID, "mul_mat_id: ids must be 4-byte aligned");
-    moe_route_kernel<<<1, kRouteThreads, 0, s>>>(ids, ids_nb1 / 4, (int)n_selected, (int)N, (int)n_experts, counts,
+    moe_route_kernel<<<1, kRouteThreads, 0, s>>>(ids, ids_nb1 / 4, (int)n_selected, (int)N, (int)n_experts, (int)shard,
+                                                 (int)n_shards, (int)n_local, counts,
                                                  offsets, rows, tile_start, block_n, status,
                                                  static_cast<uint8_t *>(dst), dst_nb1, dst_nb2, (int)M);
     cudaError_t e = cudaGetLastError();

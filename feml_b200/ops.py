@@ -82,6 +82,34 @@ def mul_mat_id(wtype, w, x, ids, K, out=None, workspace=None, status=None):
     return out
 
 
+def local_experts(n_experts, shard, n_shards):
+    """Experts owned by `shard` when expert e lives on shard e % n_shards."""
+    return max(0, (n_experts - shard + n_shards - 1) // n_shards)
+
+
+def mul_mat_id_shard(wtype, w_local, x, ids, K, n_experts, shard, n_shards, out, workspace=None, status=None):
+    """Expert-sharded mul_mat_id: w_local holds the experts e with
+    e % n_shards == shard (local index e // n_shards). Writes only the
+    out[t, s, :] slots routed to those experts (invalid ids: zeros + status)."""
+    E_loc, M = w_local.shape[0], w_local.shape[1]
+    if E_loc != local_experts(n_experts, shard, n_shards):
+        raise FemlError("msg", f"mul_mat_id_shard: shard {shard}/{n_shards} of {n_experts} experts holds "
+                               f"{local_experts(n_experts, shard, n_shards)} experts, got {E_loc}")
+    N, n_sel = ids.shape
+    es = w_local.element_size()
+    need = mul_mat_id_workspace(wtype, K, M, N, n_sel, max(E_loc, 1))
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    st = _ptr(status) if status is not None else ctypes.c_void_p()
+    w_nb2 = w_local.stride(0) * es if E_loc > 0 else 0
+    _check(_L.lib().feml_b200_mul_mat_id_shard(int(wtype), _ptr(w_local), w_local.stride(1) * es, w_nb2, n_experts,
+                                               shard, n_shards, _ptr(x), x.stride(0) * 4, _ptr(ids),
+                                               ids.stride(0) * 4, n_sel, _ptr(out), out.stride(1) * 4,
+                                               out.stride(0) * 4, K, M, N, _ptr(workspace), workspace.numel(), st,
+                                               _stream()))
+    return out
+
+
 def moe_route(ids, n_experts, status=None):
     """ids int32 [N, n_sel] -> (counts, offsets, rows) int32 device tensors."""
     N, n_sel = ids.shape
@@ -104,5 +132,6 @@ def block_dots(wtype, w, xq, K):
     return out
 
 
-__all__ = ["quantize", "mul_mat", "mul_mat_workspace", "mul_mat_id", "mul_mat_id_workspace", "moe_route",
+__all__ = ["quantize", "mul_mat", "mul_mat_workspace", "mul_mat_id", "mul_mat_id_workspace", "mul_mat_id_shard",
+           "local_experts", "moe_route",
            "block_dots", "row_bytes", "FemlError"]

@@ -1,0 +1,142 @@
+"""Multi-GPU mul_mat / mul_mat_id: one process per GPU over torch.distributed.
+
+The reference runs one backend per process and has no multi-device code
+(feml-core/src/backend.rs:96-165 is a single-device trait), so these wrappers
+are new. They shard the two operators of the path the natural way:
+
+* `RowShardedMulMat` -- rank r owns the weight rows [r*R, min(M, (r+1)*R)),
+  R = ceil(M / world). In the ggml layout those rows are one contiguous byte
+  range (feml-core/src/layout.rs:38-40). Each rank computes its [N, R] slice
+  of y = W x straight into its all-gather send buffer, one all-gather over
+  NCCL assembles [world, N, R], and a permute gives y [N, M] on every rank.
+  With N == 1 the gathered buffer already is y (no permute).
+* `ExpertShardedMulMatId` -- rank r owns the experts e with e % world == r
+  (local index e // world). Each rank computes the dst slots routed to its
+  experts (feml_b200_mul_mat_id_shard leaves the other slots untouched in a
+  zeroed buffer) and a sum all-reduce combines them: every slot has exactly
+  one non-zero contributor, so the combine is exact. Invalid expert ids give
+  zero slots on every rank, as on one device.
+
+The compute step defaults to the CUDA entry points of libfeml_b200.so
+(feml_b200.ops); `compute` / `compute_id` can be replaced, which the CPU
+tests use to run the sharding and collective logic on gloo ranks.
+"""
+import torch
+import torch.distributed as dist
+
+from . import DType, FemlError
+
+
+def row_range(M, rank, world):
+    """Rows [lo, hi) of an M-row weight owned by `rank`, and the padded
+    per-rank row count R = ceil(M / world) every rank gathers."""
+    R = -(-M // world)
+    lo = min(M, rank * R)
+    return lo, min(M, lo + R), R
+
+
+def local_experts(n_experts, shard, n_shards):
+    """Experts owned by `shard`: e = shard, shard + n_shards, ..."""
+    return max(0, (n_experts - shard + n_shards - 1) // n_shards)
+
+
+def _cuda_mul_mat(wtype, w_local, x, K, out):
+    from . import ops
+    return ops.mul_mat(wtype, w_local, x, K, out=out)
+
+
+def _cuda_mul_mat_id(wtype, w_local, x, ids, K, n_experts, shard, n_shards, out):
+    from . import ops
+    return ops.mul_mat_id_shard(wtype, w_local, x, ids, K, n_experts, shard, n_shards, out)
+
+
+def _world(group):
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def _gather(out, send, group):
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, send, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), send, group=group)
+
+
+class RowShardedMulMat:
+    """y [N, M] = W x with W row-sharded across the ranks of `group`.
+
+    `w` is either the full weight (uint8 [M, row_bytes], or f32 [M, K] for
+    F32) from which this rank keeps its rows, or (local=True) this rank's
+    rows already.
+    """
+
+    def __init__(self, wtype, w, K, M, group=None, local=False, compute=None):
+        self.wtype = DType(wtype)
+        self.K, self.M = K, M
+        self.group = group
+        self.rank, self.world = _world(group)
+        self.lo, self.hi, self.R = row_range(M, self.rank, self.world)
+        if local:
+            if w.shape[0] != self.hi - self.lo:
+                raise FemlError("shape", f"rank {self.rank} holds rows [{self.lo}, {self.hi}), "
+                                         f"got {w.shape[0]} rows")
+            self.w_local = w
+        else:
+            if w.shape[0] != M:
+                raise FemlError("shape", f"weight has {w.shape[0]} rows, expected {M}")
+            self.w_local = w[self.lo:self.hi]
+        self.compute = compute or _cuda_mul_mat
+
+    def __call__(self, x):
+        N = x.shape[0]
+        if x.shape[1] != self.K:
+            raise FemlError("shape", f"activation has K={x.shape[1]}, expected {self.K}")
+        send = torch.empty((N, self.R), dtype=torch.float32, device=x.device)
+        m_loc = self.hi - self.lo
+        if m_loc < self.R:
+            send[:, m_loc:].zero_()
+        if m_loc:
+            self.compute(self.wtype, self.w_local, x, self.K, send[:, :m_loc])
+        gathered = torch.empty((self.world, N, self.R), dtype=torch.float32, device=x.device)
+        _gather(gathered, send, self.group)
+        if N == 1:
+            return gathered.view(1, self.world * self.R)[:, :self.M]
+        return gathered.permute(1, 0, 2).reshape(N, self.world * self.R)[:, :self.M]
+
+
+class ExpertShardedMulMatId:
+    """out [N, n_sel, M] = mul_mat_id(W, x, ids) with experts sharded across
+    the ranks of `group` (expert e on rank e % world).
+
+    `w` is either all experts (uint8 [E, M, row_bytes]) from which this rank
+    keeps its own, or (local=True) this rank's experts already, in local
+    order.
+    """
+
+    def __init__(self, wtype, w, K, n_experts, group=None, local=False, compute_id=None):
+        self.wtype = DType(wtype)
+        self.K, self.E = K, n_experts
+        self.group = group
+        self.rank, self.world = _world(group)
+        n_loc = local_experts(n_experts, self.rank, self.world)
+        if local:
+            if w.shape[0] != n_loc:
+                raise FemlError("shape", f"rank {self.rank} owns {n_loc} experts, got {w.shape[0]}")
+            self.w_local = w
+        else:
+            if w.shape[0] != n_experts:
+                raise FemlError("shape", f"weight has {w.shape[0]} experts, expected {n_experts}")
+            self.w_local = w[self.rank::self.world]
+        self.M = w.shape[1]
+        self.compute_id = compute_id or _cuda_mul_mat_id
+
+    def __call__(self, x, ids):
+        N, n_sel = ids.shape
+        if x.shape[0] != N or x.shape[1] != self.K:
+            raise FemlError("shape", f"activation {tuple(x.shape)} does not match ids {tuple(ids.shape)} / K={self.K}")
+        out = torch.zeros((N, n_sel, self.M), dtype=torch.float32, device=x.device)
+        self.compute_id(self.wtype, self.w_local, x, ids, self.K, self.E, self.rank, self.world, out)
+        dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)
+        return out
+
+
+__all__ = ["RowShardedMulMat", "ExpertShardedMulMatId", "row_range", "local_experts"]

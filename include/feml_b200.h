@@ -289,6 +289,19 @@ int feml_b200_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t 
                          void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t K, int64_t M, int64_t N,
                          void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream);
 
+/* Expert-sharded mul_mat_id (no counterpart in the reference, which has no
+ * multi-GPU code): expert e belongs to shard e % n_shards as local expert
+ * e / n_shards; w_local holds this shard's local experts (j-th at
+ * w_local + j*w_nb2). Writes the dst columns of slots routed to this shard's
+ * experts and leaves other shards' columns untouched; invalid ids give zeros
+ * and bit 1 of *status as in feml_b200_mul_mat_id. Workspace:
+ * feml_b200_mul_mat_id_workspace with n_experts = the local expert count. */
+int feml_b200_mul_mat_id_shard(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,
+                               int64_t shard, int64_t n_shards, const void *x, uint64_t x_nb1, const int32_t *ids,
+                               uint64_t ids_nb1, int64_t n_selected, void *dst, uint64_t dst_nb1, uint64_t dst_nb2,
+                               int64_t K, int64_t M, int64_t N, void *workspace, uint64_t workspace_bytes,
+                               int32_t *status, void *stream);
+
 /* mul_mat_id routing tables: counts[e], offsets[e] (exclusive prefix sum)
  * and rows[offsets[e] + r] = r-th slot index i = s + t*n_selected routed to
  * e, ascending. Bad ids are skipped and flagged in *status. */

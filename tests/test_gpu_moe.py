@@ -88,3 +88,39 @@ def test_mul_mat_id_equivalent_to_per_expert_mul_mat(b200):
     y1 = ops.mul_mat(DType.Q8_0, wt[1], xt[N // 2:], K).cpu().numpy()
     assert np.array_equal(got[: N // 2, 0], y0)
     assert np.array_equal(got[N // 2:, 0], y1)
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_K, DType.F32])
+@pytest.mark.parametrize("n_shards", [2, 3, 8])
+def test_mul_mat_id_shards_compose(b200, dt, n_shards):
+    """Every shard writes only the slots of its own experts; the union over
+    shards equals the unsharded mul_mat_id bit for bit (same per-output
+    arithmetic) and the oracle within tolerance. Invalid ids are zeroed by
+    every shard and reported."""
+    rng = np.random.default_rng(40 + n_shards)
+    E, M, K, N, n_sel = 5, 72, 512, 33, 2
+    wb = _expert_weights(rng, dt, E, M, K)
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    ids = topk_ids(rng, N, n_sel, E)
+    ids[3, 1] = -1
+    wt = torch.from_numpy(np.ascontiguousarray(wb)).cuda()
+    xt = torch.from_numpy(x).cuda()
+    it = torch.from_numpy(ids).cuda()
+    full = ops.mul_mat_id(dt, wt, xt, it, K)
+    sentinel = torch.full((N, n_sel, M), float("nan"), device="cuda")
+    union = torch.zeros_like(sentinel)
+    for r in range(n_shards):
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        part = sentinel.clone()
+        ops.mul_mat_id_shard(dt, wt[r::n_shards], xt, it, K, E, r, n_shards, part, status=status)
+        torch.cuda.synchronize()
+        assert int(status.item()) & 2, "invalid id not reported"
+        mine = torch.from_numpy((ids % n_shards == r) & (ids >= 0) & (ids < E)).cuda()
+        bad = torch.from_numpy((ids < 0) | (ids >= E)).cuda()
+        assert torch.isnan(part[~(mine | bad)]).all(), "a shard wrote another shard's slot"
+        assert (part[bad] == 0).all()
+        union[mine] = part[mine]
+    assert torch.equal(union, torch.nan_to_num(full.masked_fill(torch.from_numpy((ids < 0)[..., None]).cuda(), 0)))
+    want = O.mul_mat_id_ref(QT[dt], wb, x, ids, K, quantize_act=dt != DType.F32)
+    ok, err = tol_ok(union.cpu().numpy(), want)
+    assert ok, err
