@@ -115,6 +115,8 @@ SIGNATURES = [
     ("feml_b200_quantize", c_int, [c_i32, vp, c_u64, vp, c_i64, c_i64, vp]),
     ("feml_b200_mul_mat_workspace", c_int, [c_i32, c_i64, c_i64, c_i64, ctypes.POINTER(c_u64)]),
     ("feml_b200_mul_mat", c_int, [c_i32, vp, c_u64, vp, c_u64, vp, c_u64, c_i64, c_i64, c_i64, vp, c_u64, vp]),
+    ("feml_b200_mul_mat_noalloc", c_int, [c_i32, vp, c_u64, vp, c_u64, vp, c_u64, c_i64, c_i64, c_i64, vp]),
+    ("feml_b200_mul_mat_noalloc_limit", c_u64, []),
     ("feml_b200_mul_mat_id_workspace", c_int, [c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, ctypes.POINTER(c_u64)]),
     ("feml_b200_mul_mat_id", c_int, [c_i32, vp, c_u64, c_u64, c_i64, vp, c_u64, vp, c_u64, c_i64, vp, c_u64,
                                      c_u64, c_i64, c_i64, c_i64, vp, c_u64, vp, vp]),

@@ -57,6 +57,19 @@ def mul_mat(wtype, w, x, K, out=None, workspace=None):
     return out
 
 
+def mul_mat_noalloc(wtype, w, x, K, out):
+    """feml_b200_mul_mat_noalloc: mul_mat with the library's fixed device
+    scratch (no workspace, no allocation inside the call); `out` is given."""
+    M, N = w.shape[0], x.shape[0]
+    _check(_L.lib().feml_b200_mul_mat_noalloc(int(wtype), _ptr(w), w.stride(0) * w.element_size(), _ptr(x),
+                                              x.stride(0) * 4, _ptr(out), out.stride(0) * 4, K, M, N, _stream()))
+    return out
+
+
+def mul_mat_noalloc_limit():
+    return int(_L.lib().feml_b200_mul_mat_noalloc_limit())
+
+
 def mul_mat_id_workspace(wtype, K, M, N, n_selected, n_experts):
     v = ctypes.c_uint64()
     _check(_L.lib().feml_b200_mul_mat_id_workspace(int(wtype), K, M, N, n_selected, n_experts, ctypes.byref(v)))
@@ -132,6 +145,6 @@ def block_dots(wtype, w, xq, K):
     return out
 
 
-__all__ = ["quantize", "mul_mat", "mul_mat_workspace", "mul_mat_id", "mul_mat_id_workspace", "mul_mat_id_shard",
+__all__ = ["quantize", "mul_mat", "mul_mat_workspace", "mul_mat_noalloc", "mul_mat_noalloc_limit", "mul_mat_id", "mul_mat_id_workspace", "mul_mat_id_shard",
            "local_experts", "moe_route",
            "block_dots", "row_bytes", "FemlError"]

@@ -276,6 +276,21 @@ int feml_b200_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *
                       uint64_t dst_nb1, int64_t K, int64_t M, int64_t N, void *workspace, uint64_t workspace_bytes,
                       void *stream);
 
+/* feml_b200_mul_mat without a workspace argument: the scratch is a fixed
+ * 16 MiB device array inside this library (one per device), so the call
+ * allocates nothing. No counterpart in the reference (its backends allocate
+ * per call or plan every byte ahead). Same kernels and results as
+ * feml_b200_mul_mat. The first call on each device looks the array up
+ * (cudaGetSymbolAddress, with that device current) and should come before
+ * any stream capture. All calls on a device share the array: calls whose
+ * kernels can overlap (unordered streams) race; calls on one stream are
+ * safe. Nothing in it needs to start at zero. Shapes whose scratch
+ * (feml_b200_mul_mat_workspace) exceeds feml_b200_mul_mat_noalloc_limit()
+ * bytes return FB_ERR_UNSUPPORTED without queuing work. */
+int feml_b200_mul_mat_noalloc(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *dst,
+                              uint64_t dst_nb1, int64_t K, int64_t M, int64_t N, void *stream);
+uint64_t feml_b200_mul_mat_noalloc_limit(void);
+
 int feml_b200_mul_mat_id_workspace(int32_t wtype, int64_t K, int64_t M, int64_t N, int64_t n_selected,
                                    int64_t n_experts, uint64_t *bytes);
 
