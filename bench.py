@@ -253,11 +253,14 @@ def kernels_per_step(cfg, N):
 def dominant_kernel(cfg, N):
     from feml_b200 import DType
     dt = DType[cfg["wtype"]]
+    tc = dt in (DType.Q8_0, DType.Q4_0) and cfg["K"] % 256 == 0
     if "E" in cfg:
-        return "gemm_q_kernel (grouped)"
+        return "gemm_tc_kernel (grouped, tcgen05)" if tc else "gemm_q_kernel (grouped)"
     if dt == DType.F32:
-        return "gemm_f32_kernel"
-    return "gemv_kernel" if N <= 4 else "gemm_q_kernel"
+        return "gemm_f32_exact_kernel"
+    if N <= 4:
+        return "gemv_kernel"
+    return "gemm_tc_kernel (tcgen05)" if tc else "gemm_q_kernel"
 
 
 # ---------------------------------------------------------------------------
@@ -361,7 +364,7 @@ def run_b200(args, cfg, N):
         achieved = ops_step / sec_step / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"],
-                "peak_note": f"bf16 dense {peaks['source']} (the kernel issues int8 MMA; int8 peak not measured)"}
+                "peak_note": f"bf16 dense {peaks['source']} (the kernel issues f16 tcgen05 MMAs on exact integer / split operands)"}
     else:
         achieved = alg_bytes / sec_step / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",

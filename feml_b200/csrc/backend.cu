@@ -60,11 +60,19 @@ uint64_t align256(uint64_t v) { return (v + 255) / 256 * 256; }
 // mul_mat / mul_mat_id dispatch on device pointers (shared by graph_compute
 // and the kernel-level entry points).
 // ---------------------------------------------------------------------------
+// Shapes for the tcgen05 GEMM, decided from the shape alone so that the
+// workspace query and the launch agree (unaligned operands fall back to the
+// mma.sync GEMM, which the workspace also covers).
+bool tc_shape(int32_t wtype, int64_t K, int64_t M, int64_t N) {
+    return (wtype == FB_Q8_0 || wtype == FB_Q4_0) && !fbk::gemv_supported(wtype, K, N) &&
+           fbk::gemm_tc_supported(wtype, K, M, N, nullptr, 0);
+}
+
 uint64_t mul_mat_ws(int32_t wtype, int64_t K, int64_t M, int64_t N) {
-    (void)M;
     if (wtype == FB_F32) return 0;
     if (fbk::gemv_supported(wtype, K, N) && fbk::gemv_fused_ok(K, N)) return 0;
-    return fbk::q8_planar_bytes(K, N);
+    const uint64_t planar = fbk::q8_planar_bytes(K, N);
+    return tc_shape(wtype, K, M, N) ? std::max<uint64_t>(planar, fbk::xhilo_bytes(K, N)) : planar;
 }
 
 int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
@@ -83,6 +91,13 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
         return set_error(FB_ERR_INVALID, "mul_mat: workspace of %lu bytes needed, %lu given", (unsigned long)need,
                          (unsigned long)ws_bytes);
     if (need == 0) return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, nullptr, status, s, true);
+    if (tc_shape(wtype, K, M, N) && fbk::gemm_tc_supported(wtype, K, M, N, w, w_nb1) &&
+        ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0) {
+        const fbk::XHiLo xh = fbk::xhilo_carve(ws, K, N);
+        int rc = fbk::launch_quantize_q8_hilo(x, x_nb1, K, N, xh, nullptr, s);
+        if (rc) return rc;
+        return fbk::launch_gemm_tc(wtype, w, w_nb1, xh, K, M, N, y, y_nb1, nullptr, status, s);
+    }
 
     const fbk::Q8Planar xq = fbk::q8_planar_carve(ws, K, N);
     int rc = fbk::launch_quantize_q8_planar(x, x_nb1, K, N, xq, s);
@@ -110,6 +125,11 @@ struct IdWorkspace {
     uint64_t total;
 };
 
+// mul_mat_id shapes for the tcgen05 GEMM (shape-only, as for mul_mat).
+bool id_tc_shape(int32_t wtype, int64_t K, int64_t N, int64_t n_sel) {
+    return (wtype == FB_Q8_0 || wtype == FB_Q4_0) && fbk::gemm_tc_supported(wtype, K, 1, N * n_sel, nullptr, 0);
+}
+
 IdWorkspace id_ws_layout(void *base, int32_t wtype, int64_t K, int64_t N, int64_t n_sel, int64_t E) {
     IdWorkspace L{};
     uint8_t *p = static_cast<uint8_t *>(base);
@@ -123,7 +143,9 @@ IdWorkspace id_ws_layout(void *base, int32_t wtype, int64_t K, int64_t N, int64_
     L.offsets = reinterpret_cast<int32_t *>(take(4 * E));
     L.tile_start = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
     L.rows = reinterpret_cast<int32_t *>(take(4 * n_sel * N));
-    L.xq = wtype == FB_F32 ? nullptr : take(fbk::q8_planar_bytes(K, N));
+    uint64_t xq_bytes = fbk::q8_planar_bytes(K, N);
+    if (id_tc_shape(wtype, K, N, n_sel)) xq_bytes = std::max<uint64_t>(xq_bytes, fbk::xhilo_bytes(K, N * n_sel));
+    L.xq = wtype == FB_F32 ? nullptr : take(xq_bytes);
     L.total = off;
     return L;
 }
@@ -149,8 +171,13 @@ int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, 
         return set_error(FB_ERR_INVALID, "mul_mat_id: workspace of %lu bytes needed, %lu given",
                          (unsigned long)need.total, (unsigned long)ws_bytes);
     const IdWorkspace L = id_ws_layout(ws, wtype, K, N, n_sel, n_local);
-    const int block_n = wtype == FB_F32 ? fbk::gemm_f32_block_n() : fbk::gemm_q_block_n();
-    if (wtype != FB_F32 && !fbk::gemm_q_supported(wtype, K, w, w_nb1))
+    const bool use_tc = id_tc_shape(wtype, K, N, n_sel) && n_local > 0 &&
+                        fbk::gemm_tc_supported(wtype, K, M, N * n_sel, w, w_nb1) && (w_nb2 & 15) == 0 &&
+                        ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0;
+    const int block_n = wtype == FB_F32 ? fbk::gemm_f32_block_n()
+                        : use_tc        ? fbk::gemm_tc_block_n()
+                                        : fbk::gemm_q_block_n();
+    if (wtype != FB_F32 && !use_tc && !fbk::gemm_q_supported(wtype, K, w, w_nb1))
         return set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: quantized experts need K %% 256 == 0 and 16-byte aligned rows");
     int rc = fbk::launch_moe_route(ids, ids_nb1, n_sel, N, E, shard, n_shards, L.counts, L.offsets, L.rows,
                                    L.tile_start, block_n, status, dst, dst_nb1, dst_nb2, M, s);
@@ -168,6 +195,12 @@ int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, 
     g.max_tiles = (int32_t)((n_sel * N + block_n - 1) / block_n + n_local);
     if (n_local == 0) return FB_OK;
     if (wtype == FB_F32) return fbk::launch_gemm_f32_grouped(w, w_nb1, x, x_nb1, K, M, dst, g, s);
+    if (use_tc) {
+        const fbk::XHiLo xh = fbk::xhilo_carve(L.xq, K, N * n_sel);
+        rc = fbk::launch_quantize_q8_hilo(x, x_nb1, K, N, xh, &g, s);
+        if (rc) return rc;
+        return fbk::launch_gemm_tc(wtype, w, w_nb1, xh, K, M, N, dst, 0, &g, status, s);
+    }
     const fbk::Q8Planar xq = fbk::q8_planar_carve(L.xq, K, N);
     rc = fbk::launch_quantize_q8_planar(x, x_nb1, K, N, xq, s);
     if (rc) return rc;

@@ -64,6 +64,29 @@ int launch_gemm_q(int32_t wtype, const void *w, uint64_t w_nb1, const Q8Planar &
                   void *y, uint64_t y_nb1, const GroupMap *groups, cudaStream_t s);
 int gemm_q_block_n();
 
+// gemm_tc.cu: tcgen05/TMEM GEMM for Q8_0 / Q4_0 weights (K % 256 == 0,
+// 16-byte aligned rows). Activations come as XHiLo: per row n, per block b,
+// 64 f16 [hi 32 | lo 32] of the Q8_0-dequantized values scaled by
+// 1/rscale[n] (x at row pitch K/32*128 bytes), rscale a power of two.
+struct XHiLo {
+    void *x;
+    float *rscale;
+};
+uint64_t xhilo_bytes(int64_t K, int64_t N);
+XHiLo xhilo_carve(void *base, int64_t K, int64_t N);
+bool gemm_tc_supported(int32_t wtype, int64_t K, int64_t M, int64_t N, const void *w, uint64_t w_nb1);
+struct GroupMap;
+// With `routed` (mul_mat_id), the N * n_selected output rows are the routed
+// slots in expert order (row r from token routed->rows[r] / n_selected).
+int launch_quantize_q8_hilo(const void *x, uint64_t x_nb1, int64_t K, int64_t N, XHiLo out, const GroupMap *routed,
+                            cudaStream_t s);
+// With `groups` (mul_mat_id): expert planes w + e*groups->w_group_stride,
+// activation rows = routed slots (N tokens x n_selected), outputs through
+// the group map. Column tiles of groups->tile_start use gemm_tc_block_n().
+int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XHiLo &xhl, int64_t K, int64_t M, int64_t N,
+                   void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s);
+int gemm_tc_block_n();
+
 // Per-block int32 sums (bit-exactness probe); xq in ggml Q8_0 layout.
 int launch_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *xq, int64_t K, int64_t M, int64_t N,
                       int32_t *out, cudaStream_t s);

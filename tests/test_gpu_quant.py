@@ -77,7 +77,7 @@ SHAPES = [
     (256, 7, 1), (512, 33, 2), (1024, 130, 3), (4096, 256, 4),     # decode GEMV, fused quantization
     (8192, 40, 4),                                                  # GEMV with a pre-quantized activation buffer
     (512, 100, 5), (1024, 64, 8), (256, 300, 16), (2048, 200, 64),  # GEMM path
-    (768, 150, 33), (256, 1, 100), (4096, 257, 128),
+    (768, 150, 33), (256, 1, 100), (4096, 257, 128), (512, 130, 300),
 ]
 
 
@@ -149,3 +149,27 @@ def test_repeated_calls_are_deterministic(b200):
     a = run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
     b = run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0])
+def test_large_activations_stay_in_tolerance(b200, dt):
+    """Activations far beyond the f16 range (rows up to 1e6, one row of
+    zeros) through the large-N path: per-row power-of-two normalisation
+    keeps every operand finite."""
+    rng = np.random.default_rng(77)
+    K, M, N = 1024, 160, 40
+    wq = O.quantize(QT[dt], weights(rng, M, K))
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    x *= np.logspace(-3, 6, N, dtype=np.float32)[:, None]
+    x[7] = 0.0
+    got = run_mul_mat(b200, dt, wq, x, K, M)
+    want = O.mul_mat_quant_ref(QT[dt], wq, x, K)
+    assert np.isfinite(got).all()
+    # at these magnitudes any two f32 summation orders differ by a few ulps of
+    # the partial sums, so the bound scales with sum_k |W||X| (the sum's
+    # condition), not with |y|
+    wd = np.abs(O.dequantize(QT[dt], wq, K)).astype(np.float64)
+    xd = np.abs(O.dequantize(O.DT_Q8_0, O.quantize(O.DT_Q8_0, x), K)).astype(np.float64)
+    bound = 1e-3 + 2e-5 * (xd @ wd.T)
+    err = np.abs(got.astype(np.float64) - want)
+    assert (err <= bound).all(), f"max err/bound {float((err / bound).max())}"

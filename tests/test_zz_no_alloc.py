@@ -19,7 +19,7 @@ QT = {DType.Q8_0: O.DT_Q8_0, DType.Q4_0: O.DT_Q4_0, DType.Q4_K: O.DT_Q4_K}
     (DType.Q8_0, 4096, 4096, 8),    # quantized activations in scratch, GEMV on 8 columns
     (DType.Q4_0, 1024, 300, 33),    # tiled GEMM over the scratch activations
     (DType.Q4_K, 2048, 256, 1),     # fused GEMV: no scratch used
-    (DType.Q8_0, 4096, 512, 1500),  # large scratch (about 7.7 MB)
+    (DType.Q8_0, 4096, 512, 600),   # large scratch (about 9.8 MB)
 ])
 def test_noalloc_matches_workspace_entry_point(dt, K, M, N):
     torch.cuda.set_device(0)
