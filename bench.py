@@ -247,7 +247,18 @@ def kernels_per_step(cfg, N):
     if dt == DType.F32:
         return 1
     from feml_b200 import ops
-    return 1 if ops.mul_mat_workspace(dt, cfg["K"], cfg["M"], N) == 0 else 2
+    if ops.mul_mat_workspace(dt, cfg["K"], cfg["M"], N) == 0:
+        return 1  # fused GEMV
+    tc = dt in (DType.Q8_0, DType.Q4_0) and cfg["K"] % 256 == 0 and N > 4
+    split = (not tc and N > 4 and cfg["K"] % 256 == 0 and
+             ops.mul_mat_workspace(dt, cfg["K"], cfg["M"], N) > _planar_bytes(cfg["K"], N))
+    return 3 if split else 2  # activation quantizer + GEMM (+ split-K reduction)
+
+
+def _planar_bytes(K, N):
+    """Planar Q8_0 activation bytes (qs, d, sum, each padded to 256 B)."""
+    pad = lambda v: (v + 255) // 256 * 256  # noqa: E731
+    return pad(N * K) + 2 * pad(N * (K // 32) * 4)
 
 
 def dominant_kernel(cfg, N):

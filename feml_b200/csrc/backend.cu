@@ -8,10 +8,11 @@
 //    32-bit handles; every byte range is checked before any copy.
 //  - write/read are blocking (feml-cuda/src/backend.rs:96-141); fill and
 //    graph_compute are asynchronous until synchronize().
-//  - graph_compute allocates nothing: intermediates (Q8_0 activations, MoE
-//    routing tables) live in a device scratch arena sized whenever a Compute
-//    buffer is created (scratch >= compute buffer bytes covers every node whose
-//    activations live in that buffer).
+//  - Intermediates (quantized activations, split-K partials, MoE routing
+//    tables) live in one device scratch arena. It is sized when a Compute
+//    buffer is created and, if a plan's largest node needs more, grown once
+//    (synchronizing the device) at that plan's first graph_compute; after
+//    that graph_compute allocates nothing.
 //  - Kernels record data-dependent failures (bad mul_mat_id ids, a wait that
 //    ran out) in a device status word that synchronize() reads and clears.
 #include <cuda_runtime.h>
@@ -64,15 +65,16 @@ uint64_t align256(uint64_t v) { return (v + 255) / 256 * 256; }
 // workspace query and the launch agree (unaligned operands fall back to the
 // mma.sync GEMM, which the workspace also covers).
 bool tc_shape(int32_t wtype, int64_t K, int64_t M, int64_t N) {
-    return (wtype == FB_Q8_0 || wtype == FB_Q4_0) && !fbk::gemv_supported(wtype, K, N) &&
-           fbk::gemm_tc_supported(wtype, K, M, N, nullptr, 0);
+    return !fbk::gemv_supported(wtype, K, N) && fbk::gemm_tc_supported(wtype, K, M, N, nullptr, 0);
 }
 
 uint64_t mul_mat_ws(int32_t wtype, int64_t K, int64_t M, int64_t N) {
     if (wtype == FB_F32) return 0;
     if (fbk::gemv_supported(wtype, K, N) && fbk::gemv_fused_ok(K, N)) return 0;
-    const uint64_t planar = fbk::q8_planar_bytes(K, N);
-    return tc_shape(wtype, K, M, N) ? std::max<uint64_t>(planar, fbk::xhilo_bytes(K, N)) : planar;
+    // planar activations + split-K partials for the mma.sync GEMM; the
+    // tcgen05 path needs the hi/lo activations instead
+    const uint64_t planar = fbk::q8_planar_bytes(K, N) + fbk::gemm_q_split_bytes(K, M, N);
+    return tc_shape(wtype, K, M, N) ? std::max<uint64_t>(planar, fbk::xq16_bytes(K, N, M, false)) : planar;
 }
 
 int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
@@ -93,10 +95,10 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
     if (need == 0) return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, nullptr, status, s, true);
     if (tc_shape(wtype, K, M, N) && fbk::gemm_tc_supported(wtype, K, M, N, w, w_nb1) &&
         ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0) {
-        const fbk::XHiLo xh = fbk::xhilo_carve(ws, K, N);
-        int rc = fbk::launch_quantize_q8_hilo(x, x_nb1, K, N, xh, nullptr, s);
+        const fbk::XQ16 xa = fbk::xq16_carve(ws, K, N);
+        int rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, nullptr, s);
         if (rc) return rc;
-        return fbk::launch_gemm_tc(wtype, w, w_nb1, xh, K, M, N, y, y_nb1, nullptr, status, s);
+        return fbk::launch_gemm_tc(wtype, w, w_nb1, xa, K, M, N, y, y_nb1, nullptr, status, s);
     }
 
     const fbk::Q8Planar xq = fbk::q8_planar_carve(ws, K, N);
@@ -105,7 +107,8 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
     if (fbk::gemv_supported(wtype, K, N))
         return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, &xq, status, s, true);
     if (fbk::gemm_q_supported(wtype, K, w, w_nb1))
-        return fbk::launch_gemm_q(wtype, w, w_nb1, xq, K, M, N, y, y_nb1, nullptr, s);
+        return fbk::launch_gemm_q(wtype, w, w_nb1, xq, K, M, N, y, y_nb1, nullptr, s,
+                                  static_cast<uint8_t *>(ws) + fbk::q8_planar_bytes(K, N));
     // Shapes the GEMM cannot tile (K % 256 != 0, unaligned rows): the GEMV on
     // groups of up to 4 columns of the already-quantized activations.
     const int64_t nblk = K / 32;
@@ -127,7 +130,7 @@ struct IdWorkspace {
 
 // mul_mat_id shapes for the tcgen05 GEMM (shape-only, as for mul_mat).
 bool id_tc_shape(int32_t wtype, int64_t K, int64_t N, int64_t n_sel) {
-    return (wtype == FB_Q8_0 || wtype == FB_Q4_0) && fbk::gemm_tc_supported(wtype, K, 1, N * n_sel, nullptr, 0);
+    return fbk::gemm_tc_supported(wtype, K, 1, N * n_sel, nullptr, 0);
 }
 
 IdWorkspace id_ws_layout(void *base, int32_t wtype, int64_t K, int64_t N, int64_t n_sel, int64_t E) {
@@ -144,7 +147,7 @@ IdWorkspace id_ws_layout(void *base, int32_t wtype, int64_t K, int64_t N, int64_
     L.tile_start = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
     L.rows = reinterpret_cast<int32_t *>(take(4 * n_sel * N));
     uint64_t xq_bytes = fbk::q8_planar_bytes(K, N);
-    if (id_tc_shape(wtype, K, N, n_sel)) xq_bytes = std::max<uint64_t>(xq_bytes, fbk::xhilo_bytes(K, N * n_sel));
+    if (id_tc_shape(wtype, K, N, n_sel)) xq_bytes = std::max<uint64_t>(xq_bytes, fbk::xq16_bytes(K, N * n_sel, 0, true));
     L.xq = wtype == FB_F32 ? nullptr : take(xq_bytes);
     L.total = off;
     return L;
@@ -196,10 +199,10 @@ int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, 
     if (n_local == 0) return FB_OK;
     if (wtype == FB_F32) return fbk::launch_gemm_f32_grouped(w, w_nb1, x, x_nb1, K, M, dst, g, s);
     if (use_tc) {
-        const fbk::XHiLo xh = fbk::xhilo_carve(L.xq, K, N * n_sel);
-        rc = fbk::launch_quantize_q8_hilo(x, x_nb1, K, N, xh, &g, s);
+        const fbk::XQ16 xa = fbk::xq16_carve(L.xq, K, N * n_sel);
+        rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, &g, s);
         if (rc) return rc;
-        return fbk::launch_gemm_tc(wtype, w, w_nb1, xh, K, M, N, dst, 0, &g, status, s);
+        return fbk::launch_gemm_tc(wtype, w, w_nb1, xa, K, M, N, dst, 0, &g, status, s);
     }
     const fbk::Q8Planar xq = fbk::q8_planar_carve(L.xq, K, N);
     rc = fbk::launch_quantize_q8_planar(x, x_nb1, K, N, xq, s);
@@ -592,13 +595,41 @@ int feml_b200_supports_op(fb_backend *, int32_t op, const int32_t *dt, int32_t n
     }
 }
 
+// Scratch bytes a node needs (0 for shapes the launch checks reject anyway).
+uint64_t node_scratch(const fb_plan *plan, const fb_plan_tensor &node) {
+    auto src = [&](int k) -> const fb_plan_tensor * {
+        if (k >= node.n_srcs || node.srcs[k] < 0 || node.srcs[k] >= plan->n_tensors) return nullptr;
+        return &plan->tensors[node.srcs[k]];
+    };
+    const fb_plan_tensor *w = src(0), *x = src(1);
+    if (!w || !x || !is_weight_dtype(w->dtype)) return 0;
+    const int64_t K = w->ne[0], M = w->ne[1], N = x->ne[1];
+    if (K <= 0 || M <= 0 || N <= 0 || K > (int64_t(1) << 31) || N > (int64_t(1) << 31)) return 0;
+    if (node.op == FB_OP_MUL_MAT) return mul_mat_ws(w->dtype, K, M, N);
+    const fb_plan_tensor *ids = src(2);
+    if (node.op == FB_OP_MUL_MAT_ID && ids && ids->ne[0] > 0 && ids->ne[0] <= 1024 && w->ne[2] > 0)
+        return id_ws_layout(nullptr, w->dtype, K, N, ids->ne[0], w->ne[2]).total;
+    return 0;
+}
+
 int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
     if (!b || !plan) return set_error(FB_ERR_INVALID, "graph_compute: null argument");
     std::lock_guard<std::mutex> lk(b->mu);
     DeviceGuard g(b->device);
+    // scratch for the largest node; grows (with a device synchronize) only the
+    // first time a plan needs more than the arena holds
+    uint64_t need = 0;
     for (int64_t i = 0; i < plan->n_nodes; i++) {
         const int64_t ti = plan->nodes[i];
         if (ti < 0 || ti >= plan->n_tensors) return set_error(FB_ERR_INVALID, "graph_compute: bad node index");
+        need = std::max(need, node_scratch(plan, plan->tensors[ti]));
+    }
+    if (need > b->scratch_bytes) {
+        const int rc = grow_scratch(b, need);
+        if (rc) return rc;
+    }
+    for (int64_t i = 0; i < plan->n_nodes; i++) {
+        const int64_t ti = plan->nodes[i];
         const fb_plan_tensor &node = plan->tensors[ti];
         int rc;
         switch (node.op) {

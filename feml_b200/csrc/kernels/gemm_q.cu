@@ -57,6 +57,10 @@ struct GemmQParams {
     uint64_t y_nb1;
     GroupMap g;
     bool grouped;
+    // split-K: CTA z of gridDim.z walks chunks [z*split_chunks, ...) and
+    // writes its partial tile to partial[z][n][m] (reduced afterwards)
+    int split_chunks;
+    float *partial;
 };
 
 template <int WT, int BM>
@@ -184,11 +188,13 @@ __global__ void __launch_bounds__(THREADS) gemm_q_kernel(const GemmQParams p) {
 #pragma unroll
             for (int k = 0; k < 4; k++) acc[i][j][k] = 0.0f;
 
-    load_stage(0, 0);
+    const int c_begin = p.partial ? (int)blockIdx.z * p.split_chunks : 0;
+    const int c_end = p.partial ? min(nchunks, c_begin + p.split_chunks) : nchunks;
+    load_stage(0, c_begin);
     cp_async_commit();
-    for (int c = 0; c < nchunks; c++) {
-        const int st = c & 1;
-        if (c + 1 < nchunks) {
+    for (int c = c_begin; c < c_end; c++) {
+        const int st = (c - c_begin) & 1;
+        if (c + 1 < c_end) {
             load_stage(st ^ 1, c + 1);
             cp_async_commit();
             cp_async_wait<1>();
@@ -297,7 +303,12 @@ __global__ void __launch_bounds__(THREADS) gemm_q_kernel(const GemmQParams p) {
             for (int i = 0; i < 4; i++) {
                 const int r = m0 + wm * 32 + mt * 16 + g + 8 * (i >> 1);
                 const int col = wn * WN + nt * 8 + t4 * 2 + (i & 1);
-                if (r < p.M && csrc[col] >= 0) reinterpret_cast<float *>(p.y + cdst[col])[r] = acc[mt][nt][i];
+                if (r < p.M && csrc[col] >= 0) {
+                    if (p.partial)
+                        p.partial[((uint64_t)blockIdx.z * p.N + csrc[col]) * p.M + r] = acc[mt][nt][i];
+                    else
+                        reinterpret_cast<float *>(p.y + cdst[col])[r] = acc[mt][nt][i];
+                }
             }
 }
 
@@ -314,16 +325,30 @@ int launch_bm(const GemmQParams &p, int tiles_n, cudaStream_t s) {
         if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_q: smem attribute: %s", cudaGetErrorString(e));
         if (dev >= 0 && dev < 64) smem_set[dev] = true;
     }
-    dim3 grid((p.M + BM - 1) / BM, tiles_n);
+    const int splits = p.partial ? (p.K / KC + p.split_chunks - 1) / p.split_chunks : 1;
+    dim3 grid((p.M + BM - 1) / BM, tiles_n, splits);
     kern<<<grid, THREADS, S::total, s>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_q launch: %s", cudaGetErrorString(e));
     return FB_OK;
 }
 
+// y[n][m] = sum over z in order of partial[z][n][m] (deterministic).
+__global__ void split_reduce_kernel(const float *__restrict__ partial, int splits, int M, int N, uint8_t *y,
+                                    uint64_t y_nb1) {
+    const int64_t total = (int64_t)M * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        float acc = partial[i];
+        for (int z = 1; z < splits; z++) acc += partial[(int64_t)z * total + i];
+        const int n = (int)(i / M), m = (int)(i % M);
+        reinterpret_cast<float *>(y + (uint64_t)n * y_nb1)[m] = acc;
+    }
+}
+
 template <int WT>
 int launch_wt(const GemmQParams &p, int tiles_n, cudaStream_t s) {
     const int64_t sms = sm_count();
+    if (p.partial) return launch_bm<WT, 128>(p, tiles_n, s);
     const int64_t t128 = (int64_t)((p.M + 127) / 128) * tiles_n;
     const int64_t t64 = (int64_t)((p.M + 63) / 64) * tiles_n;
     if (t128 >= 2 * sms) return launch_bm<WT, 128>(p, tiles_n, s);
@@ -392,6 +417,24 @@ __global__ void block_dots_kernel(const uint8_t *w, uint64_t w_nb1, const uint8_
 
 int gemm_q_block_n() { return BN; }
 
+// Split-K plan of the ungrouped GEMM: used when the BM = 128 tile grid would
+// leave most SMs idle; every split walks at least two chunks.
+int gemm_q_splits(int64_t K, int64_t M, int64_t N) {
+    const int64_t nchunks = K / KC;
+    const int64_t tiles = ((M + 127) / 128) * ((N + BN - 1) / BN);
+    const int64_t sms = sm_count();
+    if (nchunks < 4 || tiles >= sms) return 1;
+    int64_t splits = std::min<int64_t>({(2 * sms + tiles - 1) / tiles, nchunks / 2, 16});
+    if (splits < 2) return 1;
+    const int64_t per = (nchunks + splits - 1) / splits;
+    return (int)((nchunks + per - 1) / per);
+}
+
+uint64_t gemm_q_split_bytes(int64_t K, int64_t M, int64_t N) {
+    const int sp = gemm_q_splits(K, M, N);
+    return sp > 1 ? (uint64_t)sp * (uint64_t)M * (uint64_t)N * 4 : 0;
+}
+
 bool gemm_q_supported(int32_t wtype, int64_t K, const void *w, uint64_t w_nb1) {
     if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K) return false;
     if (K <= 0 || K % KC) return false;
@@ -399,7 +442,7 @@ bool gemm_q_supported(int32_t wtype, int64_t K, const void *w, uint64_t w_nb1) {
 }
 
 int launch_gemm_q(int32_t wtype, const void *w, uint64_t w_nb1, const Q8Planar &xq, int64_t K, int64_t M, int64_t N,
-                  void *y, uint64_t y_nb1, const GroupMap *groups, cudaStream_t s) {
+                  void *y, uint64_t y_nb1, const GroupMap *groups, cudaStream_t s, void *split_ws) {
     if (!gemm_q_supported(wtype, K, w, w_nb1))
         return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_q: needs K %% 256 == 0 and 16-byte aligned weight rows");
     if (K > INT32_MAX || M > INT32_MAX || N > INT32_MAX) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_q: too large");
@@ -426,11 +469,25 @@ int launch_gemm_q(int32_t wtype, const void *w, uint64_t w_nb1, const Q8Planar &
     }
     if (M == 0 || tiles_n == 0) return FB_OK;
     if (tiles_n > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_q: too many column tiles");
-    switch (wtype) {
-    case WT_Q8_0: return launch_wt<WT_Q8_0>(p, tiles_n, s);
-    case WT_Q4_0: return launch_wt<WT_Q4_0>(p, tiles_n, s);
-    default: return launch_wt<WT_Q4_K>(p, tiles_n, s);
+    const int splits = groups ? 1 : gemm_q_splits(K, M, N);
+    if (splits > 1 && split_ws) {
+        const int nchunks = (int)(K / KC);
+        p.split_chunks = (nchunks + splits - 1) / splits;
+        p.partial = static_cast<float *>(split_ws);
     }
+    int rc;
+    switch (wtype) {
+    case WT_Q8_0: rc = launch_wt<WT_Q8_0>(p, tiles_n, s); break;
+    case WT_Q4_0: rc = launch_wt<WT_Q4_0>(p, tiles_n, s); break;
+    default: rc = launch_wt<WT_Q4_K>(p, tiles_n, s); break;
+    }
+    if (rc || !p.partial) return rc;
+    const int64_t total = M * N;
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
+    split_reduce_kernel<<<blocks, 256, 0, s>>>(p.partial, splits, (int)M, (int)N, static_cast<uint8_t *>(y), y_nb1);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_q split reduce launch: %s", cudaGetErrorString(e));
+    return FB_OK;
 }
 
 int launch_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *xq, int64_t K, int64_t M, int64_t N,

@@ -1,41 +1,46 @@
 // Quantized mul_mat on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
 // Arithmetic. The reference result is the F32 mul_mat of the dequantized
-// weights W[m,k] = dw[m,b] * qw[m,k] and the dequantized Q8_0 activations
-// X[n,k] = dx[n,b] * qx[n,k] (b = k / 32; feml-cpu/src/ops/mul_mat.rs:36-57
-// on dequantized operands). Per 32-element block b this kernel computes
-//     T_b[m,n] = sum_{k in b} qw[m,k] * X[n,k]
-// on the tensor core in f32 with f16 operands that are exact:
-//   * qw is an integer in [-128, 127] (Q8_0) or [-8, 7] (Q4_0): exact in f16;
-//   * X[n,k] (an f32 with at most 11 + 8 significant bits) is split into
-//     X = hi + lo, hi = f16(X), lo = f16(X - hi), both exact in f16 for the
-//     activation range after a per-row power-of-two normalisation;
-// so T_b = qw.hi + qw.lo takes two MMAs of K = 32 (four of K = 16) into one
-// TMEM accumulator slot, and the epilogue applies the row's block scale in
-// FP32:  acc[m,n] += dw[m,b] * T_b[m,n]  (one FFMA per element and block).
-// Products qw*hi and qw*lo are exact in f32; only the f32 sums round, so the
-// result is within the path's tolerance of the reference (not bit-exact).
+// weights and the dequantized Q8_0 activations X[n,k] = dx[n,b] * qx[n,k]
+// (b = k / 32; feml-cpu/src/ops/mul_mat.rs:36-57 on dequantized operands).
+// Per 32-element block b the tensor core computes the integer dot product
+//     T_b[m,n] = sum_{k in b} qw[m,k] * qx[n,k]
+// with f16 operands holding exact integers (qx in [-127, 127]; qw in
+// [-128, 127] for Q8_0, [-8, 7] for Q4_0, [0, 15] for Q4_K) and an f32
+// accumulator that represents every partial sum exactly (|T| < 2^19). The
+// epilogue applies the block scales in FP32:
+//     Q8_0 / Q4_0:  acc += T_b * (dw[m,b] * dx[n,b])
+//     Q4_K:         acc += T_b * (d*sc[m,b] * dx[n,b]) - dmin*m[m,b] * (dx[n,b] * sum_k qx[n,k])
+// so T is exact and only the scale products and the f32 sum round: results
+// are within the path's tolerance of the reference, not bit-identical.
 //
-// Tiles and roles (one CTA of 512 threads per SM, BM = 128 rows, BN = 128
-// columns, full K):
-//   warp 0      TMA producer: raw weight chunks (8 blocks x 128 rows) into a
-//               ring (2D tensor map over the ggml rows, no swizzle).
-//   warp 1      TMA producer: activation panels [hi 32 | lo 32] per block,
-//               128-byte swizzled, two blocks per stage.
-//   warp 2      allocates TMEM (512 columns = 4 slots of 128) and issues the
-//               MMAs from one thread (kind::f16, M = 128, N = 128, K = 16).
-//   warps 4-7   converters: unpack each weight row's blocks into integer
-//               f16 (bit tricks, no conversion instructions), store them in
-//               the 128-byte swizzled K-major layout the MMA reads, and
-//               publish the block scales.
-//   warps 8-15  epilogue: per block, read the slot (tcgen05.ld 32x32b),
-//               acc += dw * T, release the slot; finally store acc.
+// Tiles and roles: one CTA of 512 threads per SM computes a 128 x 128
+// output tile (rows m, activation rows n) over a K range (all of K, or a
+// split-K slice written to a partial buffer and summed afterwards in a fixed
+// order).
+//   warp 0      TMA: raw weight rows, 8 blocks x 128 rows per chunk (tensor
+//               map over the ggml rows; rank 3 for mul_mat_id experts).
+//   warp 1      TMA: activation panels (128 rows x 64 f16 integers = two
+//               blocks, 128-byte swizzle).
+//   warp 3      stages the activation block scales of each pair (one pair
+//               ahead) into the scale ring for the epilogue.
+//   warp 2      allocates TMEM (2 slots of 2 x 128 f32 columns, one block
+//               pair each) and issues the MMAs (kind::f16, M = 128, N = 128,
+//               K = 16) from one thread, one commit per pair.
+//   warps 4-7   converters: one weight row each; unpack blocks into integer
+//               f16 (prmt/lop3 + one half2 add, no conversion instructions),
+//               store them in the swizzled K-major layout the MMA reads,
+//               publish the row's block scales.
+//   warps 8-15  epilogue: per block, read the slot with tcgen05.ld 32x32b,
+//               apply the scales, release the slot; store at the end.
 // Every barrier wait is bounded; on timeout the CTA raises STATUS_TIMEOUT,
-// drains the copies and MMAs it issued and frees its TMEM before returning.
+// lets the copies and MMAs it issued land and frees its TMEM before it
+// returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "../host_common.h"
@@ -49,26 +54,35 @@ namespace {
 constexpr int TC_BM = 128;
 constexpr int TC_BN = 128;
 constexpr int TC_THREADS = 512;
-constexpr int TC_SLOTS = 4;           // TMEM accumulator slots (one block each)
-constexpr int TC_TMEM_COLS = 512;     // TC_SLOTS * TC_BN
-constexpr int TC_NS = 8;              // block-scale ring (pairs)
-constexpr int A_STAGE = TC_BM * 128;  // one pair of blocks: 128 rows x 64 f16
-constexpr int B_PANEL = TC_BN * 128;  // one block: BN rows x [hi 32 | lo 32] f16
-constexpr int B_STAGE = 2 * B_PANEL;
+constexpr int TC_PSLOTS = 2;           // TMEM accumulator slots, one block pair (2 x 128 columns) each
+constexpr int TC_TMEM_COLS = 512;      // TC_PSLOTS * 2 * TC_BN f32 columns
+constexpr int TC_ND = 8;               // pair-done barrier ring (one MMA commit per pair)
+constexpr int TC_NS = 8;               // scale ring depth (block pairs)
+constexpr int A_STAGE = TC_BM * 128;   // a block pair: 128 rows x 64 f16
+constexpr int B_STAGE = TC_BN * 128;   // a block pair: 128 rows x 64 f16
+constexpr int CHUNK_PAIRS = 4;         // 8 blocks per raw weight chunk
 
 template <int WT>
 struct TcCfg;
 template <>
 struct TcCfg<WT_Q8_0> {
     static constexpr int RAWB = 8 * Q8_0_BYTES;  // 272 bytes: 8 blocks of one row
-    static constexpr int NR = 2, NA = 3, NB = 3;
+    static constexpr int NR = 2, NA = 4, NB = 4, SCN = 2;
 };
 template <>
 struct TcCfg<WT_Q4_0> {
     static constexpr int RAWB = 8 * Q4_0_BYTES;  // 144
-    static constexpr int NR = 2, NA = 4, NB = 3;
+    static constexpr int NR = 4, NA = 4, NB = 4, SCN = 2;
+};
+template <>
+struct TcCfg<WT_Q4_K> {
+    static constexpr int RAWB = Q4_K_BYTES;  // 144: one super-block
+    static constexpr int NR = 3, NA = 4, NB = 4, SCN = 4;
 };
 
+// Scale ring entry (per block pair): SCN planes x 2 blocks x 128 floats.
+// plane 0: weight scale per row (Q4_K: d*sc), plane 1: activation scale per
+// column; Q4_K adds plane 2: dmin*m per row, plane 3: dx*sum(qx) per column.
 template <int WT>
 struct TcLayout {
     using C = TcCfg<WT>;
@@ -77,26 +91,27 @@ struct TcLayout {
     static constexpr int OFF_B = OFF_A + C::NA * A_STAGE;
     static constexpr int OFF_RAW = OFF_B + C::NB * B_STAGE;
     static constexpr int OFF_SC = OFF_RAW + ((C::NR * RAW_STAGE + 1023) / 1024) * 1024;
-    static constexpr int OFF_BAR = OFF_SC + TC_NS * 2 * TC_BM * 4;
-    static constexpr int N_BARS = 2 * (C::NR + C::NA + C::NB + TC_SLOTS + TC_NS) + 1;
+    static constexpr int SC_PAIR = C::SCN * 2 * 128;  // floats per ring entry
+    static constexpr int OFF_BAR = OFF_SC + TC_NS * SC_PAIR * 4;
+    static constexpr int N_BARS = 2 * C::NR + C::NA + C::NB + TC_PSLOTS + TC_ND + 2 * TC_NS + 1;
     static constexpr int OFF_MISC = OFF_BAR + N_BARS * 8;
     static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 };
 
 struct TcParams {
-    int M, N, K;
+    int M, N, K;          // N: activation rows of the operand buffer
     uint8_t *y;
     uint64_t y_nb1;
-    const float *rscale;  // per activation row: 2^e undone in the epilogue
+    const float *dxT;     // [K/32][N] activation block scales
+    const float *xsdT;    // [K/32][N] dx * sum(qx) (Q4_K)
     int32_t *status;
-    // grouped mode (mul_mat_id): activation rows are the routed slots in
-    // expert order; column tile blockIdx.y belongs to the expert whose
-    // tile_start range holds it, and weights come from that expert's plane
-    bool grouped;
+    bool grouped;         // mul_mat_id: column tiles through the group map
     GroupMap g;
+    int split_pairs;      // split-K: pairs per CTA along blockIdx.z (0: none)
+    float *partial;       // [splits][N][M] when split
 };
 
-// ---- tcgen05 / TMA primitives (inline PTX) -----------------------------------
+// ---- TMA / tcgen05 primitives (inline PTX) -----------------------------------
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -122,7 +137,7 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                  : "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, f16 inputs, f32 accumulate.
+// D[tmem] (+)= A[smem] * B[smem]^T, f16 operands, f32 accumulator.
 __device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
     asm volatile(
@@ -170,9 +185,9 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
     return false;
 }
 
-// Warp-uniform form for roles that then run .sync.aligned instructions: lane
-// 0 polls, the verdict is broadcast, and every lane re-reads the completed
-// phase (acquire) before touching the data it guards.
+// Warp-uniform form for roles that then run .sync.aligned instructions or
+// read what the barrier guards: lane 0 polls, the verdict is broadcast, and
+// every lane re-reads the completed phase (acquire).
 __device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int lane) {
     int ok = 0;
     if (lane == 0) ok = tc_wait(bar, parity, abort_flag) ? 1 : 0;
@@ -189,23 +204,23 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t sel) {
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
-// 4 signed bytes -> 4 f16 integers (two half2 words), exact.
-// (0x6400 | (b ^ 0x80)) is the f16 1024 + (b + 128); subtracting 1152 gives b.
+// 4 signed bytes -> 4 f16 integers (two half2 words), exact:
+// (0x6400 | (b ^ 0x80)) is the f16 1024 + (b + 128); minus 1152 gives b.
 __device__ __forceinline__ void q8_word_to_f16(uint32_t w, uint32_t &lo, uint32_t &hi) {
     const __half2 off = __half2half2(__ushort_as_half(0x6480));  // 1152
-    const uint32_t a = (prmt(w, 0x4140) ^ 0x00800080u) | 0x64006400u;
-    const uint32_t b = (prmt(w, 0x4342) ^ 0x00800080u) | 0x64006400u;
-    lo = h2_bits(__hsub2(bits_h2(a), off));
-    hi = h2_bits(__hsub2(bits_h2(b), off));
+    lo = h2_bits(__hsub2(bits_h2((prmt(w, 0x4140) ^ 0x00800080u) | 0x64006400u), off));
+    hi = h2_bits(__hsub2(bits_h2((prmt(w, 0x4342) ^ 0x00800080u) | 0x64006400u), off));
 }
 
-// 4 Q4_0 bytes -> low nibbles (elements j..j+3) and high nibbles (j+16..j+19)
-// as f16 integers minus 8, exact. Low: 1024 + n - 1032; high: the nibble sits
-// at bit 4, (1024 + 16 n) / 16 - 72 = n - 8.
-__device__ __forceinline__ void q4_word_to_f16(uint32_t w, uint32_t (&lo)[2], uint32_t (&hi)[2]) {
-    const __half2 off_lo = __half2half2(__ushort_as_half(0x6408));   // 1032
-    const __half2 sc_hi = __half2half2(__ushort_as_half(0x2C00));    // 1/16
-    const __half2 off_hi = __half2half2(__ushort_as_half(0xD480));   // -72
+// 4 nibble bytes -> low nibbles (4 values) and high nibbles (4 values) as f16
+// integers minus `bias` (8 for Q4_0, 0 for Q4_K), exact. Low: the f16
+// 1024 + n minus (1024 + bias); high: the nibble sits at bit 4,
+// (1024 + 16 n) / 16 - (64 + bias).
+template <int BIAS>
+__device__ __forceinline__ void nib_word_to_f16(uint32_t w, uint32_t (&lo)[2], uint32_t (&hi)[2]) {
+    const __half2 off_lo = __half2half2(__ushort_as_half(BIAS == 8 ? 0x6408 : 0x6400));  // 1032 / 1024
+    const __half2 sc_hi = __half2half2(__ushort_as_half(0x2C00));                        // 1/16
+    const __half2 off_hi = __half2half2(__ushort_as_half(BIAS == 8 ? 0xD480 : 0xD400));  // -72 / -64
     const uint32_t a = prmt(w, 0x4140), b = prmt(w, 0x4342);
     lo[0] = h2_bits(__hsub2(bits_h2((a & 0x000F000Fu) | 0x64006400u), off_lo));
     lo[1] = h2_bits(__hsub2(bits_h2((b & 0x000F000Fu) | 0x64006400u), off_lo));
@@ -228,43 +243,79 @@ __device__ __forceinline__ void store_a_block(uint32_t a_stage, int row, int j, 
     }
 }
 
-// Convert block pair p (blocks 2p, 2p+1 of an 8-block raw row held in
-// registers) into f16 integers; returns the two scales.
+__device__ __forceinline__ uint32_t byte_of(const uint32_t *w, int k) { return (w[k >> 2] >> (8 * (k & 3))) & 0xFFu; }
+
+// Convert block pair p of a raw chunk row held in registers (w) into f16
+// integers. Returns the pair's row scales (sc0, sc1) and, for Q4_K, the
+// min scales (mn0, mn1).
 template <int WT>
 __device__ __forceinline__ void convert_pair(const uint32_t *w, int p, uint32_t (&v0)[16], uint32_t (&v1)[16],
-                                             float &d0, float &d1) {
+                                             float &sc0, float &sc1, float &mn0, float &mn1) {
+    mn0 = mn1 = 0.0f;
     if constexpr (WT == WT_Q8_0) {
         // block 2p at byte 68p (word 17p): d in the low half, qs from byte 2
         const int b = 17 * p;
-        d0 = f16_bits_to_f32((uint16_t)(w[b] & 0xFFFFu));
+        sc0 = f16_bits_to_f32((uint16_t)(w[b] & 0xFFFFu));
 #pragma unroll
         for (int i = 0; i < 8; i++) q8_word_to_f16(__funnelshift_r(w[b + i], w[b + i + 1], 16), v0[2 * i], v0[2 * i + 1]);
-        // block 2p+1 at byte 68p + 34: d in the high half of word 17p+8, qs word-aligned
-        d1 = f16_bits_to_f32((uint16_t)(w[b + 8] >> 16));
+        // block 2p+1 at byte 68p + 34: d in the high half of word 17p+8
+        sc1 = f16_bits_to_f32((uint16_t)(w[b + 8] >> 16));
 #pragma unroll
         for (int i = 0; i < 8; i++) q8_word_to_f16(w[b + 9 + i], v1[2 * i], v1[2 * i + 1]);
-    } else {
-        // Q4_0: block 2p at byte 36p (word 9p), block 2p+1 at byte 36p + 18
+    } else if constexpr (WT == WT_Q4_0) {
+        // block 2p at byte 36p (word 9p), block 2p+1 at byte 36p + 18
         const int b = 9 * p;
-        d0 = f16_bits_to_f32((uint16_t)(w[b] & 0xFFFFu));
+        sc0 = f16_bits_to_f32((uint16_t)(w[b] & 0xFFFFu));
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             uint32_t lo[2], hi[2];
-            q4_word_to_f16(__funnelshift_r(w[b + i], w[b + i + 1], 16), lo, hi);
+            nib_word_to_f16<8>(__funnelshift_r(w[b + i], w[b + i + 1], 16), lo, hi);
             v0[2 * i] = lo[0];
             v0[2 * i + 1] = lo[1];
             v0[8 + 2 * i] = hi[0];
             v0[8 + 2 * i + 1] = hi[1];
         }
-        d1 = f16_bits_to_f32((uint16_t)(w[b + 4] >> 16));
+        sc1 = f16_bits_to_f32((uint16_t)(w[b + 4] >> 16));
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             uint32_t lo[2], hi[2];
-            q4_word_to_f16(w[b + 5 + i], lo, hi);
+            nib_word_to_f16<8>(w[b + 5 + i], lo, hi);
             v1[2 * i] = lo[0];
             v1[2 * i + 1] = lo[1];
             v1[8 + 2 * i] = hi[0];
             v1[8 + 2 * i + 1] = hi[1];
+        }
+    } else {
+        // Q4_K super-block: d (f16), dmin (f16), 12 bytes of 6-bit scales and
+        // mins, 128 bytes of nibbles. Sub-blocks 2p and 2p+1 are the low and
+        // high nibbles of bytes 16 + 32p .. 16 + 32p + 31.
+        const float d = f16_bits_to_f32((uint16_t)(w[0] & 0xFFFFu));
+        const float dmin = f16_bits_to_f32((uint16_t)(w[0] >> 16));
+        int sc[2], mn[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int j = 2 * p + h;
+            if (j < 4) {
+                sc[h] = (int)(byte_of(w, 4 + j) & 63u);
+                mn[h] = (int)(byte_of(w, 8 + j) & 63u);
+            } else {
+                sc[h] = (int)((byte_of(w, 8 + j) & 0x0Fu) | ((byte_of(w, j) >> 6) << 4));
+                mn[h] = (int)((byte_of(w, 8 + j) >> 4) | ((byte_of(w, j + 4) >> 6) << 4));
+            }
+        }
+        sc0 = d * (float)sc[0];
+        sc1 = d * (float)sc[1];
+        mn0 = dmin * (float)mn[0];
+        mn1 = dmin * (float)mn[1];
+        const int b = 4 + 8 * p;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            uint32_t lo[2], hi[2];
+            nib_word_to_f16<0>(w[b + i], lo, hi);
+            v0[2 * i] = lo[0];
+            v0[2 * i + 1] = lo[1];
+            v1[2 * i] = hi[0];
+            v1[2 * i + 1] = hi[1];
         }
     }
 }
@@ -279,23 +330,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *gbase = smem_raw + (sbase - smem_u32(smem_raw));
 
-    uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + L::OFF_BAR);
-    uint64_t *raw_full = bars;
-    uint64_t *raw_empty = raw_full + C::NR;
-    uint64_t *a_full = raw_empty + C::NR;
-    uint64_t *a_empty = a_full + C::NA;
-    uint64_t *b_full = a_empty + C::NA;
-    uint64_t *b_empty = b_full + C::NB;
-    uint64_t *t_full = b_empty + C::NB;
-    uint64_t *t_empty = t_full + TC_SLOTS;
-    uint64_t *s_full = t_empty + TC_SLOTS;
-    uint64_t *s_empty = s_full + TC_NS;
-    uint64_t *mma_done = s_empty + TC_NS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + L::OFF_MISC);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + L::OFF_MISC + 4);
-    float *scales = reinterpret_cast<float *>(gbase + L::OFF_SC);
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int m0 = blockIdx.x * TC_BM;
     // activation rows [xrow0, xrow0 + ncols) of this tile, weight plane `expert`
     int xrow0 = blockIdx.y * TC_BN, ncols = min(TC_BN, p.N - xrow0), expert = 0;
@@ -307,27 +341,46 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         xrow0 = p.g.offsets[expert] + jt * TC_BN;
         ncols = min(TC_BN, p.g.counts[expert] - jt * TC_BN);
     }
-    const int nblk = p.K / QK, npairs = nblk / 2, nchunks = p.K / QKK;
+    // K range in block pairs (split-K: a slice per blockIdx.z); chunks of 4 pairs
+    const int total_pairs = p.K / (2 * QK);
+    const int pair0 = p.split_pairs ? (int)blockIdx.z * p.split_pairs : 0;
+    const int npairs = p.split_pairs ? min(p.split_pairs, total_pairs - pair0) : total_pairs;
+    const int chunk0 = pair0 / CHUNK_PAIRS, nchunks = npairs / CHUNK_PAIRS;
+
+    // Barriers. tcgen05.commit arrivals complete one after another (a few
+    // hundred cycles each), so the MMA thread commits once per block pair:
+    // pair_done[q % TC_ND] completes when pair q's MMAs have finished, which
+    // at once frees its A and B stages and hands its TMEM slot to the
+    // epilogue.
+    uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + L::OFF_BAR);
+    uint64_t *raw_full = bars;
+    uint64_t *raw_empty = raw_full + C::NR;
+    uint64_t *a_full = raw_empty + C::NR;
+    uint64_t *b_full = a_full + C::NA;
+    uint64_t *t_empty = b_full + C::NB;
+    uint64_t *pair_done = t_empty + TC_PSLOTS;
+    uint64_t *s_full = pair_done + TC_ND;
+    uint64_t *s_empty = s_full + TC_NS;
+    uint64_t *mma_done = s_empty + TC_NS;
+    // phase parity of pair_done for pair q
+    auto done_parity = [](int q) { return (uint32_t)((q / TC_ND) & 1); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + L::OFF_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + L::OFF_MISC + 4);
+    float *ring = reinterpret_cast<float *>(gbase + L::OFF_SC);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
         for (int i = 0; i < C::NR; i++) {
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], 128);
         }
-        for (int i = 0; i < C::NA; i++) {
-            mbar_init(&a_full[i], 128);
-            mbar_init(&a_empty[i], 1);
-        }
-        for (int i = 0; i < C::NB; i++) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 1);
-        }
-        for (int i = 0; i < TC_SLOTS; i++) {
-            mbar_init(&t_full[i], 1);
-            mbar_init(&t_empty[i], 8);
-        }
+        for (int i = 0; i < C::NA; i++) mbar_init(&a_full[i], 128);
+        for (int i = 0; i < C::NB; i++) mbar_init(&b_full[i], 1);
+        for (int i = 0; i < TC_PSLOTS; i++) mbar_init(&t_empty[i], 8);
+        for (int i = 0; i < TC_ND; i++) mbar_init(&pair_done[i], 1);
         for (int i = 0; i < TC_NS; i++) {
-            mbar_init(&s_full[i], 128);
+            mbar_init(&s_full[i], 128 + 32);  // converter rows + the activation-scale warp
             mbar_init(&s_empty[i], 8);
         }
         mbar_init(mma_done, 1);
@@ -354,7 +407,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int s = c % C::NR;
                 if (!tc_wait(&raw_empty[s], ((c / C::NR) & 1) ^ 1, abort_flag)) break;
                 mbar_arrive_expect_tx(&raw_full[s], L::RAW_STAGE);
-                const int x0 = WT == WT_Q8_0 ? c * (C::RAWB / 2) : c * C::RAWB;
+                const int gc = chunk0 + c;
+                const int x0 = WT == WT_Q8_0 ? gc * (C::RAWB / 2) : gc * C::RAWB;
                 tma_load_3d(sbase + L::OFF_RAW + s * L::RAW_STAGE, &tm_w, x0, m0, expert, smem_u32(&raw_full[s]));
                 armed[s] = (c / C::NR) & 1;
             }
@@ -369,16 +423,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int i = 0; i < C::NB; i++) armed[i] = -1;
             for (int q = 0; q < npairs; q++) {
                 const int s = q % C::NB;
-                if (!tc_wait(&b_empty[s], ((q / C::NB) & 1) ^ 1, abort_flag)) break;
+                if (q >= C::NB && !tc_wait(&pair_done[(q - C::NB) % TC_ND], done_parity(q - C::NB), abort_flag)) break;
                 mbar_arrive_expect_tx(&b_full[s], B_STAGE);
-                const uint32_t dst = sbase + L::OFF_B + s * B_STAGE;
-                tma_load_2d(dst, &tm_x, (2 * q) * 64, xrow0, smem_u32(&b_full[s]));
-                tma_load_2d(dst + B_PANEL, &tm_x, (2 * q + 1) * 64, xrow0, smem_u32(&b_full[s]));
+                tma_load_2d(sbase + L::OFF_B + s * B_STAGE, &tm_x, (pair0 + q) * 64, xrow0, smem_u32(&b_full[s]));
                 armed[s] = (q / C::NB) & 1;
             }
             if (*abort_flag)
                 for (int i = 0; i < C::NB; i++)
                     if (armed[i] >= 0) mbar_wait_bounded(&b_full[i], (uint32_t)armed[i]);
+        }
+    } else if (warp == 3) {
+        // ---- activation block scales into the scale ring (one pair ahead) -------
+        // lane l stages columns 4l..4l+3 of both blocks of a pair
+        constexpr int NP = C::SCN / 2;  // per-column planes: dx (+ dx*sum(qx) for Q4_K)
+        auto load = [&](int q, float4 (&v)[NP][2]) {
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const uint64_t base = (uint64_t)(2 * (pair0 + q) + j) * (uint64_t)p.N + xrow0;
+#pragma unroll
+                for (int pl = 0; pl < NP; pl++) {
+                    const float *src = pl == 0 ? p.dxT : p.xsdT;
+                    float t[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) t[i] = (4 * lane + i < ncols) ? src[base + 4 * lane + i] : 0.0f;
+                    v[pl][j] = make_float4(t[0], t[1], t[2], t[3]);
+                }
+            }
+        };
+        float4 cur[NP][2], nxt[NP][2];
+        if (npairs > 0) load(0, cur);
+        for (int q = 0; q < npairs; q++) {
+            if (q + 1 < npairs) load(q + 1, nxt);
+            const int ss = q % TC_NS;
+            if (!tc_wait_warp(&s_empty[ss], ((q / TC_NS) & 1) ^ 1, abort_flag, lane)) break;
+            float *e = ring + ss * L::SC_PAIR;
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+#pragma unroll
+                for (int pl = 0; pl < NP; pl++)
+                    *reinterpret_cast<float4 *>(e + ((1 + 2 * pl) * 2 + j) * 128 + 4 * lane) = cur[pl][j];
+            mbar_arrive(&s_full[ss]);
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+#pragma unroll
+                for (int pl = 0; pl < NP; pl++) cur[pl][j] = nxt[pl][j];
         }
     } else if (warp == 2) {
         // ---- MMA issue (one thread) ---------------------------------------------
@@ -392,27 +480,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     ok = false;
                     break;
                 }
+                const int ps = q % TC_PSLOTS;
+                if (!tc_wait(&t_empty[ps], ((q / TC_PSLOTS) & 1) ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t a_addr = sbase + L::OFF_A + sa * A_STAGE;
                 const uint32_t b_addr = sbase + L::OFF_B + sb * B_STAGE;
+#pragma unroll
                 for (int j = 0; j < 2; j++) {
-                    const int blk = 2 * q + j, slot = blk % TC_SLOTS;
-                    if (!tc_wait(&t_empty[slot], ((blk / TC_SLOTS) & 1) ^ 1, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t d = tmem + (uint32_t)(slot * TC_BN);
-                    const uint32_t aj = a_addr + 64u * j, bj = b_addr + (uint32_t)B_PANEL * j;
-                    tc_mma_f16(d, sw128_desc(aj), sw128_desc(bj), idesc, 0u);            // hi, k 0-15
-                    tc_mma_f16(d, sw128_desc(aj + 32), sw128_desc(bj + 32), idesc, 1u);  // hi, k 16-31
-                    tc_mma_f16(d, sw128_desc(aj), sw128_desc(bj + 64), idesc, 1u);       // lo, k 0-15
-                    tc_mma_f16(d, sw128_desc(aj + 32), sw128_desc(bj + 96), idesc, 1u);  // lo, k 16-31
-                    tc_commit(smem_u32(&t_full[slot]));
+                    const uint32_t d = tmem + (uint32_t)((2 * ps + j) * TC_BN);
+                    const uint32_t aj = a_addr + 64u * j, bj = b_addr + 64u * j;
+                    tc_mma_f16(d, sw128_desc(aj), sw128_desc(bj), idesc, 0u);            // k 0-15
+                    tc_mma_f16(d, sw128_desc(aj + 32), sw128_desc(bj + 32), idesc, 1u);  // k 16-31
                 }
-                if (!ok) break;
-                tc_commit(smem_u32(&a_empty[sa]));
-                tc_commit(smem_u32(&b_empty[sb]));
+                tc_commit(smem_u32(&pair_done[q % TC_ND]));
             }
             // all issued MMAs complete before TMEM can be released
             tc_commit(smem_u32(mma_done));
@@ -438,22 +521,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_arrive(&raw_empty[s]);
             bool ok = true;
 #pragma unroll
-            for (int pp = 0; pp < 4; pp++) {
-                const int q = 4 * c + pp;
+            for (int pp = 0; pp < CHUNK_PAIRS; pp++) {
+                const int q = CHUNK_PAIRS * c + pp;
                 const int sa = q % C::NA, ss = q % TC_NS;
-                if (!tc_wait_warp(&a_empty[sa], ((q / C::NA) & 1) ^ 1, abort_flag, lane) ||
+                if ((q >= C::NA &&
+                     !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane)) ||
                     !tc_wait_warp(&s_empty[ss], ((q / TC_NS) & 1) ^ 1, abort_flag, lane)) {
                     ok = false;
                     break;
                 }
+                // the stage was last read by the tensor core (async proxy):
+                // order those reads before this thread's generic stores
+                fence_proxy_async_smem();
                 uint32_t v0[16], v1[16];
-                float d0, d1;
-                convert_pair<WT>(w, pp, v0, v1, d0, d1);
+                float sc0, sc1, mn0, mn1;
+                convert_pair<WT>(w, pp, v0, v1, sc0, sc1, mn0, mn1);
                 const uint32_t a_addr = sbase + L::OFF_A + sa * A_STAGE;
                 store_a_block(a_addr, row, 0, v0);
                 store_a_block(a_addr, row, 1, v1);
-                scales[(ss * 2 + 0) * TC_BM + row] = d0;
-                scales[(ss * 2 + 1) * TC_BM + row] = d1;
+                float *e = ring + ss * L::SC_PAIR;
+                e[0 * 128 + row] = sc0;
+                e[1 * 128 + row] = sc1;
+                if constexpr (C::SCN == 4) {
+                    e[4 * 128 + row] = mn0;
+                    e[5 * 128 + row] = mn1;
+                }
                 fence_proxy_async_smem();
                 mbar_arrive(&a_full[sa]);
                 mbar_arrive(&s_full[ss]);
@@ -474,15 +566,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 ok = false;
                 break;
             }
+            const float *e = ring + ss * L::SC_PAIR;
+            const int ps = q % TC_PSLOTS;
+            if (!tc_wait_warp(&pair_done[q % TC_ND], done_parity(q), abort_flag, lane)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
 #pragma unroll
             for (int j = 0; j < 2; j++) {
-                const int blk = 2 * q + j, slot = blk % TC_SLOTS;
-                if (!tc_wait_warp(&t_full[slot], (blk / TC_SLOTS) & 1, abort_flag, lane)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const float dw = scales[(ss * 2 + j) * TC_BM + row];
+                const int slot = 2 * ps + j;
+                const float sw = e[(0 * 2 + j) * 128 + row];
+                const float mw = C::SCN == 4 ? e[(2 * 2 + j) * 128 + row] : 0.0f;
+                const float4 *dxv = reinterpret_cast<const float4 *>(e + (1 * 2 + j) * 128 + 64 * h);
+                const float4 *xsv = reinterpret_cast<const float4 *>(e + (3 * 2 + j) * 128 + 64 * h);
                 const uint32_t taddr = tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(slot * TC_BN + 64 * h);
 #pragma unroll
                 for (int cc = 0; cc < 2; cc++) {
@@ -490,14 +587,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     tc_ld32(taddr + 32u * cc, r);
                     tc_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) acc[32 * cc + i] = fmaf(__uint_as_float(r[i]), dw, acc[32 * cc + i]);
+                    for (int i4 = 0; i4 < 8; i4++) {
+                        const float4 dx = dxv[8 * cc + i4];
+                        const float dxa[4] = {dx.x, dx.y, dx.z, dx.w};
+                        if constexpr (C::SCN == 4) {
+                            const float4 xs = xsv[8 * cc + i4];
+                            const float xsa[4] = {xs.x, xs.y, xs.z, xs.w};
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                const int i = 32 * cc + 4 * i4 + u;
+                                acc[i] = fmaf(-mw, xsa[u], fmaf(__uint_as_float(r[4 * i4 + u]), sw * dxa[u], acc[i]));
+                            }
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                const int i = 32 * cc + 4 * i4 + u;
+                                acc[i] = fmaf(__uint_as_float(r[4 * i4 + u]), sw * dxa[u], acc[i]);
+                            }
+                        }
+                    }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&t_empty[slot]);
             }
+            tc_fence_before();
             __syncwarp();
-            if (ok && lane == 0) mbar_arrive(&s_empty[ss]);
+            if (lane == 0) {
+                mbar_arrive(&t_empty[ps]);
+                mbar_arrive(&s_empty[ss]);
+            }
         }
         if (ok) {
             const int m = m0 + row;
@@ -507,15 +623,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const int c = 64 * h + i;
                     if (c < ncols) {
                         const int r = xrow0 + c;
-                        uint64_t off;
-                        if (p.grouped) {
-                            const int slot = p.g.rows[r];
-                            off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 +
-                                  (uint64_t)(slot / p.g.n_selected) * p.g.dst_nb2;
+                        if (p.partial) {
+                            p.partial[((uint64_t)blockIdx.z * p.N + r) * p.M + m] = acc[i];
                         } else {
-                            off = (uint64_t)r * p.y_nb1;
+                            uint64_t off;
+                            if (p.grouped) {
+                                const int slot = p.g.rows[r];
+                                off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 +
+                                      (uint64_t)(slot / p.g.n_selected) * p.g.dst_nb2;
+                            } else {
+                                off = (uint64_t)r * p.y_nb1;
+                            }
+                            reinterpret_cast<float *>(p.y + off)[m] = acc[i];
                         }
-                        reinterpret_cast<float *>(p.y + off)[m] = acc[i] * p.rscale[r];
                     }
                 }
             }
@@ -532,50 +652,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
-// ---- activations: Q8_0 quantize, dequantize, split into f16 hi + lo ---------
-// One CTA per activation row. The row is scaled by 2^-e (e >= 0, chosen so
-// |X| stays below 2^14 and hi never overflows f16); rscale[n] = 2^e is
-// multiplied back in the GEMM epilogue (exact: powers of two).
-constexpr int HL_THREADS = 256;
+// ---- activations: Q8_0 quantize into exact f16 integers + block scales -------
+// One CTA per activation row r (with `routed`, the activation of routed slot
+// r: token g.rows[r] / n_selected, for r < sum(counts)). Writes q16[r][k]
+// (f16 integer), dxT[b][r] = dx (the f16 block scale as f32) and
+// xsdT[b][r] = dx * sum(qx) (both [K/32][rows]).
+constexpr int QF_THREADS = 256;
 
-// With `routed` (mul_mat_id), output row r is the activation of routed slot
-// r (token rows[r] / n_selected) for the r < sum(counts) routed slots.
-__global__ void __launch_bounds__(HL_THREADS) quantize_q8_hilo_kernel(const uint8_t *__restrict__ x, uint64_t x_nb1,
-                                                                     int K, uint8_t *__restrict__ out,
-                                                                     float *__restrict__ rscale, bool routed,
-                                                                     GroupMap g) {
-    __shared__ float red[HL_THREADS / 32];
-    const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
-    int src = n;
+__global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8_t *__restrict__ x, uint64_t x_nb1,
+                                                                    int K, int rows, __half *__restrict__ q16,
+                                                                    float *__restrict__ dxT, float *__restrict__ xsdT,
+                                                                    bool routed, GroupMap g) {
+    const int r = blockIdx.x, tid = threadIdx.x;
+    int src = r;
     if (routed) {
-        if (g.n_groups == 0 || n >= g.offsets[g.n_groups - 1] + g.counts[g.n_groups - 1]) return;
-        src = g.rows[n] / g.n_selected;
+        if (g.n_groups == 0 || r >= g.offsets[g.n_groups - 1] + g.counts[g.n_groups - 1]) return;
+        src = g.rows[r] / g.n_selected;
     }
     const float *xr = reinterpret_cast<const float *>(x + (uint64_t)src * x_nb1);
-    float amax = 0.0f;
-    for (int k = tid * 4; k < K; k += HL_THREADS * 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(xr + k);
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-    amax = warp_max(amax);
-    if (lane == 0) red[tid >> 5] = amax;
-    __syncthreads();
-    amax = red[0];
-#pragma unroll
-    for (int i = 1; i < HL_THREADS / 32; i++) amax = fmaxf(amax, red[i]);
-    // 2^-e with amax * 2^-e < 2^14 (the f16-rounded block scale can exceed amax by 2^-11)
-    int e = 0;
-    if (amax >= 16384.0f && amax <= 3.0e38f) e = min(126, (int)ceilf(log2f(amax / 16384.0f)) + 1);
-    const float down = exp2f((float)-e);
-    if (tid == 0) rscale[n] = exp2f((float)e);
-
     const int nblk = K / QK;
-    uint16_t *orow = reinterpret_cast<uint16_t *>(out + (uint64_t)n * nblk * 128);
+    __half *orow = q16 + (uint64_t)r * K;
     // 8 lanes per block, 4 elements per lane; every lane of the warp calls the
     // quantize routine (uniform trip count)
-    const int groups = (nblk + 31) / 32;  // 32 blocks per CTA pass
-    for (int g = 0; g < groups; g++) {
-        const int b = g * 32 + (tid >> 3);
+    for (int base = 0; base < nblk; base += QF_THREADS / 8) {
+        const int b = base + (tid >> 3);
         const int k = b * QK + (tid & 7) * 4;
         const bool valid = b < nblk;
         const float4 v = valid ? *reinterpret_cast<const float4 *>(xr + k) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -583,20 +683,27 @@ __global__ void __launch_bounds__(HL_THREADS) quantize_q8_hilo_kernel(const uint
         int qsum;
         const uint32_t q = quantize_q8_0_quad(v, dbits, qsum);
         if (!valid) continue;
-        const float d = f16_bits_to_f32(dbits);
-        uint16_t hi[4], lo[4];
+        __half hq[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int qi = (int)(int8_t)((q >> (8 * i)) & 0xFFu);
-            const float xd = __fmul_rn(__fmul_rn(d, (float)qi), down);
-            const __half hh = __float2half_rn(xd);
-            hi[i] = __half_as_ushort(hh);
-            lo[i] = __half_as_ushort(__float2half_rn(__fsub_rn(xd, __half2float(hh))));
+        for (int i = 0; i < 4; i++) hq[i] = __int2half_rn((int)(int8_t)((q >> (8 * i)) & 0xFFu));
+        *reinterpret_cast<uint2 *>(orow + k) = *reinterpret_cast<const uint2 *>(hq);
+        if ((tid & 7) == 0) {
+            const float d = f16_bits_to_f32(dbits);
+            dxT[(uint64_t)b * rows + r] = d;
+            xsdT[(uint64_t)b * rows + r] = d * (float)qsum;
         }
-        uint16_t *ob = orow + b * 64 + (tid & 7) * 4;
-        *reinterpret_cast<uint2 *>(ob) = make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
-        *reinterpret_cast<uint2 *>(ob + 32) =
-            make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
+    }
+}
+
+// y[n][m] = sum over z in order of partial[z][n][m] (deterministic).
+__global__ void tc_split_reduce_kernel(const float *__restrict__ partial, int splits, int M, int N, uint8_t *y,
+                                       uint64_t y_nb1) {
+    const int64_t total = (int64_t)M * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        float acc = partial[i];
+        for (int z = 1; z < splits; z++) acc += partial[(int64_t)z * total + i];
+        const int n = (int)(i / M), m = (int)(i % M);
+        reinterpret_cast<float *>(y + (uint64_t)n * y_nb1)[m] = acc;
     }
 }
 
@@ -605,11 +712,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static std::once_flag once;
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        void *q = nullptr;
+        cudaDriverEntryPointQueryResult res;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &res) == cudaSuccess &&
+            res == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(q);
     });
     return fn;
 }
@@ -631,12 +738,12 @@ int encode_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint6
     return FB_OK;
 }
 
-// N: activation rows in the hi/lo buffer; n_planes / w_nb2: weight planes
-// (experts) for the grouped mode (1 / unused otherwise).
+// rows: activation rows in the operand buffer; n_planes / w_nb2: weight
+// planes (experts) of the grouped mode (1 / unused otherwise).
 template <int WT>
-int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_planes, const void *xhl,
-                    const float *rscale, int64_t K, int64_t M, int64_t N, void *y, uint64_t y_nb1,
-                    const GroupMap *groups, int32_t *status, cudaStream_t s) {
+int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_planes, const XQ16 &xa, int64_t K,
+                    int64_t M, int64_t rows, void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status,
+                    int splits, cudaStream_t s) {
     using C = TcCfg<WT>;
     using L = TcLayout<WT>;
     static_assert(L::BYTES <= 232448, "gemm_tc shared memory");
@@ -650,9 +757,8 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
         rc = encode_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, w_nb1, (uint64_t)M, planes, w_nb1, pstride, C::RAWB,
                         TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    const uint64_t nblk = (uint64_t)K / QK;
-    rc = encode_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xhl, nblk * 64, (uint64_t)N, 0, nblk * 128, 0, 64, TC_BN,
-                    CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = encode_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xa.q16, (uint64_t)K, (uint64_t)rows, 0, (uint64_t)K * 2, 0,
+                    64, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     static int configured[64] = {0};
     int dev = 0;
@@ -664,67 +770,108 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     }
     TcParams p{};
     p.M = (int)M;
-    p.N = (int)N;
+    p.N = (int)rows;
     p.K = (int)K;
     p.y = static_cast<uint8_t *>(y);
     p.y_nb1 = y_nb1;
-    p.rscale = rscale;
+    p.dxT = xa.dxT;
+    p.xsdT = xa.xsdT;
     p.status = status;
     p.grouped = groups != nullptr;
     if (groups) p.g = *groups;
-    const unsigned tiles_n = groups ? (unsigned)groups->max_tiles : (unsigned)((N + TC_BN - 1) / TC_BN);
+    const int total_pairs = (int)(K / (2 * QK));
+    if (splits > 1) {
+        const int per_chunks = (int)((K / QKK + splits - 1) / splits);
+        p.split_pairs = per_chunks * CHUNK_PAIRS;
+        splits = (total_pairs + p.split_pairs - 1) / p.split_pairs;
+        p.partial = xa.partial;
+    }
+    const unsigned tiles_n = groups ? (unsigned)groups->max_tiles : (unsigned)((rows + TC_BN - 1) / TC_BN);
     if (tiles_n == 0 || M == 0) return FB_OK;
     if (tiles_n > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_tc: too many column tiles");
-    dim3 grid((unsigned)((M + TC_BM - 1) / TC_BM), tiles_n);
+    dim3 grid((unsigned)((M + TC_BM - 1) / TC_BM), tiles_n, (unsigned)std::max(splits, 1));
     gemm_tc_kernel<WT><<<grid, TC_THREADS, L::BYTES, s>>>(tw, tx, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc launch: %s", cudaGetErrorString(e));
+    if (p.partial) {
+        const int64_t total = M * rows;
+        const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
+        tc_split_reduce_kernel<<<blocks, 256, 0, s>>>(p.partial, splits, (int)M, (int)rows, static_cast<uint8_t *>(y),
+                                                      y_nb1);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc split reduce launch: %s", cudaGetErrorString(e));
+    }
     return FB_OK;
 }
 
+uint64_t pad256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
 }  // namespace
 
-uint64_t xhilo_bytes(int64_t K, int64_t N) {
-    const uint64_t a = ((uint64_t)N * (uint64_t)K * 4 + 255) & ~uint64_t(255);
-    return a + (((uint64_t)N * 4 + 255) & ~uint64_t(255));
-}
-
-XHiLo xhilo_carve(void *base, int64_t K, int64_t N) {
-    XHiLo r;
-    r.x = base;
-    r.rscale = reinterpret_cast<float *>(static_cast<uint8_t *>(base) +
-                                         (((uint64_t)N * (uint64_t)K * 4 + 255) & ~uint64_t(255)));
-    return r;
-}
-
 bool gemm_tc_supported(int32_t wtype, int64_t K, int64_t M, int64_t N, const void *w, uint64_t w_nb1) {
-    if (wtype != WT_Q8_0 && wtype != WT_Q4_0) return false;
-    if (K <= 0 || K % QKK || K > (1 << 24) || M <= 0 || N <= 0 || M > INT32_MAX || N > INT32_MAX) return false;
+    if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K) return false;
+    if (K <= 0 || K % QKK || K > (1 << 24) || M <= 0 || N <= 0 || M > INT32_MAX || N > INT32_MAX / 64) return false;
     if (((reinterpret_cast<uintptr_t>(w) | w_nb1) & 15) != 0) return false;
     return (N + TC_BN - 1) / TC_BN <= 65535;
 }
 
 int gemm_tc_block_n() { return TC_BN; }
 
-int launch_quantize_q8_hilo(const void *x, uint64_t x_nb1, int64_t K, int64_t N, XHiLo out, const GroupMap *routed,
-                            cudaStream_t s) {
+// Split-K when the tile grid leaves most SMs idle (ungrouped only): one CTA
+// per SM in a single wave, every split at least two weight chunks.
+int gemm_tc_splits(int64_t K, int64_t M, int64_t N) {
+    const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+    const int64_t nchunks = K / QKK, sms = sm_count();
+    if (tiles * 2 > sms || nchunks < 4) return 1;
+    const int64_t splits = std::min<int64_t>({sms / tiles, nchunks / 2, 16});
+    if (splits < 2) return 1;
+    const int64_t per = (nchunks + splits - 1) / splits;
+    return (int)((nchunks + per - 1) / per);
+}
+
+uint64_t xq16_bytes(int64_t K, int64_t rows, int64_t M, bool grouped) {
+    const uint64_t nblk = (uint64_t)K / QK;
+    uint64_t b = pad256((uint64_t)rows * (uint64_t)K * 2) + 2 * pad256(nblk * (uint64_t)rows * 4);
+    if (!grouped) {
+        const int sp = gemm_tc_splits(K, M, rows);
+        if (sp > 1) b += pad256((uint64_t)sp * (uint64_t)M * (uint64_t)rows * 4);
+    }
+    return b;
+}
+
+XQ16 xq16_carve(void *base, int64_t K, int64_t rows) {
+    const uint64_t nblk = (uint64_t)K / QK;
+    uint8_t *p = static_cast<uint8_t *>(base);
+    XQ16 r;
+    r.q16 = p;
+    p += pad256((uint64_t)rows * (uint64_t)K * 2);
+    r.dxT = reinterpret_cast<float *>(p);
+    p += pad256(nblk * (uint64_t)rows * 4);
+    r.xsdT = reinterpret_cast<float *>(p);
+    p += pad256(nblk * (uint64_t)rows * 4);
+    r.partial = reinterpret_cast<float *>(p);
+    return r;
+}
+
+int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, const XQ16 &out,
+                           const GroupMap *routed, cudaStream_t s) {
     const int64_t rows = routed ? N * routed->n_selected : N;
     if (rows == 0) return FB_OK;
     if (K % QK || K <= 0 || K > INT32_MAX / 4 || rows > INT32_MAX)
-        return fb::set_error(FB_ERR_UNSUPPORTED, "quantize_q8_hilo: unsupported shape");
+        return fb::set_error(FB_ERR_UNSUPPORTED, "quantize_q8_f16: unsupported shape");
     if ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15)
-        return fb::set_error(FB_ERR_INVALID, "quantize_q8_hilo: activations must be 16-byte aligned");
+        return fb::set_error(FB_ERR_INVALID, "quantize_q8_f16: activations must be 16-byte aligned");
     GroupMap g{};
     if (routed) g = *routed;
-    quantize_q8_hilo_kernel<<<(unsigned)rows, HL_THREADS, 0, s>>>(static_cast<const uint8_t *>(x), x_nb1, (int)K,
-                                                                 static_cast<uint8_t *>(out.x), out.rscale,
-                                                                 routed != nullptr, g);
+    quantize_q8_f16_kernel<<<(unsigned)rows, QF_THREADS, 0, s>>>(
+        static_cast<const uint8_t *>(x), x_nb1, (int)K, (int)rows, static_cast<__half *>(out.q16), out.dxT, out.xsdT,
+        routed != nullptr, g);
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "quantize_q8_hilo launch: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "quantize_q8_f16 launch: %s", cudaGetErrorString(e));
     return FB_OK;
 }
 
-int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XHiLo &xhl, int64_t K, int64_t M, int64_t N,
+int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa, int64_t K, int64_t M, int64_t N,
                    void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s) {
     const int64_t rows = groups ? N * groups->n_selected : N;
     if (!gemm_tc_supported(wtype, K, M, rows, w, w_nb1))
@@ -734,11 +881,15 @@ int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XHiLo &xh
     if (groups && (groups->n_groups < 1 || (w_nb2 & 15) || ((groups->dst_nb1 | groups->dst_nb2) & 3)))
         return fb::set_error(FB_ERR_INVALID, "gemm_tc: grouped strides");
     if ((reinterpret_cast<uintptr_t>(y) | y_nb1) & 3) return fb::set_error(FB_ERR_INVALID, "gemm_tc: output alignment");
-    if (wtype == WT_Q8_0)
-        return launch_tc_typed<WT_Q8_0>(w, w_nb1, w_nb2, planes, xhl.x, xhl.rscale, K, M, rows, y, y_nb1, groups,
-                                        status, s);
-    return launch_tc_typed<WT_Q4_0>(w, w_nb1, w_nb2, planes, xhl.x, xhl.rscale, K, M, rows, y, y_nb1, groups, status,
-                                    s);
+    const int splits = groups ? 1 : gemm_tc_splits(K, M, rows);
+    switch (wtype) {
+    case WT_Q8_0:
+        return launch_tc_typed<WT_Q8_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s);
+    case WT_Q4_0:
+        return launch_tc_typed<WT_Q4_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s);
+    default:
+        return launch_tc_typed<WT_Q4_K>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s);
+    }
 }
 
 }  // namespace fbk

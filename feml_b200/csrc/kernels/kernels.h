@@ -60,30 +60,38 @@ int launch_gemm_f32_grouped(const void *w, uint64_t w_nb1, const void *x, uint64
                             void *dst, const GroupMap &g, cudaStream_t s);
 int gemm_f32_block_n();
 bool gemm_q_supported(int32_t wtype, int64_t K, const void *w, uint64_t w_nb1);
+// split_ws (ungrouped only): gemm_q_split_bytes(K, M, N) bytes for the
+// split-K partial tiles; null runs without split-K.
 int launch_gemm_q(int32_t wtype, const void *w, uint64_t w_nb1, const Q8Planar &xq, int64_t K, int64_t M, int64_t N,
-                  void *y, uint64_t y_nb1, const GroupMap *groups, cudaStream_t s);
+                  void *y, uint64_t y_nb1, const GroupMap *groups, cudaStream_t s, void *split_ws = nullptr);
 int gemm_q_block_n();
+int gemm_q_splits(int64_t K, int64_t M, int64_t N);
+uint64_t gemm_q_split_bytes(int64_t K, int64_t M, int64_t N);
 
-// gemm_tc.cu: tcgen05/TMEM GEMM for Q8_0 / Q4_0 weights (K % 256 == 0,
-// 16-byte aligned rows). Activations come as XHiLo: per row n, per block b,
-// 64 f16 [hi 32 | lo 32] of the Q8_0-dequantized values scaled by
-// 1/rscale[n] (x at row pitch K/32*128 bytes), rscale a power of two.
-struct XHiLo {
-    void *x;
-    float *rscale;
+// gemm_tc.cu: tcgen05/TMEM GEMM for Q8_0 / Q4_0 / Q4_K weights (K % 256 == 0,
+// 16-byte aligned rows). Activations come quantized to Q8_0 as XQ16: q16
+// [rows][K] exact f16 integers, dxT / xsdT [K/32][rows] (block scale and
+// scale * integer sum), and room for split-K partial tiles.
+struct XQ16 {
+    void *q16;
+    float *dxT;
+    float *xsdT;
+    float *partial;
 };
-uint64_t xhilo_bytes(int64_t K, int64_t N);
-XHiLo xhilo_carve(void *base, int64_t K, int64_t N);
+// Bytes of an XQ16 buffer for `rows` activation rows (plus the split-K
+// partials of an ungrouped M x rows GEMM).
+uint64_t xq16_bytes(int64_t K, int64_t rows, int64_t M, bool grouped);
+XQ16 xq16_carve(void *base, int64_t K, int64_t rows);
 bool gemm_tc_supported(int32_t wtype, int64_t K, int64_t M, int64_t N, const void *w, uint64_t w_nb1);
-struct GroupMap;
-// With `routed` (mul_mat_id), the N * n_selected output rows are the routed
+int gemm_tc_splits(int64_t K, int64_t M, int64_t N);
+// With `routed` (mul_mat_id), the N * n_selected operand rows are the routed
 // slots in expert order (row r from token routed->rows[r] / n_selected).
-int launch_quantize_q8_hilo(const void *x, uint64_t x_nb1, int64_t K, int64_t N, XHiLo out, const GroupMap *routed,
-                            cudaStream_t s);
+int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, const XQ16 &out,
+                           const GroupMap *routed, cudaStream_t s);
 // With `groups` (mul_mat_id): expert planes w + e*groups->w_group_stride,
 // activation rows = routed slots (N tokens x n_selected), outputs through
 // the group map. Column tiles of groups->tile_start use gemm_tc_block_n().
-int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XHiLo &xhl, int64_t K, int64_t M, int64_t N,
+int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa, int64_t K, int64_t M, int64_t N,
                    void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s);
 int gemm_tc_block_n();
 
