@@ -162,6 +162,17 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms
 // 1024 bytes apart (start address, LBO unused = 1, SBO = 1024, version 1,
 // layout SWIZZLE_128B = 2).
@@ -175,11 +186,15 @@ __host__ __device__ constexpr uint32_t f16_idesc(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// Bounded wait that also gives up when another role has aborted.
-__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+// Bounded wait that also gives up when another role has aborted. Roles off
+// the MMA thread's critical path back off between polls (`sleep_ns`): a
+// dozen warps polling mbarriers slow down everyone's barrier operations.
+__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                        uint32_t sleep_ns = 0) {
     for (uint32_t i = 0; i < kWaitLimit; i++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 63u && *abort_flag) return false;
+        if (sleep_ns) __nanosleep(sleep_ns);
     }
     *abort_flag = 1;
     return false;
@@ -188,12 +203,39 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
 // Warp-uniform form for roles that then run .sync.aligned instructions or
 // read what the barrier guards: lane 0 polls, the verdict is broadcast, and
 // every lane re-reads the completed phase (acquire).
-__device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int lane) {
+__device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int lane,
+                                             uint32_t sleep_ns = 32) {
     int ok = 0;
-    if (lane == 0) ok = tc_wait(bar, parity, abort_flag) ? 1 : 0;
+    if (lane == 0) ok = tc_wait(bar, parity, abort_flag, sleep_ns) ? 1 : 0;
     ok = __shfl_sync(0xffffffffu, ok, 0);
     if (ok) mbar_try_wait(bar, parity);
     return ok != 0;
+}
+
+// Packed f32x2 arithmetic (sm_100): one instruction for two lanes' worth of
+// FP32 work, halving the epilogue's issue slots.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_pack_bits(uint32_t a, uint32_t b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t sel) {
@@ -405,7 +447,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int i = 0; i < C::NR; i++) armed[i] = -1;
             for (int c = 0; c < nchunks; c++) {
                 const int s = c % C::NR;
-                if (!tc_wait(&raw_empty[s], ((c / C::NR) & 1) ^ 1, abort_flag)) break;
+                if (!tc_wait(&raw_empty[s], ((c / C::NR) & 1) ^ 1, abort_flag, 64)) break;
                 mbar_arrive_expect_tx(&raw_full[s], L::RAW_STAGE);
                 const int gc = chunk0 + c;
                 const int x0 = WT == WT_Q8_0 ? gc * (C::RAWB / 2) : gc * C::RAWB;
@@ -423,7 +465,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int i = 0; i < C::NB; i++) armed[i] = -1;
             for (int q = 0; q < npairs; q++) {
                 const int s = q % C::NB;
-                if (q >= C::NB && !tc_wait(&pair_done[(q - C::NB) % TC_ND], done_parity(q - C::NB), abort_flag)) break;
+                if (q >= C::NB &&
+                    !tc_wait(&pair_done[(q - C::NB) % TC_ND], done_parity(q - C::NB), abort_flag, 64))
+                    break;
                 mbar_arrive_expect_tx(&b_full[s], B_STAGE);
                 tma_load_2d(sbase + L::OFF_B + s * B_STAGE, &tm_x, (pair0 + q) * 64, xrow0, smem_u32(&b_full[s]));
                 armed[s] = (q / C::NB) & 1;
@@ -556,9 +600,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---- epilogue: warp w reads TMEM lanes 32*(w%4).., columns 64*h.. -------
         const int sub = warp & 3, h = (warp - 8) >> 2;
         const int row = 32 * sub + lane;
-        float acc[64];
+        uint64_t acc2[32];  // columns (2i, 2i+1) as f32x2
 #pragma unroll
-        for (int i = 0; i < 64; i++) acc[i] = 0.0f;
+        for (int i = 0; i < 32; i++) acc2[i] = 0;
         bool ok = true;
         for (int q = 0; q < npairs && ok; q++) {
             const int ss = q % TC_NS;
@@ -573,40 +617,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 break;
             }
             tc_fence_after();
+            // 8 chunks of 16 columns (2 blocks x 4); the load of chunk k+1 is in
+            // flight while chunk k is scaled and accumulated
+            const uint32_t tbase = tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(2 * ps * TC_BN + 64 * h);
+            uint32_t ra[16], rb[16];
+            tc_ld16(tbase, ra);
+            tc_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int slot = 2 * ps + j;
+            for (int k = 0; k < 8; k++) {
+                const int j = k >> 2, cc = k & 3;
+                if (k + 1 < 8) {
+                    const int jn = (k + 1) >> 2, cn = (k + 1) & 3;
+                    if (k & 1)
+                        tc_ld16(tbase + (uint32_t)(jn * TC_BN + 16 * cn), ra);
+                    else
+                        tc_ld16(tbase + (uint32_t)(jn * TC_BN + 16 * cn), rb);
+                }
+                const uint32_t(&r)[16] = (k & 1) ? rb : ra;
                 const float sw = e[(0 * 2 + j) * 128 + row];
-                const float mw = C::SCN == 4 ? e[(2 * 2 + j) * 128 + row] : 0.0f;
-                const float4 *dxv = reinterpret_cast<const float4 *>(e + (1 * 2 + j) * 128 + 64 * h);
-                const float4 *xsv = reinterpret_cast<const float4 *>(e + (3 * 2 + j) * 128 + 64 * h);
-                const uint32_t taddr = tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(slot * TC_BN + 64 * h);
+                const uint64_t sw2 = f2_pack(sw, sw);
+                const float mw = C::SCN == 4 ? -e[(2 * 2 + j) * 128 + row] : 0.0f;
+                const uint64_t mw2 = f2_pack(mw, mw);
+                const float4 *dxv = reinterpret_cast<const float4 *>(e + (1 * 2 + j) * 128 + 64 * h + 16 * cc);
+                const float4 *xsv = reinterpret_cast<const float4 *>(e + (3 * 2 + j) * 128 + 64 * h + 16 * cc);
 #pragma unroll
-                for (int cc = 0; cc < 2; cc++) {
-                    uint32_t r[32];
-                    tc_ld32(taddr + 32u * cc, r);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int i4 = 0; i4 < 8; i4++) {
-                        const float4 dx = dxv[8 * cc + i4];
-                        const float dxa[4] = {dx.x, dx.y, dx.z, dx.w};
-                        if constexpr (C::SCN == 4) {
-                            const float4 xs = xsv[8 * cc + i4];
-                            const float xsa[4] = {xs.x, xs.y, xs.z, xs.w};
-#pragma unroll
-                            for (int u = 0; u < 4; u++) {
-                                const int i = 32 * cc + 4 * i4 + u;
-                                acc[i] = fmaf(-mw, xsa[u], fmaf(__uint_as_float(r[4 * i4 + u]), sw * dxa[u], acc[i]));
-                            }
-                        } else {
-#pragma unroll
-                            for (int u = 0; u < 4; u++) {
-                                const int i = 32 * cc + 4 * i4 + u;
-                                acc[i] = fmaf(__uint_as_float(r[4 * i4 + u]), sw * dxa[u], acc[i]);
-                            }
-                        }
+                for (int i4 = 0; i4 < 4; i4++) {
+                    const float4 dq = dxv[i4];
+                    const uint64_t s01 = f2_mul(sw2, f2_pack(dq.x, dq.y));
+                    const uint64_t s23 = f2_mul(sw2, f2_pack(dq.z, dq.w));
+                    uint64_t &a01 = acc2[8 * cc + 2 * i4];
+                    uint64_t &a23 = acc2[8 * cc + 2 * i4 + 1];
+                    a01 = f2_fma(f2_pack_bits(r[4 * i4], r[4 * i4 + 1]), s01, a01);
+                    a23 = f2_fma(f2_pack_bits(r[4 * i4 + 2], r[4 * i4 + 3]), s23, a23);
+                    if constexpr (C::SCN == 4) {
+                        const float4 xq = xsv[i4];
+                        a01 = f2_fma(mw2, f2_pack(xq.x, xq.y), a01);
+                        a23 = f2_fma(mw2, f2_pack(xq.z, xq.w), a23);
                     }
                 }
+                if (k + 1 < 8) tc_wait_ld();
             }
             tc_fence_before();
             __syncwarp();
@@ -616,6 +665,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         }
         if (ok) {
+            float acc[64];
+#pragma unroll
+            for (int i = 0; i < 32; i++) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
             const int m = m0 + row;
             if (m < p.M) {
 #pragma unroll

@@ -124,3 +124,15 @@ def test_mul_mat_id_shards_compose(b200, dt, n_shards):
     want = O.mul_mat_id_ref(QT[dt], wb, x, ids, K, quantize_act=dt != DType.F32)
     ok, err = tol_ok(union.cpu().numpy(), want)
     assert ok, err
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0, DType.Q4_K])
+def test_mul_mat_id_repeated_calls_are_deterministic(b200, dt):
+    rng = np.random.default_rng(31)
+    E, M, K, N, n_sel = 8, 1024, 2048, 400, 2
+    wt = torch.from_numpy(np.ascontiguousarray(_expert_weights(rng, dt, E, M, K))).cuda()
+    xt = torch.from_numpy(rng.standard_normal((N, K)).astype(np.float32)).cuda()
+    it = torch.from_numpy(topk_ids(rng, N, n_sel, E)).cuda()
+    outs = [ops.mul_mat_id(dt, wt, xt, it, K) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
