@@ -724,7 +724,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=2000)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
-    ap.add_argument("--n", type=int, default=None, help="activation columns (c4: 1, 8 or 64)")
+    ap.add_argument("--tokens", type=int, default=None, help="activation columns N (c4: 1, 8 or 64)")
     ap.add_argument("--e2e-steps", type=int, default=5000)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -732,7 +732,7 @@ def main():
                     help="strong-scaling split of one workload across the ranks (c4: rows, c5: experts)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
-    N = args.n if args.n is not None else cfg["N"]
+    N = args.tokens if args.tokens is not None else cfg["N"]
     if args.impl == "reference":
         run_reference(args, cfg, N)
         return
