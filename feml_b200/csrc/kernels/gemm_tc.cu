@@ -14,7 +14,7 @@
 // so T is exact and only the scale products and the f32 sum round: results
 // are within the path's tolerance of the reference, not bit-identical.
 //
-// Tiles and roles: one CTA of 512 threads per SM computes a 128 x 128
+// Tiles and roles: one CTA of 768 threads per SM computes a 128 x 128
 // output tile (rows m, activation rows n) over a K range (all of K, or a
 // split-K slice written to a partial buffer and summed afterwards in a fixed
 // order).
@@ -31,8 +31,9 @@
 //               f16 (prmt/lop3 + one half2 add, no conversion instructions),
 //               store them in the swizzled K-major layout the MMA reads,
 //               publish the row's block scales.
-//   warps 8-15  epilogue: per block, read the slot with tcgen05.ld 32x32b,
-//               apply the scales, release the slot; store at the end.
+//   warps 8-23  epilogue: 16 warps, each 32 lanes (rows) x 32 columns; per
+//               block read the slot with tcgen05.ld 32x32b, apply the
+//               scales, release the slot; store at the end.
 // Every barrier wait is bounded; on timeout the CTA raises STATUS_TIMEOUT,
 // lets the copies and MMAs it issued land and frees its TMEM before it
 // returns.
@@ -53,7 +54,8 @@ namespace {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BN = 128;
-constexpr int TC_THREADS = 512;
+constexpr int TC_THREADS = 768;      // 4 helper warps, 4 converter warps, 16 epilogue warps
+constexpr int TC_EPI_WARPS = 16;
 constexpr int TC_PSLOTS = 2;           // TMEM accumulator slots, one block pair (2 x 128 columns) each
 constexpr int TC_TMEM_COLS = 512;      // TC_PSLOTS * 2 * TC_BN f32 columns
 constexpr int TC_ND = 8;               // pair-done barrier ring (one MMA commit per pair)
@@ -287,16 +289,39 @@ __device__ __forceinline__ void store_a_block(uint32_t a_stage, int row, int j, 
 
 __device__ __forceinline__ uint32_t byte_of(const uint32_t *w, int k) { return (w[k >> 2] >> (8 * (k & 3))) & 0xFFu; }
 
-// Convert block pair p of a raw chunk row held in registers (w) into f16
-// integers. Returns the pair's row scales (sc0, sc1) and, for Q4_K, the
-// min scales (mn0, mn1).
+// Words of block pair p of a raw chunk row: Q8_0 17 (68 bytes at 68p, 4-byte
+// aligned), Q4_0 9 (36 bytes at 36p), Q4_K 8 (the 32 nibble bytes at
+// 16 + 32p; the super-block header comes separately).
 template <int WT>
-__device__ __forceinline__ void convert_pair(const uint32_t *w, int p, uint32_t (&v0)[16], uint32_t (&v1)[16],
-                                             float &sc0, float &sc1, float &mn0, float &mn1) {
+struct PairWords {
+    static constexpr int N = WT == WT_Q8_0 ? 17 : (WT == WT_Q4_0 ? 9 : 8);
+};
+
+template <int WT>
+__device__ __forceinline__ void load_pair_words(const uint8_t *row, int p, uint32_t (&w)[PairWords<WT>::N]) {
+    if constexpr (WT == WT_Q4_K) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(row + 16 + 32 * p);
+        const uint4 a = src[0], b = src[1];
+        w[0] = a.x, w[1] = a.y, w[2] = a.z, w[3] = a.w;
+        w[4] = b.x, w[5] = b.y, w[6] = b.z, w[7] = b.w;
+    } else {
+        constexpr int PB = WT == WT_Q8_0 ? 68 : 36;
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(row + PB * p);
+#pragma unroll
+        for (int i = 0; i < PairWords<WT>::N; i++) w[i] = src[i];
+    }
+}
+
+// Convert one block pair (its words w; for Q4_K also the super-block header
+// hdr and the pair index p) into f16 integers. Returns the pair's row scales
+// (sc0, sc1) and, for Q4_K, the min scales (mn0, mn1).
+template <int WT>
+__device__ __forceinline__ void convert_pair(const uint32_t *w, const uint32_t *hdr, int p, uint32_t (&v0)[16],
+                                             uint32_t (&v1)[16], float &sc0, float &sc1, float &mn0, float &mn1) {
     mn0 = mn1 = 0.0f;
     if constexpr (WT == WT_Q8_0) {
-        // block 2p at byte 68p (word 17p): d in the low half, qs from byte 2
-        const int b = 17 * p;
+        // block 2p: d in the low half of word 0, qs from byte 2
+        const int b = 0;
         sc0 = f16_bits_to_f32((uint16_t)(w[b] & 0xFFFFu));
 #pragma unroll
         for (int i = 0; i < 8; i++) q8_word_to_f16(__funnelshift_r(w[b + i], w[b + i + 1], 16), v0[2 * i], v0[2 * i + 1]);
@@ -305,8 +330,8 @@ __device__ __forceinline__ void convert_pair(const uint32_t *w, int p, uint32_t 
 #pragma unroll
         for (int i = 0; i < 8; i++) q8_word_to_f16(w[b + 9 + i], v1[2 * i], v1[2 * i + 1]);
     } else if constexpr (WT == WT_Q4_0) {
-        // block 2p at byte 36p (word 9p), block 2p+1 at byte 36p + 18
-        const int b = 9 * p;
+        // block 2p at word 0, block 2p+1 at byte 18
+        const int b = 0;
         sc0 = f16_bits_to_f32((uint16_t)(w[b] & 0xFFFFu));
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -331,29 +356,28 @@ __device__ __forceinline__ void convert_pair(const uint32_t *w, int p, uint32_t 
         // Q4_K super-block: d (f16), dmin (f16), 12 bytes of 6-bit scales and
         // mins, 128 bytes of nibbles. Sub-blocks 2p and 2p+1 are the low and
         // high nibbles of bytes 16 + 32p .. 16 + 32p + 31.
-        const float d = f16_bits_to_f32((uint16_t)(w[0] & 0xFFFFu));
-        const float dmin = f16_bits_to_f32((uint16_t)(w[0] >> 16));
+        const float d = f16_bits_to_f32((uint16_t)(hdr[0] & 0xFFFFu));
+        const float dmin = f16_bits_to_f32((uint16_t)(hdr[0] >> 16));
         int sc[2], mn[2];
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const int j = 2 * p + h;
             if (j < 4) {
-                sc[h] = (int)(byte_of(w, 4 + j) & 63u);
-                mn[h] = (int)(byte_of(w, 8 + j) & 63u);
+                sc[h] = (int)(byte_of(hdr, 4 + j) & 63u);
+                mn[h] = (int)(byte_of(hdr, 8 + j) & 63u);
             } else {
-                sc[h] = (int)((byte_of(w, 8 + j) & 0x0Fu) | ((byte_of(w, j) >> 6) << 4));
-                mn[h] = (int)((byte_of(w, 8 + j) >> 4) | ((byte_of(w, j + 4) >> 6) << 4));
+                sc[h] = (int)((byte_of(hdr, 8 + j) & 0x0Fu) | ((byte_of(hdr, j) >> 6) << 4));
+                mn[h] = (int)((byte_of(hdr, 8 + j) >> 4) | ((byte_of(hdr, j + 4) >> 6) << 4));
             }
         }
         sc0 = d * (float)sc[0];
         sc1 = d * (float)sc[1];
         mn0 = dmin * (float)mn[0];
         mn1 = dmin * (float)mn[1];
-        const int b = 4 + 8 * p;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             uint32_t lo[2], hi[2];
-            nib_word_to_f16<0>(w[b + i], lo, hi);
+            nib_word_to_f16<0>(w[i], lo, hi);
             v0[2 * i] = lo[0];
             v0[2 * i + 1] = lo[1];
             v1[2 * i] = hi[0];
@@ -419,11 +443,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int i = 0; i < C::NA; i++) mbar_init(&a_full[i], 128);
         for (int i = 0; i < C::NB; i++) mbar_init(&b_full[i], 1);
-        for (int i = 0; i < TC_PSLOTS; i++) mbar_init(&t_empty[i], 8);
+        for (int i = 0; i < TC_PSLOTS; i++) mbar_init(&t_empty[i], TC_EPI_WARPS);
         for (int i = 0; i < TC_ND; i++) mbar_init(&pair_done[i], 1);
         for (int i = 0; i < TC_NS; i++) {
             mbar_init(&s_full[i], 128 + 32);  // converter rows + the activation-scale warp
-            mbar_init(&s_empty[i], 8);
+            mbar_init(&s_empty[i], TC_EPI_WARPS);
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
@@ -546,28 +570,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_wait_bounded(mma_done, 0);
         }
     } else if (warp >= 4 && warp < 8) {
-        // ---- converters: one weight row per thread ------------------------------
+        // ---- converters: one weight row per thread, one block pair at a time ----
         const int row = tid - 128;
-        constexpr int NW = C::RAWB / 4;
         for (int c = 0; c < nchunks; c++) {
             const int s = c % C::NR;
             if (!tc_wait_warp(&raw_full[s], (c / C::NR) & 1, abort_flag, lane)) break;
-            uint32_t w[NW];
-            const uint4 *src = reinterpret_cast<const uint4 *>(gbase + L::OFF_RAW + s * L::RAW_STAGE + row * C::RAWB);
-#pragma unroll
-            for (int i = 0; i < NW / 4; i++) {
-                const uint4 v = src[i];
-                w[4 * i] = v.x;
-                w[4 * i + 1] = v.y;
-                w[4 * i + 2] = v.z;
-                w[4 * i + 3] = v.w;
+            const uint8_t *rrow = gbase + L::OFF_RAW + s * L::RAW_STAGE + row * C::RAWB;
+            uint32_t hdr[4] = {0u, 0u, 0u, 0u};
+            if constexpr (WT == WT_Q4_K) {
+                const uint4 hv = *reinterpret_cast<const uint4 *>(rrow);
+                hdr[0] = hv.x, hdr[1] = hv.y, hdr[2] = hv.z, hdr[3] = hv.w;
             }
-            mbar_arrive(&raw_empty[s]);
             bool ok = true;
 #pragma unroll
             for (int pp = 0; pp < CHUNK_PAIRS; pp++) {
                 const int q = CHUNK_PAIRS * c + pp;
                 const int sa = q % C::NA, ss = q % TC_NS;
+                uint32_t w[PairWords<WT>::N];
+                load_pair_words<WT>(rrow, pp, w);
+                if (pp == CHUNK_PAIRS - 1) mbar_arrive(&raw_empty[s]);  // the chunk is in registers
                 if ((q >= C::NA &&
                      !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane)) ||
                     !tc_wait_warp(&s_empty[ss], ((q / TC_NS) & 1) ^ 1, abort_flag, lane)) {
@@ -579,7 +600,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 fence_proxy_async_smem();
                 uint32_t v0[16], v1[16];
                 float sc0, sc1, mn0, mn1;
-                convert_pair<WT>(w, pp, v0, v1, sc0, sc1, mn0, mn1);
+                convert_pair<WT>(w, hdr, pp, v0, v1, sc0, sc1, mn0, mn1);
                 const uint32_t a_addr = sbase + L::OFF_A + sa * A_STAGE;
                 store_a_block(a_addr, row, 0, v0);
                 store_a_block(a_addr, row, 1, v1);
@@ -597,12 +618,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (!ok) break;
         }
     } else if (warp >= 8) {
-        // ---- epilogue: warp w reads TMEM lanes 32*(w%4).., columns 64*h.. -------
-        const int sub = warp & 3, h = (warp - 8) >> 2;
+        // ---- epilogue: warp w reads TMEM lanes 32*(w%4).., columns 32*qc.. ------
+        const int sub = warp & 3, qc = (warp - 8) >> 2;  // lane quarter, column quarter
         const int row = 32 * sub + lane;
-        uint64_t acc2[32];  // columns (2i, 2i+1) as f32x2
+        uint64_t acc2[16];  // columns (2i, 2i+1) of the warp's 32, as f32x2
 #pragma unroll
-        for (int i = 0; i < 32; i++) acc2[i] = 0;
+        for (int i = 0; i < 16; i++) acc2[i] = 0;
         bool ok = true;
         for (int q = 0; q < npairs && ok; q++) {
             const int ss = q % TC_NS;
@@ -617,17 +638,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 break;
             }
             tc_fence_after();
-            // 8 chunks of 16 columns (2 blocks x 4); the load of chunk k+1 is in
+            // 4 chunks of 16 columns (2 blocks x 2); the load of chunk k+1 is in
             // flight while chunk k is scaled and accumulated
-            const uint32_t tbase = tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(2 * ps * TC_BN + 64 * h);
+            const uint32_t tbase = tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(2 * ps * TC_BN + 32 * qc);
             uint32_t ra[16], rb[16];
             tc_ld16(tbase, ra);
             tc_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const int j = k >> 2, cc = k & 3;
-                if (k + 1 < 8) {
-                    const int jn = (k + 1) >> 2, cn = (k + 1) & 3;
+            for (int k = 0; k < 4; k++) {
+                const int j = k >> 1, cc = k & 1;
+                if (k + 1 < 4) {
+                    const int jn = (k + 1) >> 1, cn = (k + 1) & 1;
                     if (k & 1)
                         tc_ld16(tbase + (uint32_t)(jn * TC_BN + 16 * cn), ra);
                     else
@@ -638,8 +659,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const uint64_t sw2 = f2_pack(sw, sw);
                 const float mw = C::SCN == 4 ? -e[(2 * 2 + j) * 128 + row] : 0.0f;
                 const uint64_t mw2 = f2_pack(mw, mw);
-                const float4 *dxv = reinterpret_cast<const float4 *>(e + (1 * 2 + j) * 128 + 64 * h + 16 * cc);
-                const float4 *xsv = reinterpret_cast<const float4 *>(e + (3 * 2 + j) * 128 + 64 * h + 16 * cc);
+                const float4 *dxv = reinterpret_cast<const float4 *>(e + (1 * 2 + j) * 128 + 32 * qc + 16 * cc);
+                const float4 *xsv = reinterpret_cast<const float4 *>(e + (3 * 2 + j) * 128 + 32 * qc + 16 * cc);
 #pragma unroll
                 for (int i4 = 0; i4 < 4; i4++) {
                     const float4 dq = dxv[i4];
@@ -655,7 +676,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         a23 = f2_fma(mw2, f2_pack(xq.z, xq.w), a23);
                     }
                 }
-                if (k + 1 < 8) tc_wait_ld();
+                if (k + 1 < 4) tc_wait_ld();
             }
             tc_fence_before();
             __syncwarp();
@@ -665,14 +686,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         }
         if (ok) {
-            float acc[64];
+            float acc[32];
 #pragma unroll
-            for (int i = 0; i < 32; i++) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
+            for (int i = 0; i < 16; i++) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
             const int m = m0 + row;
             if (m < p.M) {
 #pragma unroll
-                for (int i = 0; i < 64; i++) {
-                    const int c = 64 * h + i;
+                for (int i = 0; i < 32; i++) {
+                    const int c = 32 * qc + i;
                     if (c < ncols) {
                         const int r = xrow0 + c;
                         if (p.partial) {
