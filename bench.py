@@ -534,10 +534,17 @@ def run_sharded(args, cfg, N):
         def step(i):
             return mods[i % copies](x, ids)
     else:
-        mods = [RowShardedMulMat(dt, w, K, M, local=True) for w in wts]
+        if args.fused:  # one peer-buffer set; the weight copies rotate under it
+            mod = RowShardedMulMat(dt, wts[0], K, M, local=True, fused=True)
 
-        def step(i):
-            return mods[i % copies](x)
+            def step(i):
+                mod.w_local = wts[i % copies]
+                return mod(x)
+        else:
+            mods = [RowShardedMulMat(dt, w, K, M, local=True) for w in wts]
+
+            def step(i):
+                return mods[i % copies](x)
 
     chunk = max(1, min(args.steps, max(copies, 16), 256))
     for i in range(3):
@@ -600,8 +607,8 @@ def run_sharded(args, cfg, N):
         "dtype": "int8 dot / f32 scale", "data": "synthetic (seeded torch.randn weights quantized on device)",
         "config": {"workload": cfg["workload"], "config": args.config, "K": K, "M": M, "N": N,
                    "weights_dtype": cfg["wtype"], "experts": cfg.get("E"), "n_selected": cfg.get("n_sel"),
-                   "parallelism": f"{'expert' if is_moe else 'row'}-sharded x{ws} + NCCL "
-                                  f"{'all_reduce' if is_moe else 'all_gather'}",
+                   "parallelism": f"{'expert' if is_moe else 'row'}-sharded x{ws} + "
+                                  f"{'NCCL all_reduce' if is_moe else ('peer-memory stores (fused)' if args.fused else 'NCCL all_gather')}",
                    "l2": f"{copies} rotating local weight copies ({copies * local_bytes / 2**20:.0f} MiB per rank)"},
         "roofline": {"bound": "hbm", "achieved": alg_total / sec_step / 1e9, "peak": peaks["hbm_gbs"] * ws,
                      "unit": "GB/s", "frac": alg_total / sec_step / 1e9 / (peaks["hbm_gbs"] * ws), "traffic": None,
@@ -730,6 +737,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shard", default="none", choices=["none", "rows", "experts"],
                     help="strong-scaling split of one workload across the ranks (c4: rows, c5: experts)")
+    ap.add_argument("--fused", action="store_true",
+                    help="--shard rows at decode shapes: peer-memory stores + flags instead of the NCCL all-gather")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     N = args.tokens if args.tokens is not None else cfg["N"]

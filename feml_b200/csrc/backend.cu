@@ -15,6 +15,7 @@
 //    that graph_compute allocates nothing.
 //  - Kernels record data-dependent failures (bad mul_mat_id ids, a wait that
 //    ran out) in a device status word that synchronize() reads and clears.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -729,6 +730,84 @@ int feml_b200_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t 
                          void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream) {
     return do_mul_mat_id(wtype, w, w_nb1, w_nb2, n_experts, 0, 1, x, x_nb1, ids, ids_nb1, n_selected, dst, dst_nb1,
                          dst_nb2, K, M, N, workspace, workspace_bytes, status, static_cast<cudaStream_t>(stream));
+}
+
+int feml_b200_mul_mat_peer(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1,
+                           void *const *peer_dst0, void *const *peer_dst1, uint32_t *const *peer_flags,
+                           int32_t n_peers, uint64_t dst_nb1, uint32_t *counter, const uint32_t *epoch, int64_t K,
+                           int64_t M, int64_t N, int32_t *status, void *stream) {
+    if (!w || !x || !peer_dst0 || !peer_dst1 || !peer_flags || !counter || !epoch)
+        return set_error(FB_ERR_INVALID, "mul_mat_peer: null argument");
+    if (n_peers < 1 || n_peers > fbk::kMaxPeers)
+        return set_error(FB_ERR_INVALID, "mul_mat_peer: %d peers (1..%d)", n_peers, fbk::kMaxPeers);
+    if (K <= 0 || M <= 0 || N < 1)
+        return set_error(FB_ERR_INVALID, "mul_mat_peer: bad dimensions (every rank needs rows, it signals the step)");
+    if (!is_weight_dtype(wtype) || wtype == FB_F32)
+        return set_error(FB_ERR_UNSUPPORTED, "mul_mat_peer: quantized weights only");
+    if (K % fb::dtype_traits(wtype)->block_size) return set_error(FB_ERR_SHAPE, "mul_mat_peer: K not a block multiple");
+    if (!fbk::gemv_supported(wtype, K, N) || !fbk::gemv_fused_ok(K, N))
+        return set_error(FB_ERR_UNSUPPORTED, "mul_mat_peer: needs the fused decode GEMV (N <= 4, N*K <= 16384)");
+    fbk::PeerOut po{};
+    po.n = n_peers;
+    po.count = counter;
+    po.epoch = epoch;
+    for (int r = 0; r < n_peers; r++) {
+        po.y[0][r] = static_cast<uint8_t *>(peer_dst0[r]);
+        po.y[1][r] = static_cast<uint8_t *>(peer_dst1[r]);
+        po.flag[r] = peer_flags[r];
+    }
+    return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, nullptr, dst_nb1, K, M, N, nullptr, status,
+                            static_cast<cudaStream_t>(stream), true, &po);
+}
+
+int feml_b200_ipc_export(const void *ptr, void *handle, uint64_t handle_bytes, uint64_t *offset) {
+    if (!ptr || !handle || !offset || handle_bytes != sizeof(cudaIpcMemHandle_t))
+        return set_error(FB_ERR_INVALID, "ipc_export: need a pointer and a %zu-byte handle buffer",
+                         sizeof(cudaIpcMemHandle_t));
+    // the allocation that holds ptr (a caching allocator hands out pieces of
+    // larger cudaMalloc blocks; IPC shares whole blocks)
+    using GetRange = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+    static GetRange get_range = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_range = reinterpret_cast<GetRange>(f);
+    });
+    if (!get_range) return set_error(FB_ERR_CUDA, "ipc_export: cuMemGetAddressRange unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (get_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+        return set_error(FB_ERR_INVALID, "ipc_export: not a device allocation");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+    if (e != cudaSuccess) return set_error(FB_ERR_CUDA, "ipc_export: %s", cudaGetErrorString(e));
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = reinterpret_cast<uintptr_t>(ptr) - (uintptr_t)base;
+    return FB_OK;
+}
+
+int feml_b200_ipc_open(const void *handle, uint64_t handle_bytes, void **base) {
+    if (!handle || !base || handle_bytes != sizeof(cudaIpcMemHandle_t))
+        return set_error(FB_ERR_INVALID, "ipc_open: need a %zu-byte handle", sizeof(cudaIpcMemHandle_t));
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return set_error(FB_ERR_CUDA, "ipc_open: %s", cudaGetErrorString(e));
+    return FB_OK;
+}
+
+int feml_b200_ipc_close(void *base) {
+    if (!base) return set_error(FB_ERR_INVALID, "ipc_close: null");
+    cudaError_t e = cudaIpcCloseMemHandle(base);
+    if (e != cudaSuccess) return set_error(FB_ERR_CUDA, "ipc_close: %s", cudaGetErrorString(e));
+    return FB_OK;
+}
+
+int feml_b200_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, void *stream) {
+    return fbk::launch_peer_wait(flag, epoch, n_ranks, status, static_cast<cudaStream_t>(stream));
 }
 
 int feml_b200_mul_mat_id_shard(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,

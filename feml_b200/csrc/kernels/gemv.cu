@@ -78,6 +78,7 @@ struct GemvParams {
     int32_t *status;
     bool x_vec16;     // activation columns are 16-byte aligned
     bool copy_rows;   // rows not aligned for the pair loads: plain copies
+    PeerOut peer;     // peer.n > 0: outputs go to every peer's buffer, then a signal
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t v) { return (v + 15u) & ~15u; }
@@ -399,11 +400,60 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
 #pragma unroll
             for (int n = 0; n < NC; n++) {
                 const float v = warp_sum(acc[n]);
-                if (lane == 0) reinterpret_cast<float *>(p.y + (uint64_t)n * p.y_nb1)[row] = v;
+                if (lane == 0) {
+                    if (p.peer.n == 0) {
+                        reinterpret_cast<float *>(p.y + (uint64_t)n * p.y_nb1)[row] = v;
+                    } else {
+                        const int b = (int)((*p.peer.epoch + 1u) & 1u);
+                        for (int r = 0; r < p.peer.n; r++)  // NVLink stores into each rank's output
+                            reinterpret_cast<float *>(p.peer.y[b][r] + (uint64_t)n * p.y_nb1)[row] = v;
+                    }
+                }
                 acc[n] = 0.0f;
             }
         }
     }
+    if (p.peer.n > 0) {
+        // Every warp publishes its stores (system scope) and counts itself
+        // done; the last warp of the grid resets the counter and raises each
+        // rank's flag by one. Ranks wait for `world` raises per step.
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_system();
+            const uint32_t prev = atomicAdd(p.peer.count, 1u);
+            if (prev == gridDim.x * kGemvWarps - 1) {
+                atomicExch(p.peer.count, 0u);
+                __threadfence_system();
+                for (int r = 0; r < p.peer.n; r++) atomicAdd_system(p.peer.flag[r], 1u);
+            }
+        }
+    }
+}
+
+// Waits (one thread, bounded at about a second) until every rank has
+// signalled this step: the flag reaches (epoch + 1) * n_ranks; then advances
+// the epoch. On timeout it raises STATUS_TIMEOUT and returns, leaving the
+// context usable (the epoch stays, so later waits report too).
+// Launched with programmatic dependent launch: it lets the next step's GEMV
+// start streaming its weights right away, but reads the epoch only after the
+// preceding grids (this step's GEMV, and through it the previous wait) have
+// completed.
+__global__ void peer_wait_kernel(const uint32_t *flag, uint32_t *epoch, int n_ranks, int32_t *status) {
+    grid_launch_dependents();
+    grid_dependency_wait();
+    if (threadIdx.x != 0) return;
+    const uint32_t e = *epoch;
+    const uint32_t expected = (e + 1u) * (uint32_t)n_ranks;
+    for (uint32_t i = 0; i < (1u << 24); i++) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if ((int32_t)(v - expected) >= 0) {
+            *epoch = e + 1u;
+            return;
+        }
+        __nanosleep(32);
+    }
+    report_status(status, STATUS_TIMEOUT);
 }
 
 template <int WT, int NC>
@@ -461,14 +511,45 @@ bool gemv_supported(int32_t wtype, int64_t K, int64_t N) {
 
 bool gemv_fused_ok(int64_t K, int64_t N) { return K * N <= kFusedMaxElems; }
 
+int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s) {
+    if (!flag || !epoch || ((reinterpret_cast<uintptr_t>(flag) | reinterpret_cast<uintptr_t>(epoch)) & 3))
+        return fb::set_error(FB_ERR_INVALID, "peer_wait: bad flag or epoch");
+    if (n_ranks < 1 || n_ranks > kMaxPeers) return fb::set_error(FB_ERR_INVALID, "peer_wait: %d ranks", n_ranks);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, peer_wait_kernel, flag, epoch, (int)n_ranks, status);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "peer_wait launch: %s", cudaGetErrorString(e));
+    return FB_OK;
+}
+
 int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
-                int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status, cudaStream_t s, bool pdl) {
+                int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status, cudaStream_t s, bool pdl,
+                const PeerOut *peer) {
     if (!gemv_supported(wtype, K, N)) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: unsupported shape");
     if (M == 0) return FB_OK;
     if ((reinterpret_cast<uintptr_t>(w) & 1) || (w_nb1 & 1))
         return fb::set_error(FB_ERR_INVALID, "gemv: weight rows must be 2-byte aligned");
     if (!xq && ((reinterpret_cast<uintptr_t>(x) & 3) || (x_nb1 & 3)))
         return fb::set_error(FB_ERR_INVALID, "gemv: activations must be 4-byte aligned");
+    if (peer) {
+        if (peer->n < 1 || peer->n > kMaxPeers || !peer->count || !peer->epoch)
+            return fb::set_error(FB_ERR_INVALID, "gemv: bad peer set");
+        for (int r = 0; r < peer->n; r++)
+            if (!peer->y[0][r] || !peer->y[1][r] || !peer->flag[r] ||
+                ((reinterpret_cast<uintptr_t>(peer->y[0][r]) | reinterpret_cast<uintptr_t>(peer->y[1][r]) |
+                  reinterpret_cast<uintptr_t>(peer->flag[r])) & 3))
+                return fb::set_error(FB_ERR_INVALID, "gemv: peer %d pointers", r);
+    } else if (!y) {
+        return fb::set_error(FB_ERR_INVALID, "gemv: null output");
+    }
     if ((reinterpret_cast<uintptr_t>(y) & 3) || (y_nb1 & 3))
         return fb::set_error(FB_ERR_INVALID, "gemv: output must be 4-byte aligned");
     if (M > INT32_MAX) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: M too large");
@@ -513,6 +594,7 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     p.xq = xq ? *xq : Q8Planar{nullptr, nullptr, nullptr};
     p.status = status;
     p.x_vec16 = ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0;
+    p.peer = peer ? *peer : PeerOut{};
     p.copy_rows = ((reinterpret_cast<uintptr_t>(w) | w_nb1) % align) != 0;
     switch (wtype) {
     case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, p, grid, L.total, s, pdl);

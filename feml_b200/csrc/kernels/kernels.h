@@ -35,9 +35,26 @@ int launch_quantize_q8_planar(const void *x, uint64_t x_nb1, int64_t K, int64_t 
 // itself (fused path, no workspace).
 bool gemv_supported(int32_t wtype, int64_t K, int64_t N);
 bool gemv_fused_ok(int64_t K, int64_t N);
+// Peer outputs of a row-sharded GEMV: y[b][r] is output buffer b (0/1,
+// alternating by step) of rank r at this rank's first row (device pointers
+// valid here: own memory or an IPC mapping of a peer's), flag[r] rank r's
+// step flag, count a zeroed device counter of this rank, epoch this rank's
+// count of completed steps (buffer = (epoch + 1) & 1). The last warp of the
+// grid raises every flag by one.
+constexpr int kMaxPeers = 8;
+struct PeerOut {
+    uint8_t *y[2][kMaxPeers];
+    uint32_t *flag[kMaxPeers];
+    uint32_t *count;
+    const uint32_t *epoch;
+    int n;
+};
 int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y,
                 uint64_t y_nb1, int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status,
-                cudaStream_t s, bool pdl);
+                cudaStream_t s, bool pdl, const PeerOut *peer = nullptr);
+// Wait until this rank's flag reaches (epoch + 1) * n_ranks, then advance
+// the epoch (bounded; STATUS_TIMEOUT on expiry).
+int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s);
 
 // gemm_f32.cu: F32 mul_mat on SIMT FP32 (any N).
 int launch_gemm_f32(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,

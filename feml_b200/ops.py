@@ -123,6 +123,30 @@ def mul_mat_id_shard(wtype, w_local, x, ids, K, n_experts, shard, n_shards, out,
     return out
 
 
+def _ptr_array(ptrs):
+    arr = (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(v)) for v in ptrs])
+    return arr
+
+
+def mul_mat_peer(wtype, w_local, x, K, dst0_ptrs, dst1_ptrs, flag_ptrs, dst_nb1, counter, epoch, status=None):
+    """feml_b200_mul_mat_peer: this rank's rows of a row-sharded decode
+    mul_mat stored straight into every rank's output buffer (raw device
+    pointers, own memory or IPC mappings), then every rank's flag raised."""
+    M, N = w_local.shape[0], x.shape[0]
+    st = _ptr(status) if status is not None else ctypes.c_void_p()
+    n = len(flag_ptrs)
+    _check(_L.lib().feml_b200_mul_mat_peer(int(wtype), _ptr(w_local), w_local.stride(0) * w_local.element_size(),
+                                           _ptr(x), x.stride(0) * 4, _ptr_array(dst0_ptrs), _ptr_array(dst1_ptrs),
+                                           _ptr_array(flag_ptrs), n, dst_nb1, _ptr(counter), _ptr(epoch), K, M, N, st,
+                                           _stream()))
+
+
+def peer_wait(flag, epoch, n_ranks, status=None):
+    """Enqueue the end of a fused step: wait for every rank's signal."""
+    st = _ptr(status) if status is not None else ctypes.c_void_p()
+    _check(_L.lib().feml_b200_peer_wait(_ptr(flag), _ptr(epoch), n_ranks, st, _stream()))
+
+
 def moe_route(ids, n_experts, status=None):
     """ids int32 [N, n_sel] -> (counts, offsets, rows) int32 device tensors."""
     N, n_sel = ids.shape
@@ -146,5 +170,5 @@ def block_dots(wtype, w, xq, K):
 
 
 __all__ = ["quantize", "mul_mat", "mul_mat_workspace", "mul_mat_noalloc", "mul_mat_noalloc_limit", "mul_mat_id", "mul_mat_id_workspace", "mul_mat_id_shard",
-           "local_experts", "moe_route",
+           "local_experts", "mul_mat_peer", "peer_wait", "moe_route",
            "block_dots", "row_bytes", "FemlError"]

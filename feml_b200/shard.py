@@ -10,6 +10,13 @@ are new. They shard the two operators of the path the natural way:
   of y = W x straight into its all-gather send buffer, one all-gather over
   NCCL assembles [world, N, R], and a permute gives y [N, M] on every rank.
   With N == 1 the gathered buffer already is y (no permute).
+  With `fused=True` and a decode shape (N <= 4, N*K <= 16384) the all-gather
+  is fused into the kernel instead: every rank stores its rows straight into
+  every rank's output buffer over NVLink (peer pointers from CUDA IPC, mapped
+  once into this device's context with peer access), raises each rank's flag, and a
+  one-thread wait kernel ends the step when all ranks have signalled
+  (feml_b200_mul_mat_peer / feml_b200_peer_wait; bounded waits; no NCCL on
+  the data path). Outputs alternate between two buffers by step.
 * `ExpertShardedMulMatId` -- rank r owns the experts e with e % world == r
   (local index e // world). Each rank computes the dst slots routed to its
   experts (feml_b200_mul_mat_id_shard leaves the other slots untouched in a
@@ -69,12 +76,15 @@ class RowShardedMulMat:
     rows already.
     """
 
-    def __init__(self, wtype, w, K, M, group=None, local=False, compute=None):
+    def __init__(self, wtype, w, K, M, group=None, local=False, compute=None, fused=False, max_tokens=4):
         self.wtype = DType(wtype)
         self.K, self.M = K, M
         self.group = group
         self.rank, self.world = _world(group)
         self.lo, self.hi, self.R = row_range(M, self.rank, self.world)
+        self.fused = fused
+        self.max_tokens = max_tokens
+        self._peer = None
         if local:
             if w.shape[0] != self.hi - self.lo:
                 raise FemlError("shape", f"rank {self.rank} holds rows [{self.lo}, {self.hi}), "
@@ -86,10 +96,75 @@ class RowShardedMulMat:
             self.w_local = w[self.lo:self.hi]
         self.compute = compute or _cuda_mul_mat
 
+    def _setup_peers(self, device):
+        """Two output buffers, a step flag, a grid counter and an epoch per
+        rank. Every rank maps every other rank's buffers and flag into its own
+        device's context with peer access (CUDA IPC handles of the torch
+        allocations, exchanged with all_gather_object and opened through
+        feml_b200_ipc_open)."""
+        import ctypes
+        from . import _check, _lib
+        if self.hi <= self.lo:
+            raise FemlError("shape", f"fused row sharding needs rows on every rank (rank {self.rank} has none)")
+        bufs = [torch.zeros((self.max_tokens, self.M), dtype=torch.float32, device=device) for _ in range(2)]
+        flag = torch.zeros(1, dtype=torch.int32, device=device)
+        counter = torch.zeros(1, dtype=torch.int32, device=device)
+        epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        torch.cuda.synchronize(device)
+        mine = []
+        for t in (bufs[0], bufs[1], flag):
+            handle = ctypes.create_string_buffer(64)
+            offset = ctypes.c_uint64()
+            _check(_lib.lib().feml_b200_ipc_export(ctypes.c_void_p(t.data_ptr()), handle, 64, ctypes.byref(offset)))
+            mine.append((handle.raw, offset.value))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=self.group)
+        opened = {}  # one mapping per peer allocation
+        ptrs = []
+        for r, shared in enumerate(everyone):
+            if r == self.rank:
+                ptrs.append([bufs[0].data_ptr(), bufs[1].data_ptr(), flag.data_ptr()])
+                continue
+            row = []
+            for handle, offset in shared:
+                if handle not in opened:
+                    base = ctypes.c_void_p()
+                    _check(_lib.lib().feml_b200_ipc_open(handle, len(handle), ctypes.byref(base)))
+                    opened[handle] = base.value
+                row.append(opened[handle] + offset)
+            ptrs.append(row)
+        self._peer = dict(bufs=bufs, flag=flag, counter=counter, epoch=epoch, steps=0, opened=list(opened.values()),
+                          dst0=[p[0] + 4 * self.lo for p in ptrs], dst1=[p[1] + 4 * self.lo for p in ptrs],
+                          flags=[p[2] for p in ptrs])
+        dist.barrier(group=self.group)
+
+    def close(self):
+        """Unmap the peers' buffers (after the last fused step has finished)."""
+        from . import _lib
+        if self._peer is not None:
+            torch.cuda.synchronize()
+            for base in self._peer["opened"]:
+                _lib.lib().feml_b200_ipc_close(base)
+            self._peer = None
+
+    def _fused_ok(self, N):
+        return (self.fused and N <= self.max_tokens and N * self.K <= 16384 and self.wtype != DType.F32
+                and self.compute is _cuda_mul_mat)
+
     def __call__(self, x):
         N = x.shape[0]
         if x.shape[1] != self.K:
             raise FemlError("shape", f"activation has K={x.shape[1]}, expected {self.K}")
+        if self._fused_ok(N):
+            from . import ops
+            if self._peer is None:
+                self._setup_peers(x.device)
+            pe = self._peer
+            ops.mul_mat_peer(self.wtype, self.w_local, x, self.K, pe["dst0"], pe["dst1"], pe["flags"], 4 * self.M,
+                             pe["counter"], pe["epoch"])
+            ops.peer_wait(pe["flag"], pe["epoch"], self.world)
+            pe["steps"] += 1
+            return pe["bufs"][pe["steps"] & 1][:N]
         send = torch.empty((N, self.R), dtype=torch.float32, device=x.device)
         m_loc = self.hi - self.lo
         if m_loc < self.R:

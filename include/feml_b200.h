@@ -304,6 +304,41 @@ int feml_b200_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t 
                          void *dst, uint64_t dst_nb1, uint64_t dst_nb2, int64_t K, int64_t M, int64_t N,
                          void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream);
 
+/* Row-sharded decode mul_mat with the all-gather fused into the kernel (no
+ * counterpart in the reference, which has no multi-device code). This rank
+ * holds weight rows [row0, row0 + M) of the full matrix. Each rank owns two
+ * output buffers used alternately by step; peer_dst0[r] / peer_dst1[r] are
+ * rank r's buffers already offset to row0 (device pointers valid on this
+ * device: its own memory or a CUDA IPC mapping of the peer's), column n at
+ * + n*dst_nb1. Every output value is stored into every rank's buffer of this
+ * step (buffer (*epoch + 1) & 1) over NVLink; when the grid is done each
+ * peer_flags[r] (a uint32 in rank r's memory) is raised by one. `counter` is
+ * a zeroed uint32 of this rank used by the grid (left at zero) and `epoch`
+ * this rank's completed-step count (advanced by feml_b200_peer_wait).
+ * Quantized weights, N <= 4 and N*K <= 16384 (the fused-quantization GEMV).
+ * Both calls take only device state, so a step can be captured in a CUDA
+ * graph and replayed. */
+int feml_b200_mul_mat_peer(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1,
+                           void *const *peer_dst0, void *const *peer_dst1, uint32_t *const *peer_flags,
+                           int32_t n_peers, uint64_t dst_nb1, uint32_t *counter, const uint32_t *epoch, int64_t K,
+                           int64_t M, int64_t N, int32_t *status, void *stream);
+
+/* Map another process's device allocation (a 64-byte cudaIpcMemHandle_t)
+ * into the current device's context with peer access enabled, so kernels on
+ * this device can load and store it over NVLink; *base is the start of the
+ * allocation. No counterpart in the reference. */
+int feml_b200_ipc_open(const void *handle, uint64_t handle_bytes, void **base);
+/* The IPC handle (64 bytes) of the device allocation holding ptr and ptr's
+ * byte offset in it. */
+int feml_b200_ipc_export(const void *ptr, void *handle, uint64_t handle_bytes, uint64_t *offset);
+int feml_b200_ipc_close(void *base);
+
+/* Enqueue the end of a fused step on this rank: wait (one thread, bounded at
+ * about a second) until this rank's flag reaches (*epoch + 1) * n_ranks, then
+ * advance *epoch. On timeout bit 0 of *status is set and the stream continues
+ * (the context stays usable). */
+int feml_b200_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, void *stream);
+
 /* Expert-sharded mul_mat_id (no counterpart in the reference, which has no
  * multi-GPU code): expert e belongs to shard e % n_shards as local expert
  * e / n_shards; w_local holds this shard's local experts (j-th at

@@ -62,3 +62,62 @@ def test_expert_sharded_q8_0(group):
     want = O.mul_mat_id_ref(O.DT_Q8_0, wq, x, ids, K)
     ok, err = tol_ok(out.cpu().numpy(), want)
     assert ok, err
+
+
+def test_row_sharded_fused_single_rank(group):
+    """The fused path (peer stores + flag + device-side epoch) on a one-rank
+    group: the same kernel arithmetic as the unfused GEMV, over several steps
+    (the output buffers alternate)."""
+    rng = np.random.default_rng(7)
+    K, M = 14336, 512
+    wq = O.quantize(O.DT_Q4_K, (rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+    wt = torch.from_numpy(wq).cuda()
+    fused = RowShardedMulMat(DType.Q4_K, wt, K, M, fused=True)
+    plain = RowShardedMulMat(DType.Q4_K, wt, K, M)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for step in range(3):
+        x = torch.from_numpy(rng.standard_normal((1, K)).astype(np.float32)).cuda()
+        got = fused(x).clone()
+        want = plain(x)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), step
+        ok, err = tol_ok(got.cpu().numpy(), O.mul_mat_quant_ref(O.DT_Q4_K, wq, x.cpu().numpy(), K))
+        assert ok, err
+    assert int(status.item()) == 0
+
+
+def _fused_worker(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    rng = np.random.default_rng(11)
+    K, M = 8192, 1000
+    wq = O.quantize(O.DT_Q8_0, (rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+    wt = torch.from_numpy(wq).cuda()
+    fused = RowShardedMulMat(DType.Q8_0, wt, K, M, fused=True)
+    worst = 0.0
+    for step in range(4):
+        x = torch.from_numpy(rng.standard_normal((2, K)).astype(np.float32)).cuda()
+        got = fused(x).clone()
+        want = ops.mul_mat(DType.Q8_0, wt, x, K)
+        torch.cuda.synchronize()
+        worst = max(worst, float((got - want).abs().max()))
+    np.save(os.path.join(outdir, f"r{rank}.npy"), np.array([worst]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_row_sharded_fused_two_gpus(tmp_path):
+    """Peer stores over NVLink between two processes (needs two GPUs)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_fused_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        assert float(np.load(tmp_path / f"r{r}.npy")[0]) == 0.0
