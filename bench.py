@@ -529,10 +529,18 @@ def run_sharded(args, cfg, N):
     if is_moe:
         ids_np = make_ids(cfg, 0, N)
         ids = torch.from_numpy(ids_np).cuda()
-        mods = [ExpertShardedMulMatId(dt, w, K, E, local=True) for w in wts]
+        if args.fused:  # one peer-buffer set; the weight copies rotate under it
+            mod = ExpertShardedMulMatId(dt, wts[0], K, E, local=True, fused=True, max_tokens=N,
+                                        max_selected=n_sel)
 
-        def step(i):
-            return mods[i % copies](x, ids)
+            def step(i):
+                mod.w_local = wts[i % copies]
+                return mod(x, ids)
+        else:
+            mods = [ExpertShardedMulMatId(dt, w, K, E, local=True) for w in wts]
+
+            def step(i):
+                return mods[i % copies](x, ids)
     else:
         if args.fused:  # one peer-buffer set; the weight copies rotate under it
             mod = RowShardedMulMat(dt, wts[0], K, M, local=True, fused=True)
@@ -598,7 +606,8 @@ def run_sharded(args, cfg, N):
     e2e_s = reduce_max(time.perf_counter() - tt) / e2e_steps
     e2e_v, _ = metric_value(cfg, N, e2e_s)
     peaks = load_peaks()
-    n_k = 3 if is_moe else 1 + (1 if ops.mul_mat_workspace(dt, K, M, N) else 0)
+    # ours per step: route + quantize + grouped GEMM (MoE) or GEMV (+ quantize), plus the wait kernel when fused
+    n_k = (3 if is_moe else 1 + (1 if ops.mul_mat_workspace(dt, K, M, N) else 0)) + (1 if args.fused else 0)
     result = {
         "metric": f"mul_mat {'mul_mat_id expert-sharded' if is_moe else 'row-sharded'} weight-GB/s "
                   f"({args.config}: {cfg['workload']})",
@@ -607,8 +616,9 @@ def run_sharded(args, cfg, N):
         "dtype": "int8 dot / f32 scale", "data": "synthetic (seeded torch.randn weights quantized on device)",
         "config": {"workload": cfg["workload"], "config": args.config, "K": K, "M": M, "N": N,
                    "weights_dtype": cfg["wtype"], "experts": cfg.get("E"), "n_selected": cfg.get("n_sel"),
-                   "parallelism": f"{'expert' if is_moe else 'row'}-sharded x{ws} + "
-                                  f"{'NCCL all_reduce' if is_moe else ('peer-memory stores (fused)' if args.fused else 'NCCL all_gather')}",
+                   "parallelism": f"{'expert' if is_moe else 'row'}-sharded x{ws} + " + (
+                       "peer-memory stores (fused)" if args.fused else
+                       ("NCCL all_reduce" if is_moe else "NCCL all_gather")),
                    "l2": f"{copies} rotating local weight copies ({copies * local_bytes / 2**20:.0f} MiB per rank)"},
         "roofline": {"bound": "hbm", "achieved": alg_total / sec_step / 1e9, "peak": peaks["hbm_gbs"] * ws,
                      "unit": "GB/s", "frac": alg_total / sec_step / 1e9 / (peaks["hbm_gbs"] * ws), "traffic": None,
@@ -738,7 +748,8 @@ def main():
     ap.add_argument("--shard", default="none", choices=["none", "rows", "experts"],
                     help="strong-scaling split of one workload across the ranks (c4: rows, c5: experts)")
     ap.add_argument("--fused", action="store_true",
-                    help="--shard rows at decode shapes: peer-memory stores + flags instead of the NCCL all-gather")
+                    help="peer-memory stores + flags instead of the NCCL collective (--shard rows at decode "
+                         "shapes, --shard experts)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     N = args.tokens if args.tokens is not None else cfg["N"]

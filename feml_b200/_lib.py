@@ -123,6 +123,9 @@ SIGNATURES = [
     ("feml_b200_mul_mat_peer", c_int, [c_i32, vp, c_u64, vp, c_u64, vp, vp, vp, c_i32, c_u64, vp, vp, c_i64, c_i64,
                                        c_i64, vp, vp]),
     ("feml_b200_peer_wait", c_int, [vp, vp, c_i32, vp, vp]),
+    ("feml_b200_mul_mat_id_peer", c_int, [c_i32, vp, c_u64, c_u64, c_i64, c_i64, c_i64, vp, c_u64, vp, c_u64, c_i64,
+                                          vp, vp, vp, c_i32, c_u64, c_u64, vp, vp, c_i64, c_i64, c_i64, vp, c_u64, vp,
+                                          vp]),
     ("feml_b200_ipc_open", c_int, [vp, c_u64, ctypes.POINTER(vp)]),
     ("feml_b200_ipc_close", c_int, [vp]),
     ("feml_b200_ipc_export", c_int, [vp, vp, c_u64, ctypes.POINTER(c_u64)]),

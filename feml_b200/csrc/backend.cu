@@ -760,6 +760,62 @@ int feml_b200_mul_mat_peer(int32_t wtype, const void *w, uint64_t w_nb1, const v
                             static_cast<cudaStream_t>(stream), true, &po);
 }
 
+int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,
+                              int64_t shard, int64_t n_shards, const void *x, uint64_t x_nb1, const int32_t *ids,
+                              uint64_t ids_nb1, int64_t n_selected, void *const *peer_dst0, void *const *peer_dst1,
+                              uint32_t *const *peer_flags, int32_t n_peers, uint64_t dst_nb1, uint64_t dst_nb2,
+                              uint32_t *counter, const uint32_t *epoch, int64_t K, int64_t M, int64_t N,
+                              void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!w_local || !x || !ids || !peer_dst0 || !peer_dst1 || !peer_flags || !counter || !epoch)
+        return set_error(FB_ERR_INVALID, "mul_mat_id_peer: null argument");
+    if (n_peers < 1 || n_peers > fbk::kMaxPeers || n_peers != n_shards || shard < 0 || shard >= n_shards)
+        return set_error(FB_ERR_INVALID, "mul_mat_id_peer: %d peers for shard %ld of %ld", n_peers, (long)shard,
+                         (long)n_shards);
+    if (K <= 0 || M <= 0 || N <= 0 || n_selected < 1 || n_experts < 1)
+        return set_error(FB_ERR_INVALID, "mul_mat_id_peer: bad dimensions");
+    const int64_t n_local = fbk::local_experts(n_experts, shard, n_shards);
+    if (n_local < 1) return set_error(FB_ERR_INVALID, "mul_mat_id_peer: every shard needs an expert (it signals)");
+    if (!fbk::gemm_tc_supported(wtype, K, M, N * n_selected, w_local, w_nb1) || (w_nb2 & 15) ||
+        ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15))
+        return set_error(FB_ERR_UNSUPPORTED,
+                         "mul_mat_id_peer: needs the tcgen05 GEMM (quantized, K %% 256 == 0, 16-byte aligned)");
+    const IdWorkspace need = id_ws_layout(nullptr, wtype, K, N, n_selected, n_local);
+    if (need.total > workspace_bytes)
+        return set_error(FB_ERR_INVALID, "mul_mat_id_peer: workspace of %lu bytes needed, %lu given",
+                         (unsigned long)need.total, (unsigned long)workspace_bytes);
+    const IdWorkspace L = id_ws_layout(workspace, wtype, K, N, n_selected, n_local);
+    fbk::PeerOut po{};
+    po.n = n_peers;
+    po.count = counter;
+    po.epoch = epoch;
+    for (int r = 0; r < n_peers; r++) {
+        po.y[0][r] = static_cast<uint8_t *>(peer_dst0[r]);
+        po.y[1][r] = static_cast<uint8_t *>(peer_dst1[r]);
+        po.flag[r] = peer_flags[r];
+    }
+    // invalid ids: every rank zeroes the slot in its own buffer of this step
+    int rc = fbk::launch_moe_route(ids, ids_nb1, n_selected, N, n_experts, shard, n_shards, L.counts, L.offsets,
+                                   L.rows, L.tile_start, fbk::gemm_tc_block_n(), status, po.y[0][shard], dst_nb1,
+                                   dst_nb2, M, s, po.y[1][shard], epoch);
+    if (rc) return rc;
+    fbk::GroupMap g{};
+    g.counts = L.counts;
+    g.offsets = L.offsets;
+    g.rows = L.rows;
+    g.tile_start = L.tile_start;
+    g.n_groups = (int32_t)n_local;
+    g.n_selected = (int32_t)n_selected;
+    g.w_group_stride = w_nb2;
+    g.dst_nb1 = dst_nb1;
+    g.dst_nb2 = dst_nb2;
+    g.max_tiles = (int32_t)((n_selected * N + fbk::gemm_tc_block_n() - 1) / fbk::gemm_tc_block_n() + n_local);
+    const fbk::XQ16 xa = fbk::xq16_carve(L.xq, K, N * n_selected);
+    rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, &g, s);
+    if (rc) return rc;
+    return fbk::launch_gemm_tc(wtype, w_local, w_nb1, xa, K, M, N, nullptr, 0, &g, status, s, &po);
+}
+
 int feml_b200_ipc_export(const void *ptr, void *handle, uint64_t handle_bytes, uint64_t *offset) {
     if (!ptr || !handle || !offset || handle_bytes != sizeof(cudaIpcMemHandle_t))
         return set_error(FB_ERR_INVALID, "ipc_export: need a pointer and a %zu-byte handle buffer",

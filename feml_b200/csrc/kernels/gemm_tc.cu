@@ -111,7 +111,20 @@ struct TcParams {
     GroupMap g;
     int split_pairs;      // split-K: pairs per CTA along blockIdx.z (0: none)
     float *partial;       // [splits][N][M] when split
+    PeerOut peer;         // peer.n > 0 (grouped): outputs into every rank's buffer, then a signal
 };
+
+// Peer mode: count this CTA done; the grid's last CTA raises every rank's
+// flag by one (after a system-scope fence, so all CTAs' stores are visible).
+__device__ __forceinline__ void peer_cta_done(const PeerOut &pe) {
+    __threadfence_system();
+    const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(pe.count, 1u) == total - 1u) {
+        atomicExch(pe.count, 0u);
+        __threadfence_system();
+        for (int r = 0; r < pe.n; r++) atomicAdd_system(pe.flag[r], 1u);
+    }
+}
 
 // ---- TMA / tcgen05 primitives (inline PTX) -----------------------------------
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t bar) {
@@ -401,7 +414,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int xrow0 = blockIdx.y * TC_BN, ncols = min(TC_BN, p.N - xrow0), expert = 0;
     if (p.grouped) {
         const int t = blockIdx.y;
-        if (t >= p.g.tile_start[p.g.n_groups]) return;  // unused tile (uniform, before any set-up)
+        if (t >= p.g.tile_start[p.g.n_groups]) {  // unused tile (uniform, before any set-up)
+            if (p.peer.n > 0 && threadIdx.x == 0) peer_cta_done(p.peer);
+            return;
+        }
         while (p.g.tile_start[expert + 1] <= t) expert++;
         const int jt = t - p.g.tile_start[expert];
         xrow0 = p.g.offsets[expert] + jt * TC_BN;
@@ -707,7 +723,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             } else {
                                 off = (uint64_t)r * p.y_nb1;
                             }
-                            reinterpret_cast<float *>(p.y + off)[m] = acc[i];
+                            if (p.peer.n == 0) {
+                                reinterpret_cast<float *>(p.y + off)[m] = acc[i];
+                            } else {  // NVLink stores into every rank's buffer of this step
+                                const int b = (int)((*p.peer.epoch + 1u) & 1u);
+                                for (int pr = 0; pr < p.peer.n; pr++)
+                                    reinterpret_cast<float *>(p.peer.y[b][pr] + off)[m] = acc[i];
+                            }
                         }
                     }
                 }
@@ -715,9 +737,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     }
 
+    if (p.peer.n > 0) __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
     tc_fence_before();
     __syncthreads();
     if (*abort_flag && tid == 0) report_status(p.status, STATUS_TIMEOUT);
+    if (p.peer.n > 0 && tid == 0) peer_cta_done(p.peer);
     if (warp == 2) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS)
@@ -816,7 +840,7 @@ int encode_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint6
 template <int WT>
 int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_planes, const XQ16 &xa, int64_t K,
                     int64_t M, int64_t rows, void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status,
-                    int splits, cudaStream_t s) {
+                    int splits, cudaStream_t s, const PeerOut *peer) {
     using C = TcCfg<WT>;
     using L = TcLayout<WT>;
     static_assert(L::BYTES <= 232448, "gemm_tc shared memory");
@@ -852,6 +876,7 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     p.status = status;
     p.grouped = groups != nullptr;
     if (groups) p.g = *groups;
+    if (peer) p.peer = *peer;
     const int total_pairs = (int)(K / (2 * QK));
     if (splits > 1) {
         const int per_chunks = (int)((K / QKK + splits - 1) / splits);
@@ -945,7 +970,10 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
 }
 
 int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa, int64_t K, int64_t M, int64_t N,
-                   void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s) {
+                   void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s,
+                   const PeerOut *peer) {
+    if (peer && (!groups || peer->n < 1 || peer->n > kMaxPeers || !peer->count || !peer->epoch))
+        return fb::set_error(FB_ERR_INVALID, "gemm_tc: peer outputs need the grouped mode and a full peer set");
     const int64_t rows = groups ? N * groups->n_selected : N;
     if (!gemm_tc_supported(wtype, K, M, rows, w, w_nb1))
         return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_tc: unsupported shape or alignment");
@@ -957,11 +985,14 @@ int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa,
     const int splits = groups ? 1 : gemm_tc_splits(K, M, rows);
     switch (wtype) {
     case WT_Q8_0:
-        return launch_tc_typed<WT_Q8_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s);
+        return launch_tc_typed<WT_Q8_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
+                                        peer);
     case WT_Q4_0:
-        return launch_tc_typed<WT_Q4_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s);
+        return launch_tc_typed<WT_Q4_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
+                                        peer);
     default:
-        return launch_tc_typed<WT_Q4_K>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s);
+        return launch_tc_typed<WT_Q4_K>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
+                                        peer);
     }
 }
 

@@ -108,8 +108,12 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
 // With `groups` (mul_mat_id): expert planes w + e*groups->w_group_stride,
 // activation rows = routed slots (N tokens x n_selected), outputs through
 // the group map. Column tiles of groups->tile_start use gemm_tc_block_n().
+// With `peer` (grouped mode only): each output value is stored into every
+// rank's buffer of this step instead of y (see PeerOut), then every rank's
+// flag is raised once by the grid's last CTA.
 int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa, int64_t K, int64_t M, int64_t N,
-                   void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s);
+                   void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s,
+                   const PeerOut *peer = nullptr);
 int gemm_tc_block_n();
 
 // Per-block int32 sums (bit-exactness probe); xq in ggml Q8_0 layout.
@@ -120,14 +124,17 @@ int launch_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *
 // When dst is non-null, output columns of slots with an invalid id are
 // zeroed (and STATUS_BAD_ID is raised).
 // Expert sharding: expert e belongs to shard e % n_shards as local expert
-// e / n_shards; other shards' slots are skipped (no write).
+// e / n_shards; other shards' slots are skipped (no write). With `epoch`
+// (fused multi-GPU steps) the zeroed buffer is dst_alt when (*epoch + 1) is
+// odd, dst otherwise.
 inline int64_t local_experts(int64_t n_experts, int64_t shard, int64_t n_shards) {
     return n_experts > shard ? (n_experts - shard + n_shards - 1) / n_shards : 0;
 }
 int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
                      int64_t shard, int64_t n_shards, int32_t *counts, int32_t *offsets, int32_t *rows,
                      int32_t *tile_start, int32_t block_n, int32_t *status, void *dst, uint64_t dst_nb1,
-                     uint64_t dst_nb2, int64_t M, cudaStream_t s);
+                     uint64_t dst_nb2, int64_t M, cudaStream_t s, void *dst_alt = nullptr,
+                     const uint32_t *epoch = nullptr);
 
 int sm_count();
 

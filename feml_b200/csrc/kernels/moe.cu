@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
                                                                    int32_t *offsets, int32_t *rows,
                                                                    int32_t *tile_start, int block_n, int32_t *status,
                                                                    uint8_t *dst, uint64_t dst_nb1, uint64_t dst_nb2,
-                                                                   int M) {
+                                                                   int M, uint8_t *dst_alt, const uint32_t *epoch) {
     __shared__ int cnt[kMaxExperts];
     __shared__ int base[kMaxExperts];
     __shared__ int off[kMaxExperts];
@@ -58,6 +58,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
     }
     const int any_bad = __syncthreads_or(bad);
     if (any_bad && tid == 0) report_status(status, STATUS_BAD_ID);
+    if (epoch && ((*epoch + 1u) & 1u)) dst = dst_alt;  // this step's buffer of a fused multi-GPU step
     if (any_bad && dst) {  // slots with an invalid id produce zeros
         for (int i = 0; i < n_slots; i++) {
             const int t = i / n_sel, s = i % n_sel;
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
 int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
                      int64_t shard, int64_t n_shards, int32_t *counts, int32_t *offsets, int32_t *rows,
                      int32_t *tile_start, int32_t block_n, int32_t *status, void *dst, uint64_t dst_nb1,
-                     uint64_t dst_nb2, int64_t M, cudaStream_t s) {
+                     uint64_t dst_nb2, int64_t M, cudaStream_t s, void *dst_alt, const uint32_t *epoch) {
     if (n_experts < 1 || n_experts > kMaxExperts)
         return fb::set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: n_experts %ld not in [1, %d]", (long)n_experts, kMaxExperts);
     if (n_shards < 1 || shard < 0 || shard >= n_shards)
@@ -127,7 +128,8 @@ int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, i
     moe_route_kernel<<<1, kRouteThreads, 0, s>>>(ids, ids_nb1 / 4, (int)n_selected, (int)N, (int)n_experts, (int)shard,
                                                  (int)n_shards, (int)n_local, counts,
                                                  offsets, rows, tile_start, block_n, status,
-                                                 static_cast<uint8_t *>(dst), dst_nb1, dst_nb2, (int)M);
+                                                 static_cast<uint8_t *>(dst), dst_nb1, dst_nb2, (int)M,
+                                                 static_cast<uint8_t *>(dst_alt), epoch);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "moe_route launch: %s", cudaGetErrorString(e));
     return FB_OK;

@@ -141,6 +141,26 @@ def mul_mat_peer(wtype, w_local, x, K, dst0_ptrs, dst1_ptrs, flag_ptrs, dst_nb1,
                                            _stream()))
 
 
+def mul_mat_id_peer(wtype, w_local, x, ids, K, n_experts, shard, n_shards, dst0_ptrs, dst1_ptrs, flag_ptrs,
+                    dst_nb1, dst_nb2, M, counter, epoch, workspace, status=None):
+    """feml_b200_mul_mat_id_peer: this shard's experts of an expert-sharded
+    mul_mat_id, every output slot stored straight into every rank's output
+    buffer of this step, then every rank's flag raised."""
+    E_loc = w_local.shape[0]
+    if E_loc != local_experts(n_experts, shard, n_shards):
+        raise FemlError("msg", f"mul_mat_id_peer: shard {shard}/{n_shards} of {n_experts} experts holds "
+                               f"{local_experts(n_experts, shard, n_shards)} experts, got {E_loc}")
+    N, n_sel = ids.shape
+    es = w_local.element_size()
+    st = _ptr(status) if status is not None else ctypes.c_void_p()
+    _check(_L.lib().feml_b200_mul_mat_id_peer(int(wtype), _ptr(w_local), w_local.stride(1) * es,
+                                              w_local.stride(0) * es, n_experts, shard, n_shards, _ptr(x),
+                                              x.stride(0) * 4, _ptr(ids), ids.stride(0) * 4, n_sel,
+                                              _ptr_array(dst0_ptrs), _ptr_array(dst1_ptrs), _ptr_array(flag_ptrs),
+                                              len(flag_ptrs), dst_nb1, dst_nb2, _ptr(counter), _ptr(epoch), K, M, N,
+                                              _ptr(workspace), workspace.numel(), st, _stream()))
+
+
 def peer_wait(flag, epoch, n_ranks, status=None):
     """Enqueue the end of a fused step: wait for every rank's signal."""
     st = _ptr(status) if status is not None else ctypes.c_void_p()
@@ -170,5 +190,5 @@ def block_dots(wtype, w, xq, K):
 
 
 __all__ = ["quantize", "mul_mat", "mul_mat_workspace", "mul_mat_noalloc", "mul_mat_noalloc_limit", "mul_mat_id", "mul_mat_id_workspace", "mul_mat_id_shard",
-           "local_experts", "mul_mat_peer", "peer_wait", "moe_route",
+           "local_experts", "mul_mat_peer", "mul_mat_id_peer", "peer_wait", "moe_route",
            "block_dots", "row_bytes", "FemlError"]

@@ -22,7 +22,12 @@ are new. They shard the two operators of the path the natural way:
   experts (feml_b200_mul_mat_id_shard leaves the other slots untouched in a
   zeroed buffer) and a sum all-reduce combines them: every slot has exactly
   one non-zero contributor, so the combine is exact. Invalid expert ids give
-  zero slots on every rank, as on one device.
+  zero slots on every rank, as on one device. With `fused=True` (quantized
+  weights, K % 256 == 0, at most `max_tokens` tokens and `max_selected`
+  experts per token) the combine is fused into the grouped GEMM instead: its
+  epilogue stores every slot into every rank's output buffer over NVLink and
+  the same flag / epoch wait as above ends the step
+  (feml_b200_mul_mat_id_peer).
 
 The compute step defaults to the CUDA entry points of libfeml_b200.so
 (feml_b200.ops); `compute` / `compute_id` can be replaced, which the CPU
@@ -68,6 +73,67 @@ def _gather(out, send, group):
         dist.all_gather(list(out.unbind(0)), send, group=group)
 
 
+class _PeerBuffers:
+    """The peer-memory state of a fused step: two output buffers, a step flag,
+    a grid counter and an epoch per rank. Every rank maps every other rank's
+    buffers and flag into its own device's context with peer access (CUDA IPC
+    handles of the torch allocations, exchanged with all_gather_object and
+    opened through feml_b200_ipc_open). dst0 / dst1 / flags hold, per rank,
+    the address this rank's kernels write (byte `offset` into the buffers)."""
+
+    def __init__(self, shape, device, group, offset=0):
+        import ctypes
+        from . import _check, _lib
+        self.rank, world = _world(group)
+        self.bufs = [torch.zeros(shape, dtype=torch.float32, device=device) for _ in range(2)]
+        self.flag = torch.zeros(1, dtype=torch.int32, device=device)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.steps = 0
+        torch.cuda.synchronize(device)
+        mine = []
+        for t in (self.bufs[0], self.bufs[1], self.flag):
+            handle = ctypes.create_string_buffer(64)
+            off = ctypes.c_uint64()
+            _check(_lib.lib().feml_b200_ipc_export(ctypes.c_void_p(t.data_ptr()), handle, 64, ctypes.byref(off)))
+            mine.append((handle.raw, off.value))
+        everyone = [None] * world
+        dist.all_gather_object(everyone, mine, group=group)
+        opened = {}  # one mapping per peer allocation
+        ptrs = []
+        for r, shared in enumerate(everyone):
+            if r == self.rank:
+                ptrs.append([self.bufs[0].data_ptr(), self.bufs[1].data_ptr(), self.flag.data_ptr()])
+                continue
+            row = []
+            for handle, off in shared:
+                if handle not in opened:
+                    base = ctypes.c_void_p()
+                    _check(_lib.lib().feml_b200_ipc_open(handle, len(handle), ctypes.byref(base)))
+                    opened[handle] = base.value
+                row.append(opened[handle] + off)
+            ptrs.append(row)
+        self.opened = list(opened.values())
+        self.dst0 = [p[0] + offset for p in ptrs]
+        self.dst1 = [p[1] + offset for p in ptrs]
+        self.flags = [p[2] for p in ptrs]
+        dist.barrier(group=group)
+
+    def finish(self, world):
+        """Enqueue the wait for every rank's signal; returns this step's buffer."""
+        from . import ops
+        ops.peer_wait(self.flag, self.epoch, world)
+        self.steps += 1
+        return self.bufs[self.steps & 1]
+
+    def close(self):
+        from . import _lib
+        torch.cuda.synchronize()
+        for base in self.opened:
+            _lib.lib().feml_b200_ipc_close(base)
+        self.opened = []
+
+
 class RowShardedMulMat:
     """y [N, M] = W x with W row-sharded across the ranks of `group`.
 
@@ -97,54 +163,14 @@ class RowShardedMulMat:
         self.compute = compute or _cuda_mul_mat
 
     def _setup_peers(self, device):
-        """Two output buffers, a step flag, a grid counter and an epoch per
-        rank. Every rank maps every other rank's buffers and flag into its own
-        device's context with peer access (CUDA IPC handles of the torch
-        allocations, exchanged with all_gather_object and opened through
-        feml_b200_ipc_open)."""
-        import ctypes
-        from . import _check, _lib
         if self.hi <= self.lo:
             raise FemlError("shape", f"fused row sharding needs rows on every rank (rank {self.rank} has none)")
-        bufs = [torch.zeros((self.max_tokens, self.M), dtype=torch.float32, device=device) for _ in range(2)]
-        flag = torch.zeros(1, dtype=torch.int32, device=device)
-        counter = torch.zeros(1, dtype=torch.int32, device=device)
-        epoch = torch.zeros(1, dtype=torch.int32, device=device)
-        torch.cuda.synchronize(device)
-        mine = []
-        for t in (bufs[0], bufs[1], flag):
-            handle = ctypes.create_string_buffer(64)
-            offset = ctypes.c_uint64()
-            _check(_lib.lib().feml_b200_ipc_export(ctypes.c_void_p(t.data_ptr()), handle, 64, ctypes.byref(offset)))
-            mine.append((handle.raw, offset.value))
-        everyone = [None] * self.world
-        dist.all_gather_object(everyone, mine, group=self.group)
-        opened = {}  # one mapping per peer allocation
-        ptrs = []
-        for r, shared in enumerate(everyone):
-            if r == self.rank:
-                ptrs.append([bufs[0].data_ptr(), bufs[1].data_ptr(), flag.data_ptr()])
-                continue
-            row = []
-            for handle, offset in shared:
-                if handle not in opened:
-                    base = ctypes.c_void_p()
-                    _check(_lib.lib().feml_b200_ipc_open(handle, len(handle), ctypes.byref(base)))
-                    opened[handle] = base.value
-                row.append(opened[handle] + offset)
-            ptrs.append(row)
-        self._peer = dict(bufs=bufs, flag=flag, counter=counter, epoch=epoch, steps=0, opened=list(opened.values()),
-                          dst0=[p[0] + 4 * self.lo for p in ptrs], dst1=[p[1] + 4 * self.lo for p in ptrs],
-                          flags=[p[2] for p in ptrs])
-        dist.barrier(group=self.group)
+        self._peer = _PeerBuffers((self.max_tokens, self.M), device, self.group, 4 * self.lo)
 
     def close(self):
         """Unmap the peers' buffers (after the last fused step has finished)."""
-        from . import _lib
         if self._peer is not None:
-            torch.cuda.synchronize()
-            for base in self._peer["opened"]:
-                _lib.lib().feml_b200_ipc_close(base)
+            self._peer.close()
             self._peer = None
 
     def _fused_ok(self, N):
@@ -160,11 +186,9 @@ class RowShardedMulMat:
             if self._peer is None:
                 self._setup_peers(x.device)
             pe = self._peer
-            ops.mul_mat_peer(self.wtype, self.w_local, x, self.K, pe["dst0"], pe["dst1"], pe["flags"], 4 * self.M,
-                             pe["counter"], pe["epoch"])
-            ops.peer_wait(pe["flag"], pe["epoch"], self.world)
-            pe["steps"] += 1
-            return pe["bufs"][pe["steps"] & 1][:N]
+            ops.mul_mat_peer(self.wtype, self.w_local, x, self.K, pe.dst0, pe.dst1, pe.flags, 4 * self.M,
+                             pe.counter, pe.epoch)
+            return pe.finish(self.world)[:N]
         send = torch.empty((N, self.R), dtype=torch.float32, device=x.device)
         m_loc = self.hi - self.lo
         if m_loc < self.R:
@@ -187,11 +211,15 @@ class ExpertShardedMulMatId:
     order.
     """
 
-    def __init__(self, wtype, w, K, n_experts, group=None, local=False, compute_id=None):
+    def __init__(self, wtype, w, K, n_experts, group=None, local=False, compute_id=None, fused=False,
+                 max_tokens=512, max_selected=8):
         self.wtype = DType(wtype)
         self.K, self.E = K, n_experts
         self.group = group
         self.rank, self.world = _world(group)
+        self.fused = fused
+        self.max_tokens, self.max_selected = max_tokens, max_selected
+        self._peer = None
         n_loc = local_experts(n_experts, self.rank, self.world)
         if local:
             if w.shape[0] != n_loc:
@@ -204,10 +232,37 @@ class ExpertShardedMulMatId:
         self.M = w.shape[1]
         self.compute_id = compute_id or _cuda_mul_mat_id
 
+    def close(self):
+        """Unmap the peers' buffers (after the last fused step has finished)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+
+    def _fused_ok(self, N, n_sel):
+        return (self.fused and N <= self.max_tokens and n_sel <= self.max_selected and self.K % 256 == 0
+                and self.wtype != DType.F32 and self.compute_id is _cuda_mul_mat_id and self.world <= 8)
+
     def __call__(self, x, ids):
         N, n_sel = ids.shape
         if x.shape[0] != N or x.shape[1] != self.K:
             raise FemlError("shape", f"activation {tuple(x.shape)} does not match ids {tuple(ids.shape)} / K={self.K}")
+        if self._fused_ok(N, n_sel):
+            from . import ops
+            if self._peer is None:
+                if self.w_local.shape[0] < 1:
+                    raise FemlError("shape", f"fused expert sharding needs an expert on every rank "
+                                             f"(rank {self.rank} has none)")
+                self._peer = _PeerBuffers((self.max_tokens, self.max_selected, self.M), x.device, self.group)
+                self._ws = torch.empty(ops.mul_mat_id_workspace(self.wtype, self.K, self.M, self.max_tokens,
+                                                                self.max_selected, self.w_local.shape[0]),
+                                       dtype=torch.uint8, device=x.device)
+            pe = self._peer
+            # slot (t, s) at t * nb2 + s * nb1 of the [max_tokens, n_sel, M] view of each buffer
+            nb1, nb2 = 4 * self.M, 4 * self.M * n_sel
+            ops.mul_mat_id_peer(self.wtype, self.w_local, x, ids, self.K, self.E, self.rank, self.world, pe.dst0,
+                                pe.dst1, pe.flags, nb1, nb2, self.M, pe.counter, pe.epoch, self._ws)
+            buf = pe.finish(self.world)
+            return buf.view(-1)[:N * n_sel * self.M].view(N, n_sel, self.M)
         out = torch.zeros((N, n_sel, self.M), dtype=torch.float32, device=x.device)
         self.compute_id(self.wtype, self.w_local, x, ids, self.K, self.E, self.rank, self.world, out)
         dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)

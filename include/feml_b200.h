@@ -333,6 +333,25 @@ int feml_b200_ipc_open(const void *handle, uint64_t handle_bytes, void **base);
 int feml_b200_ipc_export(const void *ptr, void *handle, uint64_t handle_bytes, uint64_t *offset);
 int feml_b200_ipc_close(void *base);
 
+/* Expert-sharded mul_mat_id with the combine fused into the GEMM epilogue (no
+ * counterpart in the reference): this rank (shard of n_shards == n_peers)
+ * computes the slots routed to its experts (expert e on shard e % n_shards,
+ * local index e / n_shards) and stores every output column into every rank's
+ * output buffer of this step (peer_dst0 / peer_dst1 alternate by *epoch
+ * parity as for feml_b200_mul_mat_peer; each buffer holds the full ggml dst,
+ * slot (s, t) at + s*dst_nb1 + t*dst_nb2). Slots with an invalid id are zeroed
+ * by every rank in its own buffer. The grid's last CTA raises every rank's
+ * flag; feml_b200_peer_wait ends the step. Workspace:
+ * feml_b200_mul_mat_id_workspace with n_experts = this shard's expert count.
+ * Needs the tcgen05 GEMM shapes (quantized, K % 256 == 0, 16-byte aligned
+ * rows and activations) and at least one expert per shard. */
+int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,
+                              int64_t shard, int64_t n_shards, const void *x, uint64_t x_nb1, const int32_t *ids,
+                              uint64_t ids_nb1, int64_t n_selected, void *const *peer_dst0, void *const *peer_dst1,
+                              uint32_t *const *peer_flags, int32_t n_peers, uint64_t dst_nb1, uint64_t dst_nb2,
+                              uint32_t *counter, const uint32_t *epoch, int64_t K, int64_t M, int64_t N,
+                              void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream);
+
 /* Enqueue the end of a fused step on this rank: wait (one thread, bounded at
  * about a second) until this rank's flag reaches (*epoch + 1) * n_ranks, then
  * advance *epoch. On timeout bit 0 of *status is set and the stream continues

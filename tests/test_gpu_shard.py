@@ -86,6 +86,33 @@ def test_row_sharded_fused_single_rank(group):
     assert int(status.item()) == 0
 
 
+def test_expert_sharded_fused_single_rank(group):
+    """The fused expert-sharded combine (grouped tcgen05 epilogue storing into
+    the peer buffers) on a one-rank group: bitwise the unfused result over
+    several steps, an invalid id giving a zero slot in both."""
+    rng = np.random.default_rng(8)
+    E, M, K, N, n_sel = 4, 300, 512, 40, 2
+    wq = np.stack([O.quantize(O.DT_Q4_K, (rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+                   for _ in range(E)])
+    wt = torch.from_numpy(wq).cuda()
+    fused = ExpertShardedMulMatId(DType.Q4_K, wt, K, E, fused=True, max_tokens=64, max_selected=4)
+    plain = ExpertShardedMulMatId(DType.Q4_K, wt, K, E)
+    for step in range(3):
+        n = N - 7 * step  # ragged token counts reuse the same buffers
+        x = torch.from_numpy(rng.standard_normal((n, K)).astype(np.float32)).cuda()
+        ids_np = np.stack([rng.permutation(E)[:n_sel] for _ in range(n)]).astype(np.int32)
+        ids_np[3, 1] = E  # invalid id: zero slot
+        ids = torch.from_numpy(ids_np).cuda()
+        got = fused(x, ids).clone()
+        want = plain(x, ids)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), step
+        assert not got[3, 1].any()
+    fused.close()
+    ok, err = tol_ok(got.cpu().numpy(), O.mul_mat_id_ref(O.DT_Q4_K, wq, x.cpu().numpy(), ids_np, K))
+    assert ok, err
+
+
 def _fused_worker(rank, world, port, outdir):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -105,19 +132,49 @@ def _fused_worker(rank, world, port, outdir):
         want = ops.mul_mat(DType.Q8_0, wt, x, K)
         torch.cuda.synchronize()
         worst = max(worst, float((got - want).abs().max()))
+    fused.close()
     np.save(os.path.join(outdir, f"r{rank}.npy"), np.array([worst]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_row_sharded_fused_two_gpus(tmp_path):
-    """Peer stores over NVLink between two processes (needs two GPUs)."""
+def _fused_id_worker(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    rng = np.random.default_rng(12)
+    E, M, K, N, n_sel = 8, 200, 1024, 70, 2
+    wq = np.stack([O.quantize(O.DT_Q8_0, (rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+                   for _ in range(E)])
+    wt = torch.from_numpy(wq).cuda()
+    fused = ExpertShardedMulMatId(DType.Q8_0, wt, K, E, fused=True, max_tokens=N, max_selected=n_sel)
+    worst = 0.0
+    for step in range(4):
+        x = torch.from_numpy(rng.standard_normal((N, K)).astype(np.float32)).cuda()
+        ids = torch.from_numpy(np.stack([rng.permutation(E)[:n_sel] for _ in range(N)]).astype(np.int32)).cuda()
+        got = fused(x, ids).clone()
+        want = ops.mul_mat_id(DType.Q8_0, wt, x, ids, K)
+        torch.cuda.synchronize()
+        worst = max(worst, float((got - want).abs().max()))
+    fused.close()
+    np.save(os.path.join(outdir, f"r{rank}.npy"), np.array([worst]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("worker", [_fused_worker, _fused_id_worker], ids=["rows", "experts"])
+def test_sharded_fused_two_gpus(tmp_path, worker):
+    """Peer stores over NVLink between two processes (needs two GPUs): the
+    gathered rows / combined expert slots equal the one-GPU result bitwise."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.start_processes(_fused_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
     for r in range(2):
         assert float(np.load(tmp_path / f"r{r}.npy")[0]) == 0.0
