@@ -399,7 +399,7 @@ __device__ __forceinline__ void convert_pair(const uint32_t *w, const uint32_t *
     }
 }
 
-template <int WT>
+template <int WT, bool PEER>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const TcParams p) {
@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (p.grouped) {
         const int t = blockIdx.y;
         if (t >= p.g.tile_start[p.g.n_groups]) {  // unused tile (uniform, before any set-up)
-            if (p.peer.n > 0 && threadIdx.x == 0) peer_cta_done(p.peer);
+            if (PEER && threadIdx.x == 0) peer_cta_done(p.peer);
             return;
         }
         while (p.g.tile_start[expert + 1] <= t) expert++;
@@ -451,6 +451,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     float *ring = reinterpret_cast<float *>(gbase + L::OFF_SC);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // epilogue warps with columns: a narrow tile (a group's or the matrix's
+    // last columns) leaves whole column quarters empty, and their warps sit
+    // the tile out instead of polling the pipeline's barriers
+    const int epi_live = 4 * min(4, (ncols + 31) / 32);
 
     if (tid == 0) {
         for (int i = 0; i < C::NR; i++) {
@@ -459,11 +463,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int i = 0; i < C::NA; i++) mbar_init(&a_full[i], 128);
         for (int i = 0; i < C::NB; i++) mbar_init(&b_full[i], 1);
-        for (int i = 0; i < TC_PSLOTS; i++) mbar_init(&t_empty[i], TC_EPI_WARPS);
+        for (int i = 0; i < TC_PSLOTS; i++) mbar_init(&t_empty[i], epi_live);
         for (int i = 0; i < TC_ND; i++) mbar_init(&pair_done[i], 1);
         for (int i = 0; i < TC_NS; i++) {
             mbar_init(&s_full[i], 128 + 32);  // converter rows + the activation-scale warp
-            mbar_init(&s_empty[i], TC_EPI_WARPS);
+            mbar_init(&s_empty[i], epi_live);
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
@@ -555,6 +559,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 2) {
         // ---- MMA issue (one thread) ---------------------------------------------
         if (lane == 0) {
+            // a narrow tile multiplies only its columns, rounded up to the
+            // MMA's N granularity of 16 (M = 128: N = 16..256, N % 16 == 0)
             constexpr uint32_t idesc = f16_idesc(TC_BM, TC_BN);
             bool ok = true;
             for (int q = 0; q < npairs && ok; q++) {
@@ -637,10 +643,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---- epilogue: warp w reads TMEM lanes 32*(w%4).., columns 32*qc.. ------
         const int sub = warp & 3, qc = (warp - 8) >> 2;  // lane quarter, column quarter
         const int row = 32 * sub + lane;
+        const bool live = 32 * qc < ncols;
         uint64_t acc2[16];  // columns (2i, 2i+1) of the warp's 32, as f32x2
 #pragma unroll
         for (int i = 0; i < 16; i++) acc2[i] = 0;
-        bool ok = true;
+        bool ok = live;
         for (int q = 0; q < npairs && ok; q++) {
             const int ss = q % TC_NS;
             if (!tc_wait_warp(&s_full[ss], (q / TC_NS) & 1, abort_flag, lane)) {
@@ -723,7 +730,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             } else {
                                 off = (uint64_t)r * p.y_nb1;
                             }
-                            if (p.peer.n == 0) {
+                            if constexpr (!PEER) {
                                 reinterpret_cast<float *>(p.y + off)[m] = acc[i];
                             } else {  // NVLink stores into every rank's buffer of this step
                                 const int b = (int)((*p.peer.epoch + 1u) & 1u);
@@ -737,11 +744,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     }
 
-    if (p.peer.n > 0) __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
+    if (PEER) __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
     tc_fence_before();
     __syncthreads();
     if (*abort_flag && tid == 0) report_status(p.status, STATUS_TIMEOUT);
-    if (p.peer.n > 0 && tid == 0) peer_cta_done(p.peer);
+    if (PEER && tid == 0) peer_cta_done(p.peer);
     if (warp == 2) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS)
@@ -857,13 +864,16 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     rc = encode_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xa.q16, (uint64_t)K, (uint64_t)rows, 0, (uint64_t)K * 2, 0,
                     64, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    static int configured[64] = {0};
+    // the peer-store variant is a separate instantiation, so the plain kernel
+    // carries none of its registers
+    const auto kern = peer ? gemm_tc_kernel<WT, true> : gemm_tc_kernel<WT, false>;
+    static int configured[64][2] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+    if (dev >= 0 && dev < 64 && !configured[dev][peer ? 1 : 0]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
         if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc smem attribute: %s", cudaGetErrorString(e));
-        configured[dev] = 1;
+        configured[dev][peer ? 1 : 0] = 1;
     }
     TcParams p{};
     p.M = (int)M;
@@ -888,7 +898,7 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     if (tiles_n == 0 || M == 0) return FB_OK;
     if (tiles_n > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_tc: too many column tiles");
     dim3 grid((unsigned)((M + TC_BM - 1) / TC_BM), tiles_n, (unsigned)std::max(splits, 1));
-    gemm_tc_kernel<WT><<<grid, TC_THREADS, L::BYTES, s>>>(tw, tx, p);
+    kern<<<grid, TC_THREADS, L::BYTES, s>>>(tw, tx, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc launch: %s", cudaGetErrorString(e));
     if (p.partial) {
