@@ -53,83 +53,101 @@ __device__ __forceinline__ void make_shifted(const uint32_t (&w)[8], uint32_t (&
     }
 }
 
+// The activation words one block pair of Q8_0 / Q4_0 weights is dotted with:
+// the even block's shifted words (e0, e1, e2: words 0..9; Q8_0 uses 0..8) and
+// the odd block's 8 packed words (o0, o1). Held in registers by callers that
+// reuse one pair's activations across many weight rows.
+struct XFrag {
+    uint4 e0, e1;
+    uint2 e2;
+    uint4 o0, o1;
+};
+
+// `xe` the even block's shifted words (16-byte aligned), `xo` the odd block's
+// 8 words (16-byte aligned).
+__device__ __forceinline__ XFrag load_xfrag(const uint32_t *xe, const uint32_t *xo) {
+    XFrag f;
+    f.e0 = *reinterpret_cast<const uint4 *>(xe);
+    f.e1 = *reinterpret_cast<const uint4 *>(xe + 4);
+    f.e2 = *reinterpret_cast<const uint2 *>(xe + 8);
+    f.o0 = *reinterpret_cast<const uint4 *>(xo);
+    f.o1 = *reinterpret_cast<const uint4 *>(xo + 4);
+    return f;
+}
+
 // Block-pair integer sums. `wp` is the pair's first byte (4-byte aligned);
-// `xe` the even block's shifted words, `xo` the odd block's 8 words; xsum_*
-// the activation block sums (Q4_0 offset). Returns sums s0 (even block),
-// s1 (odd block) and the blocks' f16 scales as f32.
+// `x` the pair's activation words; xsum_* the activation block sums (Q4_0
+// offset). Returns sums s0 (even block), s1 (odd block) and the blocks' f16
+// scales as f32.
 template <int WT>
-__device__ __forceinline__ void pair_dot(const uint32_t *wp, const uint32_t *xe, const uint32_t *xo, int xsum0,
-                                         int xsum1, int &s0, int &s1, float &d0, float &d1) {
+__device__ __forceinline__ void pair_dot_frag(const uint32_t *wp, const XFrag &x, int xsum0, int xsum1, int &s0,
+                                              int &s1, float &d0, float &d1) {
     if constexpr (WT == WT_Q8_0) {
         uint32_t w[17];
 #pragma unroll
         for (int i = 0; i < 17; i++) w[i] = wp[i];
-        const uint4 e0 = *reinterpret_cast<const uint4 *>(xe);
-        const uint4 e1 = *reinterpret_cast<const uint4 *>(xe + 4);
-        const uint32_t e8 = xe[8];
-        const uint4 o0 = *reinterpret_cast<const uint4 *>(xo);
-        const uint4 o1 = *reinterpret_cast<const uint4 *>(xo + 4);
         // four independent chains (even lo/hi, odd lo/hi) for ILP
         int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-        a0 = dp4a_ss(w[0], e0.x, a0);
-        a1 = dp4a_ss(w[1], e0.y, a1);
-        b0 = dp4a_ss(w[9], o0.x, b0);
-        b1 = dp4a_ss(w[10], o0.y, b1);
-        a0 = dp4a_ss(w[2], e0.z, a0);
-        a1 = dp4a_ss(w[3], e0.w, a1);
-        b0 = dp4a_ss(w[11], o0.z, b0);
-        b1 = dp4a_ss(w[12], o0.w, b1);
-        a0 = dp4a_ss(w[4], e1.x, a0);
-        a1 = dp4a_ss(w[5], e1.y, a1);
-        b0 = dp4a_ss(w[13], o1.x, b0);
-        b1 = dp4a_ss(w[14], o1.y, b1);
-        a0 = dp4a_ss(w[6], e1.z, a0);
-        a1 = dp4a_ss(w[7], e1.w, a1);
-        b0 = dp4a_ss(w[15], o1.z, b0);
-        b1 = dp4a_ss(w[16], o1.w, b1);
-        a0 = dp4a_ss(w[8], e8, a0);
-        const int a = a0 + a1, b = b0 + b1;
-        s0 = a;
-        s1 = b;
+        a0 = dp4a_ss(w[0], x.e0.x, a0);
+        a1 = dp4a_ss(w[1], x.e0.y, a1);
+        b0 = dp4a_ss(w[9], x.o0.x, b0);
+        b1 = dp4a_ss(w[10], x.o0.y, b1);
+        a0 = dp4a_ss(w[2], x.e0.z, a0);
+        a1 = dp4a_ss(w[3], x.e0.w, a1);
+        b0 = dp4a_ss(w[11], x.o0.z, b0);
+        b1 = dp4a_ss(w[12], x.o0.w, b1);
+        a0 = dp4a_ss(w[4], x.e1.x, a0);
+        a1 = dp4a_ss(w[5], x.e1.y, a1);
+        b0 = dp4a_ss(w[13], x.o1.x, b0);
+        b1 = dp4a_ss(w[14], x.o1.y, b1);
+        a0 = dp4a_ss(w[6], x.e1.z, a0);
+        a1 = dp4a_ss(w[7], x.e1.w, a1);
+        b0 = dp4a_ss(w[15], x.o1.z, b0);
+        b1 = dp4a_ss(w[16], x.o1.w, b1);
+        a0 = dp4a_ss(w[8], x.e2.x, a0);
+        s0 = a0 + a1;
+        s1 = b0 + b1;
         d0 = f16_bits_to_f32((uint16_t)(w[0] & 0xffffu));
         d1 = f16_bits_to_f32((uint16_t)(w[8] >> 16));
     } else {  // Q4_0: 36 bytes
         uint32_t w[9];
 #pragma unroll
         for (int i = 0; i < 9; i++) w[i] = wp[i];
-        const uint4 e0 = *reinterpret_cast<const uint4 *>(xe);
-        const uint4 e1 = *reinterpret_cast<const uint4 *>(xe + 4);
-        const uint2 e2 = *reinterpret_cast<const uint2 *>(xe + 8);
-        const uint4 o0 = *reinterpret_cast<const uint4 *>(xo);
-        const uint4 o1 = *reinterpret_cast<const uint4 *>(xo + 4);
         const uint32_t lo = 0x0f0f0f0fu, hi = 0xf0f0f0f0u;
         // even block: low nibbles vs shifted x0..15 (words 0..4), high vs x16..31 (words 5..9)
         int el = 0, eh = 0;
-        el = dp4a_ss(w[0] & lo, e0.x, el);
-        el = dp4a_ss(w[1] & lo, e0.y, el);
-        el = dp4a_ss(w[2] & lo, e0.z, el);
-        el = dp4a_ss(w[3] & lo, e0.w, el);
-        el = dp4a_ss(w[4] & lo, e1.x, el);
-        eh = dp4a_us(w[0] & hi, e1.y, eh);
-        eh = dp4a_us(w[1] & hi, e1.z, eh);
-        eh = dp4a_us(w[2] & hi, e1.w, eh);
-        eh = dp4a_us(w[3] & hi, e2.x, eh);
-        eh = dp4a_us(w[4] & hi, e2.y, eh);
+        el = dp4a_ss(w[0] & lo, x.e0.x, el);
+        el = dp4a_ss(w[1] & lo, x.e0.y, el);
+        el = dp4a_ss(w[2] & lo, x.e0.z, el);
+        el = dp4a_ss(w[3] & lo, x.e0.w, el);
+        el = dp4a_ss(w[4] & lo, x.e1.x, el);
+        eh = dp4a_us(w[0] & hi, x.e1.y, eh);
+        eh = dp4a_us(w[1] & hi, x.e1.z, eh);
+        eh = dp4a_us(w[2] & hi, x.e1.w, eh);
+        eh = dp4a_us(w[3] & hi, x.e2.x, eh);
+        eh = dp4a_us(w[4] & hi, x.e2.y, eh);
         // odd block: words 5..8
         int ol = 0, oh = 0;
-        ol = dp4a_ss(w[5] & lo, o0.x, ol);
-        ol = dp4a_ss(w[6] & lo, o0.y, ol);
-        ol = dp4a_ss(w[7] & lo, o0.z, ol);
-        ol = dp4a_ss(w[8] & lo, o0.w, ol);
-        oh = dp4a_us(w[5] & hi, o1.x, oh);
-        oh = dp4a_us(w[6] & hi, o1.y, oh);
-        oh = dp4a_us(w[7] & hi, o1.z, oh);
-        oh = dp4a_us(w[8] & hi, o1.w, oh);
+        ol = dp4a_ss(w[5] & lo, x.o0.x, ol);
+        ol = dp4a_ss(w[6] & lo, x.o0.y, ol);
+        ol = dp4a_ss(w[7] & lo, x.o0.z, ol);
+        ol = dp4a_ss(w[8] & lo, x.o0.w, ol);
+        oh = dp4a_us(w[5] & hi, x.o1.x, oh);
+        oh = dp4a_us(w[6] & hi, x.o1.y, oh);
+        oh = dp4a_us(w[7] & hi, x.o1.z, oh);
+        oh = dp4a_us(w[8] & hi, x.o1.w, oh);
         s0 = el + (eh >> 4) - 8 * xsum0;
         s1 = ol + (oh >> 4) - 8 * xsum1;
         d0 = f16_bits_to_f32((uint16_t)(w[0] & 0xffffu));
         d1 = f16_bits_to_f32((uint16_t)(w[4] >> 16));
     }
+}
+
+// pair_dot_frag with the activation words read from shared memory.
+template <int WT>
+__device__ __forceinline__ void pair_dot(const uint32_t *wp, const uint32_t *xe, const uint32_t *xo, int xsum0,
+                                         int xsum1, int &s0, int &s1, float &d0, float &d1) {
+    pair_dot_frag<WT>(wp, load_xfrag(xe, xo), xsum0, xsum1, s0, s1, d0, d1);
 }
 
 // One even block with no odd partner (odd block count): Q8_0 / Q4_0 sums

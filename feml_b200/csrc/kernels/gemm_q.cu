@@ -372,7 +372,7 @@ __global__ void block_dots_kernel(const uint8_t *w, uint64_t w_nb1, const uint8_
         const int b0 = 2 * pr;
         const bool single = b0 + 1 >= nblk;
         // activation blocks b0, b0+1 as packed words, their sums, the shifted form
-        uint32_t xw[2][8];
+        __align__(16) uint32_t xw[2][8];
         int xs[2] = {0, 0};
         for (int k = 0; k < 2; k++) {
             const int b = b0 + k;
@@ -399,7 +399,7 @@ __global__ void block_dots_kernel(const uint8_t *w, uint64_t w_nb1, const uint8_
             const uint8_t *up = row + (uint64_t)b0 * UBY;
             const int nb = single ? UBY : 2 * UBY;
             for (int l = 0; l < (int)sizeof(wbuf); l++) wb8[l] = l < nb ? up[l] : 0;
-            uint32_t sh[kShiftWords];
+            __align__(16) uint32_t sh[kShiftWords];
             make_shifted<WT>(xw[0], sh);
             float d0, d1;
             if (single)

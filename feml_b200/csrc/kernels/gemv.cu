@@ -106,12 +106,10 @@ __host__ __device__ inline SmemLayout smem_layout(int K, int ncols, bool shifted
 // (d = amax/127, id = 1/d, q = roundf(x*id)). Writes the block's packed
 // integers, f16-rounded scale and integer sum, and for even blocks of Q8_0 /
 // Q4_0 the shifted copy read by the pair kernels. All 32 lanes of the warp
-// must call it (`valid` false for padding groups).
-template <int WT>
-__device__ __forceinline__ void quantize_block_quarter(const float *xb, bool vec, bool valid, bool even, int8_t *sq_blk,
-                                                       uint32_t *sx2_blk, float *sd_b, int32_t *ss_b) {
+// must call it (`valid` false for padding groups). The load is separate so a
+// caller can issue the loads of several blocks before quantizing any.
+__device__ __forceinline__ void load_block_quarter(const float *xb, bool vec, bool valid, float (&v)[8]) {
     const int t = threadIdx.x & 3;  // quarter of the block
-    float v[8];
     if (valid) {
         const float *xe = xb + 8 * t;
         if (vec) {
@@ -127,6 +125,12 @@ __device__ __forceinline__ void quantize_block_quarter(const float *xb, bool vec
 #pragma unroll
         for (int i = 0; i < 8; i++) v[i] = 0.0f;
     }
+}
+
+template <int WT>
+__device__ __forceinline__ void quantize_block_quarter(const float (&v)[8], bool valid, bool even, int8_t *sq_blk,
+                                                       uint32_t *sx2_blk, float *sd_b, int32_t *ss_b) {
+    const int t = threadIdx.x & 3;  // quarter of the block
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
@@ -177,8 +181,13 @@ __device__ __forceinline__ void quantize_block_quarter(const float *xb, bool vec
     }
 }
 
-template <int WT, int NC>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p) {
+// XR > 0: every row is one chunk and a lane's XR block pairs (lane, lane+32,
+// ...) are the same in every row, so their activation words stay in
+// registers instead of being re-read from shared memory for every row (the
+// shared-memory reads of a row then are its weights only). Register use is
+// capped so the next launch's CTA still fits beside this one.
+template <int WT, int NC, int XR>
+__global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int UB = Fmt<WT>::kUnitBytes;
     constexpr bool SH = Fmt<WT>::kShifted;
@@ -258,16 +267,43 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     // Activations -> Q8_0 in shared memory.
     if (p.xq.qs == nullptr) {
         constexpr int kGroups = kGemvThreads / 4;  // 4 lanes per block
-#pragma unroll 2
-        for (int base = 0; base < NC * nblk; base += kGroups) {  // uniform trip count
+        auto block_of = [&](int base, bool &valid, int &n, int &b) {
             const int t = base + (int)(threadIdx.x >> 2);
-            const bool valid = t < NC * nblk;
-            const int n = !valid ? 0 : (NC == 1 ? 0 : t / nblk);
-            const int b = !valid ? 0 : t - n * nblk;
-            const float *xb = reinterpret_cast<const float *>(p.x + (uint64_t)n * p.x_nb1) + b * QK;
-            quantize_block_quarter<WT>(xb, p.x_vec16, valid, SH && !(b & 1), sq + n * K + b * QK,
-                                       sx2 + (n * npair_blk + b / 2) * kShiftWords, sd + n * nbp + b,
-                                       ss + n * nbp + b);
+            valid = t < NC * nblk;
+            n = !valid ? 0 : (NC == 1 ? 0 : t / nblk);
+            b = !valid ? 0 : t - n * nblk;
+        };
+        auto xptr = [&](int n, int b) {
+            return reinterpret_cast<const float *>(p.x + (uint64_t)n * p.x_nb1) + b * QK;
+        };
+        if (NC * nblk <= 2 * kGroups) {
+            // both blocks' loads in flight before either is quantized (this
+            // phase sits between the dependency wait and the first dot product)
+            bool v0, v1;
+            int n0, b0, n1, b1;
+            block_of(0, v0, n0, b0);
+            block_of(kGroups, v1, n1, b1);
+            float x0[8], x1[8];
+            load_block_quarter(xptr(n0, b0), p.x_vec16, v0, x0);
+            load_block_quarter(xptr(n1, b1), p.x_vec16, v1, x1);
+            quantize_block_quarter<WT>(x0, v0, SH && !(b0 & 1), sq + n0 * K + b0 * QK,
+                                       sx2 + (n0 * npair_blk + b0 / 2) * kShiftWords, sd + n0 * nbp + b0,
+                                       ss + n0 * nbp + b0);
+            quantize_block_quarter<WT>(x1, v1, SH && !(b1 & 1), sq + n1 * K + b1 * QK,
+                                       sx2 + (n1 * npair_blk + b1 / 2) * kShiftWords, sd + n1 * nbp + b1,
+                                       ss + n1 * nbp + b1);
+        } else {
+#pragma unroll 2
+            for (int base = 0; base < NC * nblk; base += kGroups) {  // uniform trip count
+                bool valid;
+                int n, b;
+                block_of(base, valid, n, b);
+                float xv[8];
+                load_block_quarter(xptr(n, b), p.x_vec16, valid, xv);
+                quantize_block_quarter<WT>(xv, valid, SH && !(b & 1), sq + n * K + b * QK,
+                                           sx2 + (n * npair_blk + b / 2) * kShiftWords, sd + n * nbp + b,
+                                           ss + n * nbp + b);
+            }
         }
     } else {
         const int4 *src = reinterpret_cast<const int4 *>(p.xq.qs);
@@ -300,6 +336,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     float acc[kMaxCols];
 #pragma unroll
     for (int n = 0; n < kMaxCols; n++) acc[n] = 0.0f;
+
+    constexpr int XRN = XR > 0 ? XR : 1;
+    XFrag xf[XRN];
+    int2 xsr[XRN];
+    float2 dxr[XRN];
+    if constexpr (XR > 0) {
+#pragma unroll
+        for (int j = 0; j < XR; j++) {
+            const int pr = lane + 32 * j, b0 = 2 * pr;
+            if (2 * pr + 1 < nblk) {
+                xf[j] = load_xfrag(sx2 + (b0 / 2) * kShiftWords, reinterpret_cast<const uint32_t *>(sq + (b0 + 1) * QK));
+                xsr[j] = *reinterpret_cast<const int2 *>(ss + b0);
+                dxr[j] = *reinterpret_cast<const float2 *>(sd + b0);
+            }
+        }
+    }
 
     for (int i = 0; i < n_items; i++) {
         const int stage = i % p.nstage;
@@ -360,6 +412,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
                     acc[n] += dx.x * (dsc0 * (float)s0 - dmm0 * (float)xs.x) +
                               dx.y * (dsc1 * (float)s1 - dmm1 * (float)xs.y);
                 }
+            }
+        } else if constexpr (XR > 0) {
+#pragma unroll
+            for (int j = 0; j < XR; j++) {
+                const int pr = lane + 32 * j;  // u0 == 0: every row is one chunk
+                if (pr < np) {
+                    int s0, s1;
+                    float d0, d1;
+                    pair_dot_frag<WT>(reinterpret_cast<const uint32_t *>(p0 + 2 * UB * pr), xf[j], xsr[j].x,
+                                      xsr[j].y, s0, s1, d0, d1);
+                    acc[0] += (d0 * dxr[j].x) * (float)s0 + (d1 * dxr[j].y) * (float)s1;
+                }
+            }
+            if ((nu & 1) && lane == (np & 31)) {  // trailing unpaired block of an odd-length row
+                const int b0 = 2 * np;
+                float d0;
+                const int s0 = single_even_dot<WT>(reinterpret_cast<const uint32_t *>(p0 + 2 * UB * np),
+                                                   sx2 + (b0 / 2) * kShiftWords, ss[b0], d0);
+                acc[0] += (d0 * sd[b0]) * (float)s0;
             }
         } else {
 #pragma unroll 2
@@ -456,9 +527,9 @@ __global__ void peer_wait_kernel(const uint32_t *flag, uint32_t *epoch, int n_ra
     report_status(status, STATUS_TIMEOUT);
 }
 
-template <int WT, int NC>
+template <int WT, int NC, int XR>
 int launch_typed(const GemvParams &p, int grid, uint32_t smem, cudaStream_t s, bool pdl) {
-    auto kern = gemv_kernel<WT, NC>;
+    auto kern = gemv_kernel<WT, NC, XR>;
     static bool smem_set[64] = {false};  // per device: the dynamic smem limit was raised
     int dev = 0;
     cudaGetDevice(&dev);
@@ -483,13 +554,18 @@ int launch_typed(const GemvParams &p, int grid, uint32_t smem, cudaStream_t s, b
     return FB_OK;
 }
 
+// xr: activation pairs per lane held in registers (0: read from shared memory)
 template <int WT>
-int launch_cols(int ncols, const GemvParams &p, int grid, uint32_t smem, cudaStream_t s, bool pdl) {
+int launch_cols(int ncols, int xr, const GemvParams &p, int grid, uint32_t smem, cudaStream_t s, bool pdl) {
+    if constexpr (WT != WT_Q4_K) {
+        if (ncols == 1 && xr == 1) return launch_typed<WT, 1, 1>(p, grid, smem, s, pdl);
+        if (ncols == 1 && xr == 2) return launch_typed<WT, 1, 2>(p, grid, smem, s, pdl);
+    }
     switch (ncols) {
-    case 1: return launch_typed<WT, 1>(p, grid, smem, s, pdl);
-    case 2: return launch_typed<WT, 2>(p, grid, smem, s, pdl);
-    case 3: return launch_typed<WT, 3>(p, grid, smem, s, pdl);
-    default: return launch_typed<WT, 4>(p, grid, smem, s, pdl);
+    case 1: return launch_typed<WT, 1, 0>(p, grid, smem, s, pdl);
+    case 2: return launch_typed<WT, 2, 0>(p, grid, smem, s, pdl);
+    case 3: return launch_typed<WT, 3, 0>(p, grid, smem, s, pdl);
+    default: return launch_typed<WT, 4, 0>(p, grid, smem, s, pdl);
     }
 }
 
@@ -596,10 +672,12 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     p.x_vec16 = ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0;
     p.peer = peer ? *peer : PeerOut{};
     p.copy_rows = ((reinterpret_cast<uintptr_t>(w) | w_nb1) % align) != 0;
+    // whole rows per chunk and at most two pairs per lane: activations in registers
+    const int xr = (N == 1 && nchunks == 1 && !p.copy_rows) ? (nunits <= 64 ? 1 : (nunits <= 128 ? 2 : 0)) : 0;
     switch (wtype) {
-    case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, p, grid, L.total, s, pdl);
-    case WT_Q4_0: return launch_cols<WT_Q4_0>((int)N, p, grid, L.total, s, pdl);
-    default: return launch_cols<WT_Q4_K>((int)N, p, grid, L.total, s, pdl);
+    case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, xr, p, grid, L.total, s, pdl);
+    case WT_Q4_0: return launch_cols<WT_Q4_0>((int)N, xr, p, grid, L.total, s, pdl);
+    default: return launch_cols<WT_Q4_K>((int)N, xr, p, grid, L.total, s, pdl);
     }
 }
 
