@@ -5,7 +5,7 @@
 // d_x * (d*sc, dmin*m terms) for Q4_K sub-blocks.
 //
 // B200 mapping. The kernel is HBM-bound (weights are read once):
-//  - one CTA per SM with at most ~100 KB of shared memory, so the CTA of the
+//  - one CTA per SM with at most 112 KB of shared memory, so the CTA of the
 //    next launch fits beside it; launches are chained with programmatic
 //    dependent launch (PDL): a CTA streams its weights before waiting for the
 //    preceding grid, so the weight stream of launch i+1 overlaps launch i;
@@ -18,7 +18,10 @@
 //    thread per 32-element block), or copied from a planar buffer written by a
 //    preceding quantize kernel (large N*K);
 //  - the dot products run on 64-element pairs with aligned shared-memory loads
-//    (kernels/dot.cuh);
+//    (kernels/dot.cuh); for one column and rows of at most 128 blocks the
+//    activation words of a lane's pairs stay in registers for all rows and a
+//    warp takes its rows two at a time (the time after the dependency wait,
+//    not HBM, bounds a small decode GEMV chained with PDL);
 //  - rows whose bytes are not 4-byte (Q4_K: 16-byte) aligned are copied into
 //    the stage with plain loads instead of TMA; rows that are aligned but not
 //    16-byte aligned get their ragged head/tail bytes by plain loads.
@@ -40,7 +43,9 @@ constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kMaxCols = 4;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int kFusedMaxElems = 16384;            // N*K up to which each CTA quantizes x itself
-constexpr uint32_t kCoResidentCta = 100 * 1024;  // per-CTA smem that leaves room for the next launch
+// per-CTA smem that leaves room for the next launch's CTA (2 x (112 + 1
+// reserved) KB of the SM's 228 KB)
+constexpr uint32_t kCoResidentCta = 112 * 1024;
 constexpr uint32_t kCoResidentActs = 40 * 1024;  // activation bytes up to which that budget is used
 
 template <int WT>
@@ -353,7 +358,86 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
         }
     }
 
-    for (int i = 0; i < n_items; i++) {
+    // output row `row`, column n: this rank's buffer or every peer's
+    auto store_row = [&](int n, int row, float v) {
+        if (p.peer.n == 0) {
+            reinterpret_cast<float *>(p.y + (uint64_t)n * p.y_nb1)[row] = v;
+        } else {
+            const int b = (int)((*p.peer.epoch + 1u) & 1u);
+            for (int r = 0; r < p.peer.n; r++)  // NVLink stores into each rank's output
+                reinterpret_cast<float *>(p.peer.y[b][r] + (uint64_t)n * p.y_nb1)[row] = v;
+        }
+    };
+
+    if constexpr (XR > 0) {
+        // Whole 16-byte-aligned rows, two at a time: the two rows' dot
+        // products and warp reductions interleave, and both stages are
+        // re-armed together.
+        const int nu = nblk, np = nu / 2;
+        for (int i = 0; i < n_items; i += 2) {
+            const bool two = i + 1 < n_items;
+            bool ok = mbar_wait_bounded(&bars[i % p.nstage], (uint32_t)(i / p.nstage) & 1u);
+            if (two) ok = ok && mbar_wait_bounded(&bars[(i + 1) % p.nstage], (uint32_t)((i + 1) / p.nstage) & 1u);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0) {
+                    report_status(p.status, STATUS_TIMEOUT);
+                    for (int j = i; j < issued; j++)
+                        mbar_wait_bounded(&bars[j % p.nstage], (uint32_t)(j / p.nstage) & 1u);
+                }
+                __syncwarp();
+                return;
+            }
+            const uint8_t *r0 = ring + (uint32_t)(i % p.nstage) * p.stage_bytes;
+            const uint8_t *r1 = ring + (uint32_t)((i + 1) % p.nstage) * p.stage_bytes;
+            float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < XR; j++) {
+                const int pr = lane + 32 * j;
+                if (pr < np) {
+                    int s0, s1;
+                    float d0, d1;
+                    pair_dot_frag<WT>(reinterpret_cast<const uint32_t *>(r0 + 2 * UB * pr), xf[j], xsr[j].x,
+                                      xsr[j].y, s0, s1, d0, d1);
+                    a0 += (d0 * dxr[j].x) * (float)s0 + (d1 * dxr[j].y) * (float)s1;
+                    if (two) {
+                        pair_dot_frag<WT>(reinterpret_cast<const uint32_t *>(r1 + 2 * UB * pr), xf[j], xsr[j].x,
+                                          xsr[j].y, s0, s1, d0, d1);
+                        a1 += (d0 * dxr[j].x) * (float)s0 + (d1 * dxr[j].y) * (float)s1;
+                    }
+                }
+            }
+            if ((nu & 1) && lane == (np & 31)) {  // trailing unpaired block of an odd-length row
+                const int b0 = 2 * np;
+                const uint32_t *xe = sx2 + (b0 / 2) * kShiftWords;
+                float d0;
+                const int s0 = single_even_dot<WT>(reinterpret_cast<const uint32_t *>(r0 + 2 * UB * np), xe, ss[b0], d0);
+                a0 += (d0 * sd[b0]) * (float)s0;
+                if (two) {
+                    const int s1 = single_even_dot<WT>(reinterpret_cast<const uint32_t *>(r1 + 2 * UB * np), xe,
+                                                       ss[b0], d0);
+                    a1 += (d0 * sd[b0]) * (float)s1;
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && issued < n_items) {
+                fence_proxy_async_smem();
+                issue(issued);
+                if (two && issued + 1 < n_items) issue(issued + 1);
+            }
+            issued = min(issued + (two ? 2 : 1), n_items);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {  // the two rows' butterflies interleaved
+                a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+                a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+            }
+            if (lane == 0) {
+                store_row(0, w_begin + i, a0);
+                if (two) store_row(0, w_begin + i + 1, a1);
+            }
+        }
+    }
+
+    for (int i = 0; i < (XR > 0 ? 0 : n_items); i++) {
         const int stage = i % p.nstage;
         const bool ok = mbar_wait_bounded(&bars[stage], (uint32_t)(i / p.nstage) & 1u);
         if (!__all_sync(0xffffffffu, ok)) {
@@ -413,25 +497,6 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
                               dx.y * (dsc1 * (float)s1 - dmm1 * (float)xs.y);
                 }
             }
-        } else if constexpr (XR > 0) {
-#pragma unroll
-            for (int j = 0; j < XR; j++) {
-                const int pr = lane + 32 * j;  // u0 == 0: every row is one chunk
-                if (pr < np) {
-                    int s0, s1;
-                    float d0, d1;
-                    pair_dot_frag<WT>(reinterpret_cast<const uint32_t *>(p0 + 2 * UB * pr), xf[j], xsr[j].x,
-                                      xsr[j].y, s0, s1, d0, d1);
-                    acc[0] += (d0 * dxr[j].x) * (float)s0 + (d1 * dxr[j].y) * (float)s1;
-                }
-            }
-            if ((nu & 1) && lane == (np & 31)) {  // trailing unpaired block of an odd-length row
-                const int b0 = 2 * np;
-                float d0;
-                const int s0 = single_even_dot<WT>(reinterpret_cast<const uint32_t *>(p0 + 2 * UB * np),
-                                                   sx2 + (b0 / 2) * kShiftWords, ss[b0], d0);
-                acc[0] += (d0 * sd[b0]) * (float)s0;
-            }
         } else {
 #pragma unroll 2
             for (int pr = lane; pr < np; pr += 32) {
@@ -471,15 +536,7 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
 #pragma unroll
             for (int n = 0; n < NC; n++) {
                 const float v = warp_sum(acc[n]);
-                if (lane == 0) {
-                    if (p.peer.n == 0) {
-                        reinterpret_cast<float *>(p.y + (uint64_t)n * p.y_nb1)[row] = v;
-                    } else {
-                        const int b = (int)((*p.peer.epoch + 1u) & 1u);
-                        for (int r = 0; r < p.peer.n; r++)  // NVLink stores into each rank's output
-                            reinterpret_cast<float *>(p.peer.y[b][r] + (uint64_t)n * p.y_nb1)[row] = v;
-                    }
-                }
+                if (lane == 0) store_row(n, row, v);
                 acc[n] = 0.0f;
             }
         }
@@ -673,7 +730,8 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     p.peer = peer ? *peer : PeerOut{};
     p.copy_rows = ((reinterpret_cast<uintptr_t>(w) | w_nb1) % align) != 0;
     // whole rows per chunk and at most two pairs per lane: activations in registers
-    const int xr = (N == 1 && nchunks == 1 && !p.copy_rows) ? (nunits <= 64 ? 1 : (nunits <= 128 ? 2 : 0)) : 0;
+    const bool rows16 = ((reinterpret_cast<uintptr_t>(w) | w_nb1) & 15) == 0;
+    const int xr = (N == 1 && nchunks == 1 && rows16) ? (nunits <= 64 ? 1 : (nunits <= 128 ? 2 : 0)) : 0;
     switch (wtype) {
     case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, xr, p, grid, L.total, s, pdl);
     case WT_Q4_0: return launch_cols<WT_Q4_0>((int)N, xr, p, grid, L.total, s, pdl);
