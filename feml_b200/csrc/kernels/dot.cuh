@@ -175,15 +175,14 @@ __device__ __forceinline__ int single_even_dot(const uint32_t *wp, const uint32_
 // Q4_K sub-block pair g (0..3) of the super-block at `sb` (16-byte aligned):
 // integer sums s0 (sub-block 2g, low nibbles), s1 (sub-block 2g+1, high
 // nibbles) and the scale terms d*sc, dmin*m of both.
-__device__ __forceinline__ void q4k_pair_dot(const uint8_t *sb, int g, const uint32_t *xa, const uint32_t *xb,
-                                             int &s0, int &s1, float &dsc0, float &dmm0, float &dsc1, float &dmm1) {
+// Activation words by value: a0, a1 = sub-block 2g (32 int8), b0, b1 =
+// sub-block 2g+1.
+__device__ __forceinline__ void q4k_pair_dot_x(const uint8_t *sb, int g, const uint4 a0, const uint4 a1,
+                                               const uint4 b0, const uint4 b1, int &s0, int &s1, float &dsc0,
+                                               float &dmm0, float &dsc1, float &dmm1) {
     const uint4 h = *reinterpret_cast<const uint4 *>(sb);
     const uint4 q0 = *reinterpret_cast<const uint4 *>(sb + 16 + 32 * g);
     const uint4 q1 = *reinterpret_cast<const uint4 *>(sb + 32 + 32 * g);
-    const uint4 a0 = *reinterpret_cast<const uint4 *>(xa);
-    const uint4 a1 = *reinterpret_cast<const uint4 *>(xa + 4);
-    const uint4 b0 = *reinterpret_cast<const uint4 *>(xb);
-    const uint4 b1 = *reinterpret_cast<const uint4 *>(xb + 4);
     const uint32_t lo = 0x0f0f0f0fu, hi = 0xf0f0f0f0u;
     int l0 = 0, l1 = 0, u0 = 0, u1 = 0;  // independent chains for ILP
     l0 = dp4a_ss(q0.x & lo, a0.x, l0);
@@ -230,6 +229,14 @@ __device__ __forceinline__ void q4k_pair_dot(const uint8_t *sb, int g, const uin
     dmm0 = dmin * (float)m0;
     dsc1 = d * (float)sc1;
     dmm1 = dmin * (float)m1;
+}
+
+// The same with the activation words read from `xa` / `xb` (16-byte aligned).
+__device__ __forceinline__ void q4k_pair_dot(const uint8_t *sb, int g, const uint32_t *xa, const uint32_t *xb,
+                                             int &s0, int &s1, float &dsc0, float &dmm0, float &dsc1, float &dmm1) {
+    q4k_pair_dot_x(sb, g, *reinterpret_cast<const uint4 *>(xa), *reinterpret_cast<const uint4 *>(xa + 4),
+                   *reinterpret_cast<const uint4 *>(xb), *reinterpret_cast<const uint4 *>(xb + 4), s0, s1, dsc0,
+                   dmm0, dsc1, dmm1);
 }
 
 }  // namespace fbk

@@ -47,6 +47,7 @@
 #include "../host_common.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "tmap.h"
 
 namespace fbk {
 
@@ -127,14 +128,6 @@ __device__ __forceinline__ void peer_cta_done(const PeerOut &pe) {
 }
 
 // ---- TMA / tcgen05 primitives (inline PTX) -----------------------------------
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-        : "memory");
-}
-
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
                                             uint32_t bar) {
     asm volatile(
@@ -830,7 +823,7 @@ int encode_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint6
                uint64_t dim2, uint64_t stride1, uint64_t stride2, uint32_t box0, uint32_t box1,
                CUtensorMapSwizzle swz) {
     auto fn = encode_fn();
-    if (!fn) return fb::set_error(FB_ERR_CUDA, "gemm_tc: cuTensorMapEncodeTiled unavailable");
+    if (!fn) return fb::set_error(FB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const cuuint32_t rank = dim2 ? 3 : 2;
     const cuuint64_t dims[3] = {dim0, dim1, dim2 ? dim2 : 1};
     const cuuint64_t strides[2] = {stride1, stride2};
@@ -838,7 +831,7 @@ int encode_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint6
     const cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(map, dt, rank, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fb::set_error(FB_ERR_CUDA, "gemm_tc: tensor map encode failed (%d)", (int)r);
+    if (r != CUDA_SUCCESS) return fb::set_error(FB_ERR_CUDA, "tensor map encode failed (%d)", (int)r);
     return FB_OK;
 }
 
@@ -915,6 +908,11 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
 uint64_t pad256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 
 }  // namespace
+
+int encode_tensor_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t dim0, uint64_t dim1,
+                         uint64_t stride1, uint32_t box0, uint32_t box1) {
+    return encode_map(map, dt, base, dim0, dim1, 0, stride1, 0, box0, box1, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
 
 bool gemm_tc_supported(int32_t wtype, int64_t K, int64_t M, int64_t N, const void *w, uint64_t w_nb1) {
     if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K) return false;

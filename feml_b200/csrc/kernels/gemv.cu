@@ -33,6 +33,7 @@
 #include "common.cuh"
 #include "dot.cuh"
 #include "kernels.h"
+#include "tmap.h"
 
 namespace fbk {
 
@@ -558,6 +559,202 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
     }
 }
 
+// ---- K-split decode GEMV for wide Q4_K rows, one column ---------------------
+// Every warp of a CTA takes one eighth of K (a run of whole super-blocks) for
+// all the CTA's rows, so a lane's activation words (one or two sub-block
+// pairs of the warp's slice) are the same for the whole launch: the lane
+// quantizes them itself, straight into registers, right after the dependency
+// wait (no shared-memory activations and no CTA barrier before the rows).
+// Boxes of kKsRows rows x the warp's slice come by 2D TMA into a per-warp
+// ring; the eight slices' partial sums of a row meet in shared memory and are
+// added in warp order.
+constexpr int kKsRows = 4;    // rows per TMA box
+constexpr int kKsStages = 3;  // ring stages per warp
+
+struct KsParams {
+    const float *x;
+    uint8_t *y;
+    int M;
+    int nsb;             // super-blocks per row
+    uint32_t box_bytes;  // bytes of one row of a box (the widest warp slice)
+    uint32_t ring_off;   // shared-memory offset of the rings
+    int32_t *status;
+    bool x_vec16;
+    PeerOut peer;        // peer.n > 0: outputs go to every peer's buffer, then a signal
+};
+
+// One 32-element activation block quantized by a single lane: the operations
+// of quantize_block_quarter (d = amax/127 rounded to f16 for the scale,
+// q = roundf(x * (1/d))), giving the packed int8 words, the scale and the
+// integer sum.
+__device__ __forceinline__ void quantize_block_lane(const float *xb, bool vec, uint4 &w0, uint4 &w1, float &dq,
+                                                    int &sum) {
+    float v[QK];
+    if (vec) {
+#pragma unroll
+        for (int i = 0; i < QK / 4; i++) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(xb) + i);
+            v[4 * i] = a.x, v[4 * i + 1] = a.y, v[4 * i + 2] = a.z, v[4 * i + 3] = a.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < QK; i++) v[i] = __ldg(xb + i);
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < QK; i++) amax = fmaxf(amax, fabsf(v[i]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    uint32_t w[8];
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int q0 = (int)roundf(__fmul_rn(v[4 * k], id));
+        const int q1 = (int)roundf(__fmul_rn(v[4 * k + 1], id));
+        const int q2 = (int)roundf(__fmul_rn(v[4 * k + 2], id));
+        const int q3 = (int)roundf(__fmul_rn(v[4 * k + 3], id));
+        s += q0 + q1 + q2 + q3;
+        w[k] = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+               ((uint32_t)(q3 & 0xff) << 24);
+    }
+    w0 = make_uint4(w[0], w[1], w[2], w[3]);
+    w1 = make_uint4(w[4], w[5], w[6], w[7]);
+    dq = f16_bits_to_f32(__half_as_ushort(__float2half_rn(d)));
+    sum = s;
+}
+
+// XP: sub-block pairs per lane (the widest warp slice has at most 32 * XP).
+template <int XP>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_ks_kernel(const __grid_constant__ CUtensorMap tm,
+                                                                  const KsParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r_begin = (int)((int64_t)blockIdx.x * p.M / gridDim.x);
+    const int r_end = (int)((int64_t)(blockIdx.x + 1) * p.M / gridDim.x);
+    const int rows = r_end - r_begin;
+    const int n_items = (rows + kKsRows - 1) / kKsRows;
+    const int sb0 = warp * p.nsb / kGemvWarps, sb1 = (warp + 1) * p.nsb / kGemvWarps;
+    const int npairs = 4 * (sb1 - sb0);  // sub-block pairs of this warp's slice
+    const uint32_t box_total = kKsRows * p.box_bytes;                  // bytes one box writes
+    const uint32_t stage_bytes = (box_total + 127u) & ~127u;           // stages start 128-byte aligned
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kKsStages;
+    float *part = reinterpret_cast<float *>(smem + 256);  // [rows][warp]
+    uint8_t *ring = smem + p.ring_off + (uint32_t)warp * kKsStages * stage_bytes;
+
+    auto issue = [&](int i) {  // lane 0 only
+        uint64_t *bar = &bars[i % kKsStages];
+        mbar_arrive_expect_tx(bar, box_total);
+        tma_load_2d(smem_u32(ring + (uint32_t)(i % kKsStages) * stage_bytes), &tm, sb0 * (Q4_K_BYTES / 8),
+                    r_begin + i * kKsRows, smem_u32(bar));
+    };
+    if (lane == 0) {
+        for (int st = 0; st < kKsStages; st++) mbar_init(&bars[st], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    // weight boxes before the dependency wait (weights are never written by
+    // the kernels this one waits for)
+    int issued = 0;
+    if (lane == 0)
+        for (; issued < min(kKsStages, n_items); issued++) issue(issued);
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+
+    grid_launch_dependents();
+    grid_dependency_wait();
+
+    uint4 xa0[XP], xa1[XP], xb0[XP], xb1[XP];
+    float dxa[XP], dxb[XP];
+    int sxa[XP], sxb[XP];
+#pragma unroll
+    for (int j = 0; j < XP; j++) {
+        const int q = lane + 32 * j;
+        if (q < npairs) {
+            const float *xp = p.x + (size_t)(sb0 + q / 4) * QKK + (q % 4) * 2 * QK;
+            quantize_block_lane(xp, p.x_vec16, xa0[j], xa1[j], dxa[j], sxa[j]);
+            quantize_block_lane(xp + QK, p.x_vec16, xb0[j], xb1[j], dxb[j], sxb[j]);
+        } else {
+            xa0[j] = xa1[j] = xb0[j] = xb1[j] = make_uint4(0u, 0u, 0u, 0u);
+            dxa[j] = dxb[j] = 0.0f;
+            sxa[j] = sxb[j] = 0;
+        }
+    }
+
+    for (int i = 0; i < n_items; i++) {
+        const int stage = i % kKsStages;
+        const bool ok = mbar_wait_bounded(&bars[stage], (uint32_t)(i / kKsStages) & 1u);
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) {
+                report_status(p.status, STATUS_TIMEOUT);
+                for (int j = i; j < issued; j++)
+                    mbar_wait_bounded(&bars[j % kKsStages], (uint32_t)(j / kKsStages) & 1u);
+            }
+            break;
+        }
+        const uint8_t *st = ring + (uint32_t)stage * stage_bytes;
+        float a[kKsRows];
+#pragma unroll
+        for (int r = 0; r < kKsRows; r++) {
+            a[r] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < XP; j++) {
+                const int q = lane + 32 * j;
+                if (q < npairs) {
+                    int s0, s1;
+                    float dsc0, dmm0, dsc1, dmm1;
+                    q4k_pair_dot_x(st + r * p.box_bytes + (q / 4) * Q4_K_BYTES, q % 4, xa0[j], xa1[j], xb0[j],
+                                   xb1[j], s0, s1, dsc0, dmm0, dsc1, dmm1);
+                    a[r] += dxa[j] * (dsc0 * (float)s0 - dmm0 * (float)sxa[j]) +
+                            dxb[j] * (dsc1 * (float)s1 - dmm1 * (float)sxb[j]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && issued < n_items) {
+            fence_proxy_async_smem();
+            issue(issued);
+        }
+        issued = min(issued + 1, n_items);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int r = 0; r < kKsRows; r++) a[r] += __shfl_xor_sync(0xffffffffu, a[r], o);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < kKsRows; r++) {
+                const int row = i * kKsRows + r;
+                if (row < rows) part[row * kGemvWarps + warp] = a[r];
+            }
+        }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < rows; t += kGemvThreads) {
+        float v = part[t * kGemvWarps];
+#pragma unroll
+        for (int w = 1; w < kGemvWarps; w++) v += part[t * kGemvWarps + w];
+        if (p.peer.n == 0) {
+            reinterpret_cast<float *>(p.y)[r_begin + t] = v;
+        } else {
+            const int b = (int)((*p.peer.epoch + 1u) & 1u);
+            for (int r = 0; r < p.peer.n; r++)  // NVLink stores into each rank's output
+                reinterpret_cast<float *>(p.peer.y[b][r])[r_begin + t] = v;
+        }
+    }
+    if (p.peer.n > 0) {
+        // every thread publishes its stores (system scope), then the CTA
+        // counts itself done; the grid's last CTA resets the counter and
+        // raises each rank's flag by one (ranks wait for `world` raises)
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            if (atomicAdd(p.peer.count, 1u) == gridDim.x - 1) {
+                atomicExch(p.peer.count, 0u);
+                __threadfence_system();
+                for (int r = 0; r < p.peer.n; r++) atomicAdd_system(p.peer.flag[r], 1u);
+            }
+        }
+    }
+}
+
 // Waits (one thread, bounded at about a second) until every rank has
 // signalled this step: the flag reaches (epoch + 1) * n_ranks; then advances
 // the epoch. On timeout it raises STATUS_TIMEOUT and returns, leaving the
@@ -631,6 +828,61 @@ uint32_t unit_bytes_of(int32_t wtype) {
     return wtype == WT_Q8_0 ? Q8_0_BYTES : (wtype == WT_Q4_0 ? Q4_0_BYTES : Q4_K_BYTES / 8);
 }
 
+// The K-split path for one column of wide Q4_K rows; returns -1 (nothing
+// launched) when the shape does not fit it.
+int launch_gemv_ks(const void *w, uint64_t w_nb1, const void *x, void *y, int64_t K, int64_t M, int32_t *status,
+                   cudaStream_t s, bool pdl, const PeerOut *peer) {
+    const int nsb = (int)(K / QKK);
+    const int widest = (nsb + kGemvWarps - 1) / kGemvWarps;  // super-blocks in the widest slice
+    const uint32_t box_bytes = (uint32_t)widest * Q4_K_BYTES;
+    // at least six super-blocks per warp (24 of 32 lanes busy); the box's
+    // inner extent (8-byte elements) at most 256
+    // at most 32 sub-block pairs per slice (one per lane)
+    if (nsb < 6 * kGemvWarps || widest > 8 || M > INT32_MAX / 2) return -1;
+    const int grid = std::max<int>(1, (int)std::min<int64_t>(sm_count(), (M + 1) / 2));
+    const int64_t rows_max = (M + grid - 1) / grid + 1;
+    const uint32_t ring_off = (uint32_t)((256 + rows_max * kGemvWarps * 4 + 127) / 128 * 128);
+    const uint64_t stage_bytes = ((uint64_t)kKsRows * box_bytes + 127) / 128 * 128;
+    const uint64_t smem = ring_off + (uint64_t)kGemvWarps * kKsStages * stage_bytes;
+    if (smem > kCoResidentCta) return -1;
+    CUtensorMap tm;
+    int rc = encode_tensor_map_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, (uint64_t)nsb * Q4_K_BYTES / 8,
+                                  (uint64_t)M, w_nb1, box_bytes / 8, kKsRows);
+    if (rc) return rc;
+    KsParams p;
+    p.x = static_cast<const float *>(x);
+    p.y = static_cast<uint8_t *>(y);
+    p.M = (int)M;
+    p.nsb = nsb;
+    p.box_bytes = box_bytes;
+    p.ring_off = ring_off;
+    p.status = status;
+    p.x_vec16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    p.peer = peer ? *peer : PeerOut{};
+    auto kern = gemv_ks_kernel<1>;
+    static bool smem_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCoResidentCta);
+        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
+        if (dev >= 0 && dev < 64) smem_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tm, p);
+    if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemv launch: %s", cudaGetErrorString(e));
+    return FB_OK;
+}
+
 }  // namespace
 
 bool gemv_supported(int32_t wtype, int64_t K, int64_t N) {
@@ -687,6 +939,12 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
         return fb::set_error(FB_ERR_INVALID, "gemv: output must be 4-byte aligned");
     if (M > INT32_MAX) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: M too large");
 
+    const bool rows16 = ((reinterpret_cast<uintptr_t>(w) | w_nb1) & 15) == 0;
+    if (wtype == WT_Q4_K && N == 1 && !xq && rows16) {
+        const int rc = launch_gemv_ks(w, w_nb1, x, y, K, M, status, s, pdl, peer);
+        if (rc >= 0) return rc;  // launched, or an error; -1: not this path
+    }
+
     const int nunits = (int)(K / QK);
     const uint32_t ub = unit_bytes_of(wtype);
     const bool sh = shifted_of(wtype);
@@ -730,7 +988,6 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     p.peer = peer ? *peer : PeerOut{};
     p.copy_rows = ((reinterpret_cast<uintptr_t>(w) | w_nb1) % align) != 0;
     // whole rows per chunk and at most two pairs per lane: activations in registers
-    const bool rows16 = ((reinterpret_cast<uintptr_t>(w) | w_nb1) & 15) == 0;
     const int xr = (N == 1 && nchunks == 1 && rows16) ? (nunits <= 64 ? 1 : (nunits <= 128 ? 2 : 0)) : 0;
     switch (wtype) {
     case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, xr, p, grid, L.total, s, pdl);

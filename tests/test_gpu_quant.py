@@ -94,6 +94,43 @@ def test_mul_mat_quant_matches_oracle(b200, dt, K, M, N):
     assert ok, f"max abs err {err}"
 
 
+@pytest.mark.parametrize("K,M", [(12288, 1000), (13056, 300), (14336, 5), (14336, 1), (16384, 37), (14336, 3584)])
+def test_q4_k_wide_rows_one_column(b200, K, M):
+    """Wide Q4_K rows at one column: the K-split GEMV (each warp one slice of
+    K for all its CTA's rows, activations quantized per lane into registers,
+    slices added in warp order). Ragged slices (13056 = 51 super-blocks),
+    tiny M, repeated calls bit-identical."""
+    rng = np.random.default_rng(K + 5 * M)
+    w = weights(rng, M, K)
+    x = _inputs(K + 1, 1, K)
+    wq = O.quantize(O.DT_Q4_K, w)
+    got = run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
+    ok, err = tol_ok(got, O.mul_mat_quant_ref(O.DT_Q4_K, wq, x, K))
+    assert ok, f"max abs err {err}"
+    wt = torch.from_numpy(wq).cuda()
+    xt = torch.from_numpy(x).cuda()
+    outs = [ops.mul_mat(DType.Q4_K, wt, xt, K) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    assert np.array_equal(outs[0].cpu().numpy(), got)
+
+
+def test_q4_k_wide_rows_padded_stride(b200):
+    """Row stride larger than the row (16-byte multiple): the 2D tensor map
+    walks rows by the stride, not the row size."""
+    K, M = 14336, 700
+    rng = np.random.default_rng(99)
+    wq = O.quantize(O.DT_Q4_K, weights(rng, M, K))
+    rb = wq.shape[1]
+    buf = torch.full((M, rb + 48), 0xAB, dtype=torch.uint8, device="cuda")
+    buf[:, :rb] = torch.from_numpy(wq).cuda()
+    x = _inputs(3, 1, K)
+    got = ops.mul_mat(DType.Q4_K, buf[:, :rb], torch.from_numpy(x).cuda(), K)
+    torch.cuda.synchronize()
+    ok, err = tol_ok(got.cpu().numpy(), O.mul_mat_quant_ref(O.DT_Q4_K, wq, x, K))
+    assert ok, err
+
+
 @pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0])
 @pytest.mark.parametrize("K,M,N", [(96, 40, 1), (160, 9, 6), (32, 3, 2), (288, 70, 12)])
 def test_mul_mat_ragged_k(b200, dt, K, M, N):
