@@ -41,6 +41,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
+GEMV_MAX_COLS = 8  # widest activation the decode GEMV takes (gemv.cu kMaxCols)
 
 CONFIGS = {
     "c1": dict(wtype="F32", K=4096, M=4096, N=32, seed=0, dist="uniform", metric="weight-GB/s",
@@ -249,8 +250,8 @@ def kernels_per_step(cfg, N):
     from feml_b200 import ops
     if ops.mul_mat_workspace(dt, cfg["K"], cfg["M"], N) == 0:
         return 1  # fused GEMV
-    tc = dt in (DType.Q8_0, DType.Q4_0) and cfg["K"] % 256 == 0 and N > 4
-    split = (not tc and N > 4 and cfg["K"] % 256 == 0 and
+    tc = dt in (DType.Q8_0, DType.Q4_0) and cfg["K"] % 256 == 0 and N > GEMV_MAX_COLS
+    split = (not tc and N > GEMV_MAX_COLS and cfg["K"] % 256 == 0 and
              ops.mul_mat_workspace(dt, cfg["K"], cfg["M"], N) > _planar_bytes(cfg["K"], N))
     return 3 if split else 2  # activation quantizer + GEMM (+ split-K reduction)
 
@@ -269,7 +270,7 @@ def dominant_kernel(cfg, N):
         return "gemm_tc_kernel (grouped, tcgen05)" if tc else "gemm_q_kernel (grouped)"
     if dt == DType.F32:
         return "gemm_f32_exact_kernel"
-    if N <= 4:
+    if N <= GEMV_MAX_COLS:
         return "gemv_kernel"
     return "gemm_tc_kernel (tcgen05)" if tc else "gemm_q_kernel"
 

@@ -86,7 +86,7 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
     if (!is_weight_dtype(wtype)) return set_error(FB_ERR_UNSUPPORTED, "mul_mat: weight dtype %d not supported", wtype);
     const fb::DTypeTraits *t = fb::dtype_traits(wtype);
     if (K % t->block_size) return set_error(FB_ERR_SHAPE, "mul_mat: K %ld not a multiple of %ld", (long)K, (long)t->block_size);
-    if (wtype == FB_F32) return fbk::launch_gemm_f32(w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, s);
+    if (wtype == FB_F32) return fbk::launch_gemm_f32(w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, status, s);
     if (K == 0) return set_error(FB_ERR_SHAPE, "mul_mat: K == 0");
 
     const uint64_t need = mul_mat_ws(wtype, K, M, N);
@@ -111,10 +111,11 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
         return fbk::launch_gemm_q(wtype, w, w_nb1, xq, K, M, N, y, y_nb1, nullptr, s,
                                   static_cast<uint8_t *>(ws) + fbk::q8_planar_bytes(K, N));
     // Shapes the GEMM cannot tile (K % 256 != 0, unaligned rows): the GEMV on
-    // groups of up to 4 columns of the already-quantized activations.
-    const int64_t nblk = K / 32;
-    for (int64_t n0 = 0; n0 < N; n0 += 4) {
-        const int64_t nc = std::min<int64_t>(4, N - n0);
+    // groups of up to gemv_max_cols() columns of the already-quantized
+    // activations.
+    const int64_t nblk = K / 32, ncol = fbk::gemv_max_cols();
+    for (int64_t n0 = 0; n0 < N; n0 += ncol) {
+        const int64_t nc = std::min<int64_t>(ncol, N - n0);
         fbk::Q8Planar sub{xq.qs + n0 * K, xq.d + n0 * nblk, xq.sum + n0 * nblk};
         rc = fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, static_cast<uint8_t *>(y) + n0 * y_nb1, y_nb1, K, M, nc,
                               &sub, status, s, false);
@@ -746,7 +747,7 @@ int feml_b200_mul_mat_peer(int32_t wtype, const void *w, uint64_t w_nb1, const v
         return set_error(FB_ERR_UNSUPPORTED, "mul_mat_peer: quantized weights only");
     if (K % fb::dtype_traits(wtype)->block_size) return set_error(FB_ERR_SHAPE, "mul_mat_peer: K not a block multiple");
     if (!fbk::gemv_supported(wtype, K, N) || !fbk::gemv_fused_ok(K, N))
-        return set_error(FB_ERR_UNSUPPORTED, "mul_mat_peer: needs the fused decode GEMV (N <= 4, N*K <= 16384)");
+        return set_error(FB_ERR_UNSUPPORTED, "mul_mat_peer: needs the fused decode GEMV (N <= 8, N*K <= 16384)");
     fbk::PeerOut po{};
     po.n = n_peers;
     po.count = counter;

@@ -172,17 +172,18 @@ __device__ __forceinline__ int single_even_dot(const uint32_t *wp, const uint32_
     return s;
 }
 
-// Q4_K sub-block pair g (0..3) of the super-block at `sb` (16-byte aligned):
-// integer sums s0 (sub-block 2g, low nibbles), s1 (sub-block 2g+1, high
-// nibbles) and the scale terms d*sc, dmin*m of both.
-// Activation words by value: a0, a1 = sub-block 2g (32 int8), b0, b1 =
-// sub-block 2g+1.
-__device__ __forceinline__ void q4k_pair_dot_x(const uint8_t *sb, int g, const uint4 a0, const uint4 a1,
-                                               const uint4 b0, const uint4 b1, int &s0, int &s1, float &dsc0,
-                                               float &dmm0, float &dsc1, float &dmm1) {
-    const uint4 h = *reinterpret_cast<const uint4 *>(sb);
-    const uint4 q0 = *reinterpret_cast<const uint4 *>(sb + 16 + 32 * g);
-    const uint4 q1 = *reinterpret_cast<const uint4 *>(sb + 32 + 32 * g);
+// One Q4_K sub-block pair g (0..3) of a super-block, weight side: the 32
+// nibble bytes the two sub-blocks share and their scale terms d*sc, dmin*m.
+struct Q4kPair {
+    uint4 q0, q1;
+    float dsc0, dmm0, dsc1, dmm1;
+};
+
+// Integer sums of a pair against activation words a0, a1 (sub-block 2g, 32
+// int8) and b0, b1 (sub-block 2g+1): s0 from the low nibbles, s1 from the
+// high ones.
+__device__ __forceinline__ void q4k_pair_sums(const uint4 q0, const uint4 q1, const uint4 a0, const uint4 a1,
+                                              const uint4 b0, const uint4 b1, int &s0, int &s1) {
     const uint32_t lo = 0x0f0f0f0fu, hi = 0xf0f0f0f0u;
     int l0 = 0, l1 = 0, u0 = 0, u1 = 0;  // independent chains for ILP
     l0 = dp4a_ss(q0.x & lo, a0.x, l0);
@@ -204,6 +205,12 @@ __device__ __forceinline__ void q4k_pair_dot_x(const uint8_t *sb, int g, const u
     const int l = l0 + l1, u = u0 + u1;
     s0 = l;
     s1 = u >> 4;
+}
+
+// Scale terms of sub-blocks 2g, 2g+1 from the super-block's first 16 bytes
+// `h` (f16 d, f16 dmin, 12 bytes of packed 6-bit scales and mins).
+__device__ __forceinline__ void q4k_pair_scales(const uint4 h, int g, float &dsc0, float &dmm0, float &dsc1,
+                                                float &dmm1) {
     // 6-bit (scale, min) pairs j0 = 2g, j1 = 2g+1 (public ggml get_scale_min_k4
     // layout) from scale bytes 0..11 = words h.y, h.z, h.w
     auto byte = [&](int j) -> int {
@@ -229,6 +236,32 @@ __device__ __forceinline__ void q4k_pair_dot_x(const uint8_t *sb, int g, const u
     dmm0 = dmin * (float)m0;
     dsc1 = d * (float)sc1;
     dmm1 = dmin * (float)m1;
+}
+
+// The weight side of pair g of the super-block at `sb` (16-byte aligned).
+__device__ __forceinline__ Q4kPair q4k_pair_load(const uint8_t *sb, int g) {
+    Q4kPair w;
+    const uint4 h = *reinterpret_cast<const uint4 *>(sb);
+    w.q0 = *reinterpret_cast<const uint4 *>(sb + 16 + 32 * g);
+    w.q1 = *reinterpret_cast<const uint4 *>(sb + 32 + 32 * g);
+    q4k_pair_scales(h, g, w.dsc0, w.dmm0, w.dsc1, w.dmm1);
+    return w;
+}
+
+// Q4_K sub-block pair g (0..3) of the super-block at `sb` (16-byte aligned):
+// integer sums s0 (sub-block 2g, low nibbles), s1 (sub-block 2g+1, high
+// nibbles) and the scale terms d*sc, dmin*m of both.
+// Activation words by value: a0, a1 = sub-block 2g (32 int8), b0, b1 =
+// sub-block 2g+1.
+__device__ __forceinline__ void q4k_pair_dot_x(const uint8_t *sb, int g, const uint4 a0, const uint4 a1,
+                                               const uint4 b0, const uint4 b1, int &s0, int &s1, float &dsc0,
+                                               float &dmm0, float &dsc1, float &dmm1) {
+    const Q4kPair w = q4k_pair_load(sb, g);
+    q4k_pair_sums(w.q0, w.q1, a0, a1, b0, b1, s0, s1);
+    dsc0 = w.dsc0;
+    dmm0 = w.dmm0;
+    dsc1 = w.dsc1;
+    dmm1 = w.dmm1;
 }
 
 // The same with the activation words read from `xa` / `xb` (16-byte aligned).

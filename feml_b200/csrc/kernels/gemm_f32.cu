@@ -6,13 +6,29 @@
 // rounded separately (__fmul_rn / __fadd_rn: no contraction, no reordering),
 // so results equal the reference CPU backend exactly.
 //
-// Tiling: a CTA owns a 32x32 output tile; each of its 128 threads owns a
-// 4 (rows) x 2 (columns) micro-tile, i.e. 8 independent chains (the ILP that
-// hides the add latency). K is walked in 32-wide slabs staged through a
-// two-stage cp.async ring; the weight slab is stored k-major so a thread
-// reads its 4 rows with one 16-byte load. Optional column grouping
-// (mul_mat_id with F32 experts) reuses the routing tables.
+// Two kernels share that arithmetic:
+//  - gemm_f32_pipe_kernel (16-byte aligned operands, K % 4 == 0, ungrouped):
+//    a CTA owns 8*W rows x 32 columns (W <= 4 compute warps, one per SM
+//    sub-partition). A producer warp streams 128-wide k chunks of the CTA's
+//    weight rows and activation columns into a 4-stage shared-memory ring
+//    with bulk async copies (cp.async.bulk, one per row or column chunk,
+//    completing on the stage's mbarrier), about 100 KB per SM in flight. A
+//    compute warp owns 8 rows x 32 columns; each lane a 4-row x 2-column
+//    micro-tile (8 chains), reading 4 k values of each of its rows and
+//    columns with 16-byte loads issued one step ahead of the arithmetic:
+//    6 shared loads per 32 multiply-adds, staged rows and columns padded to
+//    528 bytes and columns interleaved (even, odd) so the loads are
+//    conflict-free. The sequential chains leave the kernel bound by FP32
+//    issue (two instructions per multiply-add), not by HBM.
+//  - gemm_f32_exact_kernel (everything else, and mul_mat_id with F32
+//    experts): a CTA owns a 32x32 output tile; each of its 128 threads owns a
+//    4 (rows) x 2 (columns) micro-tile, i.e. 8 independent chains. K is walked
+//    in 32-wide slabs staged through a two-stage cp.async ring; the weight
+//    slab is stored k-major so a thread reads its 4 rows with one 16-byte
+//    load. Optional column grouping (mul_mat_id) reuses the routing tables.
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "../host_common.h"
 #include "common.cuh"
@@ -159,6 +175,212 @@ __global__ void __launch_bounds__(THREADS) gemm_f32_exact_kernel(const F32Params
     }
 }
 
+// ---- pipelined path ---------------------------------------------------------
+// A warp owns 8 rows x 32 columns: lane l takes columns 2*(l%16) and
+// 2*(l%16)+1 and rows 4*(l/16) .. 4*(l/16)+3 of the warp's rows (8 chains).
+constexpr int kWarpRows = 8;
+constexpr int kMaxWarps = 4;          // compute warps per CTA
+constexpr int kChunk = 128;           // k values per stage
+constexpr int kStride = kChunk + 4;   // floats per staged row / column (528 B: 16 mod 128)
+constexpr int kPipeStages = 4;
+constexpr int kPipeCols = 32;         // columns per CTA
+constexpr uint32_t kPipeBarBytes = 128;
+
+struct F32PipeParams {
+    const uint8_t *w;
+    uint64_t w_nb1;
+    const uint8_t *x;
+    uint64_t x_nb1;
+    uint8_t *y;
+    uint64_t y_nb1;
+    int K, M, N;
+    int warps;  // compute warps; the CTA owns kWarpRows * warps rows
+    int32_t *status;
+    bool y_vec16;
+};
+
+__host__ __device__ inline uint32_t pipe_stage_bytes(int warps) {
+    return (uint32_t)((kWarpRows * warps + kPipeCols) * kStride) * 4u;
+}
+
+// Staged column slot: even columns in slots 0..15, odd ones in 16..31, so
+// the 16 distinct column addresses of one 16-byte load fall in distinct banks.
+__host__ __device__ inline int col_slot(int c) { return (c >> 1) + 16 * (c & 1); }
+
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) gemm_f32_pipe_kernel(const F32PipeParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kPipeStages;
+    uint8_t *stages = smem + kPipeBarBytes;
+    const uint32_t stage_bytes = pipe_stage_bytes(p.warps);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bm = kWarpRows * p.warps;
+    const int m0 = blockIdx.x * bm, n0 = blockIdx.y * kPipeCols;
+    const int rows = min(bm, p.M - m0), cols = min(kPipeCols, p.N - n0);
+    const int nchunks = (p.K + kChunk - 1) / kChunk;
+    const uint32_t wbytes = (uint32_t)bm * kStride * 4u;  // weight part of a stage
+
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kPipeStages; st++) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], (uint32_t)p.warps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == p.warps) {
+        // Producer: chunk c goes to stage c % 4 once the compute warps have
+        // released that stage's previous chunk.
+        int c = 0;
+        bool ok = true;
+        for (; c < nchunks; c++) {
+            const int st = c % kPipeStages;
+            if (c >= kPipeStages) {
+                bool free_ok = true;
+                if (lane == 0) free_ok = mbar_wait_bounded(&empty[st], (uint32_t)(c / kPipeStages - 1) & 1u);
+                if (!__shfl_sync(0xffffffffu, free_ok, 0)) {
+                    ok = false;
+                    break;
+                }
+            }
+            const int k0 = c * kChunk;
+            const uint32_t bytes = (uint32_t)min(kChunk, p.K - k0) * 4u;
+            uint8_t *sw = stages + (uint32_t)st * stage_bytes;
+            uint8_t *sx = sw + wbytes;
+            if (lane == 0) {
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(&full[st], bytes * (uint32_t)(rows + cols));
+            }
+            __syncwarp();
+            for (int i = lane; i < rows; i += 32)
+                bulk_g2s(sw + (uint32_t)i * kStride * 4u, p.w + (uint64_t)(m0 + i) * p.w_nb1 + (uint64_t)k0 * 4u,
+                         bytes, &full[st]);
+            for (int j = lane; j < cols; j += 32)
+                bulk_g2s(sx + (uint32_t)col_slot(j) * kStride * 4u,
+                         p.x + (uint64_t)(n0 + j) * p.x_nb1 + (uint64_t)k0 * 4u, bytes, &full[st]);
+        }
+        if (lane == 0) {
+            if (!ok) report_status(p.status, STATUS_TIMEOUT);
+            // the CTA ends only after every copy it issued has landed (chunks
+            // before c - 4 were released by the compute warps, so they had)
+            for (int j = max(0, c - kPipeStages); j < c; j++)
+                mbar_wait_bounded(&full[j % kPipeStages], (uint32_t)(j / kPipeStages) & 1u);
+        }
+        return;
+    }
+
+    // Compute warps.
+    const int cp = lane & 15;                          // column pair: columns 2cp, 2cp+1
+    const int r0 = warp * kWarpRows + 4 * (lane >> 4);  // first of this lane's 4 rows in the CTA
+    float acc[4][2];
+#pragma unroll
+    for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = 0.0f;
+
+    bool ok = true;
+    for (int c = 0; c < nchunks; c++) {
+        const int st = c % kPipeStages;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (uint32_t)(c / kPipeStages) & 1u))) {
+            ok = false;
+            break;
+        }
+        const uint8_t *base = stages + (uint32_t)st * stage_bytes;
+        const float *sw = reinterpret_cast<const float *>(base) + r0 * kStride;
+        const float *sxa = reinterpret_cast<const float *>(base + wbytes) + cp * kStride;  // column 2cp
+        const float *sxb = sxa + 16 * kStride;                                            // column 2cp+1
+        const int kc = min(kChunk, p.K - c * kChunk);  // a multiple of 4
+        // shared loads one step ahead of the arithmetic (the last step
+        // reloads its own values instead of reading past the chunk)
+        float4 xa = *reinterpret_cast<const float4 *>(sxa);
+        float4 xb = *reinterpret_cast<const float4 *>(sxb);
+        float4 wv[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) wv[r] = *reinterpret_cast<const float4 *>(sw + r * kStride);
+#pragma unroll 2
+        for (int kk = 0; kk < kc; kk += 4) {
+            const int kn = min(kk + 4, kc - 4);
+            const float4 nxa = *reinterpret_cast<const float4 *>(sxa + kn);
+            const float4 nxb = *reinterpret_cast<const float4 *>(sxb + kn);
+            float4 nw[4];
+#pragma unroll
+            for (int r = 0; r < 4; r++) nw[r] = *reinterpret_cast<const float4 *>(sw + r * kStride + kn);
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(wv[r].x, xa.x));
+                acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(wv[r].x, xb.x));
+            }
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(wv[r].y, xa.y));
+                acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(wv[r].y, xb.y));
+            }
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(wv[r].z, xa.z));
+                acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(wv[r].z, xb.z));
+            }
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(wv[r].w, xa.w));
+                acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(wv[r].w, xb.w));
+            }
+            xa = nxa;
+            xb = nxb;
+#pragma unroll
+            for (int r = 0; r < 4; r++) wv[r] = nw[r];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    if (!ok) {
+        if (lane == 0) report_status(p.status, STATUS_TIMEOUT);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int col = 2 * cp + j;
+        if (col >= cols || r0 >= rows) continue;
+        float *yc = reinterpret_cast<float *>(p.y + (uint64_t)(n0 + col) * p.y_nb1);
+        const int m = m0 + r0;  // a multiple of 4
+        if (p.y_vec16 && r0 + 4 <= rows) {
+            *reinterpret_cast<float4 *>(yc + m) = make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
+        } else {
+#pragma unroll
+            for (int r = 0; r < 4; r++)
+                if (r0 + r < rows) yc[m + r] = acc[r][j];
+        }
+    }
+}
+
+// Compute warps per CTA: enough row tiles times column tiles to cover the
+// SMs once where the matrix allows (one warp per SM sub-partition at most).
+int pipe_warps(int64_t M, int64_t N) {
+    const int64_t col_tiles = (N + kPipeCols - 1) / kPipeCols;
+    const int64_t sms = sm_count();
+    const int64_t rows_per_cta = (M * col_tiles + sms - 1) / sms;
+    return (int)std::min<int64_t>(kMaxWarps, std::max<int64_t>(1, (rows_per_cta + kWarpRows - 1) / kWarpRows));
+}
+
+int launch_f32_pipe(const F32PipeParams &p, cudaStream_t s) {
+    static bool smem_set[64] = {};  // per device: the dynamic smem limit was raised
+    const uint32_t smem = kPipeBarBytes + kPipeStages * pipe_stage_bytes(p.warps);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaError_t e = cudaSuccess;
+    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
+        e = cudaFuncSetAttribute(gemm_f32_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(kPipeBarBytes + kPipeStages * pipe_stage_bytes(kMaxWarps)));
+        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_f32: smem attribute: %s", cudaGetErrorString(e));
+        if (dev >= 0 && dev < 64) smem_set[dev] = true;
+    }
+    const int bm = kWarpRows * p.warps;
+    dim3 grid((unsigned)((p.M + bm - 1) / bm), (unsigned)((p.N + kPipeCols - 1) / kPipeCols));
+    gemm_f32_pipe_kernel<<<grid, (p.warps + 1) * 32, smem, s>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_f32 launch: %s", cudaGetErrorString(e));
+    return FB_OK;
+}
+
 int launch_f32(const F32Params &p, int tiles_n, cudaStream_t s) {
     if (p.M == 0 || tiles_n == 0) return FB_OK;
     if (tiles_n > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "mul_mat f32: too many column tiles");
@@ -172,13 +394,31 @@ int launch_f32(const F32Params &p, int tiles_n, cudaStream_t s) {
 }  // namespace
 
 int launch_gemm_f32(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1, int64_t K,
-                    int64_t M, int64_t N, cudaStream_t s) {
+                    int64_t M, int64_t N, int32_t *status, cudaStream_t s) {
     if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | w_nb1 |
          x_nb1 | y_nb1) & 3)
         return fb::set_error(FB_ERR_INVALID, "mul_mat f32: operands must be 4-byte aligned");
     if (K > INT32_MAX || M > INT32_MAX || N > INT32_MAX)
         return fb::set_error(FB_ERR_UNSUPPORTED, "mul_mat f32: dimension too large");
     if (N == 0 || M == 0) return FB_OK;
+    const bool aligned16 =
+        ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | w_nb1 | x_nb1) & 15) == 0;
+    if (aligned16 && K > 0 && K % 4 == 0 && (N + kPipeCols - 1) / kPipeCols <= 65535) {
+        F32PipeParams q{};
+        q.w = static_cast<const uint8_t *>(w);
+        q.w_nb1 = w_nb1;
+        q.x = static_cast<const uint8_t *>(x);
+        q.x_nb1 = x_nb1;
+        q.y = static_cast<uint8_t *>(y);
+        q.y_nb1 = y_nb1;
+        q.K = (int)K;
+        q.M = (int)M;
+        q.N = (int)N;
+        q.warps = pipe_warps(M, N);
+        q.status = status;
+        q.y_vec16 = ((reinterpret_cast<uintptr_t>(y) | y_nb1) & 15) == 0;
+        return launch_f32_pipe(q, s);
+    }
     F32Params p{};
     p.w = static_cast<const uint8_t *>(w);
     p.w_nb1 = w_nb1;

@@ -1,4 +1,4 @@
-// Decode-path mul_mat for quantized weights and small N (1..4 columns):
+// Decode-path mul_mat for quantized weights and small N (1..8 columns):
 //   y[m, n] = sum_b scale(m, b, n) * sumi(m, b, n)
 // with sumi the int32 dot product of one 32-element weight block and the
 // matching Q8_0 activation block (dp4a), scale = d_w * d_x (Q8_0, Q4_0) or
@@ -41,7 +41,7 @@ namespace {
 
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kMaxCols = 4;
+constexpr int kMaxCols = 8;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int kFusedMaxElems = 16384;            // N*K up to which each CTA quantizes x itself
 // per-CTA smem that leaves room for the next launch's CTA (2 x (112 + 1
@@ -755,6 +755,135 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_ks_kernel(const __grid_c
     }
 }
 
+// ---- K-split decode GEMV for wide Q4_K rows, 2..8 columns -------------------
+// The same slices and 2D boxes as gemv_ks_kernel; the activations were
+// quantized by a preceding kernel into planar form (read after the
+// programmatic-dependent-launch wait, through L1). A lane holds the weight
+// words and scale terms of its sub-block pair for all rows of a box in
+// registers and walks the columns, loading each column's activation words
+// once per box. The box's kKsRows x NC partial sums (padded to 32) are
+// reduced across the warp with a transposing butterfly (31 shuffles, lane l
+// ends with value l) and meet the other slices in shared memory, added in
+// warp order.
+struct KsColsParams {
+    Q8Planar xq;
+    uint8_t *y;
+    uint64_t y_nb1;
+    int K;
+    int M;
+    int nsb;
+    uint32_t box_bytes;
+    uint32_t ring_off;
+    int32_t *status;
+};
+
+template <int NC>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_ks_cols_kernel(const __grid_constant__ CUtensorMap tm,
+                                                                       const KsColsParams p) {
+    static_assert(kKsRows * NC <= 32, "one reduced value per lane");
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r_begin = (int)((int64_t)blockIdx.x * p.M / gridDim.x);
+    const int r_end = (int)((int64_t)(blockIdx.x + 1) * p.M / gridDim.x);
+    const int rows = r_end - r_begin;
+    const int n_items = (rows + kKsRows - 1) / kKsRows;
+    const int sb0 = warp * p.nsb / kGemvWarps, sb1 = (warp + 1) * p.nsb / kGemvWarps;
+    const int npairs = 4 * (sb1 - sb0);
+    const uint32_t box_total = kKsRows * p.box_bytes;
+    const uint32_t stage_bytes = (box_total + 127u) & ~127u;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kKsStages;
+    float *part = reinterpret_cast<float *>(smem + 256);  // [rows][NC][warp]
+    uint8_t *ring = smem + p.ring_off + (uint32_t)warp * kKsStages * stage_bytes;
+
+    auto issue = [&](int i) {  // lane 0 only
+        uint64_t *bar = &bars[i % kKsStages];
+        mbar_arrive_expect_tx(bar, box_total);
+        tma_load_2d(smem_u32(ring + (uint32_t)(i % kKsStages) * stage_bytes), &tm, sb0 * (Q4_K_BYTES / 8),
+                    r_begin + i * kKsRows, smem_u32(bar));
+    };
+    if (lane == 0) {
+        for (int st = 0; st < kKsStages; st++) mbar_init(&bars[st], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    int issued = 0;
+    if (lane == 0)
+        for (; issued < min(kKsStages, n_items); issued++) issue(issued);
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+
+    grid_launch_dependents();
+    grid_dependency_wait();
+
+    const bool active = lane < npairs;
+    const int g = lane & 3;                              // pair within the super-block
+    const int b0 = (sb0 + (lane >> 2)) * 8 + 2 * g;      // its even sub-block in the row
+    const int nblk = p.K / QK;
+    for (int i = 0; i < n_items; i++) {
+        const int stage = i % kKsStages;
+        const bool ok = mbar_wait_bounded(&bars[stage], (uint32_t)(i / kKsStages) & 1u);
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) {
+                report_status(p.status, STATUS_TIMEOUT);
+                for (int j = i; j < issued; j++)
+                    mbar_wait_bounded(&bars[j % kKsStages], (uint32_t)(j / kKsStages) & 1u);
+            }
+            break;
+        }
+        const uint8_t *st = ring + (uint32_t)stage * stage_bytes;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = 0.0f;
+        if (active) {
+            Q4kPair wr[kKsRows];
+#pragma unroll
+            for (int r = 0; r < kKsRows; r++) wr[r] = q4k_pair_load(st + r * p.box_bytes + (lane >> 2) * Q4_K_BYTES, g);
+#pragma unroll
+            for (int n = 0; n < NC; n++) {
+                const uint4 *xa = reinterpret_cast<const uint4 *>(p.xq.qs + (size_t)n * p.K + (size_t)b0 * QK);
+                const uint4 a0 = __ldg(xa), a1 = __ldg(xa + 1), c0 = __ldg(xa + 2), c1 = __ldg(xa + 3);
+                const float2 dx = __ldg(reinterpret_cast<const float2 *>(p.xq.d + (size_t)n * nblk + b0));
+                const int2 sx = __ldg(reinterpret_cast<const int2 *>(p.xq.sum + (size_t)n * nblk + b0));
+#pragma unroll
+                for (int r = 0; r < kKsRows; r++) {
+                    int s0, s1;
+                    q4k_pair_sums(wr[r].q0, wr[r].q1, a0, a1, c0, c1, s0, s1);
+                    v[r * NC + n] = dx.x * (wr[r].dsc0 * (float)s0 - wr[r].dmm0 * (float)sx.x) +
+                                    dx.y * (wr[r].dsc1 * (float)s1 - wr[r].dmm1 * (float)sx.y);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && issued < n_items) {
+            fence_proxy_async_smem();
+            issue(issued);
+        }
+        issued = min(issued + 1, n_items);
+        // transposing butterfly: after the step with offset o a lane keeps the
+        // half of its values selected by its lane bit o, plus its partner's
+        // copy of that half; lane l ends with the warp's sum of value l
+#pragma unroll
+        for (int o = 16, cnt = 16; o >= 1; o >>= 1, cnt >>= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int j = 0; j < cnt; j++) {
+                const float send = upper ? v[j] : v[j + cnt];
+                const float keep = upper ? v[j + cnt] : v[j];
+                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+        const int r = lane / NC, n = lane % NC, row = i * kKsRows + r;
+        if (r < kKsRows && row < rows) part[(row * NC + n) * kGemvWarps + warp] = v[0];
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < rows * NC; t += kGemvThreads) {
+        float sum = part[t * kGemvWarps];
+#pragma unroll
+        for (int w = 1; w < kGemvWarps; w++) sum += part[t * kGemvWarps + w];
+        const int row = t / NC, n = t % NC;
+        reinterpret_cast<float *>(p.y + (uint64_t)n * p.y_nb1)[r_begin + row] = sum;
+    }
+}
+
 // Waits (one thread, bounded at about a second) until every rank has
 // signalled this step: the flag reaches (epoch + 1) * n_ranks; then advances
 // the epoch. On timeout it raises STATUS_TIMEOUT and returns, leaving the
@@ -819,7 +948,11 @@ int launch_cols(int ncols, int xr, const GemvParams &p, int grid, uint32_t smem,
     case 1: return launch_typed<WT, 1, 0>(p, grid, smem, s, pdl);
     case 2: return launch_typed<WT, 2, 0>(p, grid, smem, s, pdl);
     case 3: return launch_typed<WT, 3, 0>(p, grid, smem, s, pdl);
-    default: return launch_typed<WT, 4, 0>(p, grid, smem, s, pdl);
+    case 4: return launch_typed<WT, 4, 0>(p, grid, smem, s, pdl);
+    case 5: return launch_typed<WT, 5, 0>(p, grid, smem, s, pdl);
+    case 6: return launch_typed<WT, 6, 0>(p, grid, smem, s, pdl);
+    case 7: return launch_typed<WT, 7, 0>(p, grid, smem, s, pdl);
+    default: return launch_typed<WT, 8, 0>(p, grid, smem, s, pdl);
     }
 }
 
@@ -883,6 +1016,76 @@ int launch_gemv_ks(const void *w, uint64_t w_nb1, const void *x, void *y, int64_
     return FB_OK;
 }
 
+// The K-split path for 2..8 columns of wide Q4_K rows over planar
+// activations; returns -1 (nothing launched) when the shape does not fit it.
+template <int NC>
+int launch_ks_cols_typed(const CUtensorMap &tm, const KsColsParams &p, int grid, uint32_t smem, cudaStream_t s,
+                         bool pdl) {
+    auto kern = gemv_ks_cols_kernel<NC>;
+    static bool smem_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
+        if (dev >= 0 && dev < 64) smem_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tm, p);
+    if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemv launch: %s", cudaGetErrorString(e));
+    return FB_OK;
+}
+
+int launch_gemv_ks_cols(const void *w, uint64_t w_nb1, const Q8Planar &xq, void *y, uint64_t y_nb1, int64_t K,
+                        int64_t M, int64_t N, int32_t *status, cudaStream_t s, bool pdl) {
+    const int nsb = (int)(K / QKK);
+    const int widest = (nsb + kGemvWarps - 1) / kGemvWarps;
+    const uint32_t box_bytes = (uint32_t)widest * Q4_K_BYTES;
+    if (N < 2 || N > kMaxCols || nsb < 6 * kGemvWarps || widest > 8 || M > INT32_MAX / 2) return -1;
+    // planar activations: 16-byte rows of int8, 8-byte aligned scale pairs
+    if (((reinterpret_cast<uintptr_t>(xq.qs) | (uint64_t)K) & 15) || ((reinterpret_cast<uintptr_t>(xq.d) |
+                                                                         reinterpret_cast<uintptr_t>(xq.sum)) & 7))
+        return -1;
+    const int grid = std::max<int>(1, (int)std::min<int64_t>(sm_count(), (M + 1) / 2));
+    const int64_t rows_max = (M + grid - 1) / grid + 1;
+    const uint32_t ring_off = (uint32_t)((256 + rows_max * N * kGemvWarps * 4 + 127) / 128 * 128);
+    const uint64_t stage_bytes = ((uint64_t)kKsRows * box_bytes + 127) / 128 * 128;
+    const uint64_t smem = ring_off + (uint64_t)kGemvWarps * kKsStages * stage_bytes;
+    if (smem > (uint64_t)kSmemLimit) return -1;
+    CUtensorMap tm;
+    int rc = encode_tensor_map_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, (uint64_t)nsb * Q4_K_BYTES / 8,
+                                  (uint64_t)M, w_nb1, box_bytes / 8, kKsRows);
+    if (rc) return rc;
+    KsColsParams p;
+    p.xq = xq;
+    p.y = static_cast<uint8_t *>(y);
+    p.y_nb1 = y_nb1;
+    p.K = (int)K;
+    p.M = (int)M;
+    p.nsb = nsb;
+    p.box_bytes = box_bytes;
+    p.ring_off = ring_off;
+    p.status = status;
+    switch (N) {
+    case 2: return launch_ks_cols_typed<2>(tm, p, grid, (uint32_t)smem, s, pdl);
+    case 3: return launch_ks_cols_typed<3>(tm, p, grid, (uint32_t)smem, s, pdl);
+    case 4: return launch_ks_cols_typed<4>(tm, p, grid, (uint32_t)smem, s, pdl);
+    case 5: return launch_ks_cols_typed<5>(tm, p, grid, (uint32_t)smem, s, pdl);
+    case 6: return launch_ks_cols_typed<6>(tm, p, grid, (uint32_t)smem, s, pdl);
+    case 7: return launch_ks_cols_typed<7>(tm, p, grid, (uint32_t)smem, s, pdl);
+    default: return launch_ks_cols_typed<8>(tm, p, grid, (uint32_t)smem, s, pdl);
+    }
+}
+
 }  // namespace
 
 bool gemv_supported(int32_t wtype, int64_t K, int64_t N) {
@@ -895,6 +1098,8 @@ bool gemv_supported(int32_t wtype, int64_t K, int64_t N) {
 }
 
 bool gemv_fused_ok(int64_t K, int64_t N) { return K * N <= kFusedMaxElems; }
+
+int gemv_max_cols() { return kMaxCols; }
 
 int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s) {
     if (!flag || !epoch || ((reinterpret_cast<uintptr_t>(flag) | reinterpret_cast<uintptr_t>(epoch)) & 3))
@@ -943,6 +1148,10 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     if (wtype == WT_Q4_K && N == 1 && !xq && rows16) {
         const int rc = launch_gemv_ks(w, w_nb1, x, y, K, M, status, s, pdl, peer);
         if (rc >= 0) return rc;  // launched, or an error; -1: not this path
+    }
+    if (wtype == WT_Q4_K && N > 1 && xq && !peer && rows16) {
+        const int rc = launch_gemv_ks_cols(w, w_nb1, *xq, y, y_nb1, K, M, N, status, s, pdl);
+        if (rc >= 0) return rc;
     }
 
     const int nunits = (int)(K / QK);

@@ -35,6 +35,7 @@ int launch_quantize_q8_planar(const void *x, uint64_t x_nb1, int64_t K, int64_t 
 // itself (fused path, no workspace).
 bool gemv_supported(int32_t wtype, int64_t K, int64_t N);
 bool gemv_fused_ok(int64_t K, int64_t N);
+int gemv_max_cols();  // largest N the GEMV takes
 // Peer outputs of a row-sharded GEMV: y[b][r] is output buffer b (0/1,
 // alternating by step) of rank r at this rank's first row (device pointers
 // valid here: own memory or an IPC mapping of a peer's), flag[r] rank r's
@@ -56,9 +57,11 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
 // the epoch (bounded; STATUS_TIMEOUT on expiry).
 int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s);
 
-// gemm_f32.cu: F32 mul_mat on SIMT FP32 (any N).
+// gemm_f32.cu: F32 mul_mat on SIMT FP32 (any N), bit-exact with the
+// reference's sequential order. `status` receives STATUS_TIMEOUT if a bounded
+// pipeline wait gives up.
 int launch_gemm_f32(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
-                    int64_t K, int64_t M, int64_t N, cudaStream_t s);
+                    int64_t K, int64_t M, int64_t N, int32_t *status, cudaStream_t s);
 
 // gemm_q.cu: quantized mul_mat for large N on Q8Planar activations. The
 // optional gather maps (MoE) select activation columns and output columns.

@@ -10,7 +10,7 @@ are new. They shard the two operators of the path the natural way:
   of y = W x straight into its all-gather send buffer, one all-gather over
   NCCL assembles [world, N, R], and a permute gives y [N, M] on every rank.
   With N == 1 the gathered buffer already is y (no permute).
-  With `fused=True` and a decode shape (N <= 4, N*K <= 16384) the all-gather
+  With `fused=True` and a decode shape (N <= 8, N*K <= 16384) the all-gather
   is fused into the kernel instead: every rank stores its rows straight into
   every rank's output buffer over NVLink (peer pointers from CUDA IPC, mapped
   once into this device's context with peer access), raises each rank's flag, and a

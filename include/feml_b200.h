@@ -315,7 +315,7 @@ int feml_b200_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t 
  * peer_flags[r] (a uint32 in rank r's memory) is raised by one. `counter` is
  * a zeroed uint32 of this rank used by the grid (left at zero) and `epoch`
  * this rank's completed-step count (advanced by feml_b200_peer_wait).
- * Quantized weights, N <= 4 and N*K <= 16384 (the fused-quantization GEMV).
+ * Quantized weights, N <= 8 and N*K <= 16384 (the fused-quantization GEMV).
  * Both calls take only device state, so a step can be captured in a CUDA
  * graph and replayed. */
 int feml_b200_mul_mat_peer(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1,

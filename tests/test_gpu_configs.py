@@ -26,8 +26,10 @@ def test_c1_f32_4096x4096_n32(b200):
     w = rng.uniform(-1, 1, (M, K)).astype(np.float32)
     x = rng.uniform(-1, 1, (N, K)).astype(np.float32)
     got = run_mul_mat(b200, DType.F32, w, x, K, M)
-    ok, err = tol_ok(got, O.mul_mat_f32(w, x))
+    want = O.mul_mat_f32(w, x)
+    ok, err = tol_ok(got, want)
     assert ok, err
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), "not bit-exact"
 
 
 def test_c2_q8_0_gemv_4096x4096(b200):

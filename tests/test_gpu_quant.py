@@ -75,8 +75,9 @@ def test_block_dots_bit_exact(b200, dt, K, M, N):
 
 SHAPES = [
     (256, 7, 1), (512, 33, 2), (1024, 130, 3), (4096, 256, 4),     # decode GEMV, fused quantization
-    (8192, 40, 4),                                                  # GEMV with a pre-quantized activation buffer
-    (512, 100, 5), (1024, 64, 8), (256, 300, 16), (2048, 200, 64),  # GEMM path
+    (512, 100, 5), (1024, 64, 8), (2048, 70, 7),                    # ... five to eight columns
+    (8192, 40, 4), (4096, 300, 6),                                  # GEMV with a pre-quantized activation buffer
+    (256, 300, 16), (2048, 200, 64),                                # GEMM path
     (768, 150, 33), (256, 1, 100), (4096, 257, 128), (512, 130, 300),
 ]
 
@@ -115,6 +116,45 @@ def test_q4_k_wide_rows_one_column(b200, K, M):
     assert np.array_equal(outs[0].cpu().numpy(), got)
 
 
+@pytest.mark.parametrize("K,M,N", [(14336, 4096, 8), (12288, 1000, 2), (13056, 300, 5), (14336, 9, 7),
+                                   (16384, 37, 3), (14336, 1, 8), (14336, 3584, 6)])
+def test_q4_k_wide_rows_few_columns(b200, K, M, N):
+    """Wide Q4_K rows at 2..8 columns: the K-split GEMV over planar
+    activations (weight words of a box held in registers, columns walked per
+    box, transposing warp reduction). Ragged slices (13056 = 51
+    super-blocks), tiny M, repeated calls bit-identical."""
+    rng = np.random.default_rng(K + 7 * M + N)
+    wq = O.quantize(O.DT_Q4_K, weights(rng, M, K))
+    x = _inputs(K + N, N, K)
+    got = run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
+    ok, err = tol_ok(got, O.mul_mat_quant_ref(O.DT_Q4_K, wq, x, K))
+    assert ok, f"max abs err {err}"
+    wt = torch.from_numpy(wq).cuda()
+    xt = torch.from_numpy(x).cuda()
+    outs = [ops.mul_mat(DType.Q4_K, wt, xt, K) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    assert np.array_equal(outs[0].cpu().numpy(), got)
+
+
+def test_q4_k_wide_rows_few_columns_padded_stride(b200):
+    """Weight rows and output columns with strides wider than their rows."""
+    K, M, N = 14336, 700, 4
+    rng = np.random.default_rng(98)
+    wq = O.quantize(O.DT_Q4_K, weights(rng, M, K))
+    rb = wq.shape[1]
+    buf = torch.full((M, rb + 48), 0xAB, dtype=torch.uint8, device="cuda")
+    buf[:, :rb] = torch.from_numpy(wq).cuda()
+    x = _inputs(4, N, K)
+    out = torch.full((N, M + 5), float("nan"), device="cuda")
+    ops.mul_mat(DType.Q4_K, buf[:, :rb], torch.from_numpy(x).cuda(), K, out=out[:, :M])
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    ok, err = tol_ok(got[:, :M], O.mul_mat_quant_ref(O.DT_Q4_K, wq, x, K))
+    assert ok, err
+    assert np.isnan(got[:, M:]).all()
+
+
 def test_q4_k_wide_rows_padded_stride(b200):
     """Row stride larger than the row (16-byte multiple): the 2D tensor map
     walks rows by the stride, not the row size."""
@@ -144,14 +184,41 @@ def test_mul_mat_ragged_k(b200, dt, K, M, N):
     assert ok, err
 
 
-@pytest.mark.parametrize("K,M,N", [(16, 8, 32), (4096, 64, 32), (100, 37, 5), (1000, 129, 1), (64, 3, 70)])
+@pytest.mark.parametrize("K,M,N", [
+    (16, 8, 32), (4096, 64, 32), (100, 37, 5), (1000, 129, 1), (64, 3, 70),  # pipelined kernel
+    (4100, 70, 33), (132, 1, 1), (256, 4001, 3),    # a 4-wide last k chunk, one row, many row tiles
+    (99, 37, 5), (6, 9, 40),                        # K % 4 != 0: the cp.async kernel
+])
 def test_mul_mat_f32_matches_oracle(b200, K, M, N):
+    """F32 mul_mat equals the reference CPU kernel's sequential f32 sums bit
+    for bit (the reference's own CUDA kernel is built with fmad=false for the
+    same reason)."""
     rng = np.random.default_rng(K + M + N)
     w = rng.uniform(-1, 1, (M, K)).astype(np.float32)
     x = rng.uniform(-1, 1, (N, K)).astype(np.float32)
     got = run_mul_mat(b200, DType.F32, w, x, K, M)
-    ok, err = tol_ok(got, O.mul_mat_f32(w, x))
+    want = O.mul_mat_f32(w, x)
+    ok, err = tol_ok(got, want)
     assert ok, err
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), "not bit-exact"
+
+
+def test_mul_mat_f32_strided_operands(b200):
+    """Row strides wider than the rows (16-byte multiples and not) on the
+    kernel-level entry point; outputs bit-exact."""
+    rng = np.random.default_rng(7)
+    K, M, N = 520, 150, 9
+    w = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    x = rng.uniform(-1, 1, (N, K)).astype(np.float32)
+    want = O.mul_mat_f32(w, x)
+    for pad in (4, 1):
+        wb = torch.zeros((M, K + pad), dtype=torch.float32, device="cuda")
+        xb = torch.zeros((N, K + pad), dtype=torch.float32, device="cuda")
+        wb[:, :K] = torch.from_numpy(w).cuda()
+        xb[:, :K] = torch.from_numpy(x).cuda()
+        got = ops.mul_mat(DType.F32, wb[:, :K], xb[:, :K], K)
+        torch.cuda.synchronize()
+        assert np.array_equal(got.cpu().numpy().view(np.uint32), want.view(np.uint32)), pad
 
 
 def test_kernel_level_entry_matches_graph_path(b200):
