@@ -269,8 +269,10 @@ def dominant_kernel(cfg, N):
     if "E" in cfg:
         return "gemm_tc_kernel (grouped, tcgen05)" if tc else "gemm_q_kernel (grouped)"
     if dt == DType.F32:
-        return "gemm_f32_exact_kernel"
+        return "gemm_f32_pipe_kernel" if cfg["K"] % 4 == 0 else "gemm_f32_exact_kernel"
     if N <= GEMV_MAX_COLS:
+        if dt == DType.Q4_K and 12288 <= cfg["K"] <= 16384:
+            return "gemv_ks_kernel" if N == 1 else "gemv_ks_cols_kernel"
         return "gemv_kernel"
     return "gemm_tc_kernel (tcgen05)" if tc else "gemm_q_kernel"
 

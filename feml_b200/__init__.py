@@ -298,6 +298,22 @@ class B200Backend(Backend):
         _check(_L.lib().feml_b200_read(self._h, int(handle), int(offset), buf, len(mv)))
         return out
 
+    def buffer_from_host_ptr(self, ptr, size, max_tensor_size):
+        """A new Weights buffer holding `size` bytes copied to HBM straight
+        from host memory at `ptr` (an int address, or any object exposing the
+        buffer protocol); returns its handle."""
+        if not isinstance(ptr, int):
+            mv = memoryview(ptr).cast("B")
+            if len(mv) < size:
+                raise FemlError("msg", f"buffer_from_host_ptr: {len(mv)} bytes given, {size} requested")
+            arr = (ctypes.c_char * len(mv)).from_buffer_copy(mv) if mv.readonly else \
+                (ctypes.c_char * len(mv)).from_buffer(mv)
+            ptr = ctypes.addressof(arr)
+        h = ctypes.c_uint32()
+        _check(_L.lib().feml_b200_buffer_from_host_ptr(self._h, ctypes.c_void_p(ptr), int(size), int(max_tensor_size),
+                                                        ctypes.byref(h)))
+        return h.value
+
     def read_ptr(self, handle, offset, host_ptr, n):
         _check(_L.lib().feml_b200_read(self._h, int(handle), int(offset), ctypes.c_void_p(host_ptr), int(n)))
 
@@ -377,8 +393,15 @@ class B200Device:
     def offload_op(self, op):
         return Op(op) in (Op.MUL_MAT, Op.MUL_MAT_ID)
 
-    def buffer_from_host_ptr(self, ptr, size, max_tensor_size):
-        raise FemlError("msg", "B200: buffer_from_host_ptr not implemented yet")
+    def buffer_from_host_ptr(self, ptr, size, max_tensor_size, backend=None):
+        """BackendDevice::buffer_from_host_ptr (feml-core/src/backend.rs:145-153).
+        Buffers here are owned by a backend (handles are backend-scoped), so
+        the backend that will own the new Weights buffer is named here; see
+        B200Backend.buffer_from_host_ptr."""
+        if backend is None:
+            raise FemlError("msg", "B200: buffer_from_host_ptr needs the backend that will own the buffer "
+                                   "(buffer handles are backend-scoped)")
+        return backend.buffer_from_host_ptr(ptr, size, max_tensor_size)
 
 
 class B200Registrar:

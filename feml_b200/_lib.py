@@ -62,6 +62,11 @@ class PlannerTensor(ctypes.Structure):
                 ("view_offset", c_u64)]
 
 
+class GgufTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 256), ("dtype", c_i32), ("ggml_type", c_u32), ("n_dims", c_i32),
+                ("ne", c_i64 * 4), ("offset", c_u64), ("nbytes", c_u64)]
+
+
 # (name, restype, argtypes) for every exported symbol in include/feml_b200.h
 SIGNATURES = [
     ("feml_b200_last_error", cp, []),
@@ -133,6 +138,21 @@ SIGNATURES = [
                                            vp, c_u64, c_u64, c_i64, c_i64, c_i64, vp, c_u64, vp, vp]),
     ("feml_b200_moe_route", c_int, [vp, c_u64, c_i64, c_i64, c_i64, vp, vp, vp, vp, vp]),
     ("feml_b200_block_dots", c_int, [c_i32, vp, c_u64, vp, c_i64, c_i64, c_i64, vp, vp]),
+    ("feml_b200_buffer_from_host_ptr", c_int, [vp, vp, c_u64, c_u64, ctypes.POINTER(c_u32)]),
+    ("feml_b200_gguf_open", c_int, [cp, ctypes.POINTER(vp)]),
+    ("feml_b200_gguf_close", c_int, [vp]),
+    ("feml_b200_gguf_info", c_int, [vp, ctypes.POINTER(c_u32), ctypes.POINTER(c_u64), ctypes.POINTER(c_u64),
+                                    ctypes.POINTER(c_i64), ctypes.POINTER(c_i64)]),
+    ("feml_b200_gguf_tensor", c_int, [vp, c_i64, ctypes.POINTER(GgufTensor)]),
+    ("feml_b200_gguf_find_tensor", c_int, [vp, cp, ctypes.POINTER(c_i64)]),
+    ("feml_b200_gguf_tensor_data", c_int, [vp, c_i64, ctypes.POINTER(vp)]),
+    ("feml_b200_gguf_kv", c_int, [vp, c_i64, ctypes.POINTER(cp), ctypes.POINTER(c_u32), ctypes.POINTER(c_u32),
+                                  ctypes.POINTER(c_u64)]),
+    ("feml_b200_gguf_find_kv", c_int, [vp, cp, ctypes.POINTER(c_i64)]),
+    ("feml_b200_gguf_kv_int", c_int, [vp, c_i64, ctypes.POINTER(c_i64)]),
+    ("feml_b200_gguf_kv_float", c_int, [vp, c_i64, ctypes.POINTER(ctypes.c_double)]),
+    ("feml_b200_gguf_kv_str", c_int, [vp, c_i64, c_i64, ctypes.POINTER(vp), ctypes.POINTER(c_u64)]),
+    ("feml_b200_gguf_kv_array_data", c_int, [vp, c_i64, ctypes.POINTER(vp)]),
 ]
 
 _lib = None

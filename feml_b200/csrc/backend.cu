@@ -437,7 +437,7 @@ int feml_b200_device_info(int32_t device, fb_device_info *info) {
     info->sm_count = prop.multiProcessorCount;
     info->device_type = 1;
     info->async_compute = 1;
-    info->host_buffer = 0;
+    info->host_buffer = 1;  // buffer_from_host_ptr (copied to HBM)
     info->events = 1;
     return FB_OK;
 }
@@ -537,6 +537,25 @@ int feml_b200_write(fb_backend *b, uint32_t h, uint64_t off, const void *src, ui
     cudaError_t e = cudaMemcpyAsync(buf->ptr + off, src, n, cudaMemcpyHostToDevice, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     return e == cudaSuccess ? FB_OK : cuda_fail(e, "write");
+}
+
+int feml_b200_buffer_from_host_ptr(fb_backend *b, const void *ptr, uint64_t size, uint64_t max_tensor_size,
+                                   uint32_t *handle) {
+    if (!b || !handle || (!ptr && size)) return set_error(FB_ERR_INVALID, "buffer_from_host_ptr: null argument");
+    if (max_tensor_size > size)
+        return set_error(FB_ERR_INVALID, "buffer_from_host_ptr: max_tensor_size %llu exceeds size %llu",
+                         (unsigned long long)max_tensor_size, (unsigned long long)size);
+    uint32_t h = 0;
+    int rc = feml_b200_create_buffer(b, size, FB_USAGE_WEIGHTS, &h);
+    if (rc) return rc;
+    rc = feml_b200_write(b, h, 0, ptr, size);  // one DMA from the caller's pages
+    if (rc) {
+        const std::string msg = fb::last_error();
+        feml_b200_release_buffer(b, h);
+        return set_error(rc, "%s", msg.c_str());
+    }
+    *handle = h;
+    return FB_OK;
 }
 
 int feml_b200_read(fb_backend *b, uint32_t h, uint64_t off, void *dst, uint64_t n) {

@@ -33,6 +33,7 @@
 #include "../host_common.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "tmap.h"
 
 namespace fbk {
 
@@ -59,6 +60,13 @@ __device__ __forceinline__ void cp_async4(float *smem_dst, const float *gsrc, bo
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
                  "r"(valid ? 4 : 0)
                  : "memory");
+}
+// 16-byte shared-memory load at a shared-window address. Volatile, so it
+// stays after the mbarrier wait that makes the data visible.
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -176,21 +184,17 @@ __global__ void __launch_bounds__(THREADS) gemm_f32_exact_kernel(const F32Params
 }
 
 // ---- pipelined path ---------------------------------------------------------
-// A warp owns 8 rows x 32 columns: lane l takes columns 2*(l%16) and
-// 2*(l%16)+1 and rows 4*(l/16) .. 4*(l/16)+3 of the warp's rows (8 chains).
+// A warp owns 8 rows x 32 columns: lane l takes columns l%16 and l%16 + 16
+// and rows 4*(l/16) .. 4*(l/16)+3 of the warp's rows (8 chains).
 constexpr int kWarpRows = 8;
 constexpr int kMaxWarps = 4;          // compute warps per CTA
-constexpr int kChunk = 128;           // k values per stage
-constexpr int kStride = kChunk + 4;   // floats per staged row / column (528 B: 16 mod 128)
+constexpr int kChunk = 128;           // k values per stage (four 32-wide boxes)
+constexpr int kBoxK = 32;             // k values per 128-byte swizzled box row
 constexpr int kPipeStages = 4;
 constexpr int kPipeCols = 32;         // columns per CTA
 constexpr uint32_t kPipeBarBytes = 128;
 
 struct F32PipeParams {
-    const uint8_t *w;
-    uint64_t w_nb1;
-    const uint8_t *x;
-    uint64_t x_nb1;
     uint8_t *y;
     uint64_t y_nb1;
     int K, M, N;
@@ -199,26 +203,31 @@ struct F32PipeParams {
     bool y_vec16;
 };
 
+// A stage: 4 weight boxes [bm rows][128 B] then 4 activation boxes
+// [32 columns][128 B], each 1024-byte aligned (bm is a multiple of 8).
 __host__ __device__ inline uint32_t pipe_stage_bytes(int warps) {
-    return (uint32_t)((kWarpRows * warps + kPipeCols) * kStride) * 4u;
+    return (uint32_t)(kChunk / kBoxK) * (uint32_t)(kWarpRows * warps + kPipeCols) * 128u;
+}
+__host__ __device__ inline uint32_t pipe_smem_bytes(int warps) {
+    return kPipeBarBytes + 1024u + kPipeStages * pipe_stage_bytes(warps);  // + 1024: alignment slack
 }
 
-// Staged column slot: even columns in slots 0..15, odd ones in 16..31, so
-// the 16 distinct column addresses of one 16-byte load fall in distinct banks.
-__host__ __device__ inline int col_slot(int c) { return (c >> 1) + 16 * (c & 1); }
-
-__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) gemm_f32_pipe_kernel(const F32PipeParams p) {
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
+    gemm_f32_pipe_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                         const F32PipeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kPipeStages;
-    uint8_t *stages = smem + kPipeBarBytes;
+    const uint32_t smem_base = smem_u32(smem);
+    const uint32_t stages = (smem_base + kPipeBarBytes + 1023u) & ~1023u;  // shared-window address
     const uint32_t stage_bytes = pipe_stage_bytes(p.warps);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bm = kWarpRows * p.warps;
     const int m0 = blockIdx.x * bm, n0 = blockIdx.y * kPipeCols;
     const int rows = min(bm, p.M - m0), cols = min(kPipeCols, p.N - n0);
     const int nchunks = (p.K + kChunk - 1) / kChunk;
-    const uint32_t wbytes = (uint32_t)bm * kStride * 4u;  // weight part of a stage
+    const uint32_t wbox = (uint32_t)bm * 128u;        // one weight box
+    const uint32_t wbytes = (kChunk / kBoxK) * wbox;  // weight part of a stage
 
     if (threadIdx.x == 0) {
         for (int st = 0; st < kPipeStages; st++) {
@@ -230,52 +239,85 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) gemm_f32_pipe_kernel(
     __syncthreads();
 
     if (warp == p.warps) {
-        // Producer: chunk c goes to stage c % 4 once the compute warps have
-        // released that stage's previous chunk.
+        // Producer (one lane): chunk c goes to stage c % 4 once the compute
+        // warps have released that stage's previous chunk; one swizzled box
+        // per 32 k values of the weight rows and of the activation columns
+        // (rows, columns and k past the matrix read as zeros and are not used).
+        if (lane != 0) return;
         int c = 0;
         bool ok = true;
         for (; c < nchunks; c++) {
             const int st = c % kPipeStages;
-            if (c >= kPipeStages) {
-                bool free_ok = true;
-                if (lane == 0) free_ok = mbar_wait_bounded(&empty[st], (uint32_t)(c / kPipeStages - 1) & 1u);
-                if (!__shfl_sync(0xffffffffu, free_ok, 0)) {
-                    ok = false;
-                    break;
-                }
+            if (c >= kPipeStages && !mbar_wait_bounded(&empty[st], (uint32_t)(c / kPipeStages - 1) & 1u)) {
+                ok = false;
+                break;
             }
             const int k0 = c * kChunk;
-            const uint32_t bytes = (uint32_t)min(kChunk, p.K - k0) * 4u;
-            uint8_t *sw = stages + (uint32_t)st * stage_bytes;
-            uint8_t *sx = sw + wbytes;
-            if (lane == 0) {
-                fence_proxy_async_smem();
-                mbar_arrive_expect_tx(&full[st], bytes * (uint32_t)(rows + cols));
+            const int nb = (min(kChunk, p.K - k0) + kBoxK - 1) / kBoxK;
+            const uint32_t sw = stages + (uint32_t)st * stage_bytes, sx = sw + wbytes;
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&full[st], (uint32_t)nb * (wbox + kPipeCols * 128u));
+            for (int b = 0; b < nb; b++) {
+                tma_load_2d(sw + (uint32_t)b * wbox, &tmw, k0 + b * kBoxK, m0, smem_u32(&full[st]));
+                tma_load_2d(sx + (uint32_t)b * (kPipeCols * 128u), &tmx, k0 + b * kBoxK, n0, smem_u32(&full[st]));
             }
-            __syncwarp();
-            for (int i = lane; i < rows; i += 32)
-                bulk_g2s(sw + (uint32_t)i * kStride * 4u, p.w + (uint64_t)(m0 + i) * p.w_nb1 + (uint64_t)k0 * 4u,
-                         bytes, &full[st]);
-            for (int j = lane; j < cols; j += 32)
-                bulk_g2s(sx + (uint32_t)col_slot(j) * kStride * 4u,
-                         p.x + (uint64_t)(n0 + j) * p.x_nb1 + (uint64_t)k0 * 4u, bytes, &full[st]);
         }
-        if (lane == 0) {
-            if (!ok) report_status(p.status, STATUS_TIMEOUT);
-            // the CTA ends only after every copy it issued has landed (chunks
-            // before c - 4 were released by the compute warps, so they had)
-            for (int j = max(0, c - kPipeStages); j < c; j++)
-                mbar_wait_bounded(&full[j % kPipeStages], (uint32_t)(j / kPipeStages) & 1u);
-        }
+        if (!ok) report_status(p.status, STATUS_TIMEOUT);
+        // the CTA ends only after every copy it issued has landed (chunks
+        // before c - 4 were released by the compute warps, so they had)
+        for (int j = max(0, c - kPipeStages); j < c; j++)
+            mbar_wait_bounded(&full[j % kPipeStages], (uint32_t)(j / kPipeStages) & 1u);
         return;
     }
 
-    // Compute warps.
-    const int cp = lane & 15;                          // column pair: columns 2cp, 2cp+1
+    // Compute warps. Row y's 16-byte unit u of a box sits at
+    // y * 128 + ((u ^ (y % 8)) * 16).
+    const int cp = lane & 15;                           // columns cp and cp + 16
     const int r0 = warp * kWarpRows + 4 * (lane >> 4);  // first of this lane's 4 rows in the CTA
+    const uint32_t wrow = (uint32_t)r0 * 128u;          // row r0 + r at wrow + r * 128
+    const uint32_t wsw = (uint32_t)(r0 & 4);            // (r0 + r) % 8 == wsw + r
+    const uint32_t xrow = (uint32_t)cp * 128u;          // column cp + 16 is 2048 bytes on
+    const uint32_t xsw = (uint32_t)((cp & 7) << 4);
     float acc[4][2];
 #pragma unroll
     for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = 0.0f;
+    struct Step {
+        float4 xa, xb, w[4];
+    };
+    // step t: k values 4t .. 4t+3 of the chunk = box t / 8, unit t % 8
+    auto load = [&](uint32_t sw, uint32_t sx, int t) {
+        Step v;
+        const uint32_t u = (uint32_t)(t & 7) << 4;
+        const uint32_t bw = sw + (uint32_t)(t >> 3) * wbox + wrow;
+        const uint32_t bx = sx + (uint32_t)(t >> 3) * (kPipeCols * 128u) + xrow + (u ^ xsw);
+        v.xa = lds_f4(bx);
+        v.xb = lds_f4(bx + 16u * 128u);
+#pragma unroll
+        for (int r = 0; r < 4; r++) v.w[r] = lds_f4(bw + (uint32_t)r * 128u + (u ^ ((wsw + (uint32_t)r) << 4)));
+        return v;
+    };
+    auto step = [&](const Step &v) {
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(v.w[r].x, v.xa.x));
+            acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(v.w[r].x, v.xb.x));
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(v.w[r].y, v.xa.y));
+            acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(v.w[r].y, v.xb.y));
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(v.w[r].z, v.xa.z));
+            acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(v.w[r].z, v.xb.z));
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(v.w[r].w, v.xa.w));
+            acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(v.w[r].w, v.xb.w));
+        }
+    };
 
     bool ok = true;
     for (int c = 0; c < nchunks; c++) {
@@ -284,50 +326,19 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) gemm_f32_pipe_kernel(
             ok = false;
             break;
         }
-        const uint8_t *base = stages + (uint32_t)st * stage_bytes;
-        const float *sw = reinterpret_cast<const float *>(base) + r0 * kStride;
-        const float *sxa = reinterpret_cast<const float *>(base + wbytes) + cp * kStride;  // column 2cp
-        const float *sxb = sxa + 16 * kStride;                                            // column 2cp+1
-        const int kc = min(kChunk, p.K - c * kChunk);  // a multiple of 4
-        // shared loads one step ahead of the arithmetic (the last step
-        // reloads its own values instead of reading past the chunk)
-        float4 xa = *reinterpret_cast<const float4 *>(sxa);
-        float4 xb = *reinterpret_cast<const float4 *>(sxb);
-        float4 wv[4];
-#pragma unroll
-        for (int r = 0; r < 4; r++) wv[r] = *reinterpret_cast<const float4 *>(sw + r * kStride);
+        const uint32_t sw = stages + (uint32_t)st * stage_bytes, sx = sw + wbytes;
+        const int nsteps = min(kChunk, p.K - c * kChunk) >> 2;  // 4 k values per step
+        // shared loads two steps ahead of the arithmetic (steps past the
+        // chunk reload its last step instead of reading beyond it)
+        Step s0 = load(sw, sx, 0), s1 = load(sw, sx, min(1, nsteps - 1));
 #pragma unroll 2
-        for (int kk = 0; kk < kc; kk += 4) {
-            const int kn = min(kk + 4, kc - 4);
-            const float4 nxa = *reinterpret_cast<const float4 *>(sxa + kn);
-            const float4 nxb = *reinterpret_cast<const float4 *>(sxb + kn);
-            float4 nw[4];
-#pragma unroll
-            for (int r = 0; r < 4; r++) nw[r] = *reinterpret_cast<const float4 *>(sw + r * kStride + kn);
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(wv[r].x, xa.x));
-                acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(wv[r].x, xb.x));
-            }
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(wv[r].y, xa.y));
-                acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(wv[r].y, xb.y));
-            }
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(wv[r].z, xa.z));
-                acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(wv[r].z, xb.z));
-            }
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(wv[r].w, xa.w));
-                acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(wv[r].w, xb.w));
-            }
-            xa = nxa;
-            xb = nxb;
-#pragma unroll
-            for (int r = 0; r < 4; r++) wv[r] = nw[r];
+        for (int t = 0; t < nsteps; t += 2) {
+            const Step n0v = load(sw, sx, min(t + 2, nsteps - 1));
+            const Step n1v = load(sw, sx, min(t + 3, nsteps - 1));
+            step(s0);
+            if (t + 1 < nsteps) step(s1);
+            s0 = n0v;
+            s1 = n1v;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
@@ -338,7 +349,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) gemm_f32_pipe_kernel(
     }
 #pragma unroll
     for (int j = 0; j < 2; j++) {
-        const int col = 2 * cp + j;
+        const int col = cp + 16 * j;
         if (col >= cols || r0 >= rows) continue;
         float *yc = reinterpret_cast<float *>(p.y + (uint64_t)(n0 + col) * p.y_nb1);
         const int m = m0 + r0;  // a multiple of 4
@@ -361,21 +372,28 @@ int pipe_warps(int64_t M, int64_t N) {
     return (int)std::min<int64_t>(kMaxWarps, std::max<int64_t>(1, (rows_per_cta + kWarpRows - 1) / kWarpRows));
 }
 
-int launch_f32_pipe(const F32PipeParams &p, cudaStream_t s) {
+int launch_f32_pipe(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, const F32PipeParams &p,
+                    cudaStream_t s) {
+    const int bm = kWarpRows * p.warps;
+    CUtensorMap tmw, tmx;
+    int rc = encode_tensor_map_2d_sw128(&tmw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w, (uint64_t)p.K, (uint64_t)p.M, w_nb1,
+                                        kBoxK, (uint32_t)bm);
+    if (rc) return rc;
+    rc = encode_tensor_map_2d_sw128(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, x, (uint64_t)p.K, (uint64_t)p.N, x_nb1,
+                                    kBoxK, kPipeCols);
+    if (rc) return rc;
     static bool smem_set[64] = {};  // per device: the dynamic smem limit was raised
-    const uint32_t smem = kPipeBarBytes + kPipeStages * pipe_stage_bytes(p.warps);
     int dev = 0;
     cudaGetDevice(&dev);
     cudaError_t e = cudaSuccess;
     if (dev < 0 || dev >= 64 || !smem_set[dev]) {
         e = cudaFuncSetAttribute(gemm_f32_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(kPipeBarBytes + kPipeStages * pipe_stage_bytes(kMaxWarps)));
+                                 (int)pipe_smem_bytes(kMaxWarps));
         if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_f32: smem attribute: %s", cudaGetErrorString(e));
         if (dev >= 0 && dev < 64) smem_set[dev] = true;
     }
-    const int bm = kWarpRows * p.warps;
     dim3 grid((unsigned)((p.M + bm - 1) / bm), (unsigned)((p.N + kPipeCols - 1) / kPipeCols));
-    gemm_f32_pipe_kernel<<<grid, (p.warps + 1) * 32, smem, s>>>(p);
+    gemm_f32_pipe_kernel<<<grid, (p.warps + 1) * 32, pipe_smem_bytes(p.warps), s>>>(tmw, tmx, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_f32 launch: %s", cudaGetErrorString(e));
     return FB_OK;
@@ -405,10 +423,6 @@ int launch_gemm_f32(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1
         ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | w_nb1 | x_nb1) & 15) == 0;
     if (aligned16 && K > 0 && K % 4 == 0 && (N + kPipeCols - 1) / kPipeCols <= 65535) {
         F32PipeParams q{};
-        q.w = static_cast<const uint8_t *>(w);
-        q.w_nb1 = w_nb1;
-        q.x = static_cast<const uint8_t *>(x);
-        q.x_nb1 = x_nb1;
         q.y = static_cast<uint8_t *>(y);
         q.y_nb1 = y_nb1;
         q.K = (int)K;
@@ -417,7 +431,7 @@ int launch_gemm_f32(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1
         q.warps = pipe_warps(M, N);
         q.status = status;
         q.y_vec16 = ((reinterpret_cast<uintptr_t>(y) | y_nb1) & 15) == 0;
-        return launch_f32_pipe(q, s);
+        return launch_f32_pipe(w, w_nb1, x, x_nb1, q, s);
     }
     F32Params p{};
     p.w = static_cast<const uint8_t *>(w);

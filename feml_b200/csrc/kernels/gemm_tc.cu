@@ -914,6 +914,11 @@ int encode_tensor_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *b
     return encode_map(map, dt, base, dim0, dim1, 0, stride1, 0, box0, box1, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+int encode_tensor_map_2d_sw128(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t dim0,
+                               uint64_t dim1, uint64_t stride1, uint32_t box0, uint32_t box1) {
+    return encode_map(map, dt, base, dim0, dim1, 0, stride1, 0, box0, box1, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 bool gemm_tc_supported(int32_t wtype, int64_t K, int64_t M, int64_t N, const void *w, uint64_t w_nb1) {
     if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K) return false;
     if (K <= 0 || K % QKK || K > (1 << 24) || M <= 0 || N <= 0 || M > INT32_MAX || N > INT32_MAX / 64) return false;

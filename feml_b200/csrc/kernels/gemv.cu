@@ -757,14 +757,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_ks_kernel(const __grid_c
 
 // ---- K-split decode GEMV for wide Q4_K rows, 2..8 columns -------------------
 // The same slices and 2D boxes as gemv_ks_kernel; the activations were
-// quantized by a preceding kernel into planar form (read after the
-// programmatic-dependent-launch wait, through L1). A lane holds the weight
-// words and scale terms of its sub-block pair for all rows of a box in
-// registers and walks the columns, loading each column's activation words
-// once per box. The box's kKsRows x NC partial sums (padded to 32) are
-// reduced across the warp with a transposing butterfly (31 shuffles, lane l
-// ends with value l) and meet the other slices in shared memory, added in
-// warp order.
+// quantized by a preceding kernel into planar form. After the
+// programmatic-dependent-launch wait each warp copies the int8 words of its
+// slice into shared memory, transposed to [column][16-byte quarter][pair] so
+// that a lane's loads of its pair are conflict-free; block scales and sums
+// are read through L1. A lane holds the weight words and scale terms of its
+// sub-block pair for all rows of a box in registers and walks the columns.
+// The box's kKsRows x NC partial sums (padded to 32) are reduced across the
+// warp with a transposing butterfly (31 shuffles, lane l ends with value l)
+// and meet the other slices in shared memory, added in warp order.
 struct KsColsParams {
     Q8Planar xq;
     uint8_t *y;
@@ -774,6 +775,7 @@ struct KsColsParams {
     int nsb;
     uint32_t box_bytes;
     uint32_t ring_off;
+    uint32_t xs_off;  // shared-memory offset of the staged activations
     int32_t *status;
 };
 
@@ -818,6 +820,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ks_cols_kernel(const __g
     const int g = lane & 3;                              // pair within the super-block
     const int b0 = (sb0 + (lane >> 2)) * 8 + 2 * g;      // its even sub-block in the row
     const int nblk = p.K / QK;
+    // this warp's activation words: [n][quarter j][pair], 16 bytes each
+    const int pmax = 4 * ((p.nsb + kGemvWarps - 1) / kGemvWarps);  // pairs of the widest slice
+    uint4 *xs = reinterpret_cast<uint4 *>(smem + p.xs_off) + (size_t)warp * NC * 4 * pmax;
+    if (active) {
+#pragma unroll
+        for (int n = 0; n < NC; n++) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.xq.qs + (size_t)n * p.K + (size_t)b0 * QK);
+            uint4 v[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[j] = __ldg(src + j);
+#pragma unroll
+            for (int j = 0; j < 4; j++) xs[(n * 4 + j) * pmax + lane] = v[j];
+        }
+    }
+    __syncwarp();
     for (int i = 0; i < n_items; i++) {
         const int stage = i % kKsStages;
         const bool ok = mbar_wait_bounded(&bars[stage], (uint32_t)(i / kKsStages) & 1u);
@@ -839,8 +856,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ks_cols_kernel(const __g
             for (int r = 0; r < kKsRows; r++) wr[r] = q4k_pair_load(st + r * p.box_bytes + (lane >> 2) * Q4_K_BYTES, g);
 #pragma unroll
             for (int n = 0; n < NC; n++) {
-                const uint4 *xa = reinterpret_cast<const uint4 *>(p.xq.qs + (size_t)n * p.K + (size_t)b0 * QK);
-                const uint4 a0 = __ldg(xa), a1 = __ldg(xa + 1), c0 = __ldg(xa + 2), c1 = __ldg(xa + 3);
+                const uint4 *xa = xs + n * 4 * pmax + lane;
+                const uint4 a0 = xa[0], a1 = xa[pmax], c0 = xa[2 * pmax], c1 = xa[3 * pmax];
                 const float2 dx = __ldg(reinterpret_cast<const float2 *>(p.xq.d + (size_t)n * nblk + b0));
                 const int2 sx = __ldg(reinterpret_cast<const int2 *>(p.xq.sum + (size_t)n * nblk + b0));
 #pragma unroll
@@ -1059,7 +1076,8 @@ int launch_gemv_ks_cols(const void *w, uint64_t w_nb1, const Q8Planar &xq, void 
     const int64_t rows_max = (M + grid - 1) / grid + 1;
     const uint32_t ring_off = (uint32_t)((256 + rows_max * N * kGemvWarps * 4 + 127) / 128 * 128);
     const uint64_t stage_bytes = ((uint64_t)kKsRows * box_bytes + 127) / 128 * 128;
-    const uint64_t smem = ring_off + (uint64_t)kGemvWarps * kKsStages * stage_bytes;
+    const uint64_t xs_off = ring_off + (uint64_t)kGemvWarps * kKsStages * stage_bytes;
+    const uint64_t smem = xs_off + (uint64_t)kGemvWarps * N * 4 * (4 * widest) * 16;
     if (smem > (uint64_t)kSmemLimit) return -1;
     CUtensorMap tm;
     int rc = encode_tensor_map_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, (uint64_t)nsb * Q4_K_BYTES / 8,
@@ -1074,6 +1092,7 @@ int launch_gemv_ks_cols(const void *w, uint64_t w_nb1, const Q8Planar &xq, void 
     p.nsb = nsb;
     p.box_bytes = box_bytes;
     p.ring_off = ring_off;
+    p.xs_off = (uint32_t)xs_off;
     p.status = status;
     switch (N) {
     case 2: return launch_ks_cols_typed<2>(tm, p, grid, (uint32_t)smem, s, pdl);

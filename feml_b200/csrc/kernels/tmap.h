@@ -10,6 +10,11 @@ namespace fbk {
 // 2D tiled tensor map, no swizzle; dim0 is contiguous, stride1 in bytes.
 int encode_tensor_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t dim0, uint64_t dim1,
                          uint64_t stride1, uint32_t box0, uint32_t box1);
+// The same with the 128-byte swizzle: box0 * element size must be 128 bytes;
+// in shared memory (box start 1024-byte aligned) row y's 16-byte unit u lands
+// at y * 128 + ((u ^ (y % 8)) * 16).
+int encode_tensor_map_2d_sw128(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t dim0,
+                               uint64_t dim1, uint64_t stride1, uint32_t box0, uint32_t box1);
 
 #ifdef __CUDACC__
 // One 2D box into shared memory, completing on `bar` (no multicast). The

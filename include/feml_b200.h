@@ -385,6 +385,66 @@ int feml_b200_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected
 int feml_b200_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *xq, int64_t K, int64_t M,
                          int64_t N, int32_t *out, void *stream);
 
+/* ---- weight ingestion: host pointers and GGUF files ----------------------- */
+
+/* BackendDevice::buffer_from_host_ptr (feml-core/src/backend.rs:145-153; the
+ * reference backends return an error, feml-cuda/src/device.rs:65-72). Wraps
+ * `size` bytes of externally owned host memory (an mmap'd model file, for
+ * instance) as a new Weights buffer of this backend: the bytes are copied to
+ * HBM once, straight from `ptr` (no staging copy), and the handle then
+ * behaves like any other buffer (plans address it by handle + offset; the
+ * kernels read HBM, not the host link). `max_tensor_size` is the largest
+ * tensor the caller will place in the buffer and must not exceed `size`.
+ * Blocking; `ptr` need only stay valid for the duration of the call. */
+int feml_b200_buffer_from_host_ptr(fb_backend *b, const void *ptr, uint64_t size, uint64_t max_tensor_size,
+                                   uint32_t *handle);
+
+/* GGUF reader (the llama.cpp / ggml model container that feml's roadmap names
+ * as the source of quantized weights, docs/DESIGN.md section 10 "GGUF": mmap +
+ * buffer_from_host_ptr). No counterpart exists in the reference yet; the
+ * format follows the public GGUF specification (versions 2 and 3). The file
+ * is mapped read-only; every pointer returned stays valid until
+ * feml_b200_gguf_close. Malformed files give FB_ERR_INVALID with the
+ * offending offset, never an out-of-range read. */
+typedef struct fb_gguf fb_gguf;
+
+/* GGUF metadata value types (public specification). */
+enum fb_gguf_type {
+    FB_GGUF_U8 = 0, FB_GGUF_I8, FB_GGUF_U16, FB_GGUF_I16, FB_GGUF_U32, FB_GGUF_I32, FB_GGUF_F32,
+    FB_GGUF_BOOL, FB_GGUF_STRING, FB_GGUF_ARRAY, FB_GGUF_U64, FB_GGUF_I64, FB_GGUF_F64
+};
+
+typedef struct {
+    char name[256];     /* NUL-terminated */
+    int32_t dtype;      /* fb_dtype, or -1 when feml has no counterpart (BF16, IQ types ...) */
+    uint32_t ggml_type; /* the file's ggml type id */
+    int32_t n_dims;
+    int64_t ne[4];      /* ggml order, ne[0] contiguous; unused dimensions are 1 */
+    uint64_t offset;    /* byte offset of the data from the start of the file */
+    uint64_t nbytes;    /* 0 when the type's block size is unknown */
+} fb_gguf_tensor;
+
+int feml_b200_gguf_open(const char *path, fb_gguf **out);
+int feml_b200_gguf_close(fb_gguf *g);
+int feml_b200_gguf_info(const fb_gguf *g, uint32_t *version, uint64_t *alignment, uint64_t *data_offset,
+                        int64_t *n_kv, int64_t *n_tensors);
+int feml_b200_gguf_tensor(const fb_gguf *g, int64_t index, fb_gguf_tensor *out);
+int feml_b200_gguf_find_tensor(const fb_gguf *g, const char *name, int64_t *index);
+/* Pointer to the tensor's bytes inside the mapping (nbytes long). */
+int feml_b200_gguf_tensor_data(const fb_gguf *g, int64_t index, const void **data);
+/* Key `index`: its name (NUL-terminated), value type, array element type
+ * (arrays) and count (array elements; string bytes; 1 for scalars). */
+int feml_b200_gguf_kv(const fb_gguf *g, int64_t index, const char **key, uint32_t *type, uint32_t *elem_type,
+                      uint64_t *count);
+int feml_b200_gguf_find_kv(const fb_gguf *g, const char *key, int64_t *index);
+/* Scalar values: integers and bools as int64, f32/f64 as double. */
+int feml_b200_gguf_kv_int(const fb_gguf *g, int64_t index, int64_t *out);
+int feml_b200_gguf_kv_float(const fb_gguf *g, int64_t index, double *out);
+/* A string value, or element `elem` of a string array (not NUL-terminated). */
+int feml_b200_gguf_kv_str(const fb_gguf *g, int64_t index, int64_t elem, const char **s, uint64_t *len);
+/* The first element of a numeric array, inside the mapping (little-endian). */
+int feml_b200_gguf_kv_array_data(const fb_gguf *g, int64_t index, const void **data);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

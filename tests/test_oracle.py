@@ -10,6 +10,11 @@ against it.
    against the committed regression vectors. The reference has no quant
    arithmetic, so this pins the oracle's reading of the formats, not the
    reference (parity for quantized types is unpinned by the reference).
+   The Q8_0 / Q4_0 quantizers and Q8_0 / Q4_0 / Q4_K dequantizers are also
+   pinned byte for byte to llama.cpp's own Python implementation of the
+   formats (gguf-py): against its committed vectors
+   (tests/golden/ggufpy_vectors.npz) and, where the package is installed,
+   live on fresh inputs.
  - Routing: against a numpy stable sort.
 """
 import json
@@ -144,6 +149,48 @@ def test_oracle_quantizers_match_committed_vectors(name, dt):
     assert np.array_equal(q, gv[name])
     deq = O.dequantize(dt, q, gv["x"].shape[1])
     assert np.array_equal(deq.view(np.uint32), gv[name + "_deq"].view(np.uint32))
+
+
+def _same_blocks(got, want, x, block_bytes):
+    """Quantized rows equal block by block, except that for a block whose
+    inputs are all zeros the scale may be +0 or -0: the Q4_0 quantizer takes
+    `max` as the first value of largest magnitude starting from +0 (ggml's C
+    reference does the same), gguf-py's numpy version takes the block's first
+    element, so an all-(-0) block gives d = -0 here and +0 there."""
+    g = got.reshape(got.shape[0], -1, block_bytes)
+    w = want.reshape(want.shape[0], -1, block_bytes)
+    zero = np.all(x.reshape(x.shape[0], -1, 32) == 0, axis=-1)
+    assert np.array_equal(g[..., 2:], w[..., 2:])
+    same_d = np.all(g[..., :2] == w[..., :2], axis=-1)
+    dg = g[..., 0].astype(np.uint16) | (g[..., 1].astype(np.uint16) << 8)
+    dw = w[..., 0].astype(np.uint16) | (w[..., 1].astype(np.uint16) << 8)
+    signed_zero = zero & ((dg & 0x7FFF) == 0) & ((dw & 0x7FFF) == 0)
+    assert np.all(same_d | signed_zero)
+
+
+@pytest.mark.parametrize("name,dt", [("q8_0", O.DT_Q8_0), ("q4_0", O.DT_Q4_0), ("q4_k", O.DT_Q4_K)])
+def test_oracle_matches_ggufpy_vectors(name, dt):
+    gv = np.load(os.path.join(GOLD, "ggufpy_vectors.npz"))
+    if name != "q4_k":  # gguf-py has no Q4_K quantizer; its dequantizer pins the layout
+        _same_blocks(O.quantize(dt, gv["x"]), gv[name], gv["x"], 34 if name == "q8_0" else 18)
+    deq = O.dequantize(dt, gv[name], gv[name + "_deq"].shape[1])
+    assert np.array_equal(deq.view(np.uint32), gv[name + "_deq"].view(np.uint32))
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_oracle_matches_ggufpy_live(seed):
+    gguf = pytest.importorskip("gguf")
+    from gguf import GGMLQuantizationType as T
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((16, 1024)) * rng.uniform(0.01, 10.0, (16, 1))).astype(np.float32)
+    for dt, t in ((O.DT_Q8_0, T.Q8_0), (O.DT_Q4_0, T.Q4_0)):
+        q = gguf.quants.quantize(x, t)
+        _same_blocks(O.quantize(dt, x), q, x, 34 if dt == O.DT_Q8_0 else 18)
+        assert np.array_equal(O.dequantize(dt, q, 1024).view(np.uint32),
+                              gguf.quants.dequantize(q, t).astype(np.float32).view(np.uint32))
+    q = O.quantize(O.DT_Q4_K, x)
+    assert np.array_equal(O.dequantize(O.DT_Q4_K, q, 1024).view(np.uint32),
+                          gguf.quants.dequantize(q, T.Q4_K).astype(np.float32).view(np.uint32))
 
 
 def test_q8_0_edge_blocks():
