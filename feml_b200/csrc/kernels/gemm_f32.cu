@@ -9,17 +9,17 @@
 // Two kernels share that arithmetic:
 //  - gemm_f32_pipe_kernel (16-byte aligned operands, K % 4 == 0, ungrouped):
 //    a CTA owns 8*W rows x 32 columns (W <= 4 compute warps, one per SM
-//    sub-partition). A producer warp streams 128-wide k chunks of the CTA's
-//    weight rows and activation columns into a 4-stage shared-memory ring
-//    with bulk async copies (cp.async.bulk, one per row or column chunk,
-//    completing on the stage's mbarrier), about 100 KB per SM in flight. A
-//    compute warp owns 8 rows x 32 columns; each lane a 4-row x 2-column
-//    micro-tile (8 chains), reading 4 k values of each of its rows and
-//    columns with 16-byte loads issued one step ahead of the arithmetic:
-//    6 shared loads per 32 multiply-adds, staged rows and columns padded to
-//    528 bytes and columns interleaved (even, odd) so the loads are
-//    conflict-free. The sequential chains leave the kernel bound by FP32
-//    issue (two instructions per multiply-add), not by HBM.
+//    sub-partition). One producer thread streams 128-wide k chunks into a
+//    4-stage shared-memory ring as 2D TMA boxes (32 k x the CTA's rows, 32 k
+//    x its 32 columns; 128-byte swizzle), 8 tensor copies per chunk: with
+//    one bulk copy per 512-byte row segment (64 per chunk) the copies, not
+//    the arithmetic, set the pace (110 us against 88 us for C1). A compute
+//    warp owns 8 rows x 32 columns; each lane a 4-row x 2-column micro-tile
+//    (8 chains), reading 4 k values of each of its rows and columns with
+//    16-byte shared loads two steps ahead of the arithmetic: 6 loads per 32
+//    multiply-adds, conflict-free through the swizzle. The sequential chains
+//    leave the kernel bound by FP32 issue (two instructions per
+//    multiply-add), not by HBM.
 //  - gemm_f32_exact_kernel (everything else, and mul_mat_id with F32
 //    experts): a CTA owns a 32x32 output tile; each of its 128 threads owns a
 //    4 (rows) x 2 (columns) micro-tile, i.e. 8 independent chains. K is walked

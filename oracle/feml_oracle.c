@@ -21,6 +21,12 @@
  *    block_q4_K = {f16 d; f16 dmin; u8 scales[12]; u8 qs[128]}); the Q4_K
  *    quantizer is this project's own deterministic scheme (ggml's iterative
  *    search is not reproduced), so Q4_K quantizer bytes are parity-unpinned.
+ *  - Q5_K / Q6_K (block_q5_K = {f16 d; f16 dmin; u8 scales[12]; u8 qh[32];
+ *    u8 qs[128]}, block_q6_K = {u8 ql[128]; u8 qh[64]; i8 scales[16];
+ *    f16 d}): dequantizers restate the public layouts; the quantizers are
+ *    this project's deterministic single-pass schemes (parity-unpinned, like
+ *    Q4_K's). The dequantizers of all K-quants are pinned to llama.cpp's
+ *    gguf-py implementation in tests.
  *  - per-block int32 dot products and MoE routing: the integer work the
  *    B200 kernels must reproduce bit-for-bit.
  *  - planner/layout golden values are checked in tests against the product
@@ -39,6 +45,8 @@
 #define Q8_0_BYTES 34
 #define Q4_0_BYTES 18
 #define Q4_K_BYTES 144
+#define Q5_K_BYTES 176
+#define Q6_K_BYTES 210
 
 /* ------------------------------------------------------------------------ */
 /* IEEE binary16 <-> binary32, round-to-nearest-even (bit-level, portable).  */
@@ -284,6 +292,182 @@ void oracle_dequantize_row_q4_k(const uint8_t *y, float *x, int64_t k) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* Q5_K and Q6_K                                                             */
+/* ------------------------------------------------------------------------ */
+/* Q5_K quantizer (this project's scheme): the Q4_K scheme with 31 levels;
+ * the 5-bit value's low nibble goes to qs (as in Q4_K), its bit 4 to qh:
+ * element l of sub-block j sets bit j of qh[l]. */
+void oracle_quantize_row_q5_k(const float *x, uint8_t *y, int64_t k) {
+    const int64_t nb = k / QK_K;
+    for (int64_t i = 0; i < nb; i++) {
+        const float *xb = x + i * QK_K;
+        uint8_t *yb = y + i * Q5_K_BYTES;
+        float scale[8], minv[8];
+        float max_scale = 0.0f, max_min = 0.0f;
+        for (int j = 0; j < 8; j++) {
+            float lo = 0.0f, hi = 0.0f;
+            for (int l = 0; l < 32; l++) {
+                const float v = xb[32 * j + l];
+                lo = v < lo ? v : lo;
+                hi = v > hi ? v : hi;
+            }
+            scale[j] = (hi - lo) / 31.0f;
+            minv[j] = -lo;
+            max_scale = scale[j] > max_scale ? scale[j] : max_scale;
+            max_min = minv[j] > max_min ? minv[j] : max_min;
+        }
+        const uint16_t dh = oracle_f32_to_f16(max_scale / 63.0f);
+        const uint16_t mh = oracle_f32_to_f16(max_min / 63.0f);
+        const float df = oracle_f16_to_f32(dh);
+        const float mf = oracle_f16_to_f32(mh);
+        int sc[8], mm[8];
+        for (int j = 0; j < 8; j++) {
+            int s = df > 0.0f ? (int)roundf(scale[j] / df) : 0;
+            int m = mf > 0.0f ? (int)roundf(minv[j] / mf) : 0;
+            sc[j] = s > 63 ? 63 : s;
+            mm[j] = m > 63 ? 63 : m;
+        }
+        wr_u16(yb, dh);
+        wr_u16(yb + 2, mh);
+        uint8_t *scales = yb + 4;
+        memset(scales, 0, 12);
+        for (int j = 0; j < 8; j++) {
+            if (j < 4) {
+                scales[j] = (uint8_t)sc[j];
+                scales[j + 4] = (uint8_t)mm[j];
+            } else {
+                scales[j + 4] = (uint8_t)((sc[j] & 0x0f) | ((mm[j] & 0x0f) << 4));
+                scales[j - 4] |= (uint8_t)((sc[j] >> 4) << 6);
+                scales[j] |= (uint8_t)((mm[j] >> 4) << 6);
+            }
+        }
+        uint8_t q[QK_K];
+        for (int j = 0; j < 8; j++) {
+            const float ds = df * (float)sc[j];
+            const float dm = mf * (float)mm[j];
+            for (int l = 0; l < 32; l++) {
+                int v = 0;
+                if (ds > 0.0f) {
+                    v = (int)roundf((xb[32 * j + l] + dm) / ds);
+                    v = v < 0 ? 0 : (v > 31 ? 31 : v);
+                }
+                q[32 * j + l] = (uint8_t)v;
+            }
+        }
+        uint8_t *qh = yb + 16, *qs = yb + 48;
+        memset(qh, 0, 32);
+        for (int g = 0; g < 4; g++)
+            for (int l = 0; l < 32; l++) {
+                const uint8_t a = q[64 * g + l], b = q[64 * g + 32 + l];
+                qs[32 * g + l] = (uint8_t)((a & 0x0f) | ((b & 0x0f) << 4));
+                qh[l] |= (uint8_t)(((a >> 4) << (2 * g)) | ((b >> 4) << (2 * g + 1)));
+            }
+    }
+}
+
+/* Value = (d*sc)*q - (dmin*m), q = low nibble + 16 * high bit. */
+void oracle_dequantize_row_q5_k(const uint8_t *y, float *x, int64_t k) {
+    const int64_t nb = k / QK_K;
+    for (int64_t i = 0; i < nb; i++) {
+        const uint8_t *yb = y + i * Q5_K_BYTES;
+        const float d = oracle_f16_to_f32(rd_u16(yb));
+        const float dmin = oracle_f16_to_f32(rd_u16(yb + 2));
+        const uint8_t *scales = yb + 4, *qh = yb + 16, *qs = yb + 48;
+        float *out = x + i * QK_K;
+        for (int g = 0; g < 4; g++) {
+            int sc, m;
+            oracle_q4k_scale_min(2 * g, scales, &sc, &m);
+            const float d1 = d * (float)sc, m1 = dmin * (float)m;
+            oracle_q4k_scale_min(2 * g + 1, scales, &sc, &m);
+            const float d2 = d * (float)sc, m2 = dmin * (float)m;
+            for (int l = 0; l < 32; l++) {
+                const int q = (qs[32 * g + l] & 0x0f) + (((qh[l] >> (2 * g)) & 1) << 4);
+                out[64 * g + l] = d1 * (float)q - m1;
+            }
+            for (int l = 0; l < 32; l++) {
+                const int q = (qs[32 * g + l] >> 4) + (((qh[l] >> (2 * g + 1)) & 1) << 4);
+                out[64 * g + 32 + l] = d2 * (float)q - m2;
+            }
+        }
+    }
+}
+
+/* Element e (0..255) of a Q6_K super-block: half h = e / 128, within it
+ * quarter t = (e % 128) / 32 and lane l = e % 32; its low 4 bits are the low
+ * (t < 2) or high (t >= 2) nibble of ql[64h + 32(t % 2) + l], its top 2 bits
+ * are bits 2t..2t+1 of qh[32h + l]; its scale is scales[8h + 2t + l / 16]. */
+static int q6k_index(int e, int *ql_byte, int *ql_hi, int *qh_byte, int *qh_shift, int *sc_index) {
+    const int h = e / 128, t = (e % 128) / 32, l = e % 32;
+    *ql_byte = 64 * h + 32 * (t % 2) + l;
+    *ql_hi = t >= 2;
+    *qh_byte = 32 * h + l;
+    *qh_shift = 2 * t;
+    *sc_index = 8 * h + 2 * t + l / 16;
+    return 0;
+}
+
+/* Q6_K quantizer (this project's scheme): per 16-element group g,
+ * scale_g = amax_g / 31; d = f16(max_g scale_g / 127);
+ * sc_g = min(127, roundf(scale_g / d)); q = clamp(roundf(x / (d*sc_g)), -32, 31)
+ * stored as q + 32. */
+void oracle_quantize_row_q6_k(const float *x, uint8_t *y, int64_t k) {
+    const int64_t nb = k / QK_K;
+    for (int64_t i = 0; i < nb; i++) {
+        const float *xb = x + i * QK_K;
+        uint8_t *yb = y + i * Q6_K_BYTES;
+        float scale[16], max_scale = 0.0f;
+        for (int g = 0; g < 16; g++) {
+            float amax = 0.0f;
+            for (int l = 0; l < 16; l++) {
+                const float a = fabsf(xb[16 * g + l]);
+                amax = a > amax ? a : amax;
+            }
+            scale[g] = amax / 31.0f;
+            max_scale = scale[g] > max_scale ? scale[g] : max_scale;
+        }
+        const uint16_t dh = oracle_f32_to_f16(max_scale / 127.0f);
+        const float df = oracle_f16_to_f32(dh);
+        memset(yb, 0, Q6_K_BYTES);
+        int8_t *scales = (int8_t *)(yb + 192);
+        for (int g = 0; g < 16; g++) {
+            int s = df > 0.0f ? (int)roundf(scale[g] / df) : 0;
+            scales[g] = (int8_t)(s > 127 ? 127 : s);
+        }
+        for (int e = 0; e < QK_K; e++) {
+            int qb, qhi, hb, hs, si;
+            q6k_index(e, &qb, &qhi, &hb, &hs, &si);
+            const float ds = df * (float)scales[si];
+            int v = 0;
+            if (ds > 0.0f) {
+                v = (int)roundf(xb[e] / ds);
+                v = v < -32 ? -32 : (v > 31 ? 31 : v);
+            }
+            const int u = v + 32;
+            yb[qb] |= (uint8_t)((u & 0x0f) << (qhi ? 4 : 0));
+            yb[128 + hb] |= (uint8_t)((u >> 4) << hs);
+        }
+        wr_u16(yb + 208, dh);
+    }
+}
+
+/* Value = (d*sc)*(q - 32). */
+void oracle_dequantize_row_q6_k(const uint8_t *y, float *x, int64_t k) {
+    const int64_t nb = k / QK_K;
+    for (int64_t i = 0; i < nb; i++) {
+        const uint8_t *yb = y + i * Q6_K_BYTES;
+        const float d = oracle_f16_to_f32(rd_u16(yb + 208));
+        const int8_t *scales = (const int8_t *)(yb + 192);
+        for (int e = 0; e < QK_K; e++) {
+            int qb, qhi, hb, hs, si;
+            q6k_index(e, &qb, &qhi, &hb, &hs, &si);
+            const int lo = qhi ? (yb[qb] >> 4) : (yb[qb] & 0x0f);
+            const int q = (lo | (((yb[128 + hb] >> hs) & 3) << 4)) - 32;
+            x[i * QK_K + e] = (d * (float)scales[si]) * (float)q;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Row-wise helpers over a [rows, k] matrix (ggml layout: row r at r*row_bytes) */
 /* ------------------------------------------------------------------------ */
 /* dtype codes follow feml-core/src/dtype.rs:14-35 discriminants. */
@@ -291,6 +475,8 @@ void oracle_dequantize_row_q4_k(const uint8_t *y, float *x, int64_t k) {
 #define DT_Q4_0 7
 #define DT_Q8_0 11
 #define DT_Q4_K 15
+#define DT_Q5_K 16
+#define DT_Q6_K 17
 
 int64_t oracle_row_bytes(int dtype, int64_t k) {
     switch (dtype) {
@@ -298,6 +484,8 @@ int64_t oracle_row_bytes(int dtype, int64_t k) {
     case DT_Q8_0: return (k / 32) * Q8_0_BYTES;
     case DT_Q4_0: return (k / 32) * Q4_0_BYTES;
     case DT_Q4_K: return (k / 256) * Q4_K_BYTES;
+    case DT_Q5_K: return (k / 256) * Q5_K_BYTES;
+    case DT_Q6_K: return (k / 256) * Q6_K_BYTES;
     default: return -1;
     }
 }
@@ -313,6 +501,8 @@ int oracle_quantize_rows(int dtype, const float *x, uint8_t *y, int64_t rows, in
         case DT_Q8_0: oracle_quantize_row_q8_0(xr, yr, k); break;
         case DT_Q4_0: oracle_quantize_row_q4_0(xr, yr, k); break;
         case DT_Q4_K: oracle_quantize_row_q4_k(xr, yr, k); break;
+        case DT_Q5_K: oracle_quantize_row_q5_k(xr, yr, k); break;
+        case DT_Q6_K: oracle_quantize_row_q6_k(xr, yr, k); break;
         }
     }
     return 0;
@@ -329,6 +519,8 @@ int oracle_dequantize_rows(int dtype, const uint8_t *y, float *x, int64_t rows, 
         case DT_Q8_0: oracle_dequantize_row_q8_0(yr, xr, k); break;
         case DT_Q4_0: oracle_dequantize_row_q4_0(yr, xr, k); break;
         case DT_Q4_K: oracle_dequantize_row_q4_k(yr, xr, k); break;
+        case DT_Q5_K: oracle_dequantize_row_q5_k(yr, xr, k); break;
+        case DT_Q6_K: oracle_dequantize_row_q6_k(yr, xr, k); break;
         }
     }
     return 0;

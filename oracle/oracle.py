@@ -10,7 +10,7 @@ import numpy as np
 
 from . import build_oracle
 
-DT_F32, DT_Q4_0, DT_Q8_0, DT_Q4_K = 5, 7, 11, 15
+DT_F32, DT_Q4_0, DT_Q8_0, DT_Q4_K, DT_Q5_K, DT_Q6_K = 5, 7, 11, 15, 16, 17
 
 _lib = None
 

@@ -10,8 +10,8 @@ independent implementation of the formats:
    x*(1/d), one huge value, constant block, alternating-sign maxima);
  - q8_0, q4_0: gguf.quants.quantize(x, ...) bytes, and *_deq their
    gguf.quants.dequantize values;
- - q4_k: seeded Q4_K blocks with finite f16 d / dmin and random 6-bit
-   scales, mins and nibbles; q4_k_deq: gguf.quants.dequantize.
+ - q4_k, q5_k, q6_k: seeded blocks with finite f16 scales and random
+   packed scales, mins, high bits and nibbles; *_deq: gguf.quants.dequantize.
 """
 import os
 
@@ -41,13 +41,14 @@ def main():
         out[name] = q
         out[name + "_deq"] = quants.dequantize(q, t).astype(np.float32)
     rows, nsb = 8, 2
-    blk = np.zeros((rows, nsb, 144), dtype=np.uint8)
-    d = (rng.uniform(0.5, 2.0, (rows, nsb, 2)) * 1e-3).astype(np.float16)
-    blk[:, :, 0:4] = d.view(np.uint8).reshape(rows, nsb, 4)
-    blk[:, :, 4:144] = rng.integers(0, 256, (rows, nsb, 140), dtype=np.uint8)
-    q4k = blk.reshape(rows, nsb * 144)
-    out["q4_k"] = q4k
-    out["q4_k_deq"] = quants.dequantize(q4k, T.Q4_K).astype(np.float32)
+    for name, t, nbytes, d_at, nd in (("q4_k", T.Q4_K, 144, 0, 2), ("q5_k", T.Q5_K, 176, 0, 2),
+                                      ("q6_k", T.Q6_K, 210, 208, 1)):
+        blk = rng.integers(0, 256, (rows, nsb, nbytes), dtype=np.uint8)
+        d = (rng.uniform(0.5, 2.0, (rows, nsb, nd)) * 1e-3).astype(np.float16)
+        blk[:, :, d_at:d_at + 2 * nd] = d.view(np.uint8).reshape(rows, nsb, 2 * nd)
+        q = blk.reshape(rows, nsb * nbytes)
+        out[name] = q
+        out[name + "_deq"] = quants.dequantize(q, t).astype(np.float32)
     np.savez_compressed(os.path.join(HERE, "ggufpy_vectors.npz"), **out)
     print("wrote ggufpy_vectors.npz")
 

@@ -168,10 +168,11 @@ def _same_blocks(got, want, x, block_bytes):
     assert np.all(same_d | signed_zero)
 
 
-@pytest.mark.parametrize("name,dt", [("q8_0", O.DT_Q8_0), ("q4_0", O.DT_Q4_0), ("q4_k", O.DT_Q4_K)])
+@pytest.mark.parametrize("name,dt", [("q8_0", O.DT_Q8_0), ("q4_0", O.DT_Q4_0), ("q4_k", O.DT_Q4_K),
+                                     ("q5_k", O.DT_Q5_K), ("q6_k", O.DT_Q6_K)])
 def test_oracle_matches_ggufpy_vectors(name, dt):
     gv = np.load(os.path.join(GOLD, "ggufpy_vectors.npz"))
-    if name != "q4_k":  # gguf-py has no Q4_K quantizer; its dequantizer pins the layout
+    if not name.endswith("_k"):  # gguf-py has no K-quant quantizers; its dequantizers pin the layouts
         _same_blocks(O.quantize(dt, gv["x"]), gv[name], gv["x"], 34 if name == "q8_0" else 18)
     deq = O.dequantize(dt, gv[name], gv[name + "_deq"].shape[1])
     assert np.array_equal(deq.view(np.uint32), gv[name + "_deq"].view(np.uint32))
@@ -188,9 +189,23 @@ def test_oracle_matches_ggufpy_live(seed):
         _same_blocks(O.quantize(dt, x), q, x, 34 if dt == O.DT_Q8_0 else 18)
         assert np.array_equal(O.dequantize(dt, q, 1024).view(np.uint32),
                               gguf.quants.dequantize(q, t).astype(np.float32).view(np.uint32))
-    q = O.quantize(O.DT_Q4_K, x)
-    assert np.array_equal(O.dequantize(O.DT_Q4_K, q, 1024).view(np.uint32),
-                          gguf.quants.dequantize(q, T.Q4_K).astype(np.float32).view(np.uint32))
+    for dt, t in ((O.DT_Q4_K, T.Q4_K), (O.DT_Q5_K, T.Q5_K), (O.DT_Q6_K, T.Q6_K)):
+        q = O.quantize(dt, x)
+        assert np.array_equal(O.dequantize(dt, q, 1024).view(np.uint32),
+                              gguf.quants.dequantize(q, t).astype(np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("dt,levels", [(O.DT_Q4_K, 15), (O.DT_Q5_K, 31), (O.DT_Q6_K, 31)])
+def test_k_quantizers_round_trip(dt, levels):
+    """The project's K-quant quantizers (parity-unpinned schemes) stay within
+    about one quantization step of the input, zero blocks stay zero."""
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal((8, 2048)) * 0.02).astype(np.float32)
+    x[0, :256] = 0.0
+    y = O.dequantize(dt, O.quantize(dt, x), 2048)
+    assert np.all(y[0, :256] == 0.0)
+    step = 2 * np.abs(x).max() / levels
+    assert np.abs(y - x).max() <= 1.5 * step
 
 
 def test_q8_0_edge_blocks():
