@@ -346,6 +346,12 @@ class B200Backend(Backend):
         _check(_L.lib().feml_b200_scratch_bytes(self._h, ctypes.byref(v)))
         return v.value
 
+    def device_allocations(self):
+        """cudaMalloc calls this backend has made (buffers and scratch)."""
+        v = ctypes.c_uint64()
+        _check(_L.lib().feml_b200_device_allocations(self._h, ctypes.byref(v)))
+        return v.value
+
     def reserve_scratch(self, n):
         _check(_L.lib().feml_b200_reserve_scratch(self._h, int(n)))
 
@@ -530,6 +536,12 @@ class GraphBuilder:
     def silu(self, x):
         out = ctypes.c_uint32()
         _check(_L.lib().fb_graph_silu(self._h, int(x), ctypes.byref(out)))
+        return out.value
+
+    def rms_norm(self, x, eps):
+        """GraphBuilder::rms_norm (feml-core/src/graph.rs:140-142)."""
+        out = ctypes.c_uint32()
+        _check(_L.lib().fb_graph_rms_norm(self._h, int(x), float(eps), ctypes.byref(out)))
         return out.value
 
     def copy(self, x):

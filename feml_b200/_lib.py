@@ -90,6 +90,7 @@ SIGNATURES = [
     ("feml_b200_stream", c_int, [vp, ctypes.POINTER(vp)]),
     ("feml_b200_scratch_bytes", c_int, [vp, ctypes.POINTER(c_u64)]),
     ("feml_b200_reserve_scratch", c_int, [vp, c_u64]),
+    ("feml_b200_device_allocations", c_int, [vp, ctypes.POINTER(c_u64)]),
     ("fb_graph_new", c_int, [ctypes.POINTER(vp)]),
     ("fb_graph_free", None, [vp]),
     ("fb_graph_input", c_int, [vp, cp, c_i32, ctypes.POINTER(c_i64), c_i32, ctypes.POINTER(c_u32)]),
@@ -98,6 +99,7 @@ SIGNATURES = [
     ("fb_graph_mul", c_int, [vp, c_u32, c_u32, ctypes.POINTER(c_u32)]),
     ("fb_graph_add", c_int, [vp, c_u32, c_u32, ctypes.POINTER(c_u32)]),
     ("fb_graph_silu", c_int, [vp, c_u32, ctypes.POINTER(c_u32)]),
+    ("fb_graph_rms_norm", c_int, [vp, c_u32, ctypes.c_float, ctypes.POINTER(c_u32)]),
     ("fb_graph_copy", c_int, [vp, c_u32, ctypes.POINTER(c_u32)]),
     ("fb_graph_mul_mat", c_int, [vp, c_u32, c_u32, ctypes.POINTER(c_u32)]),
     ("fb_graph_mul_mat_id", c_int, [vp, c_u32, c_u32, c_u32, c_u32, ctypes.POINTER(c_u32)]),

@@ -54,7 +54,10 @@ int cuda_fail(cudaError_t e, const char *what) {
     return set_error(FB_ERR_CUDA, "B200 backend error: %s: %s", what, cudaGetErrorString(e));
 }
 
+// mul_mat_id weights: the types the grouped GEMMs tile; mul_mat also takes
+// Q5_K (decode GEMV, column groups of up to eight for wider N).
 bool is_weight_dtype(int32_t d) { return d == FB_F32 || d == FB_Q8_0 || d == FB_Q4_0 || d == FB_Q4_K; }
+bool is_mul_mat_dtype(int32_t d) { return is_weight_dtype(d) || d == FB_Q5_K; }
 
 uint64_t align256(uint64_t v) { return (v + 255) / 256 * 256; }
 
@@ -78,12 +81,15 @@ uint64_t mul_mat_ws(int32_t wtype, int64_t K, int64_t M, int64_t N) {
     return tc_shape(wtype, K, M, N) ? std::max<uint64_t>(planar, fbk::xq16_bytes(K, N, M, false)) : planar;
 }
 
+// norm_eps non-null: x is rms-normalized (that eps) inside the decode GEMV
+// (graph_compute passes it only for shapes where that path runs).
 int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
-               int64_t K, int64_t M, int64_t N, void *ws, uint64_t ws_bytes, int32_t *status, cudaStream_t s) {
+               int64_t K, int64_t M, int64_t N, void *ws, uint64_t ws_bytes, int32_t *status, cudaStream_t s,
+               const float *norm_eps = nullptr) {
     if (K < 0 || M < 0 || N < 0) return set_error(FB_ERR_INVALID, "mul_mat: negative dimension");
     if (M == 0 || N == 0) return FB_OK;
     if (!w || !x || !y) return set_error(FB_ERR_INVALID, "mul_mat: null operand");
-    if (!is_weight_dtype(wtype)) return set_error(FB_ERR_UNSUPPORTED, "mul_mat: weight dtype %d not supported", wtype);
+    if (!is_mul_mat_dtype(wtype)) return set_error(FB_ERR_UNSUPPORTED, "mul_mat: weight dtype %d not supported", wtype);
     const fb::DTypeTraits *t = fb::dtype_traits(wtype);
     if (K % t->block_size) return set_error(FB_ERR_SHAPE, "mul_mat: K %ld not a multiple of %ld", (long)K, (long)t->block_size);
     if (wtype == FB_F32) return fbk::launch_gemm_f32(w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, status, s);
@@ -93,7 +99,10 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
     if (need > ws_bytes)
         return set_error(FB_ERR_INVALID, "mul_mat: workspace of %lu bytes needed, %lu given", (unsigned long)need,
                          (unsigned long)ws_bytes);
-    if (need == 0) return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, nullptr, status, s, true);
+    if (need == 0)
+        return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, nullptr, status, s, true, nullptr,
+                                norm_eps);
+    if (norm_eps) return set_error(FB_ERR_UNSUPPORTED, "mul_mat: fused rms_norm needs the decode GEMV");
     if (tc_shape(wtype, K, M, N) && fbk::gemm_tc_supported(wtype, K, M, N, w, w_nb1) &&
         ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0) {
         const fbk::XQ16 xa = fbk::xq16_carve(ws, K, N);
@@ -233,6 +242,7 @@ struct fb_backend {
     uint64_t scratch_bytes = 0;
     int32_t *status_dev = nullptr;
     int32_t *status_host = nullptr;  // pinned
+    uint64_t device_allocs = 0;      // cudaMalloc calls made for buffers and scratch
 };
 
 namespace {
@@ -272,6 +282,7 @@ int grow_scratch(fb_backend *b, uint64_t bytes) {
     b->scratch = nullptr;
     b->scratch_bytes = 0;
     e = cudaMalloc(&b->scratch, bytes);
+    b->device_allocs++;
     if (e != cudaSuccess) {
         b->scratch = nullptr;
         return cuda_fail(e, "scratch alloc");
@@ -315,15 +326,93 @@ bool overlap(const DevTensor &a, const DevTensor &c) {
     return ao < co + c.nbytes && co < ao + a.nbytes;
 }
 
+// ---- rms_norm and its fusion into mul_mat ----------------------------------
+float rms_eps(const fb_plan_tensor &t) {
+    float eps;
+    std::memcpy(&eps, &t.op_params[0], 4);
+    return eps;
+}
+
+bool ranges_overlap(const fb_plan *plan, const fb_plan_tensor &a, const fb_plan_tensor &c) {
+    if (a.buffer != c.buffer || a.buffer < 0) return false;
+    uint64_t an = 0, cn = 0;
+    if (fb_layout_nbytes(a.dtype, a.ne, a.nb, &an) || fb_layout_nbytes(c.dtype, c.ne, c.nb, &cn)) return true;
+    return a.offset < c.offset + cn && c.offset < a.offset + an;
+}
+
+// An rms_norm node runs inside the decode GEMV of its consumers instead of
+// on its own when nothing else can see its output: it is not a graph
+// output, every reader is a mul_mat taking it as activations whose shape
+// runs on the in-kernel-quantizing GEMV (quantized weights, N*K <= 16384,
+// K >= 512), those readers follow it directly in the node order, and none
+// of their outputs overlaps the normalized tensor's source (the planner may
+// reuse that memory once the rms_norm would have consumed it).
+bool rms_fused(const fb_plan *plan, int64_t ri) {
+    if (ri < 0 || ri >= plan->n_tensors) return false;
+    const fb_plan_tensor &r = plan->tensors[ri];
+    if (r.op != FB_OP_RMS_NORM || (r.flags & FB_FLAG_OUTPUT) || r.n_srcs != 1 || r.dtype != FB_F32) return false;
+    if (r.srcs[0] < 0 || r.srcs[0] >= plan->n_tensors) return false;
+    const fb_plan_tensor &x = plan->tensors[r.srcs[0]];
+    if (x.dtype != FB_F32 || x.nb[0] != 4 || x.ne[2] != 1 || x.ne[3] != 1) return false;
+    const int64_t K = x.ne[0], N = x.ne[1];
+    if (K < 512 || N < 1 || !fbk::gemv_fused_ok(K, N)) return false;
+    int64_t consumers = 0;
+    for (int64_t i = 0; i < plan->n_tensors; i++) {
+        const fb_plan_tensor &t = plan->tensors[i];
+        for (int k = 0; k < t.n_srcs && k < FB_MAX_SRC; k++) {
+            if (t.srcs[k] != ri) continue;
+            if (t.op != FB_OP_MUL_MAT || k != 1 || t.srcs[0] < 0 || t.srcs[0] >= plan->n_tensors) return false;
+            const fb_plan_tensor &w = plan->tensors[t.srcs[0]];
+            if (w.dtype == FB_F32 || !fbk::gemv_supported(w.dtype, K, N) || ranges_overlap(plan, x, t)) return false;
+            consumers++;
+        }
+    }
+    if (consumers == 0) return false;
+    int64_t pos = -1;
+    for (int64_t i = 0; i < plan->n_nodes; i++)
+        if (plan->nodes[i] == ri) pos = i;
+    if (pos < 0) return false;
+    int64_t seen = 0;
+    for (int64_t i = pos + 1; i < plan->n_nodes && seen < consumers; i++) {
+        const int64_t ti = plan->nodes[i];
+        if (ti < 0 || ti >= plan->n_tensors) return false;
+        const fb_plan_tensor &t = plan->tensors[ti];
+        if (t.op != FB_OP_MUL_MAT || t.n_srcs < 2 || t.srcs[1] != ri) return false;
+        seen++;
+    }
+    return seen == consumers;
+}
+
+int compute_rms_norm(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
+    if (node.n_srcs != 1) return set_error(FB_ERR_INVALID, "rms_norm: expected 1 source");
+    DevTensor X, Y;
+    int rc;
+    if ((rc = resolve(b, plan, node.srcs[0], &X)) || (rc = resolve(b, plan, &node - plan->tensors, &Y))) return rc;
+    const fb_plan_tensor &x = *X.t, &y = *Y.t;
+    if (x.dtype != FB_F32 || y.dtype != FB_F32) return set_error(FB_ERR_UNSUPPORTED, "B200: rms_norm needs f32");
+    for (int d = 0; d < 4; d++)
+        if (x.ne[d] != y.ne[d]) return set_error(FB_ERR_SHAPE, "shape error: rms_norm: dst shape differs from src");
+    // in place (y == x) is allowed (op.rs:98-110); any other overlap is not
+    if (overlap(X, Y) && X.ptr != Y.ptr) return set_error(FB_ERR_INVALID, "B200: rms_norm dst partly aliases src");
+    return fbk::launch_rms_norm(X.ptr, x.nb, Y.ptr, y.nb, y.ne, rms_eps(node), b->stream);
+}
+
 int compute_mul_mat(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
     if (node.n_srcs != 2) return set_error(FB_ERR_INVALID, "mul_mat: expected 2 sources");
     DevTensor A, B, C;
     int rc;
-    if ((rc = resolve(b, plan, node.srcs[0], &A)) || (rc = resolve(b, plan, node.srcs[1], &B))) return rc;
+    // activations from a fused rms_norm: read its source and normalize in the GEMV
+    const int64_t act = node.srcs[1];
+    const bool fused_norm = rms_fused(plan, act);
+    float eps = 0.0f;
+    if (fused_norm) eps = rms_eps(plan->tensors[act]);
+    if ((rc = resolve(b, plan, node.srcs[0], &A)) ||
+        (rc = resolve(b, plan, fused_norm ? plan->tensors[act].srcs[0] : act, &B)))
+        return rc;
     if ((rc = resolve(b, plan, &node - plan->tensors, &C))) return rc;
     if (overlap(A, C) || overlap(B, C)) return set_error(FB_ERR_INVALID, "B200: mul_mat dst aliases a source");
     const fb_plan_tensor &a = *A.t, &x = *B.t, &y = *C.t;
-    if (!is_weight_dtype(a.dtype) || x.dtype != FB_F32 || y.dtype != FB_F32)
+    if (!is_mul_mat_dtype(a.dtype) || x.dtype != FB_F32 || y.dtype != FB_F32)
         return set_error(FB_ERR_UNSUPPORTED, "B200: mul_mat dtypes not supported");
     const int64_t K = a.ne[0], M = a.ne[1], N = x.ne[1];
     if (x.ne[0] != K || y.ne[0] != M || y.ne[1] != N)
@@ -334,7 +423,7 @@ int compute_mul_mat(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &no
     if (a.nb[0] != (uint64_t)fb::dtype_traits(a.dtype)->type_size || x.nb[0] != 4 || y.nb[0] != 4)
         return set_error(FB_ERR_UNSUPPORTED, "B200: mul_mat needs contiguous rows");
     return do_mul_mat(a.dtype, A.ptr, a.nb[1], B.ptr, x.nb[1], C.ptr, y.nb[1], K, M, N, b->scratch, b->scratch_bytes,
-                      b->status_dev, b->stream);
+                      b->status_dev, b->stream, fused_norm ? &eps : nullptr);
 }
 
 int compute_mul_mat_id(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
@@ -500,6 +589,7 @@ int feml_b200_create_buffer(fb_backend *b, uint64_t size, int32_t usage, uint32_
     }
     void *p = nullptr;
     cudaError_t e = cudaMalloc(&p, size + kPad);
+    b->device_allocs++;
     if (e != cudaSuccess) return cuda_fail(e, "create_buffer");
     e = cudaMemsetAsync(p, 0, size + kPad, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
@@ -608,9 +698,11 @@ int feml_b200_supports_op(fb_backend *, int32_t op, const int32_t *dt, int32_t n
     case FB_OP_VIEW:
         return 1;  // zero-copy: nothing to execute
     case FB_OP_MUL_MAT:
-        return n == 2 && dt && is_weight_dtype(dt[0]) && dt[1] == FB_F32;
+        return n == 2 && dt && is_mul_mat_dtype(dt[0]) && dt[1] == FB_F32;
     case FB_OP_MUL_MAT_ID:
         return n == 3 && dt && is_weight_dtype(dt[0]) && dt[1] == FB_F32 && dt[2] == FB_I32;
+    case FB_OP_RMS_NORM:
+        return n == 1 && dt && dt[0] == FB_F32;
     default:
         return 0;
     }
@@ -623,7 +715,7 @@ uint64_t node_scratch(const fb_plan *plan, const fb_plan_tensor &node) {
         return &plan->tensors[node.srcs[k]];
     };
     const fb_plan_tensor *w = src(0), *x = src(1);
-    if (!w || !x || !is_weight_dtype(w->dtype)) return 0;
+    if (!w || !x || !is_mul_mat_dtype(w->dtype)) return 0;
     const int64_t K = w->ne[0], M = w->ne[1], N = x->ne[1];
     if (K <= 0 || M <= 0 || N <= 0 || K > (int64_t(1) << 31) || N > (int64_t(1) << 31)) return 0;
     if (node.op == FB_OP_MUL_MAT) return mul_mat_ws(w->dtype, K, M, N);
@@ -662,6 +754,9 @@ int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
             break;
         case FB_OP_MUL_MAT_ID:
             rc = compute_mul_mat_id(b, plan, node);
+            break;
+        case FB_OP_RMS_NORM:
+            rc = rms_fused(plan, ti) ? FB_OK : compute_rms_norm(b, plan, node);
             break;
         default:
             rc = set_error(FB_ERR_UNSUPPORTED, "B200: op %s not implemented", fb::op_name(node.op));
@@ -707,6 +802,13 @@ int feml_b200_scratch_bytes(fb_backend *b, uint64_t *bytes) {
     if (!b || !bytes) return set_error(FB_ERR_INVALID, "scratch_bytes: null argument");
     std::lock_guard<std::mutex> lk(b->mu);
     *bytes = b->scratch_bytes;
+    return FB_OK;
+}
+
+int feml_b200_device_allocations(fb_backend *b, uint64_t *count) {
+    if (!b || !count) return set_error(FB_ERR_INVALID, "device_allocations: null argument");
+    std::lock_guard<std::mutex> lk(b->mu);
+    *count = b->device_allocs;
     return FB_OK;
 }
 

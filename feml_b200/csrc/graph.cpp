@@ -97,9 +97,11 @@ static bool can_inplace(int32_t op) {  // op.rs:98-110
     }
 }
 
-static bool is_matmul_weight_dtype(int32_t d) {
+static bool is_matmul_id_weight_dtype(int32_t d) {
     return d == FB_F32 || d == FB_Q8_0 || d == FB_Q4_0 || d == FB_Q4_K;
 }
+
+static bool is_matmul_weight_dtype(int32_t d) { return is_matmul_id_weight_dtype(d) || d == FB_Q5_K; }
 
 // ---------------------------------------------------------------------------
 // Planner (planner.rs)
@@ -385,6 +387,17 @@ struct Graph {
         return node(op, name, mx->dtype, mx->layout.shape, {x}, id);
     }
 
+    // graph.rs:140-142 (unary; Op::RmsNorm { eps }, op.rs:26): eps travels in
+    // op_params[0] as f32 bits.
+    int rms_norm(uint32_t x, float eps, uint32_t *id) {
+        int rc = unary(FB_OP_RMS_NORM, "rms_norm", x, id);
+        if (rc) return rc;
+        uint32_t bits;
+        std::memcpy(&bits, &eps, 4);
+        get(*id)->op_params[0] = bits;
+        return FB_OK;
+    }
+
     // graph.rs:89-108
     int view(uint32_t src, uint64_t offset, const int64_t *dims, int32_t rank, uint32_t *id) {
         TensorMeta *ms = get(src);
@@ -412,7 +425,7 @@ struct Graph {
     }
 
     // graph.rs:122-138, relaxed for quantized weights: src0 in {F32, Q8_0,
-    // Q4_0, Q4_K} with src1 F32 (the dtype-equality rule of pair() does not
+    // Q4_0, Q4_K, Q5_K} with src1 F32 (the dtype-equality rule of pair() does not
     // apply), output F32 instead of src0's dtype, ne0 % block_size(src0) == 0.
     int mul_mat(uint32_t a, uint32_t b, uint32_t *id) {
         TensorMeta *ma = get(a);
@@ -448,7 +461,7 @@ struct Graph {
         if (!mx) return set_error(FB_ERR_INVALID, "mul_mat_id: unknown x");
         TensorMeta *mi = get(ids);
         if (!mi) return set_error(FB_ERR_INVALID, "mul_mat_id: unknown ids");
-        if (!is_matmul_weight_dtype(mw->dtype))
+        if (!is_matmul_id_weight_dtype(mw->dtype))
             return set_error(FB_ERR_UNSUPPORTED, "dtype %s not supported for op mul_mat_id", dtype_traits(mw->dtype)->name);
         if (mx->dtype != FB_F32)
             return set_error(FB_ERR_UNSUPPORTED, "dtype %s not supported for op mul_mat_id", dtype_traits(mx->dtype)->name);
@@ -614,6 +627,12 @@ int fb_graph_add(fb_graph *g, uint32_t a, uint32_t b, uint32_t *id) {
 int fb_graph_silu(fb_graph *g, uint32_t x, uint32_t *id) {
     GRAPH_GUARD(g)
     return g->g.unary(FB_OP_SILU, "silu", x, id);
+    GRAPH_END
+}
+
+int fb_graph_rms_norm(fb_graph *g, uint32_t x, float eps, uint32_t *id) {
+    GRAPH_GUARD(g)
+    return g->g.rms_norm(x, eps, id);
     GRAPH_END
 }
 

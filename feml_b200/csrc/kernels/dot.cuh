@@ -264,6 +264,43 @@ __device__ __forceinline__ void q4k_pair_dot_x(const uint8_t *sb, int g, const u
     dmm1 = w.dmm1;
 }
 
+// Q5_K sub-block pair g of the super-block at `sb` (16-byte aligned; d, dmin
+// and the 12 scale bytes as in Q4_K, then qh[32], then the nibbles): value
+// = nibble + 16 * fifth bit, the fifth bit of element l of sub-block j being
+// bit j of qh[l]. Integer sums s0 (sub-block 2g), s1 (2g+1) and scale terms.
+__device__ __forceinline__ void q5k_pair_dot(const uint8_t *sb, int g, const uint32_t *xa, const uint32_t *xb,
+                                             int &s0, int &s1, float &dsc0, float &dmm0, float &dsc1, float &dmm1) {
+    const uint4 h = *reinterpret_cast<const uint4 *>(sb);
+    const uint4 qh0 = *reinterpret_cast<const uint4 *>(sb + 16), qh1 = *reinterpret_cast<const uint4 *>(sb + 32);
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(sb + 48 + 32 * g);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(sb + 64 + 32 * g);
+    const uint4 a0 = *reinterpret_cast<const uint4 *>(xa), a1 = *reinterpret_cast<const uint4 *>(xa + 4);
+    const uint4 b0 = *reinterpret_cast<const uint4 *>(xb), b1 = *reinterpret_cast<const uint4 *>(xb + 4);
+    q4k_pair_sums(q0, q1, a0, a1, b0, b1, s0, s1);
+    const uint32_t m = 0x01010101u;
+    const int ea = 2 * g, eb = 2 * g + 1;  // bit of qh for sub-blocks 2g and 2g+1
+    int h0 = 0, h1 = 0;
+    h0 = dp4a_us((qh0.x >> ea) & m, a0.x, h0);
+    h1 = dp4a_us((qh0.x >> eb) & m, b0.x, h1);
+    h0 = dp4a_us((qh0.y >> ea) & m, a0.y, h0);
+    h1 = dp4a_us((qh0.y >> eb) & m, b0.y, h1);
+    h0 = dp4a_us((qh0.z >> ea) & m, a0.z, h0);
+    h1 = dp4a_us((qh0.z >> eb) & m, b0.z, h1);
+    h0 = dp4a_us((qh0.w >> ea) & m, a0.w, h0);
+    h1 = dp4a_us((qh0.w >> eb) & m, b0.w, h1);
+    h0 = dp4a_us((qh1.x >> ea) & m, a1.x, h0);
+    h1 = dp4a_us((qh1.x >> eb) & m, b1.x, h1);
+    h0 = dp4a_us((qh1.y >> ea) & m, a1.y, h0);
+    h1 = dp4a_us((qh1.y >> eb) & m, b1.y, h1);
+    h0 = dp4a_us((qh1.z >> ea) & m, a1.z, h0);
+    h1 = dp4a_us((qh1.z >> eb) & m, b1.z, h1);
+    h0 = dp4a_us((qh1.w >> ea) & m, a1.w, h0);
+    h1 = dp4a_us((qh1.w >> eb) & m, b1.w, h1);
+    s0 += 16 * h0;
+    s1 += 16 * h1;
+    q4k_pair_scales(h, g, dsc0, dmm0, dsc1, dmm1);
+}
+
 // The same with the activation words read from `xa` / `xb` (16-byte aligned).
 __device__ __forceinline__ void q4k_pair_dot(const uint8_t *sb, int g, const uint32_t *xa, const uint32_t *xb,
                                              int &s0, int &s1, float &dsc0, float &dmm0, float &dsc1, float &dmm1) {

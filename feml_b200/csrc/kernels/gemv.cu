@@ -66,6 +66,11 @@ struct Fmt<WT_Q4_K> {
     static constexpr int kUnitBytes = Q4_K_BYTES / 8;  // one 32-element sub-block
     static constexpr bool kShifted = false;
 };
+template <>
+struct Fmt<WT_Q5_K> {
+    static constexpr int kUnitBytes = Q5_K_BYTES / 8;
+    static constexpr bool kShifted = false;
+};
 
 struct GemvParams {
     const uint8_t *w;
@@ -84,6 +89,8 @@ struct GemvParams {
     int32_t *status;
     bool x_vec16;     // activation columns are 16-byte aligned
     bool copy_rows;   // rows not aligned for the pair loads: plain copies
+    bool norm;        // rms-normalize each activation column before quantizing it
+    float norm_eps;
     PeerOut peer;     // peer.n > 0: outputs go to every peer's buffer, then a signal
 };
 
@@ -166,7 +173,7 @@ __device__ __forceinline__ void quantize_block_quarter(const float (&v)[8], bool
         *sd_b = f16_bits_to_f32(__half_as_ushort(__float2half_rn(d)));
         *ss_b = s;
     }
-    if constexpr (WT != WT_Q4_K) {
+    if constexpr (WT == WT_Q8_0 || WT == WT_Q4_0) {
         if (even) {
             // byte stream shifted by 2 with zeros at the ends (see make_shifted)
             if constexpr (WT == WT_Q8_0) {
@@ -272,6 +279,49 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
 
     // Activations -> Q8_0 in shared memory.
     if (p.xq.qs == nullptr) {
+        // Fused rms_norm (a plan's rms_norm feeding this mul_mat): column n is
+        // scaled by 1 / sqrt(sum(x^2) / K + eps) before it is quantized; the
+        // warps' partial sums are added in warp order (deterministic). The
+        // scale area `sd` (not yet written) holds the partials (launch_gemv
+        // requires K >= 512, so it has room for 9 * NC floats); every thread
+        // keeps the NC scales in registers before quantization writes `sd`.
+        float nscale[kMaxCols];
+#pragma unroll
+        for (int n = 0; n < kMaxCols; n++) nscale[n] = 1.0f;
+        if (p.norm) {
+#pragma unroll
+            for (int n = 0; n < NC; n++) {
+                const float *xc = reinterpret_cast<const float *>(p.x + (uint64_t)n * p.x_nb1);
+                float ssq = 0.0f;
+                for (int k = threadIdx.x; k < K; k += kGemvThreads) {
+                    const float v = __ldg(xc + k);
+                    ssq = fmaf(v, v, ssq);
+                }
+                ssq = warp_sum(ssq);
+                if (lane == 0) sd[warp * NC + n] = ssq;
+            }
+            __syncthreads();
+            if (threadIdx.x < NC) {
+                float t = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kGemvWarps; w++) t += sd[w * NC + threadIdx.x];
+                sd[kGemvWarps * NC + threadIdx.x] = 1.0f / sqrtf(t / (float)K + p.norm_eps);
+            }
+            __syncthreads();
+#pragma unroll
+            for (int n = 0; n < NC; n++) nscale[n] = sd[kGemvWarps * NC + n];
+            __syncthreads();
+        }
+        auto normalize = [&](int n, float (&v)[8]) {
+            if (p.norm) {
+                float sc = nscale[0];
+#pragma unroll
+                for (int j = 1; j < NC; j++)
+                    if (n == j) sc = nscale[j];
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[i] *= sc;
+            }
+        };
         constexpr int kGroups = kGemvThreads / 4;  // 4 lanes per block
         auto block_of = [&](int base, bool &valid, int &n, int &b) {
             const int t = base + (int)(threadIdx.x >> 2);
@@ -292,6 +342,8 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
             float x0[8], x1[8];
             load_block_quarter(xptr(n0, b0), p.x_vec16, v0, x0);
             load_block_quarter(xptr(n1, b1), p.x_vec16, v1, x1);
+            normalize(n0, x0);
+            normalize(n1, x1);
             quantize_block_quarter<WT>(x0, v0, SH && !(b0 & 1), sq + n0 * K + b0 * QK,
                                        sx2 + (n0 * npair_blk + b0 / 2) * kShiftWords, sd + n0 * nbp + b0,
                                        ss + n0 * nbp + b0);
@@ -306,6 +358,7 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
                 block_of(base, valid, n, b);
                 float xv[8];
                 load_block_quarter(xptr(n, b), p.x_vec16, valid, xv);
+                normalize(n, xv);
                 quantize_block_quarter<WT>(xv, valid, SH && !(b & 1), sq + n * K + b * QK,
                                            sx2 + (n * npair_blk + b / 2) * kShiftWords, sd + n * nbp + b,
                                            ss + n * nbp + b);
@@ -480,18 +533,21 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
         const int u0 = c * p.chunk_units;
         const int nu = (int)(len / UB);
         const int np = nu / 2;  // pairs in this chunk
-        if constexpr (WT == WT_Q4_K) {
+        if constexpr (WT == WT_Q4_K || WT == WT_Q5_K) {
 #pragma unroll 2
             for (int pr = lane; pr < np; pr += 32) {
                 const int b0 = u0 + 2 * pr;  // sub-block index within the row
-                const uint8_t *sb = p0 + Q4_K_BYTES * (pr >> 2);
+                const uint8_t *sb = p0 + 8 * UB * (pr >> 2);  // its super-block
                 const int g = pr & 3;
 #pragma unroll
                 for (int n = 0; n < NC; n++) {
                     const uint32_t *xa = reinterpret_cast<const uint32_t *>(sq + n * K + b0 * QK);
                     int s0, s1;
                     float dsc0, dmm0, dsc1, dmm1;
-                    q4k_pair_dot(sb, g, xa, xa + 8, s0, s1, dsc0, dmm0, dsc1, dmm1);
+                    if constexpr (WT == WT_Q4_K)
+                        q4k_pair_dot(sb, g, xa, xa + 8, s0, s1, dsc0, dmm0, dsc1, dmm1);
+                    else
+                        q5k_pair_dot(sb, g, xa, xa + 8, s0, s1, dsc0, dmm0, dsc1, dmm1);
                     const float2 dx = *reinterpret_cast<const float2 *>(sd + n * nbp + b0);
                     const int2 xs = *reinterpret_cast<const int2 *>(ss + n * nbp + b0);
                     acc[n] += dx.x * (dsc0 * (float)s0 - dmm0 * (float)xs.x) +
@@ -957,7 +1013,7 @@ int launch_typed(const GemvParams &p, int grid, uint32_t smem, cudaStream_t s, b
 // xr: activation pairs per lane held in registers (0: read from shared memory)
 template <int WT>
 int launch_cols(int ncols, int xr, const GemvParams &p, int grid, uint32_t smem, cudaStream_t s, bool pdl) {
-    if constexpr (WT != WT_Q4_K) {
+    if constexpr (WT == WT_Q8_0 || WT == WT_Q4_0) {
         if (ncols == 1 && xr == 1) return launch_typed<WT, 1, 1>(p, grid, smem, s, pdl);
         if (ncols == 1 && xr == 2) return launch_typed<WT, 1, 2>(p, grid, smem, s, pdl);
     }
@@ -973,10 +1029,16 @@ int launch_cols(int ncols, int xr, const GemvParams &p, int grid, uint32_t smem,
     }
 }
 
-bool shifted_of(int32_t wtype) { return wtype != WT_Q4_K; }
+bool shifted_of(int32_t wtype) { return wtype == WT_Q8_0 || wtype == WT_Q4_0; }
 uint32_t unit_bytes_of(int32_t wtype) {
-    return wtype == WT_Q8_0 ? Q8_0_BYTES : (wtype == WT_Q4_0 ? Q4_0_BYTES : Q4_K_BYTES / 8);
+    switch (wtype) {
+    case WT_Q8_0: return Q8_0_BYTES;
+    case WT_Q4_0: return Q4_0_BYTES;
+    case WT_Q5_K: return Q5_K_BYTES / 8;
+    default: return Q4_K_BYTES / 8;
+    }
 }
+bool k_quant(int32_t wtype) { return wtype == WT_Q4_K || wtype == WT_Q5_K; }
 
 // The K-split path for one column of wide Q4_K rows; returns -1 (nothing
 // launched) when the shape does not fit it.
@@ -1108,9 +1170,9 @@ int launch_gemv_ks_cols(const void *w, uint64_t w_nb1, const Q8Planar &xq, void 
 }  // namespace
 
 bool gemv_supported(int32_t wtype, int64_t K, int64_t N) {
-    if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K) return false;
+    if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K && wtype != WT_Q5_K) return false;
     if (N < 1 || N > kMaxCols) return false;
-    if (K % (wtype == WT_Q4_K ? QKK : QK)) return false;
+    if (K % (k_quant(wtype) ? QKK : QK)) return false;
     // activations + two minimal stages per warp must fit
     const SmemLayout L = smem_layout((int)K, (int)N, shifted_of(wtype), 2, align16(8 * unit_bytes_of(wtype) + 32));
     return K <= (1 << 20) && L.total <= (uint32_t)kSmemLimit;
@@ -1141,8 +1203,10 @@ int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int
 
 int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
                 int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status, cudaStream_t s, bool pdl,
-                const PeerOut *peer) {
+                const PeerOut *peer, const float *norm_eps) {
     if (!gemv_supported(wtype, K, N)) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: unsupported shape");
+    if (norm_eps && (xq || peer || K < 512 || !gemv_fused_ok(K, N)))
+        return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: fused rms_norm needs in-kernel activation quantization and K >= 512");
     if (M == 0) return FB_OK;
     if ((reinterpret_cast<uintptr_t>(w) & 1) || (w_nb1 & 1))
         return fb::set_error(FB_ERR_INVALID, "gemv: weight rows must be 2-byte aligned");
@@ -1164,7 +1228,7 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     if (M > INT32_MAX) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: M too large");
 
     const bool rows16 = ((reinterpret_cast<uintptr_t>(w) | w_nb1) & 15) == 0;
-    if (wtype == WT_Q4_K && N == 1 && !xq && rows16) {
+    if (wtype == WT_Q4_K && N == 1 && !xq && rows16 && !norm_eps) {
         const int rc = launch_gemv_ks(w, w_nb1, x, y, K, M, status, s, pdl, peer);
         if (rc >= 0) return rc;  // launched, or an error; -1: not this path
     }
@@ -1196,7 +1260,7 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     const SmemLayout L = smem_layout((int)K, (int)N, sh, nstage, stage_bytes);
     if (L.total > (uint32_t)kSmemLimit) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: shared memory budget exceeded");
 
-    const int align = wtype == WT_Q4_K ? 16 : 4;
+    const int align = k_quant(wtype) ? 16 : 4;
     GemvParams p;
     p.w = static_cast<const uint8_t *>(w);
     p.w_nb1 = w_nb1;
@@ -1215,11 +1279,14 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     p.x_vec16 = ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0;
     p.peer = peer ? *peer : PeerOut{};
     p.copy_rows = ((reinterpret_cast<uintptr_t>(w) | w_nb1) % align) != 0;
+    p.norm = norm_eps != nullptr;
+    p.norm_eps = norm_eps ? *norm_eps : 0.0f;
     // whole rows per chunk and at most two pairs per lane: activations in registers
     const int xr = (N == 1 && nchunks == 1 && rows16) ? (nunits <= 64 ? 1 : (nunits <= 128 ? 2 : 0)) : 0;
     switch (wtype) {
     case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, xr, p, grid, L.total, s, pdl);
     case WT_Q4_0: return launch_cols<WT_Q4_0>((int)N, xr, p, grid, L.total, s, pdl);
+    case WT_Q5_K: return launch_cols<WT_Q5_K>((int)N, xr, p, grid, L.total, s, pdl);
     default: return launch_cols<WT_Q4_K>((int)N, xr, p, grid, L.total, s, pdl);
     }
 }

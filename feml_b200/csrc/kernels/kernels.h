@@ -50,12 +50,18 @@ struct PeerOut {
     const uint32_t *epoch;
     int n;
 };
+// With `norm_eps` (in-kernel quantization only: xq and peer null) every
+// activation column is rms-normalized with that eps before it is quantized.
 int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y,
                 uint64_t y_nb1, int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status,
-                cudaStream_t s, bool pdl, const PeerOut *peer = nullptr);
+                cudaStream_t s, bool pdl, const PeerOut *peer = nullptr, const float *norm_eps = nullptr);
 // Wait until this rank's flag reaches (epoch + 1) * n_ranks, then advance
 // the epoch (bounded; STATUS_TIMEOUT on expiry).
 int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s);
+
+// norm.cu: rms_norm along ne0 (y may alias x); ne[4], strides in bytes.
+int launch_rms_norm(const void *x, const uint64_t *xnb, void *y, const uint64_t *ynb, const int64_t *ne, float eps,
+                    cudaStream_t s);
 
 // gemm_f32.cu: F32 mul_mat on SIMT FP32 (any N), bit-exact with the
 // reference's sequential order. `status` receives STATUS_TIMEOUT if a bounded

@@ -178,6 +178,12 @@ int feml_b200_stream(fb_backend *b, void **stream);
  * graph_compute). */
 int feml_b200_scratch_bytes(fb_backend *b, uint64_t *bytes);
 int feml_b200_reserve_scratch(fb_backend *b, uint64_t bytes);
+/* Device allocations (cudaMalloc of buffers and of the scratch arena) this
+ * backend has made so far: the zero-allocation contract of graph_compute
+ * (docs/backend-guide.md:22; the reference checks it with a counting global
+ * allocator, feml-cpu/tests/cpu_integration.rs:11-34,230-251) is observable
+ * as this count staying unchanged across repeated graph_compute calls. */
+int feml_b200_device_allocations(fb_backend *b, uint64_t *count);
 
 /* ======================================================================== */
 /* 2. Graph builder / planner mirror (C++ restatement of feml-core's        */
@@ -199,6 +205,9 @@ int fb_graph_view(fb_graph *g, uint32_t src, uint64_t offset, const int64_t *dim
 int fb_graph_mul(fb_graph *g, uint32_t a, uint32_t b, uint32_t *id);
 int fb_graph_add(fb_graph *g, uint32_t a, uint32_t b, uint32_t *id);
 int fb_graph_silu(fb_graph *g, uint32_t x, uint32_t *id);
+/* GraphBuilder::rms_norm (graph.rs:140-142): y = x / sqrt(mean(x^2) + eps)
+ * along ne0; eps in op_params[0] (f32 bits). */
+int fb_graph_rms_norm(fb_graph *g, uint32_t x, float eps, uint32_t *id);
 int fb_graph_copy(fb_graph *g, uint32_t x, uint32_t *id);
 /* GraphBuilder::mul_mat (graph.rs:122-138), relaxed: src0 in {F32, Q8_0,
  * Q4_0, Q4_K}, src1 F32, output F32 [ne1(a), ne1(b)], ne0(a) % block == 0. */

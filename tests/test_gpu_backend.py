@@ -165,3 +165,39 @@ def test_mul_mat_rejects_aliasing_dst(b200):
         b200.graph_compute(plan)
     assert "aliases" in str(e.value)
     plan.release(b200)
+
+
+@pytest.mark.parametrize("dt,K,M,N", [(DType.Q8_0, 4096, 512, 1), (DType.Q4_0, 4096, 1024, 64),
+                                      (DType.Q4_K, 14336, 256, 8), (DType.F32, 512, 64, 32)])
+def test_second_graph_compute_allocates_nothing(b200, dt, K, M, N):
+    """The zero-allocation contract of graph_compute (docs/backend-guide.md:22,
+    checked in feml-cpu/tests/cpu_integration.rs:230-251 with a counting
+    allocator): after a plan's first graph_compute, further calls make no
+    device allocation."""
+    rng = np.random.default_rng(K + N)
+    w = (rng.standard_normal((M, K)) * 0.02).astype(np.float32)
+    wb = w if dt == DType.F32 else O.quantize({DType.Q8_0: O.DT_Q8_0, DType.Q4_0: O.DT_Q4_0,
+                                                DType.Q4_K: O.DT_Q4_K}[dt], w)
+    g = GraphBuilder()
+    wi = g.weight("w", dt, [K, M])
+    xi = g.input("x", DType.F32, [K, N])
+    o = g.mul_mat(wi, xi)
+    g.mark_output(o)
+    plan = g.compile(b200)
+    try:
+        plan.write_tensor(b200, wi, wb)
+        plan.write_tensor(b200, xi, rng.standard_normal((N, K)).astype(np.float32))
+        b200.graph_compute(plan)
+        b200.synchronize()
+        first = np.empty((N, M), np.float32)
+        plan.read_tensor(b200, o, first)
+        before = b200.device_allocations()
+        for _ in range(3):
+            b200.graph_compute(plan)
+        b200.synchronize()
+        assert b200.device_allocations() == before
+        again = np.empty((N, M), np.float32)
+        plan.read_tensor(b200, o, again)
+        assert np.array_equal(first, again)
+    finally:
+        plan.release(b200)

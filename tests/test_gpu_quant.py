@@ -155,6 +155,24 @@ def test_q4_k_wide_rows_few_columns_padded_stride(b200):
     assert np.isnan(got[:, M:]).all()
 
 
+@pytest.mark.parametrize("K,M,N", [(256, 7, 1), (4096, 300, 1), (14336, 64, 1), (1024, 130, 3), (4096, 100, 8),
+                                   (2048, 70, 12), (512, 33, 33)])
+def test_mul_mat_q5_k_matches_oracle(b200, K, M, N):
+    """Q5_K weights (block format pinned to gguf-py's dequantizer) through
+    the graph path: the decode GEMV for N <= 8 (fused or planar activation
+    quantization), column groups of eight beyond."""
+    rng = np.random.default_rng(K + 3 * M + N)
+    wq = O.quantize(O.DT_Q5_K, weights(rng, M, K))
+    x = _inputs(K + 2 * N, N, K)
+    got = run_mul_mat(b200, DType.Q5_K, wq, x, K, M)
+    ok, err = tol_ok(got, O.mul_mat_quant_ref(O.DT_Q5_K, wq, x, K))
+    assert ok, f"max abs err {err}"
+    wt, xt = torch.from_numpy(wq).cuda(), torch.from_numpy(x).cuda()
+    a, b = ops.mul_mat(DType.Q5_K, wt, xt, K), ops.mul_mat(DType.Q5_K, wt, xt, K)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and np.array_equal(a.cpu().numpy(), got)
+
+
 def test_q4_k_wide_rows_padded_stride(b200):
     """Row stride larger than the row (16-byte multiple): the 2D tensor map
     walks rows by the stride, not the row size."""

@@ -411,15 +411,38 @@ def test_b200_registrar_without_device_is_empty():
             F.B200Backend.open(0)
 
 
+def test_rms_norm_builder():
+    """graph.rs:140-142: unary, same shape and dtype as x; eps travels in
+    op_params[0] as f32 bits; rms_norm may run in place (op.rs:98-110)."""
+    import struct
+    g = F.GraphBuilder()
+    x = g.input("x", DType.F32, [4096, 3])
+    r = g.rms_norm(x, 1e-5)
+    w = g.weight("w", DType.Q8_0, [4096, 8])
+    y = g.mul_mat(w, r)
+    g.mark_output(y)
+    plan = g.compile(DummyBackend())
+    t = plan.find(r)
+    assert t.op == Op.RMS_NORM and t.dtype == DType.F32 and t.shape[:2] == [4096, 3]
+    assert t.op_params[0] == struct.unpack("<I", struct.pack("<f", 1e-5))[0]
+    assert t.srcs == [plan.tensors.index(plan.find(x))]
+    assert plan.find(y).srcs[1] == plan.tensors.index(t)
+    assert F.B200Device(0).supports_op(Op.RMS_NORM, [DType.F32])
+    assert not F.B200Device(0).supports_op(Op.RMS_NORM, [DType.F16])
+
+
 def test_supports_op_matrix():
     dev = F.B200Device(0)
     for d in (DType.F32, DType.Q8_0, DType.Q4_0, DType.Q4_K):
         assert dev.supports_op(Op.MUL_MAT, [d, DType.F32])
         assert dev.supports_op(Op.MUL_MAT_ID, [d, DType.F32, DType.I32])
     assert not dev.supports_op(Op.MUL_MAT, [DType.Q8_0, DType.Q8_0])
-    assert not dev.supports_op(Op.MUL_MAT, [DType.Q5_K, DType.F32])
+    # Q5_K: mul_mat (decode GEMV) only; Q6_K not yet
+    assert dev.supports_op(Op.MUL_MAT, [DType.Q5_K, DType.F32])
+    assert not dev.supports_op(Op.MUL_MAT_ID, [DType.Q5_K, DType.F32, DType.I32])
+    assert not dev.supports_op(Op.MUL_MAT, [DType.Q6_K, DType.F32])
     assert not dev.supports_op(Op.MUL, [DType.F32, DType.F32])
-    assert not dev.supports_op(Op.RMS_NORM, [DType.F32])
+    assert dev.supports_op(Op.RMS_NORM, [DType.F32])
 
 
 # ---- C ABI ------------------------------------------------------------------
