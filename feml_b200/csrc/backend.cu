@@ -55,9 +55,9 @@ int cuda_fail(cudaError_t e, const char *what) {
 }
 
 // mul_mat_id weights: the types the grouped GEMMs tile; mul_mat also takes
-// Q5_K (decode GEMV, column groups of up to eight for wider N).
+// Q5_K and Q6_K (decode GEMV, column groups of up to eight for wider N).
 bool is_weight_dtype(int32_t d) { return d == FB_F32 || d == FB_Q8_0 || d == FB_Q4_0 || d == FB_Q4_K; }
-bool is_mul_mat_dtype(int32_t d) { return is_weight_dtype(d) || d == FB_Q5_K; }
+bool is_mul_mat_dtype(int32_t d) { return is_weight_dtype(d) || d == FB_Q5_K || d == FB_Q6_K; }
 
 uint64_t align256(uint64_t v) { return (v + 255) / 256 * 256; }
 
@@ -243,7 +243,16 @@ struct fb_backend {
     int32_t *status_dev = nullptr;
     int32_t *status_host = nullptr;  // pinned
     uint64_t device_allocs = 0;      // cudaMalloc calls made for buffers and scratch
+    uint8_t *stage = nullptr;        // pinned staging area of small writes
+    cudaEvent_t stage_free = nullptr;  // recorded after the last staged copy
 };
+
+// Writes up to this size are copied into the pinned staging area and sent
+// to the device by an asynchronous copy on the backend stream, so write()
+// returns without a stream synchronize (the caller's bytes are already
+// copied, and every later use of the buffer is ordered after the copy on the
+// same stream). Larger writes copy directly and synchronize.
+constexpr uint64_t kStageBytes = 1u << 20;
 
 namespace {
 
@@ -548,6 +557,9 @@ int feml_b200_open(int32_t device, fb_backend **out) {
     if (e == cudaSuccess) e = cudaMalloc(&b->status_dev, 256);
     if (e == cudaSuccess) e = cudaMemset(b->status_dev, 0, 256);
     if (e == cudaSuccess) e = cudaMallocHost(&b->status_host, 256);
+    if (e == cudaSuccess) e = cudaMallocHost(&b->stage, kStageBytes);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&b->stage_free, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(b->stage_free, b->stream);
     if (e != cudaSuccess) {
         int rc = cuda_fail(e, "open");
         feml_b200_close(b);
@@ -567,6 +579,8 @@ int feml_b200_close(fb_backend *b) {
         if (b->scratch) cudaFree(b->scratch);
         if (b->status_dev) cudaFree(b->status_dev);
         if (b->status_host) cudaFreeHost(b->status_host);
+        if (b->stage) cudaFreeHost(b->stage);
+        if (b->stage_free) cudaEventDestroy(b->stage_free);
         if (b->stream) cudaStreamDestroy(b->stream);
     }
     delete b;
@@ -624,7 +638,18 @@ int feml_b200_write(fb_backend *b, uint32_t h, uint64_t off, const void *src, ui
     if (rc || (rc = check_range(*buf, h, off, n, "write"))) return rc;
     if (n == 0) return FB_OK;
     DeviceGuard g(b->device);
-    cudaError_t e = cudaMemcpyAsync(buf->ptr + off, src, n, cudaMemcpyHostToDevice, b->stream);
+    cudaError_t e;
+    if (n <= kStageBytes) {
+        // the previous staged copy has left the staging area once this event is done
+        e = cudaEventSynchronize(b->stage_free);
+        if (e == cudaSuccess) {
+            std::memcpy(b->stage, src, n);
+            e = cudaMemcpyAsync(buf->ptr + off, b->stage, n, cudaMemcpyHostToDevice, b->stream);
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(b->stage_free, b->stream);
+        return e == cudaSuccess ? FB_OK : cuda_fail(e, "write");
+    }
+    e = cudaMemcpyAsync(buf->ptr + off, src, n, cudaMemcpyHostToDevice, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     return e == cudaSuccess ? FB_OK : cuda_fail(e, "write");
 }

@@ -101,7 +101,9 @@ static bool is_matmul_id_weight_dtype(int32_t d) {
     return d == FB_F32 || d == FB_Q8_0 || d == FB_Q4_0 || d == FB_Q4_K;
 }
 
-static bool is_matmul_weight_dtype(int32_t d) { return is_matmul_id_weight_dtype(d) || d == FB_Q5_K; }
+static bool is_matmul_weight_dtype(int32_t d) {
+    return is_matmul_id_weight_dtype(d) || d == FB_Q5_K || d == FB_Q6_K;
+}
 
 // ---------------------------------------------------------------------------
 // Planner (planner.rs)
@@ -425,7 +427,7 @@ struct Graph {
     }
 
     // graph.rs:122-138, relaxed for quantized weights: src0 in {F32, Q8_0,
-    // Q4_0, Q4_K, Q5_K} with src1 F32 (the dtype-equality rule of pair() does not
+    // Q4_0, Q4_K, Q5_K, Q6_K} with src1 F32 (the dtype-equality rule of pair() does not
     // apply), output F32 instead of src0's dtype, ne0 % block_size(src0) == 0.
     int mul_mat(uint32_t a, uint32_t b, uint32_t *id) {
         TensorMeta *ma = get(a);

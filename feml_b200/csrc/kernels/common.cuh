@@ -15,9 +15,10 @@ constexpr int Q8_0_BYTES = 34;    // f16 d + 32 x i8
 constexpr int Q4_0_BYTES = 18;    // f16 d + 16 x (2 nibbles)
 constexpr int Q4_K_BYTES = 144;   // f16 d, f16 dmin, 12 B scales, 128 B nibbles
 constexpr int Q5_K_BYTES = 176;   // f16 d, f16 dmin, 12 B scales, 32 B fifth bits, 128 B nibbles
+constexpr int Q6_K_BYTES = 210;   // 128 B low nibbles, 64 B top 2 bits, 16 x i8 scales, f16 d
 
 // dtype discriminants used by the kernels (feml-core/src/dtype.rs:14-35).
-constexpr int WT_F32 = 5, WT_Q4_0 = 7, WT_Q8_0 = 11, WT_Q4_K = 15, WT_Q5_K = 16;
+constexpr int WT_F32 = 5, WT_Q4_0 = 7, WT_Q8_0 = 11, WT_Q4_K = 15, WT_Q5_K = 16, WT_Q6_K = 17;
 
 // status bits written by kernels into the backend's device status word.
 constexpr int STATUS_TIMEOUT = 1 << 0;    // a bounded wait gave up

@@ -301,6 +301,52 @@ __device__ __forceinline__ void q5k_pair_dot(const uint8_t *sb, int g, const uin
     q4k_pair_scales(h, g, dsc0, dmm0, dsc1, dmm1);
 }
 
+// Q6_K sub-block pair g (0..3) of the super-block at `sb` (2-byte aligned:
+// 210-byte super-blocks): ql[128] low 4 bits, qh[64] top 2 bits, int8
+// scales[16] (one per 16 elements), f16 d at byte 208; value =
+// d * scale * (q - 32). Pair g is half h = g / 2, quarters t = 2 (g % 2) and
+// t + 1: the nibbles of ql[64h + l] (sub-block 2g) and ql[64h + 32 + l]
+// (sub-block 2g+1), low for even g and high for odd g; their top bits are
+// bits 2t.. and 2t+2.. of qh[32h + l]; their scales are bytes 8h + 2t ..
+// 8h + 2t + 3. Returns s0, s1 = sum over each sub-block's two 16-element
+// groups of scale * sum((q - 32) * x), and d.
+__device__ __forceinline__ void q6k_pair_dot(const uint8_t *sb, int g, const uint32_t *xa, const uint32_t *xb,
+                                             int &s0, int &s1, float &d) {
+    const int h = g >> 1, t = 2 * (g & 1);
+    uint32_t ql[16], qh[8], scw[1];
+    ld_words_a2<16>(sb + 64 * h, ql);
+    ld_words_a2<8>(sb + 128 + 32 * h, qh);
+    ld_words_a2<1>(sb + 192 + 8 * h + 2 * t, scw);
+    d = f16_bits_to_f32(ld_u16(sb + 208));
+    const int nsh = (g & 1) ? 4 : 0;
+    const uint32_t m4 = 0x0f0f0f0fu, m2 = 0x03030303u, ones = 0x01010101u;
+    int sum[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {  // sub-block 2g + j
+        const uint4 xl = *reinterpret_cast<const uint4 *>(j ? xb : xa);
+        const uint4 xh = *reinterpret_cast<const uint4 *>((j ? xb : xa) + 4);
+        const uint32_t xw[8] = {xl.x, xl.y, xl.z, xl.w, xh.x, xh.y, xh.z, xh.w};
+        const int hs = 2 * (t + j);
+        int acc = 0;
+#pragma unroll
+        for (int grp = 0; grp < 2; grp++) {
+            int u = 0, hi = 0, xs = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int w = 4 * grp + i;
+                u = dp4a_us((ql[8 * j + w] >> nsh) & m4, xw[w], u);
+                hi = dp4a_us((qh[w] >> hs) & m2, xw[w], hi);
+                xs = dp4a_ss(ones, xw[w], xs);
+            }
+            const int sc = (int)(int8_t)((scw[0] >> (8 * (2 * j + grp))) & 0xffu);
+            acc += sc * (u + 16 * hi - 32 * xs);
+        }
+        sum[j] = acc;
+    }
+    s0 = sum[0];
+    s1 = sum[1];
+}
+
 // The same with the activation words read from `xa` / `xb` (16-byte aligned).
 __device__ __forceinline__ void q4k_pair_dot(const uint8_t *sb, int g, const uint32_t *xa, const uint32_t *xb,
                                              int &s0, int &s1, float &dsc0, float &dmm0, float &dsc1, float &dmm1) {

@@ -71,6 +71,16 @@ struct Fmt<WT_Q5_K> {
     static constexpr int kUnitBytes = Q5_K_BYTES / 8;
     static constexpr bool kShifted = false;
 };
+template <>
+struct Fmt<WT_Q6_K> {
+    static constexpr int kUnitBytes = 0;  // 210-byte super-blocks: sizes are counted in super-blocks
+    static constexpr bool kShifted = false;
+};
+// K-quants: chunks are whole 256-element super-blocks of this many bytes.
+template <int WT>
+constexpr int super_bytes() {
+    return WT == WT_Q4_K ? Q4_K_BYTES : (WT == WT_Q5_K ? Q5_K_BYTES : (WT == WT_Q6_K ? Q6_K_BYTES : 0));
+}
 
 struct GemvParams {
     const uint8_t *w;
@@ -221,7 +231,10 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
     const int w_begin = r_begin + cta_rows * warp / kGemvWarps;
     const int w_end = r_begin + cta_rows * (warp + 1) / kGemvWarps;
     const int n_items = (w_end - w_begin) * p.nchunks;
-    const uint32_t chunk_bytes = (uint32_t)p.chunk_units * UB;
+    constexpr bool KQ = super_bytes<WT>() > 0;
+    // bytes of `nu` 32-element units (whole super-blocks for K-quants)
+    auto units_bytes = [](uint32_t nu) -> uint32_t { return KQ ? nu / 8 * super_bytes<WT>() : nu * UB; };
+    const uint32_t chunk_bytes = units_bytes((uint32_t)p.chunk_units);
 
     auto item_range = [&](int i, uintptr_t &start, uint32_t &len, int &row, int &c) {
         row = w_begin + i / p.nchunks;
@@ -229,7 +242,7 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
         const uint32_t u0 = (uint32_t)c * p.chunk_units;
         const uint32_t nu = min((uint32_t)p.chunk_units, (uint32_t)nblk - u0);
         start = reinterpret_cast<uintptr_t>(p.w + (uint64_t)row * p.w_nb1 + (uint64_t)c * chunk_bytes);
-        len = nu * UB;
+        len = units_bytes(nu);
     };
 
     const uint64_t policy = policy_evict_first();
@@ -531,13 +544,29 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
             p0 = buf + (start - base);
         }
         const int u0 = c * p.chunk_units;
-        const int nu = (int)(len / UB);
+        const int nu = KQ ? (int)(len / super_bytes<WT>()) * 8 : (int)(len / UB);
         const int np = nu / 2;  // pairs in this chunk
-        if constexpr (WT == WT_Q4_K || WT == WT_Q5_K) {
+        if constexpr (WT == WT_Q6_K) {
 #pragma unroll 2
             for (int pr = lane; pr < np; pr += 32) {
                 const int b0 = u0 + 2 * pr;  // sub-block index within the row
-                const uint8_t *sb = p0 + 8 * UB * (pr >> 2);  // its super-block
+                const uint8_t *sb = p0 + Q6_K_BYTES * (pr >> 2);  // its super-block (2-byte aligned)
+                const int g = pr & 3;
+#pragma unroll
+                for (int n = 0; n < NC; n++) {
+                    const uint32_t *xa = reinterpret_cast<const uint32_t *>(sq + n * K + b0 * QK);
+                    int s0, s1;
+                    float d;
+                    q6k_pair_dot(sb, g, xa, xa + 8, s0, s1, d);
+                    const float2 dx = *reinterpret_cast<const float2 *>(sd + n * nbp + b0);
+                    acc[n] += dx.x * (d * (float)s0) + dx.y * (d * (float)s1);
+                }
+            }
+        } else if constexpr (WT == WT_Q4_K || WT == WT_Q5_K) {
+#pragma unroll 2
+            for (int pr = lane; pr < np; pr += 32) {
+                const int b0 = u0 + 2 * pr;  // sub-block index within the row
+                const uint8_t *sb = p0 + super_bytes<WT>() * (pr >> 2);  // its super-block
                 const int g = pr & 3;
 #pragma unroll
                 for (int n = 0; n < NC; n++) {
@@ -1030,15 +1059,26 @@ int launch_cols(int ncols, int xr, const GemvParams &p, int grid, uint32_t smem,
 }
 
 bool shifted_of(int32_t wtype) { return wtype == WT_Q8_0 || wtype == WT_Q4_0; }
+// bytes per 32-element unit, rounded up (Q6_K: 210 / 8 = 26.25), for budgets
 uint32_t unit_bytes_of(int32_t wtype) {
     switch (wtype) {
     case WT_Q8_0: return Q8_0_BYTES;
     case WT_Q4_0: return Q4_0_BYTES;
     case WT_Q5_K: return Q5_K_BYTES / 8;
+    case WT_Q6_K: return (Q6_K_BYTES + 7) / 8;
     default: return Q4_K_BYTES / 8;
     }
 }
-bool k_quant(int32_t wtype) { return wtype == WT_Q4_K || wtype == WT_Q5_K; }
+bool k_quant(int32_t wtype) { return wtype == WT_Q4_K || wtype == WT_Q5_K || wtype == WT_Q6_K; }
+// exact bytes of `units` 32-element units (a multiple of 8 for K-quants)
+uint32_t chunk_bytes_of(int32_t wtype, uint32_t units) {
+    switch (wtype) {
+    case WT_Q4_K: return units / 8 * Q4_K_BYTES;
+    case WT_Q5_K: return units / 8 * Q5_K_BYTES;
+    case WT_Q6_K: return units / 8 * Q6_K_BYTES;
+    default: return units * unit_bytes_of(wtype);
+    }
+}
 
 // The K-split path for one column of wide Q4_K rows; returns -1 (nothing
 // launched) when the shape does not fit it.
@@ -1170,11 +1210,11 @@ int launch_gemv_ks_cols(const void *w, uint64_t w_nb1, const Q8Planar &xq, void 
 }  // namespace
 
 bool gemv_supported(int32_t wtype, int64_t K, int64_t N) {
-    if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K && wtype != WT_Q5_K) return false;
+    if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && !k_quant(wtype)) return false;
     if (N < 1 || N > kMaxCols) return false;
     if (K % (k_quant(wtype) ? QKK : QK)) return false;
     // activations + two minimal stages per warp must fit
-    const SmemLayout L = smem_layout((int)K, (int)N, shifted_of(wtype), 2, align16(8 * unit_bytes_of(wtype) + 32));
+    const SmemLayout L = smem_layout((int)K, (int)N, shifted_of(wtype), 2, align16(chunk_bytes_of(wtype, 8) + 32));
     return K <= (1 << 20) && L.total <= (uint32_t)kSmemLimit;
 }
 
@@ -1254,13 +1294,13 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     const int nchunks0 = (nunits + chunk_units - 1) / chunk_units;
     chunk_units = ((nunits + nchunks0 - 1) / nchunks0 + 7) / 8 * 8;  // balance the chunks of a row
     const int nchunks = (nunits + chunk_units - 1) / chunk_units;
-    const uint32_t stage_bytes = align16((uint32_t)chunk_units * ub + 32);
+    const uint32_t stage_bytes = align16(chunk_bytes_of(wtype, (uint32_t)chunk_units) + 32);
     int nstage = 4;
     while (nstage > 2 && smem_layout((int)K, (int)N, sh, nstage, stage_bytes).total > cta_limit) nstage--;
     const SmemLayout L = smem_layout((int)K, (int)N, sh, nstage, stage_bytes);
     if (L.total > (uint32_t)kSmemLimit) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: shared memory budget exceeded");
 
-    const int align = k_quant(wtype) ? 16 : 4;
+    const int align = wtype == WT_Q6_K ? 2 : (k_quant(wtype) ? 16 : 4);  // Q6_K super-blocks are 2-byte aligned
     GemvParams p;
     p.w = static_cast<const uint8_t *>(w);
     p.w_nb1 = w_nb1;
@@ -1287,6 +1327,7 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     case WT_Q8_0: return launch_cols<WT_Q8_0>((int)N, xr, p, grid, L.total, s, pdl);
     case WT_Q4_0: return launch_cols<WT_Q4_0>((int)N, xr, p, grid, L.total, s, pdl);
     case WT_Q5_K: return launch_cols<WT_Q5_K>((int)N, xr, p, grid, L.total, s, pdl);
+    case WT_Q6_K: return launch_cols<WT_Q6_K>((int)N, xr, p, grid, L.total, s, pdl);
     default: return launch_cols<WT_Q4_K>((int)N, xr, p, grid, L.total, s, pdl);
     }
 }

@@ -151,7 +151,11 @@ int feml_b200_create_buffer(fb_backend *b, uint64_t size, int32_t usage, uint32_
 int feml_b200_release_buffer(fb_backend *b, uint32_t handle);
 /* Backend::write / read: blocking; the byte range must lie inside the
  * buffer or FB_ERR_INVALID is returned and nothing is written
- * (backend.rs:97-103). */
+ * (backend.rs:97-103). A write of at most 1 MiB returns once the bytes are
+ * copied into the backend's pinned staging area; the device copy is queued
+ * on the backend stream ahead of every later read, fill and graph_compute
+ * (the caller may reuse `src` at once; a copy error surfaces at the next
+ * synchronize or read). */
 int feml_b200_write(fb_backend *b, uint32_t handle, uint64_t offset, const void *src, uint64_t n);
 int feml_b200_read(fb_backend *b, uint32_t handle, uint64_t offset, void *dst, uint64_t n);
 /* Backend::fill (backend.rs:105-106), asynchronous like the reference CUDA

@@ -155,6 +155,24 @@ def test_q4_k_wide_rows_few_columns_padded_stride(b200):
     assert np.isnan(got[:, M:]).all()
 
 
+@pytest.mark.parametrize("K,M,N", [(256, 7, 1), (4096, 300, 1), (14336, 64, 1), (768, 130, 3), (4096, 100, 8),
+                                   (2048, 70, 12), (512, 33, 33), (11008, 40, 2)])
+def test_mul_mat_q6_k_matches_oracle(b200, K, M, N):
+    """Q6_K weights (210-byte super-blocks, 2-byte aligned: rows of K = 768
+    or 11008 are not 16-byte multiples, so chunks carry ragged head and tail
+    bytes) on the decode GEMV; layout pinned to gguf-py's dequantizer."""
+    rng = np.random.default_rng(K + 5 * M + N)
+    wq = O.quantize(O.DT_Q6_K, weights(rng, M, K))
+    x = _inputs(K + 3 * N, N, K)
+    got = run_mul_mat(b200, DType.Q6_K, wq, x, K, M)
+    ok, err = tol_ok(got, O.mul_mat_quant_ref(O.DT_Q6_K, wq, x, K))
+    assert ok, f"max abs err {err}"
+    wt, xt = torch.from_numpy(wq).cuda(), torch.from_numpy(x).cuda()
+    a, b = ops.mul_mat(DType.Q6_K, wt, xt, K), ops.mul_mat(DType.Q6_K, wt, xt, K)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and np.array_equal(a.cpu().numpy(), got)
+
+
 @pytest.mark.parametrize("K,M,N", [(256, 7, 1), (4096, 300, 1), (14336, 64, 1), (1024, 130, 3), (4096, 100, 8),
                                    (2048, 70, 12), (512, 33, 33)])
 def test_mul_mat_q5_k_matches_oracle(b200, K, M, N):

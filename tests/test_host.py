@@ -437,10 +437,11 @@ def test_supports_op_matrix():
         assert dev.supports_op(Op.MUL_MAT, [d, DType.F32])
         assert dev.supports_op(Op.MUL_MAT_ID, [d, DType.F32, DType.I32])
     assert not dev.supports_op(Op.MUL_MAT, [DType.Q8_0, DType.Q8_0])
-    # Q5_K: mul_mat (decode GEMV) only; Q6_K not yet
-    assert dev.supports_op(Op.MUL_MAT, [DType.Q5_K, DType.F32])
-    assert not dev.supports_op(Op.MUL_MAT_ID, [DType.Q5_K, DType.F32, DType.I32])
-    assert not dev.supports_op(Op.MUL_MAT, [DType.Q6_K, DType.F32])
+    # Q5_K, Q6_K: mul_mat (decode GEMV) only
+    for d in (DType.Q5_K, DType.Q6_K):
+        assert dev.supports_op(Op.MUL_MAT, [d, DType.F32])
+        assert not dev.supports_op(Op.MUL_MAT_ID, [d, DType.F32, DType.I32])
+    assert not dev.supports_op(Op.MUL_MAT, [DType.Q3_K, DType.F32])
     assert not dev.supports_op(Op.MUL, [DType.F32, DType.F32])
     assert dev.supports_op(Op.RMS_NORM, [DType.F32])
 
