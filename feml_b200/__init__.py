@@ -346,6 +346,16 @@ class B200Backend(Backend):
         _check(_L.lib().feml_b200_scratch_bytes(self._h, ctypes.byref(v)))
         return v.value
 
+    def set_plan_graphs(self, enable):
+        """Replay CUDA graphs of repeated plans (default on)."""
+        _check(_L.lib().feml_b200_set_plan_graphs(self._h, 1 if enable else 0))
+
+    def plan_graphs(self):
+        """(plans cached, plans replaying a graph)."""
+        n, r = ctypes.c_int64(), ctypes.c_int64()
+        _check(_L.lib().feml_b200_plan_graphs(self._h, ctypes.byref(n), ctypes.byref(r)))
+        return n.value, r.value
+
     def device_allocations(self):
         """cudaMalloc calls this backend has made (buffers and scratch)."""
         v = ctypes.c_uint64()

@@ -91,6 +91,8 @@ SIGNATURES = [
     ("feml_b200_scratch_bytes", c_int, [vp, ctypes.POINTER(c_u64)]),
     ("feml_b200_reserve_scratch", c_int, [vp, c_u64]),
     ("feml_b200_device_allocations", c_int, [vp, ctypes.POINTER(c_u64)]),
+    ("feml_b200_set_plan_graphs", c_int, [vp, c_i32]),
+    ("feml_b200_plan_graphs", c_int, [vp, ctypes.POINTER(c_i64), ctypes.POINTER(c_i64)]),
     ("fb_graph_new", c_int, [ctypes.POINTER(vp)]),
     ("fb_graph_free", None, [vp]),
     ("fb_graph_input", c_int, [vp, cp, c_i32, ctypes.POINTER(c_i64), c_i32, ctypes.POINTER(c_u32)]),

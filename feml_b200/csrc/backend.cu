@@ -21,6 +21,8 @@
 #include <algorithm>
 #include <cstring>
 #include <map>
+#include <unordered_map>
+#include <vector>
 #include <mutex>
 #include <new>
 
@@ -245,6 +247,16 @@ struct fb_backend {
     uint64_t device_allocs = 0;      // cudaMalloc calls made for buffers and scratch
     uint8_t *stage = nullptr;        // pinned staging area of small writes
     cudaEvent_t stage_free = nullptr;  // recorded after the last staged copy
+    // Executable CUDA graphs of plans already run, keyed by a hash of every
+    // plan field the launches depend on; `key` holds those fields for an
+    // exact comparison; exec == nullptr marks a plan whose capture failed
+    // (it runs node by node).
+    struct PlanGraph {
+        std::vector<uint64_t> key;
+        cudaGraphExec_t exec = nullptr;
+    };
+    std::unordered_map<uint64_t, PlanGraph> graphs;
+    bool use_graphs = true;
 };
 
 // Writes up to this size are copied into the pinned staging area and sent
@@ -282,11 +294,20 @@ int check_range(const Buffer &buf, uint32_t h, uint64_t off, uint64_t n, const c
     return FB_OK;
 }
 
+// Drop every cached plan graph: they hold buffer and scratch addresses.
+// Callers have synchronized the stream, so none is executing.
+void clear_plan_graphs(fb_backend *b) {
+    for (auto &kv : b->graphs)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    b->graphs.clear();
+}
+
 int grow_scratch(fb_backend *b, uint64_t bytes) {
     if (bytes <= b->scratch_bytes) return FB_OK;
     bytes = align256(bytes);
     cudaError_t e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return cuda_fail(e, "scratch sync");
+    clear_plan_graphs(b);
     if (b->scratch) cudaFree(b->scratch);
     b->scratch = nullptr;
     b->scratch_bytes = 0;
@@ -575,6 +596,7 @@ int feml_b200_close(fb_backend *b) {
     {
         DeviceGuard g(b->device);
         if (b->stream) cudaStreamSynchronize(b->stream);
+        clear_plan_graphs(b);
         for (auto &kv : b->buffers) cudaFree(kv.second.ptr);
         if (b->scratch) cudaFree(b->scratch);
         if (b->status_dev) cudaFree(b->status_dev);
@@ -625,6 +647,7 @@ int feml_b200_release_buffer(fb_backend *b, uint32_t handle) {
     if (rc) return rc;
     DeviceGuard g(b->device);
     cudaStreamSynchronize(b->stream);  // queued work may still read it
+    clear_plan_graphs(b);
     cudaFree(buf->ptr);
     b->buffers.erase(handle);
     return FB_OK;
@@ -750,22 +773,58 @@ uint64_t node_scratch(const fb_plan *plan, const fb_plan_tensor &node) {
     return 0;
 }
 
-int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
-    if (!b || !plan) return set_error(FB_ERR_INVALID, "graph_compute: null argument");
-    std::lock_guard<std::mutex> lk(b->mu);
-    DeviceGuard g(b->device);
-    // scratch for the largest node; grows (with a device synchronize) only the
-    // first time a plan needs more than the arena holds
-    uint64_t need = 0;
-    for (int64_t i = 0; i < plan->n_nodes; i++) {
-        const int64_t ti = plan->nodes[i];
-        if (ti < 0 || ti >= plan->n_tensors) return set_error(FB_ERR_INVALID, "graph_compute: bad node index");
-        need = std::max(need, node_scratch(plan, plan->tensors[ti]));
+}  // extern "C"
+
+namespace {
+
+// Every plan field the launches of graph_compute depend on, in a fixed order
+// (buffers by handle: handles are never reused, and a buffer's address never
+// changes while its handle lives).
+template <typename F>
+void visit_plan(const fb_plan *plan, F &&f) {
+    f((uint64_t)plan->n_tensors);
+    f((uint64_t)plan->n_nodes);
+    f((uint64_t)plan->n_buffers);
+    for (int64_t i = 0; i < plan->n_buffers; i++) {
+        f((uint64_t)plan->buffers[i].handle);
+        f(plan->buffers[i].size);
     }
-    if (need > b->scratch_bytes) {
-        const int rc = grow_scratch(b, need);
-        if (rc) return rc;
+    for (int64_t i = 0; i < plan->n_nodes; i++) f((uint64_t)plan->nodes[i]);
+    for (int64_t i = 0; i < plan->n_tensors; i++) {
+        const fb_plan_tensor &t = plan->tensors[i];
+        f(((uint64_t)(uint32_t)t.op << 32) | (uint32_t)t.dtype);
+        f(((uint64_t)t.op_params[0] << 32) | t.op_params[1]);
+        f(((uint64_t)(uint32_t)t.n_srcs << 32) | t.flags);
+        for (int k = 0; k < FB_MAX_SRC; k++) f((uint64_t)(int64_t)t.srcs[k]);
+        f((uint64_t)(int64_t)t.buffer);
+        f(t.offset);
+        for (int d = 0; d < 4; d++) {
+            f((uint64_t)t.ne[d]);
+            f(t.nb[d]);
+        }
     }
+}
+
+uint64_t plan_hash(const fb_plan *plan) {
+    uint64_t h = 1469598103934665603ull;  // FNV-1a over the 64-bit fields
+    visit_plan(plan, [&](uint64_t v) {
+        h ^= v;
+        h *= 1099511628211ull;
+    });
+    return h;
+}
+
+bool plan_matches(const std::vector<uint64_t> &key, const fb_plan *plan) {
+    size_t i = 0;
+    bool same = true;
+    visit_plan(plan, [&](uint64_t v) {
+        same = same && i < key.size() && key[i] == v;
+        i++;
+    });
+    return same && i == key.size();
+}
+
+int run_nodes(fb_backend *b, const fb_plan *plan) {
     for (int64_t i = 0; i < plan->n_nodes; i++) {
         const int64_t ti = plan->nodes[i];
         const fb_plan_tensor &node = plan->tensors[ti];
@@ -788,6 +847,87 @@ int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
         }
         if (rc) return rc;
     }
+    return FB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Repeated graph_compute of one plan replays a CUDA graph of its launches.
+// The first call runs the nodes one by one (setting per-kernel attributes and
+// sizing the scratch), then captures the same launches into a graph (not
+// executed) and instantiates it; later calls of a plan with identical fields
+// launch that graph: one launch instead of one or more per node, and no
+// allocation. Creating or releasing a buffer, or growing the scratch, drops
+// the cached graphs (they hold addresses). A capture that fails leaves the
+// plan on the node-by-node path.
+int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
+    if (!b || !plan) return set_error(FB_ERR_INVALID, "graph_compute: null argument");
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    // scratch for the largest node; grows (with a device synchronize) only the
+    // first time a plan needs more than the arena holds
+    uint64_t need = 0;
+    for (int64_t i = 0; i < plan->n_nodes; i++) {
+        const int64_t ti = plan->nodes[i];
+        if (ti < 0 || ti >= plan->n_tensors) return set_error(FB_ERR_INVALID, "graph_compute: bad node index");
+        need = std::max(need, node_scratch(plan, plan->tensors[ti]));
+    }
+    if (need > b->scratch_bytes) {
+        const int rc = grow_scratch(b, need);
+        if (rc) return rc;
+    }
+    uint64_t h = 0;
+    if (b->use_graphs) {
+        h = plan_hash(plan);
+        auto it = b->graphs.find(h);
+        if (it != b->graphs.end() && plan_matches(it->second.key, plan)) {
+            if (!it->second.exec) return run_nodes(b, plan);
+            const cudaError_t e = cudaGraphLaunch(it->second.exec, b->stream);
+            return e == cudaSuccess ? FB_OK : cuda_fail(e, "graph_compute: graph launch");
+        }
+    }
+    int rc = run_nodes(b, plan);
+    if (rc || !b->use_graphs || b->graphs.count(h)) return rc;  // (a hash collision keeps the first plan's graph)
+    fb_backend::PlanGraph entry;
+    visit_plan(plan, [&](uint64_t v) { entry.key.push_back(v); });
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        const int crc = run_nodes(b, plan);
+        e = cudaStreamEndCapture(b->stream, &graph);
+        if (crc == FB_OK && e == cudaSuccess && graph) e = cudaGraphInstantiate(&entry.exec, graph, 0);
+        else entry.exec = nullptr;
+        if (e != cudaSuccess) entry.exec = nullptr;
+    }
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();  // a failed capture is not an error of this call: the plan ran node by node
+    b->graphs.emplace(h, std::move(entry));
+    return FB_OK;
+}
+
+int feml_b200_set_plan_graphs(fb_backend *b, int32_t enable) {
+    if (!b) return set_error(FB_ERR_INVALID, "set_plan_graphs: null backend");
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    cudaError_t e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "set_plan_graphs");
+    clear_plan_graphs(b);
+    b->use_graphs = enable != 0;
+    return FB_OK;
+}
+
+int feml_b200_plan_graphs(fb_backend *b, int64_t *cached, int64_t *replayable) {
+    if (!b) return set_error(FB_ERR_INVALID, "plan_graphs: null backend");
+    std::lock_guard<std::mutex> lk(b->mu);
+    int64_t n = 0, r = 0;
+    for (auto &kv : b->graphs) {
+        n++;
+        r += kv.second.exec != nullptr;
+    }
+    if (cached) *cached = n;
+    if (replayable) *replayable = r;
     return FB_OK;
 }
 

@@ -188,6 +188,14 @@ int feml_b200_reserve_scratch(fb_backend *b, uint64_t bytes);
  * allocator, feml-cpu/tests/cpu_integration.rs:11-34,230-251) is observable
  * as this count staying unchanged across repeated graph_compute calls. */
 int feml_b200_device_allocations(fb_backend *b, uint64_t *count);
+/* Plan graphs (GraphPlan.uid is the reference's plan-caching hook,
+ * feml-core/src/plan.rs:38-39, graph.rs:335-347): graph_compute replays a
+ * CUDA graph of a plan's launches from its second call on (captured, not
+ * executed, during the first). Enabled by default; disabling (or enabling)
+ * synchronizes the stream and drops the cached graphs. plan_graphs reports
+ * how many plans are cached and how many of those replay a graph. */
+int feml_b200_set_plan_graphs(fb_backend *b, int32_t enable);
+int feml_b200_plan_graphs(fb_backend *b, int64_t *cached, int64_t *replayable);
 
 /* ======================================================================== */
 /* 2. Graph builder / planner mirror (C++ restatement of feml-core's        */
