@@ -824,6 +824,10 @@ bool plan_matches(const std::vector<uint64_t> &key, const fb_plan *plan) {
     return same && i == key.size();
 }
 
+// Plans whose graphs are kept at once (a process that compiles many plans
+// without releasing their buffers recaptures them after the cache is full).
+constexpr size_t kMaxPlanGraphs = 256;
+
 int run_nodes(fb_backend *b, const fb_plan *plan) {
     for (int64_t i = 0; i < plan->n_nodes; i++) {
         const int64_t ti = plan->nodes[i];
@@ -890,6 +894,12 @@ int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
     }
     int rc = run_nodes(b, plan);
     if (rc || !b->use_graphs || b->graphs.count(h)) return rc;  // (a hash collision keeps the first plan's graph)
+    if (b->graphs.size() >= kMaxPlanGraphs) {
+        // bound the cache: wait for every launch of a cached graph, then drop them all
+        const cudaError_t se = cudaStreamSynchronize(b->stream);
+        if (se != cudaSuccess) return cuda_fail(se, "graph_compute");
+        clear_plan_graphs(b);
+    }
     fb_backend::PlanGraph entry;
     visit_plan(plan, [&](uint64_t v) { entry.key.push_back(v); });
     cudaGraph_t graph = nullptr;
