@@ -214,6 +214,8 @@ int parse(fb_gguf *g) {
         uint64_t off, len;
         if (!c.str(off, len, "key")) return FB_ERR_INVALID;
         kv.key.assign(reinterpret_cast<const char *>(g->map + off), (size_t)len);
+        if (kv.key.find('\0') != std::string::npos)  // keys are handed out as C strings
+            return set_error(FB_ERR_INVALID, "gguf: key %llu contains a NUL byte", (unsigned long long)i);
         if (!c.get(kv.type, "value type") || !read_value(c, kv.type, kv, 0)) return FB_ERR_INVALID;
         if (!g->kv_index.emplace(kv.key, (int64_t)i).second)
             return set_error(FB_ERR_INVALID, "gguf: duplicate key '%s'", kv.key.c_str());
@@ -234,6 +236,8 @@ int parse(fb_gguf *g) {
         uint64_t off, len;
         if (!c.str(off, len, "tensor name")) return FB_ERR_INVALID;
         t.name.assign(reinterpret_cast<const char *>(g->map + off), (size_t)len);
+        if (t.name.find('\0') != std::string::npos)  // names are looked up as C strings
+            return set_error(FB_ERR_INVALID, "gguf: tensor %llu's name contains a NUL byte", (unsigned long long)i);
         uint32_t nd = 0;
         if (!c.get(nd, "tensor n_dims")) return FB_ERR_INVALID;
         if (nd < 1 || nd > 4)

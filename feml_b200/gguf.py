@@ -125,7 +125,9 @@ class GGUFFile:
             t = _L.GgufTensor()
             for i in range(self._n_tensors):
                 _check(L.feml_b200_gguf_tensor(h, i, ctypes.byref(t)))
-                out.append(GGUFTensorInfo(t.name.decode("utf-8", errors="replace"),
+                # names that are not UTF-8 keep their bytes (surrogate escapes), so
+                # they can be looked up again
+                out.append(GGUFTensorInfo(t.name.decode("utf-8", errors="surrogateescape"),
                                           DType(t.dtype) if t.dtype >= 0 else None, t.ggml_type,
                                           tuple(t.ne[d] for d in range(t.n_dims)), t.offset, t.nbytes))
             self._tensors = out
@@ -133,7 +135,8 @@ class GGUFFile:
 
     def _index(self, name):
         i = ctypes.c_int64()
-        _check(_L.lib().feml_b200_gguf_find_tensor(self._live(), name.encode(), ctypes.byref(i)))
+        _check(_L.lib().feml_b200_gguf_find_tensor(self._live(), name.encode("utf-8", errors="surrogateescape"),
+                                                   ctypes.byref(i)))
         return i.value
 
     def tensor(self, name):

@@ -222,7 +222,8 @@ int fb_graph_silu(fb_graph *g, uint32_t x, uint32_t *id);
 int fb_graph_rms_norm(fb_graph *g, uint32_t x, float eps, uint32_t *id);
 int fb_graph_copy(fb_graph *g, uint32_t x, uint32_t *id);
 /* GraphBuilder::mul_mat (graph.rs:122-138), relaxed: src0 in {F32, Q8_0,
- * Q4_0, Q4_K}, src1 F32, output F32 [ne1(a), ne1(b)], ne0(a) % block == 0. */
+ * Q4_0, Q4_K, Q5_K, Q6_K}, src1 F32, output F32 [ne1(a), ne1(b)], ne0(a) % block == 0
+ * (mul_mat_id: F32, Q8_0, Q4_0, Q4_K). */
 int fb_graph_mul_mat(fb_graph *g, uint32_t a, uint32_t b, uint32_t *id);
 /* GraphBuilder::mul_mat_id (graph.rs:215-250), ggml semantics: weights
  * [K, M, E], x [K, N], ids I32 [n_selected, N], output F32

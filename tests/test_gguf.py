@@ -146,7 +146,7 @@ def test_minimal_hand_written_file(tmp_path):
 
 @pytest.mark.parametrize("case", ["magic", "version", "truncated_header", "truncated_info", "data_past_eof",
                                   "misaligned", "five_dims", "bad_block", "duplicate_tensor", "bad_kv_type",
-                                  "string_past_eof", "huge_count"])
+                                  "string_past_eof", "huge_count", "nul_in_name"])
 def test_malformed_files_are_rejected(tmp_path, case):
     good = _file([_tensor_info(b"w", [64, 2], 8, 0)], 136)
     if case == "magic":
@@ -171,6 +171,8 @@ def test_malformed_files_are_rejected(tmp_path, case):
         data = _file([], 0, kvs=_s(b"k") + struct.pack("<I", 99) + b"\0" * 8, n_kv=1)
     elif case == "string_past_eof":
         data = _header(0, 1) + _s(b"k") + struct.pack("<I", 8) + struct.pack("<Q", 1 << 40) + b"abc"
+    elif case == "nul_in_name":
+        data = _file([_tensor_info(b"w\0x", [32], 8, 0)], 68)
     else:  # huge_count
         data = _header(1 << 60, 0) + b"\0" * 64
     with pytest.raises(F.FemlError) as ei:
@@ -198,3 +200,32 @@ def test_unknown_and_unmapped_types_are_listed(tmp_path):
         assert u.dtype is None and u.nbytes == 0
         with pytest.raises(F.FemlError):
             f.tensor_bytes("u")
+
+
+def test_mutated_files_never_read_out_of_range(tmp_path, gguf_path):
+    """Random byte flips and truncations of a valid file: every open either
+    succeeds (then every tensor's bytes lie inside the file) or raises
+    FemlError; none crashes the process."""
+    p, _ = gguf_path
+    good = p.read_bytes()
+    rng = np.random.default_rng(2024)
+    bad = tmp_path / "mut.gguf"
+    for trial in range(600):
+        data = bytearray(good)
+        if trial % 3 == 0:
+            data = data[: int(rng.integers(0, len(data)))]
+        else:
+            head = min(len(data), 1200)  # header, metadata and tensor table
+            for _ in range(int(rng.integers(1, 6))):
+                data[int(rng.integers(0, head))] = int(rng.integers(0, 256))
+        bad.write_bytes(bytes(data))
+        try:
+            f = GGUFFile(bad)
+        except F.FemlError:
+            continue
+        with f:
+            f.metadata  # noqa: B018 (parses every value)
+            for t in f.tensors:
+                assert t.offset + t.nbytes <= len(data)
+                if t.nbytes:
+                    assert f.tensor_bytes(t.name).size == t.nbytes
