@@ -112,7 +112,8 @@ def _spawn(fn, world, *args):
 
 
 @pytest.mark.parametrize("world", [2, 3])
-@pytest.mark.parametrize("wtype,K,M,N", [(O.DT_Q4_K, 512, 37, 1), (O.DT_Q8_0, 128, 20, 5), (O.DT_Q4_0, 64, 9, 3)])
+@pytest.mark.parametrize("wtype,K,M,N", [(O.DT_Q4_K, 512, 37, 1), (O.DT_Q8_0, 128, 20, 5), (O.DT_Q4_0, 64, 9, 3),
+                                      (O.DT_Q5_K, 256, 11, 2), (O.DT_Q6_K, 256, 13, 1)])
 def test_row_shard_matches_single_device(tmp_path, world, wtype, K, M, N):
     case = (wtype, K, M, N, 3)
     _spawn(_row_worker, world, case, str(tmp_path))
