@@ -8,16 +8,18 @@
 //
 // Two kernels share that arithmetic:
 //  - gemm_f32_pipe_kernel (16-byte aligned operands, K % 4 == 0, ungrouped):
-//    a CTA owns 8*W rows x 32 columns (W <= 4 compute warps, one per SM
-//    sub-partition). One producer thread streams 128-wide k chunks into a
+//    a CTA owns 4*W rows x 32 columns (W <= 8 compute warps, two per SM
+//    sub-partition, W even). One producer thread streams 128-wide k chunks into a
 //    4-stage shared-memory ring as 2D TMA boxes (32 k x the CTA's rows, 32 k
 //    x its 32 columns; 128-byte swizzle), 8 tensor copies per chunk: with
 //    one bulk copy per 512-byte row segment (64 per chunk) the copies, not
 //    the arithmetic, set the pace (110 us against 88 us for C1). A compute
-//    warp owns 8 rows x 32 columns; each lane a 4-row x 2-column micro-tile
-//    (8 chains), reading 4 k values of each of its rows and columns with
-//    16-byte shared loads two steps ahead of the arithmetic: 6 loads per 32
-//    multiply-adds, conflict-free through the swizzle. The sequential chains
+//    warp owns 4 rows x 32 columns; each lane a 2-row x 2-column micro-tile
+//    (4 chains), reading 4 k values of each of its rows and columns with
+//    16-byte shared loads two steps ahead of the arithmetic: 4 loads per 16
+//    multiply-adds, conflict-free through the swizzle. Two warps per SM
+//    sub-partition hide each other's latencies better than one warp with
+//    twice the chains (84 against 88 us for C1, identical outputs). The sequential chains
 //    leave the kernel bound by FP32 issue (two instructions per
 //    multiply-add), not by HBM.
 //  - gemm_f32_exact_kernel (everything else, and mul_mat_id with F32
@@ -184,10 +186,11 @@ __global__ void __launch_bounds__(THREADS) gemm_f32_exact_kernel(const F32Params
 }
 
 // ---- pipelined path ---------------------------------------------------------
-// A warp owns 8 rows x 32 columns: lane l takes columns l%16 and l%16 + 16
-// and rows 4*(l/16) .. 4*(l/16)+3 of the warp's rows (8 chains).
-constexpr int kWarpRows = 8;
-constexpr int kMaxWarps = 4;          // compute warps per CTA
+// A warp owns 4 rows x 32 columns: lane l takes columns l%16 and l%16 + 16
+// and rows 2*(l/16), 2*(l/16)+1 of the warp's rows (4 chains).
+constexpr int kLaneRows = 2;
+constexpr int kWarpRows = 2 * kLaneRows;
+constexpr int kMaxWarps = 8;          // compute warps per CTA
 constexpr int kChunk = 128;           // k values per stage (four 32-wide boxes)
 constexpr int kBoxK = 32;             // k values per 128-byte swizzled box row
 constexpr int kPipeStages = 4;
@@ -273,16 +276,16 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     // Compute warps. Row y's 16-byte unit u of a box sits at
     // y * 128 + ((u ^ (y % 8)) * 16).
     const int cp = lane & 15;                           // columns cp and cp + 16
-    const int r0 = warp * kWarpRows + 4 * (lane >> 4);  // first of this lane's 4 rows in the CTA
-    const uint32_t wrow = (uint32_t)r0 * 128u;          // row r0 + r at wrow + r * 128
-    const uint32_t wsw = (uint32_t)(r0 & 4);            // (r0 + r) % 8 == wsw + r
+    const int r0 = warp * kWarpRows + kLaneRows * (lane >> 4);
+    const uint32_t wrow = (uint32_t)r0 * 128u;
+    const uint32_t wsw = (uint32_t)(r0 & 7);            // (r0 + r) % 8 == wsw + r (r0 even, r < 2)
     const uint32_t xrow = (uint32_t)cp * 128u;          // column cp + 16 is 2048 bytes on
     const uint32_t xsw = (uint32_t)((cp & 7) << 4);
-    float acc[4][2];
+    float acc[kLaneRows][2];
 #pragma unroll
-    for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = 0.0f;
+    for (int r = 0; r < kLaneRows; r++) acc[r][0] = acc[r][1] = 0.0f;
     struct Step {
-        float4 xa, xb, w[4];
+        float4 xa, xb, w[kLaneRows];
     };
     // step t: k values 4t .. 4t+3 of the chunk = box t / 8, unit t % 8
     auto load = [&](uint32_t sw, uint32_t sx, int t) {
@@ -293,27 +296,27 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
         v.xa = lds_f4(bx);
         v.xb = lds_f4(bx + 16u * 128u);
 #pragma unroll
-        for (int r = 0; r < 4; r++) v.w[r] = lds_f4(bw + (uint32_t)r * 128u + (u ^ ((wsw + (uint32_t)r) << 4)));
+        for (int r = 0; r < kLaneRows; r++) v.w[r] = lds_f4(bw + (uint32_t)r * 128u + (u ^ ((wsw + (uint32_t)r) << 4)));
         return v;
     };
     auto step = [&](const Step &v) {
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
+        for (int r = 0; r < kLaneRows; r++) {
             acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(v.w[r].x, v.xa.x));
             acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(v.w[r].x, v.xb.x));
         }
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
+        for (int r = 0; r < kLaneRows; r++) {
             acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(v.w[r].y, v.xa.y));
             acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(v.w[r].y, v.xb.y));
         }
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
+        for (int r = 0; r < kLaneRows; r++) {
             acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(v.w[r].z, v.xa.z));
             acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(v.w[r].z, v.xb.z));
         }
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
+        for (int r = 0; r < kLaneRows; r++) {
             acc[r][0] = __fadd_rn(acc[r][0], __fmul_rn(v.w[r].w, v.xa.w));
             acc[r][1] = __fadd_rn(acc[r][1], __fmul_rn(v.w[r].w, v.xb.w));
         }
@@ -352,12 +355,12 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
         const int col = cp + 16 * j;
         if (col >= cols || r0 >= rows) continue;
         float *yc = reinterpret_cast<float *>(p.y + (uint64_t)(n0 + col) * p.y_nb1);
-        const int m = m0 + r0;  // a multiple of 4
-        if (p.y_vec16 && r0 + 4 <= rows) {
-            *reinterpret_cast<float4 *>(yc + m) = make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
+        const int m = m0 + r0;  // even
+        if (p.y_vec16 && r0 + 2 <= rows) {
+            *reinterpret_cast<float2 *>(yc + m) = make_float2(acc[0][j], acc[1][j]);
         } else {
 #pragma unroll
-            for (int r = 0; r < 4; r++)
+            for (int r = 0; r < kLaneRows; r++)
                 if (r0 + r < rows) yc[m + r] = acc[r][j];
         }
     }
@@ -369,7 +372,8 @@ int pipe_warps(int64_t M, int64_t N) {
     const int64_t col_tiles = (N + kPipeCols - 1) / kPipeCols;
     const int64_t sms = sm_count();
     const int64_t rows_per_cta = (M * col_tiles + sms - 1) / sms;
-    return (int)std::min<int64_t>(kMaxWarps, std::max<int64_t>(1, (rows_per_cta + kWarpRows - 1) / kWarpRows));
+    const int64_t w = std::min<int64_t>(kMaxWarps, std::max<int64_t>(1, (rows_per_cta + kWarpRows - 1) / kWarpRows));
+    return (int)((w + 1) / 2 * 2);  // boxes of a multiple of 8 rows keep the 1024-byte swizzle alignment
 }
 
 int launch_f32_pipe(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, const F32PipeParams &p,
