@@ -168,8 +168,11 @@ int feml_b200_synchronize(fb_backend *b);
  * MulMat: src0 in {F32, Q8_0, Q4_0, Q4_K}, src1 = F32.
  * MulMatId: src0 in the same set, src1 = F32, src2 = I32. */
 int feml_b200_supports_op(fb_backend *b, int32_t op, const int32_t *src_dtypes, int32_t n);
-/* Backend::graph_compute (backend.rs:111-114): enqueues every node on the
- * backend stream and returns; no allocation, no host synchronisation. */
+/* Backend::graph_compute (backend.rs:111-114): enqueues the plan on the
+ * backend stream and returns. The first call of a plan may grow the scratch
+ * arena (with a stream synchronize) and captures the plan's CUDA graph (see
+ * feml_b200_set_plan_graphs); later calls of the same plan allocate nothing
+ * and do not synchronize. */
 int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan);
 /* Fill a vtable bound to `b` (for compile() and other generic callers). */
 int feml_b200_backend_vtable(fb_backend *b, fb_backend_vtable *vt);
@@ -178,8 +181,9 @@ int feml_b200_backend_vtable(fb_backend *b, fb_backend_vtable *vt);
 int feml_b200_buffer_device_ptr(fb_backend *b, uint32_t handle, void **ptr, uint64_t *size);
 int feml_b200_stream(fb_backend *b, void **stream);
 /* Bytes of device scratch the backend holds for mul_mat/mul_mat_id
- * intermediates (grown when a Compute buffer is created, never inside
- * graph_compute). */
+ * intermediates (sized when a Compute buffer is created; grown at most once
+ * more, at the first graph_compute of a plan that needs more;
+ * reserve_scratch sizes it ahead of time). */
 int feml_b200_scratch_bytes(fb_backend *b, uint64_t *bytes);
 int feml_b200_reserve_scratch(fb_backend *b, uint64_t bytes);
 /* Device allocations (cudaMalloc of buffers and of the scratch arena) this
