@@ -1,6 +1,6 @@
 // GGUF reader: maps a GGUF file (the llama.cpp / ggml model container, the
 // format feml's roadmap names as the producer of quantized weights,
-// docs/DESIGN.md "量化与 GGUF") read-only and parses its header, key/value
+// docs/DESIGN.md:282-286 of the reference) read-only and parses its header, key/value
 // metadata and tensor table, so that weights can be uploaded straight from
 // the mapping into a plan's Weights buffer (feml_b200_buffer_from_host_ptr,
 // feml_b200_write) without an intermediate host copy.

@@ -1,7 +1,7 @@
 """GGUF model files through the library's reader (feml_b200_gguf_*).
 
 GGUF is the llama.cpp / ggml model container that feml's roadmap names as the
-source of quantized weights (reference docs/DESIGN.md section 10: mmap +
+source of quantized weights (docs/DESIGN.md:282-286 of the reference: mmap +
 `buffer_from_host_ptr`). The file is mapped read-only by the C++ reader;
 tensor bytes are exposed as read-only numpy views of the mapping and go to
 the device in one copy each, either into a compiled plan's weight tensor

@@ -426,7 +426,7 @@ int feml_b200_buffer_from_host_ptr(fb_backend *b, const void *ptr, uint64_t size
                                    uint32_t *handle);
 
 /* GGUF reader (the llama.cpp / ggml model container that feml's roadmap names
- * as the source of quantized weights, docs/DESIGN.md section 10 "GGUF": mmap +
+ * as the source of quantized weights, docs/DESIGN.md:282-286 of the reference: mmap +
  * buffer_from_host_ptr). No counterpart exists in the reference yet; the
  * format follows the public GGUF specification (versions 2 and 3). The file
  * is mapped read-only; every pointer returned stays valid until
