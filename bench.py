@@ -1,29 +1,46 @@
 """Benchmark of the feml mul_mat / mul_mat_id path on B200.
 
-Default workload (N=1 GPU): Q8_0 decode GEMV, weights ne=[K=4096, M=4096]
-drawn N(0, 0.02) and quantized to Q8_0, activations [4096, 1] N(0, 1)
-quantized on device to Q8_0, seed 1. A step is one mul_mat over one weight
-matrix. Other workloads (--config c1|c3|c4|c5) are the remaining shapes of
-the hot path, for measurement.
+Headline workload (the same at every GPU count, so the driver's per-N values
+form a strong-scaling curve): C5, the Q8_0 mul_mat_id MoE layer -- 8 experts
+ne=[K=4096, M=14336] drawn N(0, 0.02) and quantized to Q8_0, 512 tokens of
+N(0, 1) activations, top-2 expert ids per token drawn uniformly without
+replacement. A step is one mul_mat_id over the whole layer.
 
-  value  device-timed throughput: CUDA-graph replay of the kernel-level
-         entry point on device-resident inputs, rotating through weight
-         copies whose total exceeds 2x L2 (every step streams its weights
-         from HBM); CUDA events on the launching stream, max over ranks.
-  e2e    the same metric through the reference-facing C ABI
-         (GraphBuilder -> compile -> write x from pinned host memory ->
-         graph_compute -> read y to pinned host memory), every step.
+  N = 1    the unsharded mul_mat_id (route + activation quantization +
+           grouped tcgen05 GEMM on one GPU).
+  N > 1    expert-sharded across the ranks (expert e on rank e % N), the
+           combine inside every step: by default each slot goes to the rank
+           that owns its token (token t on rank t // ceil(512 / N)) by peer
+           stores from the GEMM epilogue plus a bounded flag wait
+           (--combine owner); --combine replicate stores every slot on every
+           rank, --combine nccl all-reduces the slot tensor.
+
+  value  device-timed throughput (weight bytes per second, whole job):
+         CUDA-graph replay of the steps on device-resident inputs, CUDA
+         events on the launching stream after a barrier and a synchronize,
+         max over ranks.
+  e2e    the same metric through the public API with host buffers: at N=1
+         the reference-facing C ABI (GraphBuilder -> compile -> write x and
+         ids from pinned host memory -> graph_compute -> read y to pinned
+         host memory); at N>1 the feml_b200.shard wrapper (x and ids copied
+         in, each rank's own tokens' slots copied out).
+  extras the other shapes of the path on the same GPUs: at N=1 the decode
+         GEMV (C2, Q8_0 4096x4096, N=1, with its own e2e), the prefill GEMM
+         (C3, Q4_0 11008x4096x512, TOPS), C4 (Q4_K 4096x14336 at N=1/8/64)
+         and C1 (F32); at N>1 the row-sharded C4 decode step and the other
+         two C5 combines.
+
+Inputs of both arms come from the same seeded numpy draws: weights of
+expert e in 512-row chunks from default_rng([seed, e, chunk]), activations
+from default_rng([seed, 1000]), ids from default_rng([seed, 2000]); the
+quantized weight bytes are the device quantizer's (bit-identical to the
+oracle's).
 
 --impl reference times the reference's CPU mul_mat (the C restatement in
-oracle/, on all host threads; the Rust reference cannot be built here) on
-the same workload; under torchrun only rank 0 runs it.
-
-Multi-GPU (torchrun, --gpus N): by default every rank runs its own replica
-of the workload on its own GPU (independent decode streams, weak scaling);
-the only collectives are the timing barrier and the max-over-ranks
-reduction. --shard rows (c4) / --shard experts (c5) split one workload
-across the ranks instead (strong scaling, feml_b200.shard), with the NCCL
-all-gather / all-reduce that reassembles the output inside every step.
+oracle/ of feml-cpu/src/ops/mul_mat.rs:36-57, on all host threads; the Rust
+reference cannot be built in this image) on a bounded row sample of the
+same workload; under torchrun only rank 0 runs it. It imports nothing from
+feml_b200.
 """
 import argparse
 import json
@@ -33,6 +50,7 @@ import subprocess
 import sys
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
@@ -41,7 +59,11 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
-GEMV_MAX_COLS = 8  # widest activation the decode GEMV takes (gemv.cu kMaxCols)
+CHUNK_ROWS = 512  # weight rows per seeded draw
+
+# ggml block size and bytes per block (feml-core/src/dtype.rs:52-72)
+BLOCK = {"F32": (1, 4), "Q8_0": (32, 34), "Q4_0": (32, 18), "Q4_K": (256, 144)}
+DT_CODE = {"F32": 5, "Q4_0": 7, "Q8_0": 11, "Q4_K": 15}  # dtype.rs:14-35 discriminants
 
 CONFIGS = {
     "c1": dict(wtype="F32", K=4096, M=4096, N=32, seed=0, dist="uniform", metric="weight-GB/s",
@@ -57,31 +79,114 @@ CONFIGS = {
 }
 
 
-def load_peaks():
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    try:
-        with open(p) as f:
-            d = json.load(f)
-        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
-                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
-    except Exception:  # noqa: BLE001
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+def row_size(wtype, K):
+    bs, ts = BLOCK[wtype]
+    return K // bs * ts
 
 
-def profile_traffic(name):
-    """DRAM bytes per launch from a committed ncu summary (a line
-    `dram_bytes_per_launch: N` in profiles/<name>.md), or None."""
-    p = os.path.join(ROOT, "profiles", name + ".md")
-    try:
-        with open(p) as f:
-            for line in f:
-                if line.strip().startswith("dram_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].strip().split()[0])
-    except OSError:
-        pass
-    return None
+def step_units(cfg, N):
+    """(weight bytes per step, algorithmic bytes W + x + y (+ ids), ops 2*M*K per output column)."""
+    K, M = cfg["K"], cfg["M"]
+    wbytes = row_size(cfg["wtype"], K) * M * cfg.get("E", 1)
+    n_cols = N * cfg.get("n_sel", 1)
+    alg = wbytes + 4 * K * N + 4 * M * n_cols + (4 * n_cols if "E" in cfg else 0)
+    return wbytes, alg, 2.0 * K * M * n_cols
 
 
+def metric_value(cfg, N, seconds_per_step):
+    wbytes, _, ops_ = step_units(cfg, N)
+    if cfg["metric"] == "TOPS":
+        return ops_ / seconds_per_step / 1e12, "TOPS"
+    return wbytes / seconds_per_step / 1e9, "GB/s"
+
+
+def metric_name(cfg_name, cfg):
+    kind = "prefill GEMM TOPS" if cfg["metric"] == "TOPS" else (
+        "mul_mat_id weight-GB/s" if "E" in cfg else "decode weight-GB/s")
+    return f"mul_mat {kind} ({cfg_name}: {cfg['workload']})"
+
+
+def config_dict(cfg_name, cfg, N, world):
+    """The config both arms print (identical by construction)."""
+    if "E" in cfg:
+        par = "single GPU" if world == 1 else f"expert-sharded x{world}"
+    else:
+        par = "single GPU" if world == 1 else f"row-sharded x{world}"
+    return {"workload": cfg["workload"], "config": cfg_name, "K": cfg["K"], "M": cfg["M"], "N": N,
+            "weights_dtype": cfg["wtype"], "experts": cfg.get("E"), "n_selected": cfg.get("n_sel"),
+            "seed": cfg["seed"], "parallelism": par}
+
+
+# ---------------------------------------------------------------------------
+# Seeded inputs, shared by both arms
+# ---------------------------------------------------------------------------
+def host_weight_rows(cfg, expert, r0, r1, threads=None):
+    """f32 rows [r0, r1) of expert `expert`'s weight (ggml ne=[K, M] rows)."""
+    K = cfg["K"]
+    out = np.empty((r1 - r0, K), np.float32)
+
+    def fill(c):
+        a, b = c * CHUNK_ROWS, min(cfg["M"], (c + 1) * CHUNK_ROWS)
+        lo, hi = max(a, r0), min(b, r1)
+        if lo >= hi:
+            return
+        rng = np.random.default_rng([cfg["seed"], expert, c])
+        if cfg["dist"] == "uniform":
+            blk = rng.random((hi - a, K), dtype=np.float32) * np.float32(2) - np.float32(1)
+        else:
+            blk = rng.standard_normal((hi - a, K), dtype=np.float32) * np.float32(0.02)
+        out[lo - r0:hi - r0] = blk[lo - a:]
+
+    chunks = range(r0 // CHUNK_ROWS, (r1 + CHUNK_ROWS - 1) // CHUNK_ROWS)
+    with ThreadPoolExecutor(threads or min(16, os.cpu_count() or 1)) as ex:
+        list(ex.map(fill, chunks))
+    return out
+
+
+def host_x(cfg, N):
+    rng = np.random.default_rng([cfg["seed"], 1000])
+    if cfg["dist"] == "uniform":
+        return rng.random((N, cfg["K"]), dtype=np.float32) * np.float32(2) - np.float32(1)
+    return rng.standard_normal((N, cfg["K"]), dtype=np.float32)
+
+
+def host_ids(cfg, N):
+    rng = np.random.default_rng([cfg["seed"], 2000])
+    return np.stack([rng.permutation(cfg["E"])[:cfg["n_sel"]] for _ in range(N)]).astype(np.int32)
+
+
+_WEIGHTS = {}
+
+
+def device_weights(cfg, experts, rows=None):
+    """Quantized weights of the listed experts on the current device, uint8
+    [len(experts), M, row_bytes] (F32: the f32 bytes), quantized by the
+    library's quantizer expert by expert (kept for the next caller)."""
+    import torch
+    from feml_b200 import DType, ops
+    K, M = cfg["K"], cfg["M"]
+    r0, r1 = rows if rows else (0, M)
+    key = (cfg["workload"], tuple(experts), r0, r1)
+    if key in _WEIGHTS:
+        return _WEIGHTS[key]
+    rb = row_size(cfg["wtype"], K)
+    out = torch.empty((len(experts), r1 - r0, rb), dtype=torch.uint8, device="cuda")
+    for j, e in enumerate(experts):
+        wf = torch.from_numpy(host_weight_rows(cfg, e, r0, r1)).cuda()
+        if cfg["wtype"] == "F32":
+            out[j] = wf.view(torch.uint8).view(r1 - r0, rb)
+        else:
+            out[j] = ops.quantize(DType[cfg["wtype"]], wf)
+        del wf
+    torch.cuda.synchronize()
+    _WEIGHTS.clear()  # keep only the latest set
+    _WEIGHTS[key] = out
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Plumbing: ranks, clocks, timing
+# ---------------------------------------------------------------------------
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
 
@@ -120,8 +225,9 @@ class ClockSampler:
         if self.thread is not None:
             self.thread.join(timeout=5)
 
-    def summary(self, t0, t1):
-        rows = [s for t, s in self.samples if t0 - 0.25 <= t <= t1 + 0.25] or [s for _, s in self.samples]
+    def summary(self, windows):
+        rows = [s for t, s in self.samples if any(a - 0.25 <= t <= b + 0.25 for a, b in windows)]
+        rows = rows or [s for _, s in self.samples]
         mhz, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -140,20 +246,17 @@ class ClockSampler:
                 "samples": len(mhz)}
 
 
-# ---------------------------------------------------------------------------
 def dist_setup():
     import torch
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
     if ws > 1:
         import datetime
         import torch.distributed as dist
-        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(local)
     return ws, rank, local
 
 
@@ -173,598 +276,603 @@ def barrier():
         dist.barrier()
 
 
-def make_weights(cfg, rank, copies):
-    """Synthetic weights on device, quantized by the library's quantizer;
-    `copies` distinct buffers holding the same values (L2 rotation)."""
+class Timer:
+    """Device time of `steps` calls of step(i), replayed as CUDA graphs.
+
+    Three eager steps first (one-time setup stays out of the capture), then
+    the steps are captured in graphs of `chunk` steps (plus a tail graph);
+    warm-up replays every graph at least once and at least `warmup` steps;
+    the timed region is one replay of the whole sequence, between CUDA
+    events on the launching stream, with a barrier and a synchronize on both
+    sides; the result is the max over ranks."""
+
+    def __init__(self, windows):
+        self.windows = windows  # wall-clock spans of timed regions (clock sampling)
+        self.graphs = []
+
+    def run(self, step, steps, warmup, chunk_hint=64):
+        import torch
+        chunk = max(1, min(steps, max(chunk_hint, 16), 512))
+        n_full, tail = divmod(steps, chunk)
+        for i in range(min(3, steps)):
+            step(i)
+        torch.cuda.synchronize()
+
+        def capture(n):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for i in range(n):
+                    step(i)
+            return g
+
+        g_main = capture(chunk) if n_full else None
+        g_tail = capture(tail) if tail else None
+        self.graphs += [g for g in (g_main, g_tail) if g is not None]
+        torch.cuda.synchronize()
+        done = 0
+        while True:  # warm-up: each graph at least once, at least `warmup` steps
+            if g_main is not None:
+                g_main.replay()
+                done += chunk
+            if g_tail is not None:
+                g_tail.replay()
+                done += tail
+            if done >= warmup:
+                break
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.time()
+        e0.record(stream)
+        for _ in range(n_full):
+            g_main.replay()
+        if g_tail is not None:
+            g_tail.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        self.windows.append((t0, time.time()))
+        barrier()
+        return reduce_max(e0.elapsed_time(e1)) / steps  # ms per step
+
+    def release(self):
+        self.graphs = []
+
+
+def auto_steps(est_ms, target_ms=400.0, lo=20, hi=20000):
+    return int(min(hi, max(lo, target_ms / max(est_ms, 1e-4))))
+
+
+def estimate_ms(step):
+    import torch
+    for i in range(2):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(5):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 5
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch from a committed ncu summary (a line
+    `dram_bytes_per_launch: N` in profiles/<name>.md), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", name + ".md")) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def roofline(cfg, N, ms, world, kernel, prof):
+    peaks = load_peaks()
+    _, alg, ops_ = step_units(cfg, N)
+    sec = ms / 1e3
+    if cfg["metric"] == "TOPS":
+        a = ops_ / sec / 1e12
+        r = {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"] * world, "unit": "TFLOP/s",
+             "peak_note": f"dense bf16 TFLOP/s x {world} GPU(s), {peaks['source']} (the kernel issues f16 "
+                          f"tcgen05 MMAs; f16 dense measured within 3% of bf16 on this pool)"}
+    else:
+        a = alg / sec / 1e9
+        r = {"bound": "hbm", "achieved": a, "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
+             "peak_note": f"HBM copy bandwidth x {world} GPU(s), {peaks['source']}"}
+    r["frac"] = r["achieved"] / r["peak"]
+    r["traffic"] = profile_traffic(prof) if world == 1 else None
+    r["kernel"] = kernel
+    r["algorithmic_bytes_per_step"] = alg
+    r["timing"] = "per-step device time over CUDA-graph-replayed steps (all kernels of the step, launch gaps included)"
+    return r
+
+
+# ---------------------------------------------------------------------------
+# Single-GPU workloads (kernel-level API on device-resident inputs)
+# ---------------------------------------------------------------------------
+def mul_mat_case(cfg, N, timer, steps, warmup):
+    """Device-timed mul_mat of one config; returns (ms per step, weights, x)."""
     import torch
     from feml_b200 import DType, ops
-    K, M = cfg["K"], cfg["M"]
-    E = cfg.get("E", 1)
-    g = torch.Generator(device="cuda").manual_seed(cfg["seed"] * 1000 + rank)
-    dt = DType[cfg["wtype"]]
-    bufs = []
-    rb = dt.row_size(K)
-    base = torch.empty((E, M, rb if dt != DType.F32 else K * 4), dtype=torch.uint8, device="cuda")
-    for e in range(E):
-        if cfg["dist"] == "uniform":
-            wf = torch.rand((M, K), generator=g, device="cuda") * 2 - 1
-        else:
-            wf = torch.randn((M, K), generator=g, device="cuda") * 0.02
-        if dt == DType.F32:
-            base[e] = wf.contiguous().view(torch.uint8).view(M, K * 4)
-        else:
-            base[e] = ops.quantize(dt, wf.contiguous())
-        del wf
-    for _ in range(copies):
-        bufs.append(base.clone())
-    del base
-    torch.cuda.synchronize()
-    return bufs
-
-
-def make_x(cfg, rank, N, copies):
-    import torch
-    g = torch.Generator(device="cuda").manual_seed(cfg["seed"] * 1000 + 500 + rank)
-    xs = []
-    for _ in range(copies):
-        if cfg["dist"] == "uniform":
-            xs.append(torch.rand((N, cfg["K"]), generator=g, device="cuda") * 2 - 1)
-        else:
-            xs.append(torch.randn((N, cfg["K"]), generator=g, device="cuda"))
-    return xs
-
-
-def make_ids(cfg, rank, N):
-    rng = np.random.default_rng(cfg["seed"] * 1000 + 900 + rank)
-    E, n_sel = cfg["E"], cfg["n_sel"]
-    return np.stack([rng.permutation(E)[:n_sel] for _ in range(N)]).astype(np.int32)
-
-
-def step_units(cfg, N):
-    """(bytes streamed per step as the metric counts them, algorithmic bytes
-    per step, ops per step)."""
-    from feml_b200 import DType
     dt = DType[cfg["wtype"]]
     K, M = cfg["K"], cfg["M"]
-    wbytes = dt.row_size(K) * M * cfg.get("E", 1)
-    n_cols = N * cfg.get("n_sel", 1)
-    alg = wbytes + 4 * K * N + 4 * M * n_cols + (4 * n_cols if "E" in cfg else 0)
-    ops_ = 2.0 * K * M * n_cols
-    return wbytes, alg, ops_
-
-
-def metric_value(cfg, N, seconds_per_step):
-    wbytes, _, ops_ = step_units(cfg, N)
-    if cfg["metric"] == "TOPS":
-        return ops_ / seconds_per_step / 1e12, "TOPS"
-    return wbytes / seconds_per_step / 1e9, "GB/s"
-
-
-def kernels_per_step(cfg, N):
-    from feml_b200 import DType
-    dt = DType[cfg["wtype"]]
-    if "E" in cfg:
-        return 3 if dt != DType.F32 else 2
+    w0 = device_weights(cfg, [0])[0]
+    wbytes = w0.numel()
+    copies = max(1, math.ceil(2.5 * L2_BYTES / wbytes))
+    wts = [w0] + [w0.clone() for _ in range(copies - 1)]
     if dt == DType.F32:
-        return 1
-    from feml_b200 import ops
-    if ops.mul_mat_workspace(dt, cfg["K"], cfg["M"], N) == 0:
-        return 1  # fused GEMV
-    tc = dt in (DType.Q8_0, DType.Q4_0) and cfg["K"] % 256 == 0 and N > GEMV_MAX_COLS
-    split = (not tc and N > GEMV_MAX_COLS and cfg["K"] % 256 == 0 and
-             ops.mul_mat_workspace(dt, cfg["K"], cfg["M"], N) > _planar_bytes(cfg["K"], N))
-    return 3 if split else 2  # activation quantizer + GEMM (+ split-K reduction)
+        wts = [w.view(torch.float32).view(M, K) for w in wts]
+    x = torch.from_numpy(host_x(cfg, N)).cuda()
+    outs = [torch.empty((N, M), dtype=torch.float32, device="cuda") for _ in range(2)]
+    wsz = ops.mul_mat_workspace(dt, K, M, N)
+    work = torch.empty(max(wsz, 1), dtype=torch.uint8, device="cuda") if wsz else None
+
+    def step(i):
+        ops.mul_mat(dt, wts[i % copies], x, K, out=outs[i % 2], workspace=work)
+
+    if steps is None:
+        steps = auto_steps(estimate_ms(step))
+    ms = timer.run(step, steps, warmup, chunk_hint=copies)
+    return ms, steps, copies, wts[0], x
 
 
-def _planar_bytes(K, N):
-    """Planar Q8_0 activation bytes (qs, d, sum, each padded to 256 B)."""
-    pad = lambda v: (v + 255) // 256 * 256  # noqa: E731
-    return pad(N * K) + 2 * pad(N * (K // 32) * 4)
+def mul_mat_kernels_per_step(cfg, N):
+    from feml_b200 import DType, ops
+    return ops.mul_mat_launches(DType[cfg["wtype"]], cfg["K"], cfg["M"], N)
 
 
 def dominant_kernel(cfg, N):
-    from feml_b200 import DType
-    dt = DType[cfg["wtype"]]
-    tc = dt in (DType.Q8_0, DType.Q4_0) and cfg["K"] % 256 == 0
+    wt = cfg["wtype"]
     if "E" in cfg:
-        return "gemm_tc_kernel (grouped, tcgen05)" if tc else "gemm_q_kernel (grouped)"
-    if dt == DType.F32:
-        return "gemm_f32_pipe_kernel" if cfg["K"] % 4 == 0 else "gemm_f32_exact_kernel"
-    if N <= GEMV_MAX_COLS:
-        if dt == DType.Q4_K and 12288 <= cfg["K"] <= 16384:
+        return "gemm_tc_kernel (grouped, tcgen05)"
+    if wt == "F32":
+        return "gemm_f32_pipe_kernel"
+    if N <= 8:
+        if wt == "Q4_K" and 12288 <= cfg["K"] <= 16384:
             return "gemv_ks_kernel" if N == 1 else "gemv_ks_cols_kernel"
         return "gemv_kernel"
-    return "gemm_tc_kernel (tcgen05)" if tc else "gemm_q_kernel"
+    return "gemm_tc_kernel (tcgen05)"
 
 
-# ---------------------------------------------------------------------------
-def run_b200(args, cfg, N):
+def mul_mat_id_case(cfg, N, timer, steps, warmup):
     import torch
     from feml_b200 import DType, ops
-    import feml_b200 as F
-
-    ws, rank, local = dist_setup()
     dt = DType[cfg["wtype"]]
-    K, M = cfg["K"], cfg["M"]
-    wbytes, alg_bytes, ops_step = step_units(cfg, N)
-    copies = max(1, math.ceil(2.5 * L2_BYTES / wbytes))
-    wts = make_weights(cfg, rank, copies)
-    xs = make_x(cfg, rank, N, min(copies, 4))
-    is_moe = "E" in cfg
-    stream = torch.cuda.current_stream()
-    if is_moe:
-        ids_np = make_ids(cfg, rank, N)
-        ids = torch.from_numpy(ids_np).cuda()
-        n_sel = cfg["n_sel"]
-        outs = [torch.empty((N, n_sel, M), dtype=torch.float32, device="cuda") for _ in range(2)]
-        wsz = ops.mul_mat_id_workspace(dt, K, M, N, n_sel, cfg["E"])
-        work = torch.empty(max(wsz, 1), dtype=torch.uint8, device="cuda")
-        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    K, M, E, n_sel = cfg["K"], cfg["M"], cfg["E"], cfg["n_sel"]
+    w0 = device_weights(cfg, list(range(E)))
+    copies = max(1, math.ceil(2.5 * L2_BYTES / w0.numel()))
+    wts = [w0] + [w0.clone() for _ in range(copies - 1)]
+    x = torch.from_numpy(host_x(cfg, N)).cuda()
+    ids = torch.from_numpy(host_ids(cfg, N)).cuda()
+    outs = [torch.empty((N, n_sel, M), dtype=torch.float32, device="cuda") for _ in range(2)]
+    work = torch.empty(ops.mul_mat_id_workspace(dt, K, M, N, n_sel, E), dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
 
-        def step(i):
-            ops.mul_mat_id(dt, wts[i % copies], xs[i % len(xs)], ids, K, out=outs[i % 2], workspace=work,
-                           status=status)
-    else:
-        outs = [torch.empty((N, M), dtype=torch.float32, device="cuda") for _ in range(2)]
-        wsz = ops.mul_mat_workspace(dt, K, M, N)
-        work = torch.empty(max(wsz, 1), dtype=torch.uint8, device="cuda") if wsz else None
-        wview = [w[0] if dt != DType.F32 else w[0].view(torch.float32) for w in wts]
+    def step(i):
+        ops.mul_mat_id(dt, wts[i % copies], x, ids, K, out=outs[i % 2], workspace=work, status=status)
 
-        def step(i):
-            ops.mul_mat(dt, wview[i % copies], xs[i % len(xs)], K, out=outs[i % 2], workspace=work)
-
-    # capture the step sequence in CUDA graphs (launch cost off the timeline)
-    chunk = min(args.steps, max(copies, 64) if args.steps >= 64 else args.steps)
-    chunk = max(1, min(chunk, 1024))
-    for i in range(3):
-        step(i)
-    torch.cuda.synchronize()
-
-    def capture(n):
-        if n == 0:
-            return None
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr):
-            for i in range(n):
-                step(i)
-        return gr
-
-    g_main = capture(chunk)
-    g_tail = capture(args.steps % chunk)
-    torch.cuda.synchronize()
-
-    def run_steps(k):
-        for _ in range(k // chunk):
-            g_main.replay()
-        if k % chunk:
-            if k == args.steps and g_tail is not None:
-                g_tail.replay()
-            else:
-                for i in range(k % chunk):
-                    step(i)
-
-    run_steps(max(args.warmup, 3))
-    torch.cuda.synchronize()
-
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.time()
-    e0.record(stream)
-    run_steps(args.steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    t1 = time.time()
-    barrier()
-    ms = e0.elapsed_time(e1)
-    ms_max = reduce_max(ms)
-    time.sleep(0.25)
-    sampler.stop()
-    clocks = sampler.summary(t0, t1)
-
-    sec_step = ms_max / 1e3 / args.steps
-    per_gpu_val, unit = metric_value(cfg, N, sec_step)
-    value = per_gpu_val * ws
-
-    # ---- e2e through the reference-facing C ABI -------------------------------
-    e2e = run_e2e(args, cfg, N, dt, wts, copies, ids_np if is_moe else None, local)
-
-    # ---- roofline of the dominant kernel ------------------------------------
-    peaks = load_peaks()
-    if cfg["metric"] == "TOPS":
-        achieved = ops_step / sec_step / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / peaks["bf16_tflops"],
-                "peak_note": f"bf16 dense {peaks['source']} (the kernel issues f16 tcgen05 MMAs on exact integer / split operands)"}
-    else:
-        achieved = alg_bytes / sec_step / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "peak_note": f"HBM copy bandwidth, {peaks['source']}"}
-    prof_name = f"{args.config}_{cfg['wtype'].lower()}_n{N}"
-    tr = profile_traffic(prof_name)
-    roof["traffic"] = tr
-    roof["kernel"] = dominant_kernel(cfg, N)
-    roof["algorithmic_bytes_per_launch"] = alg_bytes
-    roof["timing"] = "per-step device time (CUDA events over the graph-replayed steps), includes launch gaps"
-
-    result = {
-        "metric": f"mul_mat {'prefill GEMM TOPS' if cfg['metric'] == 'TOPS' else 'decode weight-GB/s'} "
-                  f"({args.config}: {cfg['workload']})",
-        "value": value, "unit": unit, "n_gpus": ws, "steps": args.steps, "warmup": max(args.warmup, 3),
-        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 dot / f32 scale" if dt != DType.F32 else "f32",
-        "data": "synthetic (seeded torch.randn weights quantized on device; seeded activations)",
-        "config": {"workload": cfg["workload"], "config": args.config, "K": K, "M": M, "N": N,
-                   "weights_dtype": cfg["wtype"], "experts": cfg.get("E"), "n_selected": cfg.get("n_sel"),
-                   "l2": f"{copies} rotating weight copies ({copies * wbytes / 2**20:.0f} MiB, > 2x L2)",
-                   "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
-        "roofline": roof,
-        "e2e": e2e,
-        "gpu_launches": args.steps * kernels_per_step(cfg, N),
-        "clocks": clocks,
-    }
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(cfg, N, wts[0], budget_s=args.cpu_seconds)
-    if rank == 0:
-        print(json.dumps(result), flush=True)
-    # release graphs before the process group goes away
-    del g_main, g_tail
-    if ws > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
+    if steps is None:
+        steps = auto_steps(estimate_ms(step))
+    ms = timer.run(step, steps, warmup, chunk_hint=copies)
+    assert int(status.item()) == 0
+    return ms, steps, copies, w0
 
 
-def run_e2e(args, cfg, N, dt, wts, copies, ids_np, local):
-    """Same metric through the C ABI with host buffers: per step, x from
-    pinned host memory -> device (write), graph_compute, y -> pinned host
-    memory (read, which synchronizes the stream)."""
+def e2e_c_abi(cfg, N, w_dev, steps, warmup, local):
+    """The metric through the reference-facing C ABI with host buffers."""
     import torch
     import feml_b200 as F
     from feml_b200 import DType, GraphBuilder
-
     K, M = cfg["K"], cfg["M"]
+    is_moe = "E" in cfg
+    dt = DType[cfg["wtype"]]
     be = F.B200Backend.open(local)
-    n_plans = min(copies, 24)
-    is_moe = ids_np is not None
-    w_host = wts[0].cpu().numpy()  # the quantized bytes, uploaded once per plan (outside the timed region)
-    plans = []
-    for p in range(n_plans):
-        g = GraphBuilder()
-        if is_moe:
-            E, n_sel = cfg["E"], cfg["n_sel"]
-            w = g.weight("w", dt, [K, M, E])
-            xi = g.input("x", DType.F32, [K, N])
-            ii = g.input("ids", DType.I32, [n_sel, N])
-            o = g.mul_mat_id(w, xi, ii, n_sel)
-        else:
-            w = g.weight("w", dt, [K, M])
-            xi = g.input("x", DType.F32, [K, N])
-            o = g.mul_mat(w, xi)
-            ii = None
-        g.mark_output(o)
-        plan = g.compile(be)
-        plan.write_tensor(be, w, w_host)
-        if is_moe:
-            plan.write_tensor(be, ii, ids_np)
-        plans.append((plan, plan.find(xi), plan.find(o), g))
-    x_host = torch.randn((N, K), dtype=torch.float32).pin_memory()
+    w_host = w_dev.cpu().numpy()
+    g = GraphBuilder()
+    if is_moe:
+        w = g.weight("w", dt, [K, M, cfg["E"]])
+        xi = g.input("x", DType.F32, [K, N])
+        ii = g.input("ids", DType.I32, [cfg["n_sel"], N])
+        o = g.mul_mat_id(w, xi, ii, cfg["n_sel"])
+    else:
+        w = g.weight("w", dt, [K, M])
+        xi = g.input("x", DType.F32, [K, N])
+        ii = None
+        o = g.mul_mat(w, xi)
+    g.mark_output(o)
+    plan = g.compile(be)
+    plan.write_tensor(be, w, w_host.reshape(-1).view(np.uint8))
+    x_host = torch.from_numpy(host_x(cfg, N)).pin_memory()
+    ids_host = torch.from_numpy(host_ids(cfg, N)).pin_memory() if is_moe else None
     y_elems = N * M * (cfg["n_sel"] if is_moe else 1)
     y_host = torch.empty(y_elems, dtype=torch.float32).pin_memory()
-    steps = min(args.steps, args.e2e_steps)
+    px, po = plan.find(xi), plan.find(o)
+    pi = plan.find(ii) if is_moe else None
     x_bytes, y_bytes = N * K * 4, y_elems * 4
+    i_bytes = ids_host.numel() * 4 if is_moe else 0
 
-    def one(i):
-        plan, px, po, _ = plans[i % n_plans]
+    def one():
         be.write_ptr(plan.buffers[px.buffer].handle, px.offset, x_host.data_ptr(), x_bytes)
+        if is_moe:
+            be.write_ptr(plan.buffers[pi.buffer].handle, pi.offset, ids_host.data_ptr(), i_bytes)
         be.graph_compute(plan)
         be.read_ptr(plan.buffers[po.buffer].handle, po.offset, y_host.data_ptr(), y_bytes)
 
-    for i in range(max(3, min(args.warmup, 50))):
-        one(i)
+    for _ in range(max(3, warmup)):
+        one()
     be.synchronize()
-    barrier()
+    if steps is None:  # about half a second of end-to-end steps
+        t0 = time.perf_counter()
+        for _ in range(3):
+            one()
+        steps = int(min(2000, max(10, 0.5 / ((time.perf_counter() - t0) / 3))))
     t0 = time.perf_counter()
-    for i in range(steps):
-        one(i)
+    for _ in range(steps):
+        one()
     be.synchronize()
-    dt_s = reduce_max(time.perf_counter() - t0)
-    v, unit = metric_value(cfg, N, dt_s / steps)
-    import torch.distributed as dist
-    ws = dist.get_world_size() if dist.is_initialized() else 1
-    for plan, *_ in plans:
-        plan.release(be)
+    dt_s = (time.perf_counter() - t0) / steps
+    plan.release(be)
     be.close()
-    return {"value": v * ws, "unit": unit, "h2d_bytes_per_step": x_bytes, "d2h_bytes_per_step": y_bytes,
-            "steps": steps, "ms_per_step": dt_s / steps * 1e3,
-            "path": "GraphBuilder->compile->write(pinned x)->graph_compute->read(pinned y), libfeml_b200 C ABI"}
+    v, unit = metric_value(cfg, N, dt_s)
+    return {"value": v, "unit": unit, "h2d_bytes_per_step": x_bytes + i_bytes, "d2h_bytes_per_step": y_bytes,
+            "steps": steps, "ms_per_step": dt_s * 1e3,
+            "path": "GraphBuilder->compile->write(pinned x" + (", ids" if is_moe else "") +
+                    ")->graph_compute->read(pinned y), libfeml_b200 C ABI"}
+
+
+def extra_line(name, cfg, N, ms, steps, copies, world=1, e2e=None):
+    v, unit = metric_value(cfg, N, ms / 1e3)
+    r = roofline(cfg, N, ms, world, dominant_kernel(cfg, N), f"{name}_{cfg['wtype'].lower()}_n{N}")
+    d = {"metric": metric_name(name, cfg), "value": v, "unit": unit, "ms_per_step": ms, "steps": steps,
+         "N": N, "roofline_frac": r["frac"], "roofline": r,
+         "l2": f"{copies} rotating weight copies" if copies > 1 else "weights larger than 2x L2"}
+    if e2e is not None:
+        d["e2e"] = e2e
+    return d
+
+
+def run_extras_single(args, timer):
+    """The other workloads of the path on this GPU (N=1 only)."""
+    import torch
+    out, launches = {}, 0
+    todo = [("c2", 1), ("c3", 512), ("c4", 1), ("c4", 8), ("c4", 64), ("c1", 32)]
+    for name, N in todo:
+        cfg = CONFIGS[name]
+        ms, steps, copies, w0, _ = mul_mat_case(cfg, N, timer, None, args.warmup)
+        e2e = None
+        if name == "c2":
+            e2e = e2e_c_abi(cfg, N, w0, None, args.warmup, torch.cuda.current_device())
+        key = f"{name}_n{N}" if name == "c4" else name
+        out[key] = extra_line(name, cfg, N, ms, steps, copies, e2e=e2e)
+        launches += steps * mul_mat_kernels_per_step(cfg, N)
+        del w0
+        torch.cuda.empty_cache()
+    return out, launches
 
 
 # ---------------------------------------------------------------------------
-def run_sharded(args, cfg, N):
-    """Strong scaling of one workload split across the ranks: --shard rows
-    (weight rows, all-gather of the output slices) or --shard experts
-    (experts e % world, sum all-reduce of the slot outputs). A step is the
-    local kernels plus the collective that leaves the full output on every
-    rank; the step sequence (NCCL calls included) is replayed as a CUDA graph."""
+# Multi-GPU workloads
+# ---------------------------------------------------------------------------
+def experts_sharded_case(cfg, N, timer, steps, warmup, combine, e2e_steps):
+    """C5 expert-sharded across the ranks with the given combine."""
     import torch
+    from feml_b200 import DType
+    from feml_b200.shard import ExpertShardedMulMatId
     import torch.distributed as dist
-    from feml_b200 import DType, ops
-    from feml_b200.shard import ExpertShardedMulMatId, RowShardedMulMat, local_experts, row_range
+    rank, ws = dist.get_rank(), dist.get_world_size()
+    dt = DType[cfg["wtype"]]
+    K, E, n_sel = cfg["K"], cfg["E"], cfg["n_sel"]
+    mine = [e for e in range(E) if e % ws == rank]
+    w_local = device_weights(cfg, mine)
+    copies = max(1, math.ceil(2.5 * L2_BYTES / max(w_local.numel(), 1)))
+    wts = [w_local] + [w_local.clone() for _ in range(copies - 1)]
+    x = torch.from_numpy(host_x(cfg, N)).cuda()
+    ids = torch.from_numpy(host_ids(cfg, N)).cuda()
+    fused = combine in ("owner", "replicate")
+    mod = ExpertShardedMulMatId(dt, wts[0], K, E, local=True, fused=fused, max_tokens=N, max_selected=n_sel,
+                                combine="owner" if combine == "owner" else "replicate")
 
-    ws, rank, local = dist_setup()
-    if ws == 1 and not dist.is_initialized():
-        import datetime
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", str(29500 + (os.getpid() % 1000)))
-        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    def step(i):
+        mod.w_local = wts[i % copies]
+        return mod(x, ids)
+
+    if steps is None:
+        steps = auto_steps(reduce_max(estimate_ms(step)))
+    ms = timer.run(step, steps, warmup, chunk_hint=copies)
+    e2e = None
+    if e2e_steps:
+        lo, hi = mod.token_range(N) if combine == "owner" else (0, N)
+        x_host = torch.from_numpy(host_x(cfg, N)).pin_memory()
+        ids_host = torch.from_numpy(host_ids(cfg, N)).pin_memory()
+        y_host = torch.empty((hi - lo) * n_sel * cfg["M"], dtype=torch.float32).pin_memory()
+
+        def one(i):
+            x.copy_(x_host, non_blocking=True)
+            ids.copy_(ids_host, non_blocking=True)
+            y_host.copy_(step(i).reshape(-1), non_blocking=True)
+
+        for i in range(max(3, warmup)):
+            one(i)
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            one(i)
+        torch.cuda.synchronize()
+        e2e_s = reduce_max(time.perf_counter() - t0) / e2e_steps
+        v, unit = metric_value(cfg, N, e2e_s)
+        e2e = {"value": v, "unit": unit, "h2d_bytes_per_step": x_host.numel() * 4 + ids_host.numel() * 4,
+               "d2h_bytes_per_step": y_host.numel() * 4, "steps": e2e_steps, "ms_per_step": e2e_s * 1e3,
+               "path": "feml_b200.shard.ExpertShardedMulMatId: pinned host x, ids -> device -> "
+                       + ("this rank's tokens' slots" if combine == "owner" else "all slots") + " -> pinned host"}
+    torch.cuda.synchronize()
+    barrier()
+    mod.close()
+    kernels = 3 + (1 if fused else 0)  # route + quantize + grouped GEMM (+ flag wait)
+    return ms, steps, copies, e2e, kernels
+
+
+def rows_sharded_case(cfg, N, timer, warmup, fused):
+    """C4 row-sharded decode step (GEMV on this rank's rows + the combine)."""
+    import torch
+    from feml_b200 import DType
+    from feml_b200.shard import RowShardedMulMat, row_range
+    import torch.distributed as dist
+    rank, ws = dist.get_rank(), dist.get_world_size()
     dt = DType[cfg["wtype"]]
     K, M = cfg["K"], cfg["M"]
-    wbytes_total, alg_total, ops_total = step_units(cfg, N)
-    rb = dt.row_size(K)
-    g = torch.Generator(device="cuda").manual_seed(cfg["seed"] * 1000)
-    is_moe = args.shard == "experts"
-    if is_moe:
-        E, n_sel = cfg["E"], cfg["n_sel"]
-        n_loc = local_experts(E, rank, ws)
-        local_w = torch.empty((max(n_loc, 1), M, rb), dtype=torch.uint8, device="cuda")
-        for e in range(E):  # every rank draws all experts from one seed and keeps its own
-            wf = torch.randn((M, K), generator=g, device="cuda") * 0.02
-            if e % ws == rank:
-                local_w[e // ws] = ops.quantize(dt, wf)
-            del wf
-        local_w = local_w[:n_loc]
-        local_bytes = n_loc * M * rb
+    lo, hi, _ = row_range(M, rank, ws)
+    w_local = device_weights(cfg, [0], rows=(lo, hi))[0]
+    copies = max(1, math.ceil(2.5 * L2_BYTES / max(w_local.numel(), 1)))
+    wts = [w_local] + [w_local.clone() for _ in range(copies - 1)]
+    x = torch.from_numpy(host_x(cfg, N)).cuda()
+    mod = RowShardedMulMat(dt, wts[0], K, M, local=True, fused=fused)
+
+    def step(i):
+        mod.w_local = wts[i % copies]
+        return mod(x)
+
+    steps = auto_steps(reduce_max(estimate_ms(step)))
+    ms = timer.run(step, steps, warmup, chunk_hint=copies)
+    torch.cuda.synchronize()
+    barrier()
+    mod.close()
+    return ms, steps, copies
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline and the reference arm
+# ---------------------------------------------------------------------------
+def cpu_sample(cfg, N, rows, threads, seconds_budget, max_iters=1000):
+    """The reference's CPU mul_mat (oracle/: feml-cpu/src/ops/mul_mat.rs:36-57
+    restated in C) on the first `rows` weight rows of every expert and every
+    output column. The reference has no quantized kernel: its path is the F32
+    mul_mat on the dequantized weights and, as on the device, Q8_0-rounded
+    activations. Returns seconds per full step (scaled by M / rows)."""
+    once = reference_sampler(cfg, N, rows, threads)
+    once()
+    t_end = time.perf_counter() + seconds_budget
+    n, tx, tm = 0, 0.0, 0.0
+    while True:
+        a, b = once()
+        tx, tm = tx + a, tm + b
+        n += 1
+        if time.perf_counter() > t_end or n >= max_iters:
+            break
+    return (tx + tm * (cfg["M"] / rows)) / n, n, tx + tm
+
+
+def sample_rows(cfg, N, macs):
+    n_cols = N * cfg.get("n_sel", 1)
+    return int(min(cfg["M"], max(8, macs // (cfg["K"] * n_cols))))
+
+
+def cpu_baseline(cfg, N, budget_s):
+    rows = sample_rows(cfg, N, 1.5e8)
+    n_cols = N * cfg.get("n_sel", 1)
+    sec1, n1, t1 = cpu_sample(cfg, N, rows, 1, budget_s)
+    threads = os.cpu_count() or 1
+    secm, nm, tm = cpu_sample(cfg, N, rows, threads, budget_s / 2)
+    v1, unit = metric_value(cfg, N, sec1)
+    vm, _ = metric_value(cfg, N, secm)
+    return {"value": v1, "unit": unit, "cores": 1, "kind": "port",
+            "sample": f"{rows}/{cfg['M']} weight rows of every expert x {n_cols} output columns per iteration, "
+                      f"{n1} iterations ({t1:.1f} s) on 1 core (the reference executes plans single-threaded, "
+                      f"docs/api-guide.md:147); value scaled to the full step",
+            "sec_per_full_step": sec1,
+            "multi_thread": {"value": vm, "unit": unit, "cores": threads, "iterations": nm,
+                             "sec_per_full_step": secm}}
+
+
+def reference_sampler(cfg, N, rows, threads):
+    """A step of the reference's CPU path on the first `rows` weight rows of
+    every expert and every output column; returns the callable."""
+    from oracle import oracle as O
+    K = cfg["K"]
+    code = DT_CODE[cfg["wtype"]]
+    experts = list(range(cfg.get("E", 1)))
+    wdeq = []
+    for e in experts:
+        wf = host_weight_rows(cfg, e, 0, rows)
+        wdeq.append(wf if cfg["wtype"] == "F32" else O.dequantize(code, O.quantize(code, wf), K))
+    x = host_x(cfg, N)
+    if "E" in cfg:
+        ids = host_ids(cfg, N)
+        groups = [(e, np.nonzero((ids == e).any(axis=1))[0]) for e in experts]
     else:
-        lo, hi, R = row_range(M, rank, ws)
-        wf = torch.randn((M, K), generator=g, device="cuda") * 0.02
-        local_w = ops.quantize(dt, wf[lo:hi].contiguous())
-        del wf
-        local_bytes = (hi - lo) * rb
-    copies = max(1, math.ceil(2.5 * L2_BYTES / max(local_bytes, 1)))
-    wts = [local_w.clone() for _ in range(copies)]
-    gx = torch.Generator(device="cuda").manual_seed(cfg["seed"] * 1000 + 500)
-    x = torch.randn((N, K), generator=gx, device="cuda")
-    if is_moe:
-        ids_np = make_ids(cfg, 0, N)
-        ids = torch.from_numpy(ids_np).cuda()
-        if args.fused:  # one peer-buffer set; the weight copies rotate under it
-            mod = ExpertShardedMulMatId(dt, wts[0], K, E, local=True, fused=True, max_tokens=N,
-                                        max_selected=n_sel)
+        groups = [(0, np.arange(N))]
 
-            def step(i):
-                mod.w_local = wts[i % copies]
-                return mod(x, ids)
-        else:
-            mods = [ExpertShardedMulMatId(dt, w, K, E, local=True) for w in wts]
+    def sample():
+        """(seconds rounding the activations -- once per full step, not scaled
+        by the row sample -- and seconds of the sampled mul_mat rows)."""
+        t0 = time.perf_counter()
+        xf = x if cfg["wtype"] == "F32" else O.dequantize(O.DT_Q8_0, O.quantize(O.DT_Q8_0, x), K)
+        t1 = time.perf_counter()
+        for e, toks in groups:
+            if len(toks):
+                O.mul_mat_f32(wdeq[e], xf[toks], nthreads=threads)
+        return t1 - t0, time.perf_counter() - t1
 
-            def step(i):
-                return mods[i % copies](x, ids)
-    else:
-        if args.fused:  # one peer-buffer set; the weight copies rotate under it
-            mod = RowShardedMulMat(dt, wts[0], K, M, local=True, fused=True)
+    return sample
 
-            def step(i):
-                mod.w_local = wts[i % copies]
-                return mod(x)
-        else:
-            mods = [RowShardedMulMat(dt, w, K, M, local=True) for w in wts]
 
-            def step(i):
-                return mods[i % copies](x)
+def run_reference(args, cfg_name, cfg, N):
+    """The reference's CPU mul_mat on all host threads (the oracle port; the
+    Rust reference cannot be built here). Each step is a bounded sample of
+    the workload (the first weight rows of every expert, all output
+    columns), sized from a calibration run so the whole run takes about a
+    minute and a half; the value is scaled to the full step. Imports nothing
+    from feml_b200."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    M = cfg["M"]
+    threads = os.cpu_count() or 1
+    total_steps = args.steps + args.warmup
+    probe_rows = min(M, 16)
+    probe = reference_sampler(cfg, N, probe_rows, threads)
+    probe()
+    t_x, t_mm = probe()
+    per_row = t_mm / probe_rows
+    target = min(2.0, max(0.05, 90.0 / total_steps))  # seconds per sample step
+    rows = int(min(M, max(probe_rows, (target - t_x) / max(per_row, 1e-9))))
+    sample = reference_sampler(cfg, N, rows, threads)
+    for _ in range(args.warmup):
+        sample()
+    tx = tm = 0.0
+    for _ in range(args.steps):
+        a, b = sample()
+        tx, tm = tx + a, tm + b
+    sec_full = (tx + tm * (M / rows)) / args.steps
+    v, unit = metric_value(cfg, N, sec_full)
+    n_cols = N * cfg.get("n_sel", 1)
+    print(json.dumps({
+        "impl": "reference", "metric": metric_name(cfg_name, cfg), "value": v, "unit": unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec_full * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded numpy draws shared with the GPU arm)",
+        "config": config_dict(cfg_name, cfg, N, world),
+        "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port",
+                         "sample": f"{rows}/{M} weight rows of every expert x {n_cols} output columns per step, "
+                                   f"scaled to the full step; F32 mul_mat (feml-cpu/src/ops/mul_mat.rs:36-57 "
+                                   f"restated in C) on dequantized weights and Q8_0-rounded activations"},
+        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
 
-    chunk = max(1, min(args.steps, max(copies, 16), 256))
-    for i in range(3):
-        step(i)
-    torch.cuda.synchronize()
-    gr = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gr):
-        for i in range(chunk):
-            step(i)
-    torch.cuda.synchronize()
-    reps = max(1, args.steps // chunk)
-    steps = reps * chunk
-    for _ in range(max(1, max(args.warmup, 3) // chunk + 1)):
-        gr.replay()
-    torch.cuda.synchronize()
+
+# ---------------------------------------------------------------------------
+def run_b200(args, cfg_name, cfg, N):
+    import torch
+    ws, rank, local = dist_setup()
+    windows = []
+    timer = Timer(windows)
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    barrier()
-    torch.cuda.synchronize()
-    stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.time()
-    e0.record(stream)
-    for _ in range(reps):
-        gr.replay()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    t1 = time.time()
-    barrier()
-    ms_max = reduce_max(e0.elapsed_time(e1))
+    is_moe = "E" in cfg
+    extras = {}
+    if ws == 1:
+        if is_moe:
+            ms, steps, copies, w0 = mul_mat_id_case(cfg, N, timer, args.steps, args.warmup)
+            launches = steps * 3
+        else:
+            ms, steps, copies, w0, _ = mul_mat_case(cfg, N, timer, args.steps, args.warmup)
+            launches = steps * mul_mat_kernels_per_step(cfg, N)
+        e2e = e2e_c_abi(cfg, N, w0, args.e2e_steps, args.warmup, local)
+        del w0
+        torch.cuda.empty_cache()
+        if not args.no_extras:
+            extras, extra_launches = run_extras_single(args, timer)
+            launches += extra_launches
+        scaling = "strong"
+    else:
+        if not is_moe:
+            raise SystemExit("the multi-GPU headline is the expert-sharded C5 (--config c5)")
+        ms, steps, copies, e2e, k = experts_sharded_case(cfg, N, timer, args.steps, args.warmup, args.combine,
+                                                         args.e2e_steps or 50)
+        launches = steps * k
+        if not args.no_extras:
+            for comb in [c for c in ("owner", "replicate", "nccl") if c != args.combine]:
+                ms_c, st_c, cp_c, _, k_c = experts_sharded_case(cfg, N, timer, None, args.warmup, comb, 0)
+                extras[f"c5_{comb}"] = extra_line("c5", cfg, N, ms_c, st_c, cp_c, world=ws)
+                extras[f"c5_{comb}"]["combine"] = comb
+                launches += st_c * k_c
+            c4 = CONFIGS["c4"]
+            ms_r, st_r, cp_r = rows_sharded_case(c4, 1, timer, args.warmup, fused=True)
+            extras["c4_rows_fused_n1"] = extra_line("c4", c4, 1, ms_r, st_r, cp_r, world=ws)
+            launches += st_r * 2
+        scaling = "strong"
     time.sleep(0.25)
     sampler.stop()
-    sec_step = ms_max / 1e3 / steps
-    value, unit = metric_value(cfg, N, sec_step)  # the whole job's work per step
-    # e2e: x from pinned host memory, the sharded op, y to pinned host memory
-    x_host = torch.randn((N, K), dtype=torch.float32).pin_memory()
-    y_elems = N * M * (cfg["n_sel"] if is_moe else 1)
-    y_host = torch.empty(y_elems, dtype=torch.float32).pin_memory()
-    e2e_steps = min(steps, args.e2e_steps)
-    for i in range(5):
-        x.copy_(x_host, non_blocking=True)
-        y_host.copy_(step(i).reshape(-1), non_blocking=True)
-    torch.cuda.synchronize()
-    barrier()
-    tt = time.perf_counter()
-    for i in range(e2e_steps):
-        x.copy_(x_host, non_blocking=True)
-        y_host.copy_(step(i).reshape(-1), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-    e2e_s = reduce_max(time.perf_counter() - tt) / e2e_steps
-    e2e_v, _ = metric_value(cfg, N, e2e_s)
-    peaks = load_peaks()
-    # ours per step: route + quantize + grouped GEMM (MoE) or GEMV (+ quantize), plus the wait kernel when fused
-    n_k = (3 if is_moe else 1 + (1 if ops.mul_mat_workspace(dt, K, M, N) else 0)) + (1 if args.fused else 0)
+    clocks = sampler.summary(windows)
+    value, unit = metric_value(cfg, N, ms / 1e3)
     result = {
-        "metric": f"mul_mat {'mul_mat_id expert-sharded' if is_moe else 'row-sharded'} weight-GB/s "
-                  f"({args.config}: {cfg['workload']})",
-        "value": value, "unit": unit, "n_gpus": ws, "steps": steps, "warmup": max(args.warmup, 3),
-        "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int8 dot / f32 scale", "data": "synthetic (seeded torch.randn weights quantized on device)",
-        "config": {"workload": cfg["workload"], "config": args.config, "K": K, "M": M, "N": N,
-                   "weights_dtype": cfg["wtype"], "experts": cfg.get("E"), "n_selected": cfg.get("n_sel"),
-                   "parallelism": f"{'expert' if is_moe else 'row'}-sharded x{ws} + " + (
-                       "peer-memory stores (fused)" if args.fused else
-                       ("NCCL all_reduce" if is_moe else "NCCL all_gather")),
-                   "l2": f"{copies} rotating local weight copies ({copies * local_bytes / 2**20:.0f} MiB per rank)"},
-        "roofline": {"bound": "hbm", "achieved": alg_total / sec_step / 1e9, "peak": peaks["hbm_gbs"] * ws,
-                     "unit": "GB/s", "frac": alg_total / sec_step / 1e9 / (peaks["hbm_gbs"] * ws), "traffic": None,
-                     "peak_note": f"{ws} x HBM copy bandwidth ({peaks['source']}); step includes the collective"},
-        "e2e": {"value": e2e_v, "unit": unit, "h2d_bytes_per_step": N * K * 4, "d2h_bytes_per_step": y_elems * 4,
-                "steps": e2e_steps, "path": "feml_b200.shard wrapper, pinned host x -> device -> pinned host y"},
-        "gpu_launches": steps * n_k,
-        "clocks": sampler.summary(t0, t1),
+        "metric": metric_name(cfg_name, cfg), "value": value, "unit": unit, "n_gpus": ws, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": "int8 dot / f32 scale" if cfg["wtype"] != "F32" else "f32",
+        "data": "synthetic (seeded numpy draws, quantized on device by the library's quantizer)",
+        "config": config_dict(cfg_name, cfg, N, ws),
+        "l2": f"{copies} rotating weight copies per rank" if copies > 1 else "weights larger than 2x L2 per rank",
+        "combine": None if ws == 1 else args.combine,
+        "roofline": roofline(cfg, N, ms, ws, dominant_kernel(cfg, N), f"{cfg_name}_{cfg['wtype'].lower()}_n{N}"),
+        "e2e": e2e,
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "extras": extras,
     }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(cfg, N, args.cpu_seconds)
     if rank == 0:
         print(json.dumps(result), flush=True)
-    del gr
-    dist.barrier()
-    dist.destroy_process_group()
-
-
-# ---------------------------------------------------------------------------
-def cpu_baseline(cfg, N, wq_dev, budget_s=10.0, threads=None):
-    """The reference's CPU mul_mat (oracle/, the C restatement of
-    feml-cpu/src/ops/mul_mat.rs:36-57) on a bounded sample of the workload.
-    The reference has no quantized kernel: its path is the F32 mul_mat on the
-    dequantized weights (dequantized once, as a user of the reference would
-    store them) and, as on the device, Q8_0-rounded activations."""
-    from oracle import oracle as O
-    from feml_b200 import DType
-    dt = DType[cfg["wtype"]]
-    K, M = cfg["K"], cfg["M"]
-    threads = threads or (os.cpu_count() or 1)
-    wq = wq_dev[0].cpu().numpy() if wq_dev.dim() == 3 else wq_dev.cpu().numpy()
-    rng = np.random.default_rng(cfg["seed"])
-    x = rng.standard_normal((N, K)).astype(np.float32)
-    # sample: enough weight rows that one sample step costs ~0.1-0.5 s
-    macs_target = 2e8
-    n_cols = N * cfg.get("n_sel", 1)
-    rows = int(min(M, max(64, macs_target // (K * n_cols))))
-    code = {DType.F32: O.DT_F32, DType.Q8_0: O.DT_Q8_0, DType.Q4_0: O.DT_Q4_0, DType.Q4_K: O.DT_Q4_K}[dt]
-    if dt == DType.F32:
-        wf = wq[:rows].view(np.float32).reshape(rows, K)
-    else:
-        wf = O.dequantize(code, wq[:rows], K)
-    xs = x if "E" not in cfg else np.repeat(x, cfg["n_sel"], axis=0)
-    t_end = time.perf_counter() + budget_s
-    n_iter, t_total = 0, 0.0
-    while True:
-        t0 = time.perf_counter()
-        xf = O.dequantize(O.DT_Q8_0, O.quantize(O.DT_Q8_0, xs), K) if dt != DType.F32 else xs
-        O.mul_mat_f32(wf, xf, nthreads=threads)
-        t_total += time.perf_counter() - t0
-        n_iter += 1
-        if time.perf_counter() > t_end or n_iter >= 1000:
-            break
-    frac = rows / M
-    sec_full_step = t_total / n_iter / frac
-    v, unit = metric_value(cfg, N, sec_full_step)
-    return {"value": v, "unit": unit, "cores": threads, "kind": "port",
-            "sample": f"{rows}/{M} weight rows x {n_cols} columns per iteration, {n_iter} iterations "
-                      f"({t_total:.1f} s); value scaled to the full step",
-            "sec_per_full_step": sec_full_step}
-
-
-def run_reference(args, cfg, N):
-    """The reference's CPU mul_mat on all host threads (the oracle port: the
-    Rust reference cannot be built in this image). Each step is a bounded
-    sample of the workload (a slice of weight rows, all columns), sized so
-    the whole run stays within about a minute; the value is scaled to the
-    full step."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    from oracle import oracle as O
-    from feml_b200 import DType
-    dt = DType[cfg["wtype"]]
-    K, M = cfg["K"], cfg["M"]
-    code = {DType.F32: O.DT_F32, DType.Q8_0: O.DT_Q8_0, DType.Q4_0: O.DT_Q4_0, DType.Q4_K: O.DT_Q4_K}[dt]
-    n_cols = N * cfg.get("n_sel", 1)
-    total_steps = args.steps + max(args.warmup, 3)
-    macs = min(2e8, max(2e5, 60.0 * 1e9 / total_steps))
-    rows = int(min(M, max(1, macs // (K * n_cols))))
-    threads = max(1, min(os.cpu_count() or 1, rows // 16))
-    rng = np.random.default_rng(cfg["seed"])
-    if cfg["dist"] == "uniform":
-        wf = rng.uniform(-1, 1, (rows, K)).astype(np.float32)
-    else:
-        wf = (rng.standard_normal((rows, K)) * 0.02).astype(np.float32)
-    wdeq = O.dequantize(code, O.quantize(code, wf), K) if dt != DType.F32 else wf
-    x = np.random.default_rng(cfg["seed"] + 1).standard_normal((n_cols, K)).astype(np.float32)
-
-    def sample():
-        xf = O.dequantize(O.DT_Q8_0, O.quantize(O.DT_Q8_0, x), K) if dt != DType.F32 else x
-        O.mul_mat_f32(wdeq, xf, nthreads=threads)
-
-    for _ in range(max(args.warmup, 3)):
-        sample()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        sample()
-    dt_s = time.perf_counter() - t0
-    sec_full = dt_s / args.steps / (rows / M)
-    v, unit = metric_value(cfg, N, sec_full)
-    print(json.dumps({
-        "impl": "reference",
-        "metric": f"mul_mat {'prefill GEMM TOPS' if cfg['metric'] == 'TOPS' else 'decode weight-GB/s'} "
-                  f"({args.config}: {cfg['workload']})",
-        "value": v, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
-        "ms_per_step": sec_full * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded numpy)",
-        "config": {"workload": cfg["workload"], "config": args.config, "K": K, "M": M, "N": N},
-        "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port",
-                         "sample": f"{rows}/{M} weight rows x {n_cols} columns per step, scaled to the full "
-                                   f"step; F32 mul_mat (feml-cpu/src/ops/mul_mat.rs:36-57 restated in C) on "
-                                   f"dequantized weights and Q8_0-rounded activations"},
-        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    timer.release()  # graphs go before the process group
+    if ws > 1:
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200000)
-    ap.add_argument("--warmup", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: about half a second of work)")
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c5", choices=sorted(CONFIGS))
     ap.add_argument("--tokens", type=int, default=None, help="activation columns N (c4: 1, 8 or 64)")
-    ap.add_argument("--e2e-steps", type=int, default=5000)
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--combine", default="owner", choices=["owner", "replicate", "nccl"],
+                    help="C5 on N>1 GPUs: slots to their token's owner rank (peer stores), to every rank (peer "
+                         "stores), or an NCCL all-reduce")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--shard", default="none", choices=["none", "rows", "experts"],
-                    help="strong-scaling split of one workload across the ranks (c4: rows, c5: experts)")
-    ap.add_argument("--fused", action="store_true",
-                    help="peer-memory stores + flags instead of the NCCL collective (--shard rows at decode "
-                         "shapes, --shard experts)")
+    ap.add_argument("--no-extras", action="store_true")
     args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
     cfg = dict(CONFIGS[args.config])
     N = args.tokens if args.tokens is not None else cfg["N"]
     if args.impl == "reference":
-        run_reference(args, cfg, N)
+        if args.steps is None:
+            args.steps = 20
+        run_reference(args, args.config, cfg, N)
         return
-    if args.shard != "none":
-        if (args.shard == "experts") != ("E" in cfg) or cfg["wtype"] == "F32":
-            ap.error("--shard rows needs a quantized mul_mat config (c2, c3, c4); --shard experts needs c5")
-        run_sharded(args, cfg, N)
-        return
-    run_b200(args, cfg, N)
+    run_b200(args, args.config, cfg, N)
 
 
 if __name__ == "__main__":

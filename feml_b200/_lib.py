@@ -42,12 +42,13 @@ FILL_FN = ctypes.CFUNCTYPE(c_int, vp, c_u32, c_u64, c_u8, c_u64)
 SYNC_FN = ctypes.CFUNCTYPE(c_int, vp)
 COMPUTE_FN = ctypes.CFUNCTYPE(c_int, vp, ctypes.POINTER(Plan))
 SUPPORTS_FN = ctypes.CFUNCTYPE(c_int, vp, c_i32, ctypes.POINTER(c_i32), c_i32)
+PREPARE_FN = ctypes.CFUNCTYPE(c_int, vp, ctypes.POINTER(Plan))
 
 
 class VTable(ctypes.Structure):
     _fields_ = [("ctx", vp), ("name", NAME_FN), ("create_buffer", CREATE_FN), ("release_buffer", RELEASE_FN),
                 ("write", WRITE_FN), ("read", READ_FN), ("fill", FILL_FN), ("synchronize", SYNC_FN),
-                ("graph_compute", COMPUTE_FN), ("supports_op", SUPPORTS_FN)]
+                ("graph_compute", COMPUTE_FN), ("supports_op", SUPPORTS_FN), ("prepare_plan", PREPARE_FN)]
 
 
 class DeviceInfo(ctypes.Structure):
@@ -85,6 +86,7 @@ SIGNATURES = [
     ("feml_b200_synchronize", c_int, [vp]),
     ("feml_b200_supports_op", c_int, [vp, c_i32, ctypes.POINTER(c_i32), c_i32]),
     ("feml_b200_graph_compute", c_int, [vp, ctypes.POINTER(Plan)]),
+    ("feml_b200_prepare_plan", c_int, [vp, ctypes.POINTER(Plan)]),
     ("feml_b200_backend_vtable", c_int, [vp, ctypes.POINTER(VTable)]),
     ("feml_b200_buffer_device_ptr", c_int, [vp, c_u32, ctypes.POINTER(vp), ctypes.POINTER(c_u64)]),
     ("feml_b200_stream", c_int, [vp, ctypes.POINTER(vp)]),
@@ -124,6 +126,7 @@ SIGNATURES = [
     ("feml_b200_quantize", c_int, [c_i32, vp, c_u64, vp, c_i64, c_i64, vp]),
     ("feml_b200_mul_mat_workspace", c_int, [c_i32, c_i64, c_i64, c_i64, ctypes.POINTER(c_u64)]),
     ("feml_b200_mul_mat", c_int, [c_i32, vp, c_u64, vp, c_u64, vp, c_u64, c_i64, c_i64, c_i64, vp, c_u64, vp]),
+    ("feml_b200_mul_mat_launches", c_int, [c_i32, c_i64, c_i64, c_i64, ctypes.POINTER(c_i32)]),
     ("feml_b200_mul_mat_noalloc", c_int, [c_i32, vp, c_u64, vp, c_u64, vp, c_u64, c_i64, c_i64, c_i64, vp]),
     ("feml_b200_mul_mat_noalloc_limit", c_u64, []),
     ("feml_b200_mul_mat_id_workspace", c_int, [c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, ctypes.POINTER(c_u64)]),
@@ -132,9 +135,13 @@ SIGNATURES = [
     ("feml_b200_mul_mat_peer", c_int, [c_i32, vp, c_u64, vp, c_u64, vp, vp, vp, c_i32, c_u64, vp, vp, c_i64, c_i64,
                                        c_i64, vp, vp]),
     ("feml_b200_peer_wait", c_int, [vp, vp, c_i32, vp, vp]),
+    ("feml_b200_peer_wait_timeout", c_int, [vp, vp, c_i32, c_u64, vp, vp]),
     ("feml_b200_mul_mat_id_peer", c_int, [c_i32, vp, c_u64, c_u64, c_i64, c_i64, c_i64, vp, c_u64, vp, c_u64, c_i64,
                                           vp, vp, vp, c_i32, c_u64, c_u64, vp, vp, c_i64, c_i64, c_i64, vp, c_u64, vp,
                                           vp]),
+    ("feml_b200_mul_mat_id_peer_owned", c_int, [c_i32, vp, c_u64, c_u64, c_i64, c_i64, c_i64, vp, c_u64, vp, c_u64,
+                                                c_i64, vp, vp, vp, c_i32, c_u64, c_u64, c_i64, vp, vp, c_i64, c_i64,
+                                                c_i64, vp, c_u64, vp, vp]),
     ("feml_b200_ipc_open", c_int, [vp, c_u64, ctypes.POINTER(vp)]),
     ("feml_b200_ipc_close", c_int, [vp]),
     ("feml_b200_ipc_export", c_int, [vp, vp, c_u64, ctypes.POINTER(c_u64)]),

@@ -83,6 +83,20 @@ uint64_t mul_mat_ws(int32_t wtype, int64_t K, int64_t M, int64_t N) {
     return tc_shape(wtype, K, M, N) ? std::max<uint64_t>(planar, fbk::xq16_bytes(K, N, M, false)) : planar;
 }
 
+// Kernel launches one do_mul_mat of this shape enqueues (16-byte aligned
+// operands), from the same dispatch decisions do_mul_mat takes.
+int mul_mat_launches(int32_t wtype, int64_t K, int64_t M, int64_t N) {
+    if (M <= 0 || N <= 0) return 0;
+    if (wtype == FB_F32) return 1;
+    if (mul_mat_ws(wtype, K, M, N) == 0) return 1;  // fused decode GEMV
+    if (tc_shape(wtype, K, M, N)) return fbk::gemm_tc_splits(K, M, N) > 1 ? 3 : 2;
+    if (fbk::gemv_supported(wtype, K, N)) return 2;
+    const int64_t rb = fb::row_size(wtype, K);
+    if (rb > 0 && fbk::gemm_q_supported(wtype, K, nullptr, (uint64_t)rb))
+        return fbk::gemm_q_splits(K, M, N) > 1 ? 3 : 2;
+    return 1 + (int)((N + fbk::gemv_max_cols() - 1) / fbk::gemv_max_cols());
+}
+
 // norm_eps non-null: x is rms-normalized (that eps) inside the decode GEMV
 // (graph_compute passes it only for shapes where that path runs).
 int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
@@ -499,6 +513,7 @@ int vt_compute(void *c, const fb_plan *p) { return feml_b200_graph_compute(stati
 int vt_supports(void *c, int32_t op, const int32_t *d, int32_t n) {
     return feml_b200_supports_op(static_cast<fb_backend *>(c), op, d, n);
 }
+int vt_prepare(void *c, const fb_plan *p) { return feml_b200_prepare_plan(static_cast<fb_backend *>(c), p); }
 
 bool is_sm100(int dev) {
     cudaDeviceProp prop;
@@ -854,34 +869,87 @@ int run_nodes(fb_backend *b, const fb_plan *plan) {
     return FB_OK;
 }
 
+// Capture the launches of `plan` into a CUDA graph (without executing them)
+// and cache it under `h`. Relaxed capture mode: the launchers may set kernel
+// attributes or load modules on their first use. A capture that fails is
+// cached as a node-by-node plan when `remember_failure`, else forgotten (the
+// plan's first graph_compute then runs it node by node and captures again).
+int capture_plan(fb_backend *b, const fb_plan *plan, uint64_t h, bool remember_failure) {
+    if (b->graphs.size() >= kMaxPlanGraphs) {
+        // bound the cache: wait for every launch of a cached graph, then drop them all
+        const cudaError_t se = cudaStreamSynchronize(b->stream);
+        if (se != cudaSuccess) return cuda_fail(se, "plan graph cache");
+        clear_plan_graphs(b);
+    }
+    fb_backend::PlanGraph entry;
+    visit_plan(plan, [&](uint64_t v) { entry.key.push_back(v); });
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeRelaxed);
+    if (e == cudaSuccess) {
+        const int crc = run_nodes(b, plan);
+        e = cudaStreamEndCapture(b->stream, &graph);
+        if (crc == FB_OK && e == cudaSuccess && graph) e = cudaGraphInstantiate(&entry.exec, graph, 0);
+        else entry.exec = nullptr;
+        if (e != cudaSuccess) entry.exec = nullptr;
+    }
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();  // a failed capture is not an error of the caller: the plan runs node by node
+    if (entry.exec || remember_failure) b->graphs.emplace(h, std::move(entry));
+    return FB_OK;
+}
+
+// Scratch bytes of the plan's largest node.
+int plan_scratch(const fb_plan *plan, uint64_t *need) {
+    *need = 0;
+    for (int64_t i = 0; i < plan->n_nodes; i++) {
+        const int64_t ti = plan->nodes[i];
+        if (ti < 0 || ti >= plan->n_tensors) return set_error(FB_ERR_INVALID, "graph_compute: bad node index");
+        *need = std::max(*need, node_scratch(plan, plan->tensors[ti]));
+    }
+    return FB_OK;
+}
+
 }  // namespace
 
 extern "C" {
 
+// Compile-time preparation (fb_graph_compile calls it through the vtable
+// once the plan's buffers exist; other callers call it after compile): the
+// scratch arena grows to the plan's largest node and the plan's launches are
+// captured into a CUDA graph, so the plan's first graph_compute already
+// allocates nothing and launches one graph.
+int feml_b200_prepare_plan(fb_backend *b, const fb_plan *plan) {
+    if (!b || !plan) return set_error(FB_ERR_INVALID, "prepare_plan: null argument");
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    uint64_t need = 0;
+    int rc = plan_scratch(plan, &need);
+    if (rc) return rc;
+    if (need > b->scratch_bytes && (rc = grow_scratch(b, need))) return rc;
+    if (!b->use_graphs) return FB_OK;
+    const uint64_t h = plan_hash(plan);
+    auto it = b->graphs.find(h);
+    if (it != b->graphs.end()) return FB_OK;
+    return capture_plan(b, plan, h, false);
+}
+
 // Repeated graph_compute of one plan replays a CUDA graph of its launches.
-// The first call runs the nodes one by one (setting per-kernel attributes and
-// sizing the scratch), then captures the same launches into a graph (not
-// executed) and instantiates it; later calls of a plan with identical fields
-// launch that graph: one launch instead of one or more per node, and no
-// allocation. Creating or releasing a buffer, or growing the scratch, drops
-// the cached graphs (they hold addresses). A capture that fails leaves the
-// plan on the node-by-node path.
+// A plan prepared at compile (feml_b200_prepare_plan) has its graph and its
+// scratch already; otherwise the first call runs the nodes one by one
+// (sizing the scratch, which may then grow once with a device synchronize)
+// and captures the same launches into a graph (not executed). Later calls of
+// a plan with identical fields launch that graph: one launch instead of one
+// or more per node, and no allocation. Releasing a buffer, or growing the
+// scratch, drops the cached graphs (they hold addresses). A capture that
+// fails leaves the plan on the node-by-node path.
 int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
     if (!b || !plan) return set_error(FB_ERR_INVALID, "graph_compute: null argument");
     std::lock_guard<std::mutex> lk(b->mu);
     DeviceGuard g(b->device);
-    // scratch for the largest node; grows (with a device synchronize) only the
-    // first time a plan needs more than the arena holds
     uint64_t need = 0;
-    for (int64_t i = 0; i < plan->n_nodes; i++) {
-        const int64_t ti = plan->nodes[i];
-        if (ti < 0 || ti >= plan->n_tensors) return set_error(FB_ERR_INVALID, "graph_compute: bad node index");
-        need = std::max(need, node_scratch(plan, plan->tensors[ti]));
-    }
-    if (need > b->scratch_bytes) {
-        const int rc = grow_scratch(b, need);
-        if (rc) return rc;
-    }
+    int rc = plan_scratch(plan, &need);
+    if (rc) return rc;
+    if (need > b->scratch_bytes && (rc = grow_scratch(b, need))) return rc;
     uint64_t h = 0;
     if (b->use_graphs) {
         h = plan_hash(plan);
@@ -892,29 +960,9 @@ int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
             return e == cudaSuccess ? FB_OK : cuda_fail(e, "graph_compute: graph launch");
         }
     }
-    int rc = run_nodes(b, plan);
+    rc = run_nodes(b, plan);
     if (rc || !b->use_graphs || b->graphs.count(h)) return rc;  // (a hash collision keeps the first plan's graph)
-    if (b->graphs.size() >= kMaxPlanGraphs) {
-        // bound the cache: wait for every launch of a cached graph, then drop them all
-        const cudaError_t se = cudaStreamSynchronize(b->stream);
-        if (se != cudaSuccess) return cuda_fail(se, "graph_compute");
-        clear_plan_graphs(b);
-    }
-    fb_backend::PlanGraph entry;
-    visit_plan(plan, [&](uint64_t v) { entry.key.push_back(v); });
-    cudaGraph_t graph = nullptr;
-    cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal);
-    if (e == cudaSuccess) {
-        const int crc = run_nodes(b, plan);
-        e = cudaStreamEndCapture(b->stream, &graph);
-        if (crc == FB_OK && e == cudaSuccess && graph) e = cudaGraphInstantiate(&entry.exec, graph, 0);
-        else entry.exec = nullptr;
-        if (e != cudaSuccess) entry.exec = nullptr;
-    }
-    if (graph) cudaGraphDestroy(graph);
-    cudaGetLastError();  // a failed capture is not an error of this call: the plan ran node by node
-    b->graphs.emplace(h, std::move(entry));
-    return FB_OK;
+    return capture_plan(b, plan, h, true);
 }
 
 int feml_b200_set_plan_graphs(fb_backend *b, int32_t enable) {
@@ -953,6 +1001,7 @@ int feml_b200_backend_vtable(fb_backend *b, fb_backend_vtable *vt) {
     vt->synchronize = vt_sync;
     vt->graph_compute = vt_compute;
     vt->supports_op = vt_supports;
+    vt->prepare_plan = vt_prepare;
     return FB_OK;
 }
 
@@ -998,6 +1047,15 @@ int feml_b200_reserve_scratch(fb_backend *b, uint64_t bytes) {
 int feml_b200_quantize(int32_t dtype, const void *x, uint64_t x_row_stride, void *y, int64_t rows, int64_t k,
                        void *stream) {
     return fbk::launch_quantize_rows(dtype, x, x_row_stride, y, rows, k, static_cast<cudaStream_t>(stream));
+}
+
+int feml_b200_mul_mat_launches(int32_t wtype, int64_t K, int64_t M, int64_t N, int32_t *count) {
+    if (!count) return set_error(FB_ERR_INVALID, "mul_mat_launches: null out");
+    *count = 0;
+    if (K < 0 || M < 0 || N < 0) return set_error(FB_ERR_INVALID, "mul_mat_launches: negative dimension");
+    if (!is_mul_mat_dtype(wtype)) return set_error(FB_ERR_UNSUPPORTED, "mul_mat_launches: dtype %d", wtype);
+    *count = mul_mat_launches(wtype, K, M, N);
+    return FB_OK;
 }
 
 int feml_b200_mul_mat_workspace(int32_t wtype, int64_t K, int64_t M, int64_t N, uint64_t *bytes) {
@@ -1057,12 +1115,13 @@ int feml_b200_mul_mat_peer(int32_t wtype, const void *w, uint64_t w_nb1, const v
                             static_cast<cudaStream_t>(stream), true, &po);
 }
 
-int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,
-                              int64_t shard, int64_t n_shards, const void *x, uint64_t x_nb1, const int32_t *ids,
-                              uint64_t ids_nb1, int64_t n_selected, void *const *peer_dst0, void *const *peer_dst1,
-                              uint32_t *const *peer_flags, int32_t n_peers, uint64_t dst_nb1, uint64_t dst_nb2,
-                              uint32_t *counter, const uint32_t *epoch, int64_t K, int64_t M, int64_t N,
-                              void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream) {
+int feml_b200_mul_mat_id_peer_owned(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2,
+                                    int64_t n_experts, int64_t shard, int64_t n_shards, const void *x, uint64_t x_nb1,
+                                    const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, void *const *peer_dst0,
+                                    void *const *peer_dst1, uint32_t *const *peer_flags, int32_t n_peers,
+                                    uint64_t dst_nb1, uint64_t dst_nb2, int64_t owner_tokens, uint32_t *counter,
+                                    const uint32_t *epoch, int64_t K, int64_t M, int64_t N, void *workspace,
+                                    uint64_t workspace_bytes, int32_t *status, void *stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (!w_local || !x || !ids || !peer_dst0 || !peer_dst1 || !peer_flags || !counter || !epoch)
         return set_error(FB_ERR_INVALID, "mul_mat_id_peer: null argument");
@@ -1071,6 +1130,9 @@ int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1
                          (long)n_shards);
     if (K <= 0 || M <= 0 || N <= 0 || n_selected < 1 || n_experts < 1)
         return set_error(FB_ERR_INVALID, "mul_mat_id_peer: bad dimensions");
+    if (owner_tokens < 0 || (owner_tokens > 0 && owner_tokens * n_shards < N))
+        return set_error(FB_ERR_INVALID, "mul_mat_id_peer: %ld tokens per owner cannot hold %ld tokens on %ld ranks",
+                         (long)owner_tokens, (long)N, (long)n_shards);
     const int64_t n_local = fbk::local_experts(n_experts, shard, n_shards);
     if (n_local < 1) return set_error(FB_ERR_INVALID, "mul_mat_id_peer: every shard needs an expert (it signals)");
     if (!fbk::gemm_tc_supported(wtype, K, M, N * n_selected, w_local, w_nb1) || (w_nb2 & 15) ||
@@ -1086,6 +1148,7 @@ int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1
     po.n = n_peers;
     po.count = counter;
     po.epoch = epoch;
+    po.owner_tokens = (int)owner_tokens;
     for (int r = 0; r < n_peers; r++) {
         po.y[0][r] = static_cast<uint8_t *>(peer_dst0[r]);
         po.y[1][r] = static_cast<uint8_t *>(peer_dst1[r]);
@@ -1094,7 +1157,7 @@ int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1
     // invalid ids: every rank zeroes the slot in its own buffer of this step
     int rc = fbk::launch_moe_route(ids, ids_nb1, n_selected, N, n_experts, shard, n_shards, L.counts, L.offsets,
                                    L.rows, L.tile_start, fbk::gemm_tc_block_n(), status, po.y[0][shard], dst_nb1,
-                                   dst_nb2, M, s, po.y[1][shard], epoch);
+                                   dst_nb2, M, s, po.y[1][shard], epoch, owner_tokens);
     if (rc) return rc;
     fbk::GroupMap g{};
     g.counts = L.counts;
@@ -1111,6 +1174,18 @@ int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1
     rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, &g, s);
     if (rc) return rc;
     return fbk::launch_gemm_tc(wtype, w_local, w_nb1, xa, K, M, N, nullptr, 0, &g, status, s, &po);
+}
+
+int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,
+                              int64_t shard, int64_t n_shards, const void *x, uint64_t x_nb1, const int32_t *ids,
+                              uint64_t ids_nb1, int64_t n_selected, void *const *peer_dst0, void *const *peer_dst1,
+                              uint32_t *const *peer_flags, int32_t n_peers, uint64_t dst_nb1, uint64_t dst_nb2,
+                              uint32_t *counter, const uint32_t *epoch, int64_t K, int64_t M, int64_t N,
+                              void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream) {
+    return feml_b200_mul_mat_id_peer_owned(wtype, w_local, w_nb1, w_nb2, n_experts, shard, n_shards, x, x_nb1, ids,
+                                           ids_nb1, n_selected, peer_dst0, peer_dst1, peer_flags, n_peers, dst_nb1,
+                                           dst_nb2, 0, counter, epoch, K, M, N, workspace, workspace_bytes, status,
+                                           stream);
 }
 
 int feml_b200_ipc_export(const void *ptr, void *handle, uint64_t handle_bytes, uint64_t *offset) {
@@ -1161,6 +1236,11 @@ int feml_b200_ipc_close(void *base) {
 
 int feml_b200_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, void *stream) {
     return fbk::launch_peer_wait(flag, epoch, n_ranks, status, static_cast<cudaStream_t>(stream));
+}
+
+int feml_b200_peer_wait_timeout(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, uint64_t timeout_us,
+                                int32_t *status, void *stream) {
+    return fbk::launch_peer_wait(flag, epoch, n_ranks, status, static_cast<cudaStream_t>(stream), timeout_us);
 }
 
 int feml_b200_mul_mat_id_shard(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2, int64_t n_experts,

@@ -776,6 +776,14 @@ int fb_graph_compile(fb_graph *gh, const fb_backend_vtable *be, fb_compiled_plan
     plan->view.n_nodes = (int64_t)plan->nodes.size();
     plan->view.buffers = plan->buffers.data();
     plan->view.n_buffers = (int64_t)plan->buffers.size();
+    if (be->prepare_plan) {
+        rc = be->prepare_plan(be->ctx, &plan->view);
+        if (rc) {
+            const std::string msg = fb::last_error();
+            for (auto &b : plan->buffers) be->release_buffer(be->ctx, b.handle);
+            return set_error(rc, "%s", msg.c_str());
+        }
+    }
     *out = plan.release();
     return FB_OK;
     GRAPH_END

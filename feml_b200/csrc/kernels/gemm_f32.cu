@@ -386,16 +386,10 @@ int launch_f32_pipe(const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1
     rc = encode_tensor_map_2d_sw128(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, x, (uint64_t)p.K, (uint64_t)p.N, x_nb1,
                                     kBoxK, kPipeCols);
     if (rc) return rc;
-    static bool smem_set[64] = {};  // per device: the dynamic smem limit was raised
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaError_t e = cudaSuccess;
-    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_f32_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)pipe_smem_bytes(kMaxWarps));
-        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_f32: smem attribute: %s", cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) smem_set[dev] = true;
-    }
+    static DeviceFlags smem_set;
+    rc = raise_smem_limit((const void *)gemm_f32_pipe_kernel, (int)pipe_smem_bytes(kMaxWarps), smem_set, "gemm_f32");
+    if (rc) return rc;
+    cudaError_t e;
     dim3 grid((unsigned)((p.M + bm - 1) / bm), (unsigned)((p.N + kPipeCols - 1) / kPipeCols));
     gemm_f32_pipe_kernel<<<grid, (p.warps + 1) * 32, pipe_smem_bytes(p.warps), s>>>(tmw, tmx, p);
     e = cudaGetLastError();

@@ -316,15 +316,10 @@ template <int WT, int BM>
 int launch_bm(const GemmQParams &p, int tiles_n, cudaStream_t s) {
     using S = Smem<WT, BM>;
     auto kern = gemm_q_kernel<WT, BM>;
-    static bool smem_set[64] = {false};  // per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaError_t e = cudaSuccess;
-    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total);
-        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_q: smem attribute: %s", cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) smem_set[dev] = true;
-    }
+    static DeviceFlags smem_set;
+    const int rc = raise_smem_limit((const void *)kern, (int)S::total, smem_set, "gemm_q");
+    if (rc) return rc;
+    cudaError_t e;
     const int splits = p.partial ? (p.K / KC + p.split_chunks - 1) / p.split_chunks : 1;
     dim3 grid((p.M + BM - 1) / BM, tiles_n, splits);
     kern<<<grid, THREADS, S::total, s>>>(p);

@@ -716,19 +716,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             p.partial[((uint64_t)blockIdx.z * p.N + r) * p.M + m] = acc[i];
                         } else {
                             uint64_t off;
+                            int owner = -1;  // peer owner mode: the one rank that receives this slot
                             if (p.grouped) {
                                 const int slot = p.g.rows[r];
-                                off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 +
-                                      (uint64_t)(slot / p.g.n_selected) * p.g.dst_nb2;
+                                int t = slot / p.g.n_selected;
+                                if (PEER && p.peer.owner_tokens > 0) {
+                                    owner = t / p.peer.owner_tokens;
+                                    t -= owner * p.peer.owner_tokens;
+                                }
+                                off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 + (uint64_t)t * p.g.dst_nb2;
                             } else {
                                 off = (uint64_t)r * p.y_nb1;
                             }
                             if constexpr (!PEER) {
                                 reinterpret_cast<float *>(p.y + off)[m] = acc[i];
-                            } else {  // NVLink stores into every rank's buffer of this step
+                            } else {  // NVLink stores into the owner's buffer, or every rank's
                                 const int b = (int)((*p.peer.epoch + 1u) & 1u);
-                                for (int pr = 0; pr < p.peer.n; pr++)
-                                    reinterpret_cast<float *>(p.peer.y[b][pr] + off)[m] = acc[i];
+                                if (owner >= 0) {
+                                    reinterpret_cast<float *>(p.peer.y[b][owner] + off)[m] = acc[i];
+                                } else {
+                                    for (int pr = 0; pr < p.peer.n; pr++)
+                                        reinterpret_cast<float *>(p.peer.y[b][pr] + off)[m] = acc[i];
+                                }
                             }
                         }
                     }
@@ -860,14 +869,9 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     // the peer-store variant is a separate instantiation, so the plain kernel
     // carries none of its registers
     const auto kern = peer ? gemm_tc_kernel<WT, true> : gemm_tc_kernel<WT, false>;
-    static int configured[64][2] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev][peer ? 1 : 0]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc smem attribute: %s", cudaGetErrorString(e));
-        configured[dev][peer ? 1 : 0] = 1;
-    }
+    static DeviceFlags configured[2];
+    rc = raise_smem_limit((const void *)kern, L::BYTES, configured[peer ? 1 : 0], "gemm_tc");
+    if (rc) return rc;
     TcParams p{};
     p.M = (int)M;
     p.N = (int)rows;

@@ -986,20 +986,30 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ks_cols_kernel(const __g
     }
 }
 
-// Waits (one thread, bounded at about a second) until every rank has
-// signalled this step: the flag reaches (epoch + 1) * n_ranks; then advances
-// the epoch. On timeout it raises STATUS_TIMEOUT and returns, leaving the
-// context usable (the epoch stays, so later waits report too).
+// Waits (one thread) until every rank has signalled this step: the flag
+// reaches (epoch + 1) * n_ranks; then advances the epoch. The wait is
+// bounded twice: by `timeout_ns` of the GPU's global timer and by a poll
+// count (each poll sleeps at least 32 ns, so the count alone ends it within
+// a few seconds). On expiry it raises STATUS_TIMEOUT and returns, leaving
+// the context usable (the epoch stays, so later waits report too).
 // Launched with programmatic dependent launch: it lets the next step's GEMV
 // start streaming its weights right away, but reads the epoch only after the
 // preceding grids (this step's GEMV, and through it the previous wait) have
 // completed.
-__global__ void peer_wait_kernel(const uint32_t *flag, uint32_t *epoch, int n_ranks, int32_t *status) {
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__global__ void peer_wait_kernel(const uint32_t *flag, uint32_t *epoch, int n_ranks, uint64_t timeout_ns,
+                                 int32_t *status) {
     grid_launch_dependents();
     grid_dependency_wait();
     if (threadIdx.x != 0) return;
     const uint32_t e = *epoch;
     const uint32_t expected = (e + 1u) * (uint32_t)n_ranks;
+    const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 0; i < (1u << 24); i++) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
@@ -1007,6 +1017,7 @@ __global__ void peer_wait_kernel(const uint32_t *flag, uint32_t *epoch, int n_ra
             *epoch = e + 1u;
             return;
         }
+        if ((i & 15u) == 15u && global_timer_ns() - t0 > timeout_ns) break;
         __nanosleep(32);
     }
     report_status(status, STATUS_TIMEOUT);
@@ -1015,15 +1026,10 @@ __global__ void peer_wait_kernel(const uint32_t *flag, uint32_t *epoch, int n_ra
 template <int WT, int NC, int XR>
 int launch_typed(const GemvParams &p, int grid, uint32_t smem, cudaStream_t s, bool pdl) {
     auto kern = gemv_kernel<WT, NC, XR>;
-    static bool smem_set[64] = {false};  // per device: the dynamic smem limit was raised
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaError_t e = cudaSuccess;
-    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) smem_set[dev] = true;
-    }
+    static DeviceFlags smem_set;
+    const int rc = raise_smem_limit((const void *)kern, kSmemLimit, smem_set, "gemv");
+    if (rc) return rc;
+    cudaError_t e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kGemvThreads);
@@ -1112,14 +1118,9 @@ int launch_gemv_ks(const void *w, uint64_t w_nb1, const void *x, void *y, int64_
     p.x_vec16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     p.peer = peer ? *peer : PeerOut{};
     auto kern = gemv_ks_kernel<1>;
-    static bool smem_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCoResidentCta);
-        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) smem_set[dev] = true;
-    }
+    static DeviceFlags smem_set;
+    rc = raise_smem_limit((const void *)kern, (int)kCoResidentCta, smem_set, "gemv");
+    if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kGemvThreads);
@@ -1141,14 +1142,9 @@ template <int NC>
 int launch_ks_cols_typed(const CUtensorMap &tm, const KsColsParams &p, int grid, uint32_t smem, cudaStream_t s,
                          bool pdl) {
     auto kern = gemv_ks_cols_kernel<NC>;
-    static bool smem_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) smem_set[dev] = true;
-    }
+    static DeviceFlags smem_set;
+    const int rc = raise_smem_limit((const void *)kern, kSmemLimit, smem_set, "gemv");
+    if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kGemvThreads);
@@ -1222,10 +1218,14 @@ bool gemv_fused_ok(int64_t K, int64_t N) { return K * N <= kFusedMaxElems; }
 
 int gemv_max_cols() { return kMaxCols; }
 
-int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s) {
+int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s,
+                     uint64_t timeout_us) {
     if (!flag || !epoch || ((reinterpret_cast<uintptr_t>(flag) | reinterpret_cast<uintptr_t>(epoch)) & 3))
         return fb::set_error(FB_ERR_INVALID, "peer_wait: bad flag or epoch");
     if (n_ranks < 1 || n_ranks > kMaxPeers) return fb::set_error(FB_ERR_INVALID, "peer_wait: %d ranks", n_ranks);
+    if (timeout_us == 0 || timeout_us > 10000000ull)
+        return fb::set_error(FB_ERR_INVALID, "peer_wait: timeout %llu us outside 1 us .. 10 s",
+                             (unsigned long long)timeout_us);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(32);
@@ -1235,7 +1235,7 @@ int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, peer_wait_kernel, flag, epoch, (int)n_ranks, status);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, peer_wait_kernel, flag, epoch, (int)n_ranks, timeout_us * 1000ull, status);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "peer_wait launch: %s", cudaGetErrorString(e));
     return FB_OK;

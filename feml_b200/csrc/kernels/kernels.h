@@ -4,9 +4,31 @@
 #pragma once
 
 #include <cuda_runtime.h>
+
+#include <atomic>
 #include <cstdint>
 
+#include "../host_common.h"
+
 namespace fbk {
+
+// Per-device "done" flags of a launcher's one-time kernel attribute setup.
+using DeviceFlags = std::atomic<bool>[64];
+
+// Raise `func`'s dynamic shared-memory limit to `bytes` the first time it is
+// launched on the current device. The flag is atomic, so host threads that
+// launch concurrently do not race on it; two threads that both see it unset
+// both set the attribute, which is idempotent.
+inline int raise_smem_limit(const void *func, int bytes, DeviceFlags &done, const char *what) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+    const bool tracked = dev >= 0 && dev < 64;
+    if (tracked && done[dev].load(std::memory_order_acquire)) return FB_OK;
+    const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
+    if (tracked) done[dev].store(true, std::memory_order_release);
+    return FB_OK;
+}
 
 // Planar Q8_0 activations: the device-internal form the quantized kernels
 // read. Column n of an activation matrix [K, N] becomes qs[n*K .. n*K+K)
@@ -42,6 +64,10 @@ int gemv_max_cols();  // largest N the GEMV takes
 // step flag, count a zeroed device counter of this rank, epoch this rank's
 // count of completed steps (buffer = (epoch + 1) & 1). The last warp of the
 // grid raises every flag by one.
+// owner_tokens > 0 (grouped GEMM only): outputs are not replicated; token t
+// belongs to rank t / owner_tokens, whose buffers hold its owner_tokens
+// tokens, and a slot of token t is stored only there, at local token
+// t % owner_tokens.
 constexpr int kMaxPeers = 8;
 struct PeerOut {
     uint8_t *y[2][kMaxPeers];
@@ -49,6 +75,7 @@ struct PeerOut {
     uint32_t *count;
     const uint32_t *epoch;
     int n;
+    int owner_tokens;
 };
 // With `norm_eps` (in-kernel quantization only: xq and peer null) every
 // activation column is rms-normalized with that eps before it is quantized.
@@ -56,8 +83,10 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
                 uint64_t y_nb1, int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status,
                 cudaStream_t s, bool pdl, const PeerOut *peer = nullptr, const float *norm_eps = nullptr);
 // Wait until this rank's flag reaches (epoch + 1) * n_ranks, then advance
-// the epoch (bounded; STATUS_TIMEOUT on expiry).
-int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s);
+// the epoch (bounded by timeout_us; STATUS_TIMEOUT on expiry).
+constexpr uint64_t kPeerWaitTimeoutUs = 1000000;  // default bound: one second
+int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, cudaStream_t s,
+                     uint64_t timeout_us = kPeerWaitTimeoutUs);
 
 // norm.cu: rms_norm along ne0 (y may alias x); ne[4], strides in bytes.
 int launch_rms_norm(const void *x, const uint64_t *xnb, void *y, const uint64_t *ynb, const int64_t *ne, float eps,
@@ -139,11 +168,14 @@ int launch_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *
 inline int64_t local_experts(int64_t n_experts, int64_t shard, int64_t n_shards) {
     return n_experts > shard ? (n_experts - shard + n_shards - 1) / n_shards : 0;
 }
+// With owner_tokens > 0 dst holds only this shard's tokens [shard *
+// owner_tokens, +owner_tokens) (token t at local index t % owner_tokens),
+// and only their invalid slots are zeroed.
 int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
                      int64_t shard, int64_t n_shards, int32_t *counts, int32_t *offsets, int32_t *rows,
                      int32_t *tile_start, int32_t block_n, int32_t *status, void *dst, uint64_t dst_nb1,
                      uint64_t dst_nb2, int64_t M, cudaStream_t s, void *dst_alt = nullptr,
-                     const uint32_t *epoch = nullptr);
+                     const uint32_t *epoch = nullptr, int64_t owner_tokens = 0);
 
 int sm_count();
 

@@ -31,7 +31,8 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
                                                                    int32_t *offsets, int32_t *rows,
                                                                    int32_t *tile_start, int block_n, int32_t *status,
                                                                    uint8_t *dst, uint64_t dst_nb1, uint64_t dst_nb2,
-                                                                   int M, uint8_t *dst_alt, const uint32_t *epoch) {
+                                                                   int M, uint8_t *dst_alt, const uint32_t *epoch,
+                                                                   int owner_tokens) {
     __shared__ int cnt[kMaxExperts];
     __shared__ int base[kMaxExperts];
     __shared__ int off[kMaxExperts];
@@ -64,7 +65,12 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
             const int t = i / n_sel, s = i % n_sel;
             const int e = ids[(uint64_t)t * ids_stride + s];
             if (local_of(e) != -2) continue;
-            float *col = reinterpret_cast<float *>(dst + (uint64_t)s * dst_nb1 + (uint64_t)t * dst_nb2);
+            int lt = t;  // token index in dst
+            if (owner_tokens > 0) {
+                if (t / owner_tokens != shard) continue;  // another rank's token: its owner zeroes it
+                lt = t % owner_tokens;
+            }
+            float *col = reinterpret_cast<float *>(dst + (uint64_t)s * dst_nb1 + (uint64_t)lt * dst_nb2);
             for (int m = tid; m < M; m += kRouteThreads) col[m] = 0.0f;
         }
     }
@@ -115,7 +121,8 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int32_t 
 int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, int64_t N, int64_t n_experts,
                      int64_t shard, int64_t n_shards, int32_t *counts, int32_t *offsets, int32_t *rows,
                      int32_t *tile_start, int32_t block_n, int32_t *status, void *dst, uint64_t dst_nb1,
-                     uint64_t dst_nb2, int64_t M, cudaStream_t s, void *dst_alt, const uint32_t *epoch) {
+                     uint64_t dst_nb2, int64_t M, cudaStream_t s, void *dst_alt, const uint32_t *epoch,
+                     int64_t owner_tokens) {
     if (n_experts < 1 || n_experts > kMaxExperts)
         return fb::set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: n_experts %ld not in [1, %d]", (long)n_experts, kMaxExperts);
     if (n_shards < 1 || shard < 0 || shard >= n_shards)
@@ -125,11 +132,14 @@ int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, i
         return fb::set_error(FB_ERR_INVALID, "mul_mat_id: bad slot count");
     if (ids_nb1 % 4 || (reinterpret_cast<uintptr_t>(ids) & 3))
         return fb::set_error(FB_ERR_INVALID, "mul_mat_id: ids must be 4-byte aligned");
+    if (owner_tokens < 0 || owner_tokens > INT32_MAX || (owner_tokens > 0 && owner_tokens * n_shards < N))
+        return fb::set_error(FB_ERR_INVALID, "mul_mat_id: %ld tokens per owner for %ld tokens on %ld shards",
+                             (long)owner_tokens, (long)N, (long)n_shards);
     moe_route_kernel<<<1, kRouteThreads, 0, s>>>(ids, ids_nb1 / 4, (int)n_selected, (int)N, (int)n_experts, (int)shard,
                                                  (int)n_shards, (int)n_local, counts,
                                                  offsets, rows, tile_start, block_n, status,
                                                  static_cast<uint8_t *>(dst), dst_nb1, dst_nb2, (int)M,
-                                                 static_cast<uint8_t *>(dst_alt), epoch);
+                                                 static_cast<uint8_t *>(dst_alt), epoch, (int)owner_tokens);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "moe_route launch: %s", cudaGetErrorString(e));
     return FB_OK;

@@ -24,7 +24,17 @@
 //   * nothing in it needs to start at zero: each call writes the quantized
 //     activations it reads before reading them.
 //   * shapes whose scratch exceeds kStaticScratchBytes are rejected with
-//     FB_ERR_UNSUPPORTED before any work is queued.
+//     FB_ERR_UNSUPPORTED before any work is queued; arguments are checked
+//     first, as feml_b200_mul_mat checks them (negative dimensions give
+//     FB_ERR_INVALID, an empty output returns FB_OK, an unsupported weight
+//     dtype gives FB_ERR_UNSUPPORTED).
+//   * when the 16 MiB are taken: this file is its own device module (the
+//     library is built without relocatable device code). Under lazy module
+//     loading (CUDA_MODULE_LOADING=LAZY, the default of CUDA 12) the module,
+//     and with it the array, is loaded into a device's context by the first
+//     call on that device; under CUDA_MODULE_LOADING=EAGER every context the
+//     process creates on any device reserves the 16 MiB at creation, whether
+//     or not it ever calls this entry point.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -68,6 +78,11 @@ uint64_t feml_b200_mul_mat_noalloc_limit(void) { return kStaticScratchBytes; }
 
 int feml_b200_mul_mat_noalloc(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *dst,
                               uint64_t dst_nb1, int64_t K, int64_t M, int64_t N, void *stream) {
+    if (K < 0 || M < 0 || N < 0) return fb::set_error(FB_ERR_INVALID, "mul_mat_noalloc: negative dimension");
+    if (M == 0 || N == 0) return FB_OK;
+    const int32_t dts[2] = {wtype, FB_F32};
+    if (!feml_b200_supports_op(nullptr, FB_OP_MUL_MAT, dts, 2))
+        return fb::set_error(FB_ERR_UNSUPPORTED, "mul_mat_noalloc: weight dtype %d not supported", wtype);
     uint64_t need = 0;
     int rc = feml_b200_mul_mat_workspace(wtype, K, M, N, &need);
     if (rc) return rc;

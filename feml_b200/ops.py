@@ -40,6 +40,13 @@ def mul_mat_workspace(wtype, K, M, N):
     return v.value
 
 
+def mul_mat_launches(wtype, K, M, N):
+    """Kernel launches one mul_mat of this shape enqueues."""
+    v = ctypes.c_int32()
+    _check(_L.lib().feml_b200_mul_mat_launches(int(wtype), K, M, N, ctypes.byref(v)))
+    return v.value
+
+
 def mul_mat(wtype, w, x, K, out=None, workspace=None):
     """w: uint8 [M, row_bytes] (or f32 [M, K] for F32); x: f32 [N, K] -> f32 [N, M]."""
     M = w.shape[0]
@@ -142,10 +149,12 @@ def mul_mat_peer(wtype, w_local, x, K, dst0_ptrs, dst1_ptrs, flag_ptrs, dst_nb1,
 
 
 def mul_mat_id_peer(wtype, w_local, x, ids, K, n_experts, shard, n_shards, dst0_ptrs, dst1_ptrs, flag_ptrs,
-                    dst_nb1, dst_nb2, M, counter, epoch, workspace, status=None):
-    """feml_b200_mul_mat_id_peer: this shard's experts of an expert-sharded
-    mul_mat_id, every output slot stored straight into every rank's output
-    buffer of this step, then every rank's flag raised."""
+                    dst_nb1, dst_nb2, M, counter, epoch, workspace, status=None, owner_tokens=0):
+    """feml_b200_mul_mat_id_peer(_owned): this shard's experts of an
+    expert-sharded mul_mat_id, every output slot stored straight into every
+    rank's output buffer of this step (owner_tokens == 0) or only into the
+    buffer of the rank that owns its token (token t on rank t // owner_tokens),
+    then every rank's flag raised."""
     E_loc = w_local.shape[0]
     if E_loc != local_experts(n_experts, shard, n_shards):
         raise FemlError("msg", f"mul_mat_id_peer: shard {shard}/{n_shards} of {n_experts} experts holds "
@@ -153,18 +162,25 @@ def mul_mat_id_peer(wtype, w_local, x, ids, K, n_experts, shard, n_shards, dst0_
     N, n_sel = ids.shape
     es = w_local.element_size()
     st = _ptr(status) if status is not None else ctypes.c_void_p()
-    _check(_L.lib().feml_b200_mul_mat_id_peer(int(wtype), _ptr(w_local), w_local.stride(1) * es,
-                                              w_local.stride(0) * es, n_experts, shard, n_shards, _ptr(x),
-                                              x.stride(0) * 4, _ptr(ids), ids.stride(0) * 4, n_sel,
-                                              _ptr_array(dst0_ptrs), _ptr_array(dst1_ptrs), _ptr_array(flag_ptrs),
-                                              len(flag_ptrs), dst_nb1, dst_nb2, _ptr(counter), _ptr(epoch), K, M, N,
-                                              _ptr(workspace), workspace.numel(), st, _stream()))
+    _check(_L.lib().feml_b200_mul_mat_id_peer_owned(int(wtype), _ptr(w_local), w_local.stride(1) * es,
+                                                    w_local.stride(0) * es, n_experts, shard, n_shards, _ptr(x),
+                                                    x.stride(0) * 4, _ptr(ids), ids.stride(0) * 4, n_sel,
+                                                    _ptr_array(dst0_ptrs), _ptr_array(dst1_ptrs),
+                                                    _ptr_array(flag_ptrs), len(flag_ptrs), dst_nb1, dst_nb2,
+                                                    int(owner_tokens), _ptr(counter), _ptr(epoch), K, M, N,
+                                                    _ptr(workspace), workspace.numel(), st, _stream()))
 
 
-def peer_wait(flag, epoch, n_ranks, status=None):
-    """Enqueue the end of a fused step: wait for every rank's signal."""
+def peer_wait(flag, epoch, n_ranks, status=None, timeout_us=None):
+    """Enqueue the end of a fused step: wait for every rank's signal (bounded
+    by `timeout_us`, default about a second; on expiry bit 0 of `status` is
+    set and the stream continues)."""
     st = _ptr(status) if status is not None else ctypes.c_void_p()
-    _check(_L.lib().feml_b200_peer_wait(_ptr(flag), _ptr(epoch), n_ranks, st, _stream()))
+    if timeout_us is None:
+        _check(_L.lib().feml_b200_peer_wait(_ptr(flag), _ptr(epoch), n_ranks, st, _stream()))
+    else:
+        _check(_L.lib().feml_b200_peer_wait_timeout(_ptr(flag), _ptr(epoch), n_ranks, int(timeout_us), st,
+                                                    _stream()))
 
 
 def moe_route(ids, n_experts, status=None):
@@ -189,6 +205,6 @@ def block_dots(wtype, w, xq, K):
     return out
 
 
-__all__ = ["quantize", "mul_mat", "mul_mat_workspace", "mul_mat_noalloc", "mul_mat_noalloc_limit", "mul_mat_id", "mul_mat_id_workspace", "mul_mat_id_shard",
+__all__ = ["quantize", "mul_mat", "mul_mat_launches", "mul_mat_workspace", "mul_mat_noalloc", "mul_mat_noalloc_limit", "mul_mat_id", "mul_mat_id_workspace", "mul_mat_id_shard",
            "local_experts", "mul_mat_peer", "mul_mat_id_peer", "peer_wait", "moe_route",
            "block_dots", "row_bytes", "FemlError"]

@@ -20,14 +20,22 @@ are new. They shard the two operators of the path the natural way:
 * `ExpertShardedMulMatId` -- rank r owns the experts e with e % world == r
   (local index e // world). Each rank computes the dst slots routed to its
   experts (feml_b200_mul_mat_id_shard leaves the other slots untouched in a
-  zeroed buffer) and a sum all-reduce combines them: every slot has exactly
-  one non-zero contributor, so the combine is exact. Invalid expert ids give
-  zero slots on every rank, as on one device. With `fused=True` (quantized
-  weights, K % 256 == 0, at most `max_tokens` tokens and `max_selected`
-  experts per token) the combine is fused into the grouped GEMM instead: its
-  epilogue stores every slot into every rank's output buffer over NVLink and
-  the same flag / epoch wait as above ends the step
-  (feml_b200_mul_mat_id_peer).
+  zeroed buffer) and the combine brings every slot to where it is needed.
+  Every slot has exactly one non-zero contributor, so the combine is exact;
+  invalid expert ids give zero slots, as on one device. Two combines:
+    - combine="replicate": every rank ends with all N tokens' slots (a sum
+      all-reduce; fused: the GEMM epilogue stores every slot into every
+      rank's buffer over NVLink, feml_b200_mul_mat_id_peer);
+    - combine="owner": token t belongs to rank t // T, T = ceil(max_tokens /
+      world), and each rank ends with only its own tokens' slots (the
+      all-to-all of expert parallelism; collective form: a sum all-reduce
+      sliced to the rank's tokens; fused: the epilogue stores each slot only
+      into its owner's buffer, feml_b200_mul_mat_id_peer_owned, so a rank
+      sends about 1/world of the slot tensor instead of all of it to every
+      peer).
+  `fused=True` needs quantized weights, K % 256 == 0, at most `max_tokens`
+  tokens and `max_selected` experts per token; the flag / epoch wait of the
+  row-sharded path ends the step.
 
 The compute step defaults to the CUDA entry points of libfeml_b200.so
 (feml_b200.ops); `compute` / `compute_id` can be replaced, which the CPU
@@ -203,8 +211,10 @@ class RowShardedMulMat:
 
 
 class ExpertShardedMulMatId:
-    """out [N, n_sel, M] = mul_mat_id(W, x, ids) with experts sharded across
-    the ranks of `group` (expert e on rank e % world).
+    """out = mul_mat_id(W, x, ids) with experts sharded across the ranks of
+    `group` (expert e on rank e % world): [N, n_sel, M] on every rank
+    (combine="replicate"), or this rank's tokens [hi - lo, n_sel, M] with
+    (lo, hi) = token_range(N) (combine="owner").
 
     `w` is either all experts (uint8 [E, M, row_bytes]) from which this rank
     keeps its own, or (local=True) this rank's experts already, in local
@@ -212,13 +222,17 @@ class ExpertShardedMulMatId:
     """
 
     def __init__(self, wtype, w, K, n_experts, group=None, local=False, compute_id=None, fused=False,
-                 max_tokens=512, max_selected=8):
+                 max_tokens=512, max_selected=8, combine="replicate"):
+        if combine not in ("replicate", "owner"):
+            raise FemlError("msg", f"combine must be 'replicate' or 'owner', got {combine!r}")
         self.wtype = DType(wtype)
         self.K, self.E = K, n_experts
         self.group = group
         self.rank, self.world = _world(group)
         self.fused = fused
+        self.combine = combine
         self.max_tokens, self.max_selected = max_tokens, max_selected
+        self.owner_tokens = -(-max_tokens // self.world)
         self._peer = None
         n_loc = local_experts(n_experts, self.rank, self.world)
         if local:
@@ -231,6 +245,13 @@ class ExpertShardedMulMatId:
             self.w_local = w[self.rank::self.world]
         self.M = w.shape[1]
         self.compute_id = compute_id or _cuda_mul_mat_id
+
+    def token_range(self, N):
+        """Tokens [lo, hi) whose slots this rank holds after an owner combine."""
+        if N > self.max_tokens:
+            raise FemlError("shape", f"{N} tokens exceed max_tokens={self.max_tokens}")
+        lo = min(N, self.rank * self.owner_tokens)
+        return lo, min(N, lo + self.owner_tokens)
 
     def close(self):
         """Unmap the peers' buffers (after the last fused step has finished)."""
@@ -246,27 +267,32 @@ class ExpertShardedMulMatId:
         N, n_sel = ids.shape
         if x.shape[0] != N or x.shape[1] != self.K:
             raise FemlError("shape", f"activation {tuple(x.shape)} does not match ids {tuple(ids.shape)} / K={self.K}")
+        owner = self.combine == "owner"
+        lo, hi = self.token_range(N) if owner else (0, N)
         if self._fused_ok(N, n_sel):
             from . import ops
             if self._peer is None:
                 if self.w_local.shape[0] < 1:
                     raise FemlError("shape", f"fused expert sharding needs an expert on every rank "
                                              f"(rank {self.rank} has none)")
-                self._peer = _PeerBuffers((self.max_tokens, self.max_selected, self.M), x.device, self.group)
+                rows = self.owner_tokens if owner else self.max_tokens
+                self._peer = _PeerBuffers((rows, self.max_selected, self.M), x.device, self.group)
                 self._ws = torch.empty(ops.mul_mat_id_workspace(self.wtype, self.K, self.M, self.max_tokens,
                                                                 self.max_selected, self.w_local.shape[0]),
                                        dtype=torch.uint8, device=x.device)
             pe = self._peer
-            # slot (t, s) at t * nb2 + s * nb1 of the [max_tokens, n_sel, M] view of each buffer
+            # slot (t, s) at t * nb2 + s * nb1 of a [tokens, n_sel, M] view of each buffer
             nb1, nb2 = 4 * self.M, 4 * self.M * n_sel
             ops.mul_mat_id_peer(self.wtype, self.w_local, x, ids, self.K, self.E, self.rank, self.world, pe.dst0,
-                                pe.dst1, pe.flags, nb1, nb2, self.M, pe.counter, pe.epoch, self._ws)
+                                pe.dst1, pe.flags, nb1, nb2, self.M, pe.counter, pe.epoch, self._ws,
+                                owner_tokens=self.owner_tokens if owner else 0)
             buf = pe.finish(self.world)
-            return buf.view(-1)[:N * n_sel * self.M].view(N, n_sel, self.M)
+            n_out = hi - lo
+            return buf.view(-1)[:n_out * n_sel * self.M].view(n_out, n_sel, self.M)
         out = torch.zeros((N, n_sel, self.M), dtype=torch.float32, device=x.device)
         self.compute_id(self.wtype, self.w_local, x, ids, self.K, self.E, self.rank, self.world, out)
         dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)
-        return out
+        return out[lo:hi] if owner else out
 
 
 __all__ = ["RowShardedMulMat", "ExpertShardedMulMatId", "row_range", "local_experts"]

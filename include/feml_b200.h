@@ -111,6 +111,11 @@ typedef struct {
     int (*synchronize)(void *ctx);
     int (*graph_compute)(void *ctx, const fb_plan *plan);
     int (*supports_op)(void *ctx, int32_t op, const int32_t *src_dtypes, int32_t n);
+    /* Optional (may be NULL; no counterpart in the Rust trait): called by
+     * fb_graph_compile once the plan's buffers exist, so the backend can size
+     * its intermediates and prepare the plan's launches at compile time
+     * instead of on the first graph_compute. */
+    int (*prepare_plan)(void *ctx, const fb_plan *plan);
 } fb_backend_vtable;
 
 const char *feml_b200_last_error(void);
@@ -176,6 +181,14 @@ int feml_b200_supports_op(fb_backend *b, int32_t op, const int32_t *src_dtypes, 
 int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan);
 /* Fill a vtable bound to `b` (for compile() and other generic callers). */
 int feml_b200_backend_vtable(fb_backend *b, fb_backend_vtable *vt);
+
+/* Prepare a compiled plan for execution (fb_graph_compile does this through
+ * the vtable; a caller that compiles elsewhere, such as the Rust
+ * GraphBuilder::compile of graph.rs:349-442, calls it once after compile):
+ * the scratch arena grows to the plan's largest node and the plan's launches
+ * are captured into a CUDA graph. graph_compute of a prepared plan then
+ * allocates nothing, from its first call on (docs/backend-guide.md:22). */
+int feml_b200_prepare_plan(fb_backend *b, const fb_plan *plan);
 
 /* Interop: device address of a buffer and the backend's CUDA stream. */
 int feml_b200_buffer_device_ptr(fb_backend *b, uint32_t handle, void **ptr, uint64_t *size);
@@ -302,6 +315,12 @@ int feml_b200_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *
                       uint64_t dst_nb1, int64_t K, int64_t M, int64_t N, void *workspace, uint64_t workspace_bytes,
                       void *stream);
 
+/* Number of kernel launches one feml_b200_mul_mat of this shape enqueues
+ * (16-byte aligned operands): the decode GEMV, the activation quantizer and
+ * GEMM, and a split-K reduction when the GEMM splits K. For benchmarks that
+ * count the kernels of a timed region. */
+int feml_b200_mul_mat_launches(int32_t wtype, int64_t K, int64_t M, int64_t N, int32_t *count);
+
 /* feml_b200_mul_mat without a workspace argument: the scratch is a fixed
  * 16 MiB device array inside this library (one per device), so the call
  * allocates nothing. No counterpart in the reference (its backends allocate
@@ -312,7 +331,12 @@ int feml_b200_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *
  * kernels can overlap (unordered streams) race; calls on one stream are
  * safe. Nothing in it needs to start at zero. Shapes whose scratch
  * (feml_b200_mul_mat_workspace) exceeds feml_b200_mul_mat_noalloc_limit()
- * bytes return FB_ERR_UNSUPPORTED without queuing work. */
+ * bytes return FB_ERR_UNSUPPORTED without queuing work; arguments are
+ * checked first as feml_b200_mul_mat checks them (negative dimensions:
+ * FB_ERR_INVALID). The array is device memory of the library's own module:
+ * under lazy module loading (the CUDA 12 default) a device holds it from the
+ * first call made there; with CUDA_MODULE_LOADING=EAGER every context the
+ * process creates holds it from creation. */
 int feml_b200_mul_mat_noalloc(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *dst,
                               uint64_t dst_nb1, int64_t K, int64_t M, int64_t N, void *stream);
 uint64_t feml_b200_mul_mat_noalloc_limit(void);
@@ -377,12 +401,37 @@ int feml_b200_mul_mat_id_peer(int32_t wtype, const void *w_local, uint64_t w_nb1
                               uint32_t *const *peer_flags, int32_t n_peers, uint64_t dst_nb1, uint64_t dst_nb2,
                               uint32_t *counter, const uint32_t *epoch, int64_t K, int64_t M, int64_t N,
                               void *workspace, uint64_t workspace_bytes, int32_t *status, void *stream);
+/* The same step with the combine sent to the token owners (the
+ * all-to-all form of the expert-parallel combine; no counterpart in the
+ * reference): token t belongs to rank t / owner_tokens (owner_tokens *
+ * n_peers >= N), each rank's two buffers hold only its owner_tokens tokens
+ * (local token t % owner_tokens at + s*dst_nb1 + (t % owner_tokens)*dst_nb2),
+ * and a slot is stored only into its owner's buffer of this step, so a rank
+ * sends about 1/n_peers of the slot tensor instead of all of it to every
+ * peer. Invalid ids are zeroed by the owner. owner_tokens == 0 is
+ * feml_b200_mul_mat_id_peer. */
+int feml_b200_mul_mat_id_peer_owned(int32_t wtype, const void *w_local, uint64_t w_nb1, uint64_t w_nb2,
+                                    int64_t n_experts, int64_t shard, int64_t n_shards, const void *x, uint64_t x_nb1,
+                                    const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, void *const *peer_dst0,
+                                    void *const *peer_dst1, uint32_t *const *peer_flags, int32_t n_peers,
+                                    uint64_t dst_nb1, uint64_t dst_nb2, int64_t owner_tokens, uint32_t *counter,
+                                    const uint32_t *epoch, int64_t K, int64_t M, int64_t N, void *workspace,
+                                    uint64_t workspace_bytes, int32_t *status, void *stream);
 
 /* Enqueue the end of a fused step on this rank: wait (one thread, bounded at
  * about a second) until this rank's flag reaches (*epoch + 1) * n_ranks, then
  * advance *epoch. On timeout bit 0 of *status is set and the stream continues
  * (the context stays usable). */
 int feml_b200_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int32_t *status, void *stream);
+/* feml_b200_peer_wait with the bound given: the wait gives up after
+ * timeout_us microseconds of the GPU's global timer (1 .. 10,000,000),
+ * sets bit 0 (STATUS_TIMEOUT) of *status, leaves *epoch unchanged and lets
+ * the stream continue. This is the failure detector of a fused step: a rank
+ * that never signals makes its peers' waits run out, not hang. The
+ * reference reports failures only as host-side error returns
+ * (feml-cpu/tests/cpu_integration.rs:131-144). */
+int feml_b200_peer_wait_timeout(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, uint64_t timeout_us,
+                                int32_t *status, void *stream);
 
 /* Expert-sharded mul_mat_id (no counterpart in the reference, which has no
  * multi-GPU code): expert e belongs to shard e % n_shards as local expert

@@ -99,7 +99,7 @@ int main(void) {
     host_backend hb;
     memset(&hb, 0, sizeof hb);
     fb_backend_vtable vt = {&hb, hb_name, hb_create, hb_release, hb_write, hb_read, hb_fill,
-                            hb_sync, hb_compute, hb_supports};
+                            hb_sync, hb_compute, hb_supports, NULL};
 
     /* x -> rms_norm -> mul_mat(w Q8_0) */
     fb_graph *g = NULL;

@@ -201,3 +201,38 @@ def test_second_graph_compute_allocates_nothing(b200, dt, K, M, N):
         assert np.array_equal(first, again)
     finally:
         plan.release(b200)
+
+
+@pytest.mark.parametrize("dt,K,M,N", [(DType.Q4_K, 14336, 4096, 64), (DType.Q4_0, 4096, 1024, 64),
+                                      (DType.Q8_0, 4096, 512, 1)])
+def test_first_graph_compute_allocates_nothing(b200, dt, K, M, N):
+    """compile prepares the plan (feml_b200_prepare_plan through the vtable):
+    the scratch is sized for its largest node (split-K partials included) and
+    its launches are captured, so even the first graph_compute allocates
+    nothing (docs/backend-guide.md:22) and replays a graph."""
+    code = {DType.Q8_0: O.DT_Q8_0, DType.Q4_0: O.DT_Q4_0, DType.Q4_K: O.DT_Q4_K}[dt]
+    rng = np.random.default_rng(K + M + N)
+    wb = O.quantize(code, (rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    g = GraphBuilder()
+    wi = g.weight("w", dt, [K, M])
+    xi = g.input("x", DType.F32, [K, N])
+    o = g.mul_mat(wi, xi)
+    g.mark_output(o)
+    plan = g.compile(b200)
+    try:
+        before = b200.device_allocations()
+        cached, replayable = b200.plan_graphs()
+        assert replayable >= 1
+        plan.write_tensor(b200, wi, wb)
+        plan.write_tensor(b200, xi, x)
+        b200.graph_compute(plan)
+        b200.synchronize()
+        assert b200.device_allocations() == before
+        assert b200.plan_graphs() == (cached, replayable)
+        got = np.empty((N, M), np.float32)
+        plan.read_tensor(b200, o, got)
+        ok, err = tol_ok(got, O.mul_mat_quant_ref(code, wb, x, K))
+        assert ok, err
+    finally:
+        plan.release(b200)

@@ -1,13 +1,14 @@
 """GPU parity at the full sizes of the benchmark workloads.
 
-Where the oracle is cheap (C1, C2, C4) every output is checked; for C3 and
-C5 a column/slot sample is checked against the oracle and the full output
-through size-independent properties: power-of-two scaling of the
-activations scales every output exactly, and permuting activation columns
-permutes output columns exactly (each column's arithmetic is independent of
-its position). Weights are drawn with numpy default_rng(seed) as in the
-workload definitions and quantized by the oracle (bytes identical to the
-device quantizer, checked in test_gpu_quant.py)."""
+Every output of every workload (C1-C5) is compared with the oracle (the
+multi-threaded C restatement of feml-cpu/src/ops/mul_mat.rs:36-57 on the
+dequantized operands); C3 and C5 also check size-independent properties of
+the whole output: power-of-two scaling of the activations scales every
+output exactly, and permuting activation columns permutes output columns
+exactly (each column's arithmetic is independent of its position). Weights
+are drawn with numpy default_rng(seed) as in the workload definitions and
+quantized by the oracle (bytes identical to the device quantizer, checked in
+test_gpu_quant.py)."""
 import numpy as np
 import pytest
 import torch
@@ -62,14 +63,12 @@ def c3_data():
     return K, M, N, wq, x
 
 
-def test_c3_q4_0_prefill_sampled_columns(b200, c3_data):
+def test_c3_q4_0_prefill_every_output(b200, c3_data):
     K, M, N, wq, x = c3_data
     got = run_mul_mat(b200, DType.Q4_0, wq, x, K, M)
-    cols = np.random.default_rng(22).choice(N, 24, replace=False)
-    want = O.mul_mat_quant_ref(O.DT_Q4_0, wq, x[cols], K)
-    ok, err = tol_ok(got[cols], want)
+    want = O.mul_mat_quant_ref(O.DT_Q4_0, wq, x, K)
+    ok, err = tol_ok(got, want)
     assert ok, err
-    assert np.isfinite(got).all()
 
 
 def test_c3_q4_0_prefill_properties(b200, c3_data):
@@ -85,36 +84,40 @@ def test_c3_q4_0_prefill_properties(b200, c3_data):
     assert torch.equal(yp, y[perm])
 
 
-def test_c5_moe_q8_0_8x4096x14336_top2(b200):
+@pytest.fixture(scope="module")
+def c5_data():
     rng = np.random.default_rng(4)
     E, M, K, N, n_sel = 8, 14336, 4096, 512, 2
-    # weights drawn and quantized on the device in expert-sized pieces
-    g = torch.Generator(device="cuda").manual_seed(4)
-    wq = torch.empty((E, M, DType.Q8_0.row_size(K)), dtype=torch.uint8, device="cuda")
-    for e in range(E):
-        wq[e] = ops.quantize(DType.Q8_0, torch.randn((M, K), generator=g, device="cuda") * 0.02)
+    wq = np.stack([O.quantize(O.DT_Q8_0, rng.standard_normal((M, K), dtype=np.float32) * np.float32(0.02))
+                   for _ in range(E)])
     x = rng.standard_normal((N, K)).astype(np.float32)
     ids = np.stack([rng.permutation(E)[:n_sel] for _ in range(N)]).astype(np.int32)
+    return E, M, K, N, n_sel, wq, x, ids
+
+
+def test_c5_moe_q8_0_every_output(b200, c5_data):
+    E, M, K, N, n_sel, wq, x, ids = c5_data
+    got = run_mul_mat_id(b200, DType.Q8_0, wq, x, ids, K, M)
+    want = O.mul_mat_id_ref(O.DT_Q8_0, wq, x, ids, K)
+    ok, err = tol_ok(got, want)
+    assert ok, err
+
+
+def test_c5_moe_q8_0_properties_and_routing(c5_data):
+    E, M, K, N, n_sel, wq, x, ids = c5_data
+    wt = torch.from_numpy(wq).cuda()
     xt, it = torch.from_numpy(x).cuda(), torch.from_numpy(ids).cuda()
-    out = ops.mul_mat_id(DType.Q8_0, wq, xt, it, K)
-    out2 = ops.mul_mat_id(DType.Q8_0, wq, xt * 2.0, it, K)
+    out = ops.mul_mat_id(DType.Q8_0, wt, xt, it, K)
+    out2 = ops.mul_mat_id(DType.Q8_0, wt, xt * 2.0, it, K)
+    perm = torch.from_numpy(np.random.default_rng(6).permutation(N)).cuda()
+    outp = ops.mul_mat_id(DType.Q8_0, wt, xt[perm].contiguous(), it[perm].contiguous(), K)
     torch.cuda.synchronize()
     assert torch.equal(out2, out * 2.0)
+    assert torch.equal(outp, out[perm])
     # routing at full size is bit-exact
     c, o, r = ops.moe_route(it, E)
     wc, wo, wr, bad = O.moe_route(ids, E)
     assert bad == 0 and np.array_equal(r.cpu().numpy(), wr) and np.array_equal(c.cpu().numpy(), wc)
-    # sampled slots x sampled rows against the oracle
-    rows = np.random.default_rng(44).choice(M, 256, replace=False)
-    slots = np.random.default_rng(45).choice(N * n_sel, 12, replace=False)
-    wq_h = wq[:, torch.from_numpy(rows).cuda()].cpu().numpy()
-    outh = out.cpu().numpy()
-    for sl in slots:
-        t, s = divmod(int(sl), n_sel)
-        e = ids[t, s]
-        want = O.mul_mat_quant_ref(O.DT_Q8_0, wq_h[e], x[t:t + 1], K)[0]
-        ok, err = tol_ok(outh[t, s, rows], want)
-        assert ok, (sl, err)
 
 
 def test_c5_through_graph_small_experts(b200):

@@ -113,6 +113,32 @@ def test_expert_sharded_fused_single_rank(group):
     assert ok, err
 
 
+def test_expert_sharded_fused_owner_single_rank(group):
+    """The owner combine (each slot stored only into the buffer of the rank
+    owning its token) on a one-rank group owns every token: bitwise the
+    unfused result over ragged steps, an invalid id giving a zero slot."""
+    rng = np.random.default_rng(9)
+    E, M, K, N, n_sel = 4, 260, 512, 40, 2
+    wq = np.stack([O.quantize(O.DT_Q8_0, (rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+                   for _ in range(E)])
+    wt = torch.from_numpy(wq).cuda()
+    fused = ExpertShardedMulMatId(DType.Q8_0, wt, K, E, fused=True, max_tokens=64, max_selected=4, combine="owner")
+    plain = ExpertShardedMulMatId(DType.Q8_0, wt, K, E)
+    for step in range(3):
+        n = N - 9 * step
+        x = torch.from_numpy(rng.standard_normal((n, K)).astype(np.float32)).cuda()
+        ids_np = np.stack([rng.permutation(E)[:n_sel] for _ in range(n)]).astype(np.int32)
+        ids_np[2, 0] = -1  # invalid id: zero slot
+        ids = torch.from_numpy(ids_np).cuda()
+        assert fused.token_range(n) == (0, n)
+        got = fused(x, ids).clone()
+        want = plain(x, ids)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), step
+        assert not got[2, 0].any()
+    fused.close()
+
+
 def _fused_worker(rank, world, port, outdir):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -165,7 +191,38 @@ def _fused_id_worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("worker", [_fused_worker, _fused_id_worker], ids=["rows", "experts"])
+def _fused_id_owner_worker(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    rng = np.random.default_rng(13)
+    E, M, K, N, n_sel = 8, 200, 1024, 70, 2
+    wq = np.stack([O.quantize(O.DT_Q8_0, (rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+                   for _ in range(E)])
+    wt = torch.from_numpy(wq).cuda()
+    fused = ExpertShardedMulMatId(DType.Q8_0, wt, K, E, fused=True, max_tokens=N, max_selected=n_sel,
+                                  combine="owner")
+    worst = 0.0
+    for step in range(4):
+        n = N - 5 * step
+        x = torch.from_numpy(rng.standard_normal((n, K)).astype(np.float32)).cuda()
+        ids = torch.from_numpy(np.stack([rng.permutation(E)[:n_sel] for _ in range(n)]).astype(np.int32)).cuda()
+        lo, hi = fused.token_range(n)
+        got = fused(x, ids).clone()
+        want = ops.mul_mat_id(DType.Q8_0, wt, x, ids, K)[lo:hi]
+        torch.cuda.synchronize()
+        worst = max(worst, float((got - want).abs().max()) if hi > lo else 0.0)
+    fused.close()
+    np.save(os.path.join(outdir, f"r{rank}.npy"), np.array([worst]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("worker", [_fused_worker, _fused_id_worker, _fused_id_owner_worker],
+                         ids=["rows", "experts", "experts-owner"])
 def test_sharded_fused_two_gpus(tmp_path, worker):
     """Peer stores over NVLink between two processes (needs two GPUs): the
     gathered rows / combined expert slots equal the one-GPU result bitwise."""

@@ -75,14 +75,16 @@ def _row_worker(rank, world, port, case, outdir):
     dist.destroy_process_group()
 
 
-def _expert_worker(rank, world, port, case, outdir):
+def _expert_worker(rank, world, port, case, outdir, combine="replicate"):
     from feml_b200.shard import ExpertShardedMulMatId
     _init(rank, world, port)
     wtype, K, M, E, N, n_sel, bad, seed = case
     wq, x, ids = _expert_case(seed, wtype, K, M, E, N, n_sel, bad)
-    op = ExpertShardedMulMatId(wtype, torch.from_numpy(wq), K, E, compute_id=_oracle_mul_mat_id)
+    op = ExpertShardedMulMatId(wtype, torch.from_numpy(wq), K, E, compute_id=_oracle_mul_mat_id, max_tokens=N,
+                               combine=combine)
     out = op(torch.from_numpy(x), torch.from_numpy(ids))
     np.save(os.path.join(outdir, f"y{rank}.npy"), out.numpy())
+    np.save(os.path.join(outdir, f"range{rank}.npy"), np.array(op.token_range(N) if combine == "owner" else (0, N)))
     dist.destroy_process_group()
 
 
@@ -136,6 +138,29 @@ def test_expert_shard_matches_single_device(tmp_path, world, bad):
         got = np.load(tmp_path / f"y{r}.npy")
         assert got.shape == want.shape
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"rank {r}"
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("bad", [False, True])
+def test_expert_shard_owner_combine(tmp_path, world, bad):
+    """combine="owner": each rank ends with exactly its own tokens' slots
+    (token t on rank t // ceil(N / world)); together they are the
+    single-device result, every token once."""
+    N = 7
+    case = (O.DT_Q8_0, 64, 12, 5, N, 2, bad, 5)
+    _spawn(_expert_worker, world, case, str(tmp_path), "owner")
+    wq, x, ids = _expert_case(5, O.DT_Q8_0, 64, 12, 5, N, 2, bad)
+    want = O.mul_mat_id_ref(O.DT_Q8_0, wq, x, ids, 64, nthreads=1)
+    covered = []
+    T = -(-N // world)
+    for r in range(world):
+        lo, hi = np.load(tmp_path / f"range{r}.npy")
+        assert (lo, hi) == (min(N, r * T), min(N, r * T + T))
+        got = np.load(tmp_path / f"y{r}.npy")
+        assert got.shape == (hi - lo,) + want.shape[1:]
+        assert np.array_equal(got.view(np.uint32), want[lo:hi].view(np.uint32)), f"rank {r}"
+        covered += list(range(lo, hi))
+    assert covered == list(range(N))
 
 
 def test_rank_that_skips_the_gather_times_out(tmp_path):
