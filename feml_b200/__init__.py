@@ -356,6 +356,13 @@ class B200Backend(Backend):
         _check(_L.lib().feml_b200_plan_graphs(self._h, ctypes.byref(n), ctypes.byref(r)))
         return n.value, r.value
 
+    def plan_fused_nodes(self, plan):
+        """Nodes of `plan` folded into a neighbouring kernel (rms_norm into a
+        decode mul_mat, bias add / silu into a mul_mat's epilogue)."""
+        n = ctypes.c_int64()
+        _check(_L.lib().feml_b200_plan_fused_nodes(self._h, plan._plan_ptr(), ctypes.byref(n)))
+        return n.value
+
     def device_allocations(self):
         """cudaMalloc calls this backend has made (buffers and scratch)."""
         v = ctypes.c_uint64()

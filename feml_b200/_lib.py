@@ -87,6 +87,7 @@ SIGNATURES = [
     ("feml_b200_supports_op", c_int, [vp, c_i32, ctypes.POINTER(c_i32), c_i32]),
     ("feml_b200_graph_compute", c_int, [vp, ctypes.POINTER(Plan)]),
     ("feml_b200_prepare_plan", c_int, [vp, ctypes.POINTER(Plan)]),
+    ("feml_b200_plan_fused_nodes", c_int, [vp, ctypes.POINTER(Plan), ctypes.POINTER(c_i64)]),
     ("feml_b200_backend_vtable", c_int, [vp, ctypes.POINTER(VTable)]),
     ("feml_b200_buffer_device_ptr", c_int, [vp, c_u32, ctypes.POINTER(vp), ctypes.POINTER(c_u64)]),
     ("feml_b200_stream", c_int, [vp, ctypes.POINTER(vp)]),

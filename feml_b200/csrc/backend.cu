@@ -99,16 +99,22 @@ int mul_mat_launches(int32_t wtype, int64_t K, int64_t M, int64_t N) {
 
 // norm_eps non-null: x is rms-normalized (that eps) inside the decode GEMV
 // (graph_compute passes it only for shapes where that path runs).
+// epi non-null: the bias / SiLU epilogue of a fused mul_mat -> add -> silu
+// chain: inside the decode GEMV and the tcgen05 GEMM, or as one pass over y
+// after the other kernels (same arithmetic, same bits).
 int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
                int64_t K, int64_t M, int64_t N, void *ws, uint64_t ws_bytes, int32_t *status, cudaStream_t s,
-               const float *norm_eps = nullptr) {
+               const float *norm_eps = nullptr, const fbk::EpiAct *epi = nullptr) {
     if (K < 0 || M < 0 || N < 0) return set_error(FB_ERR_INVALID, "mul_mat: negative dimension");
     if (M == 0 || N == 0) return FB_OK;
     if (!w || !x || !y) return set_error(FB_ERR_INVALID, "mul_mat: null operand");
     if (!is_mul_mat_dtype(wtype)) return set_error(FB_ERR_UNSUPPORTED, "mul_mat: weight dtype %d not supported", wtype);
     const fb::DTypeTraits *t = fb::dtype_traits(wtype);
     if (K % t->block_size) return set_error(FB_ERR_SHAPE, "mul_mat: K %ld not a multiple of %ld", (long)K, (long)t->block_size);
-    if (wtype == FB_F32) return fbk::launch_gemm_f32(w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, status, s);
+    const bool act = fbk::epi_active(epi);
+    // kernels without a fused epilogue: one bias / SiLU pass over y afterwards
+    auto then_act = [&](int rc) { return rc || !act ? rc : fbk::launch_bias_act(y, y_nb1, M, N, *epi, s); };
+    if (wtype == FB_F32) return then_act(fbk::launch_gemm_f32(w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, status, s));
     if (K == 0) return set_error(FB_ERR_SHAPE, "mul_mat: K == 0");
 
     const uint64_t need = mul_mat_ws(wtype, K, M, N);
@@ -117,24 +123,25 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
                          (unsigned long)ws_bytes);
     if (need == 0)
         return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, nullptr, status, s, true, nullptr,
-                                norm_eps);
+                                norm_eps, epi);
     if (norm_eps) return set_error(FB_ERR_UNSUPPORTED, "mul_mat: fused rms_norm needs the decode GEMV");
     if (tc_shape(wtype, K, M, N) && fbk::gemm_tc_supported(wtype, K, M, N, w, w_nb1) &&
         ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0) {
         const fbk::XQ16 xa = fbk::xq16_carve(ws, K, N);
         int rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, nullptr, s);
         if (rc) return rc;
-        return fbk::launch_gemm_tc(wtype, w, w_nb1, xa, K, M, N, y, y_nb1, nullptr, status, s);
+        return fbk::launch_gemm_tc(wtype, w, w_nb1, xa, K, M, N, y, y_nb1, nullptr, status, s, nullptr, epi);
     }
 
     const fbk::Q8Planar xq = fbk::q8_planar_carve(ws, K, N);
     int rc = fbk::launch_quantize_q8_planar(x, x_nb1, K, N, xq, s);
     if (rc) return rc;
     if (fbk::gemv_supported(wtype, K, N))
-        return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, &xq, status, s, true);
+        return fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, y, y_nb1, K, M, N, &xq, status, s, true, nullptr, nullptr,
+                                epi);
     if (fbk::gemm_q_supported(wtype, K, w, w_nb1))
-        return fbk::launch_gemm_q(wtype, w, w_nb1, xq, K, M, N, y, y_nb1, nullptr, s,
-                                  static_cast<uint8_t *>(ws) + fbk::q8_planar_bytes(K, N));
+        return then_act(fbk::launch_gemm_q(wtype, w, w_nb1, xq, K, M, N, y, y_nb1, nullptr, s,
+                                           static_cast<uint8_t *>(ws) + fbk::q8_planar_bytes(K, N)));
     // Shapes the GEMM cannot tile (K % 256 != 0, unaligned rows): the GEMV on
     // groups of up to gemv_max_cols() columns of the already-quantized
     // activations.
@@ -143,7 +150,7 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
         const int64_t nc = std::min<int64_t>(ncol, N - n0);
         fbk::Q8Planar sub{xq.qs + n0 * K, xq.d + n0 * nblk, xq.sum + n0 * nblk};
         rc = fbk::launch_gemv(wtype, w, w_nb1, x, x_nb1, static_cast<uint8_t *>(y) + n0 * y_nb1, y_nb1, K, M, nc,
-                              &sub, status, s, false);
+                              &sub, status, s, false, nullptr, nullptr, epi);
         if (rc) return rc;
     }
     return FB_OK;
@@ -441,7 +448,83 @@ int compute_rms_norm(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &n
     return fbk::launch_rms_norm(X.ptr, x.nb, Y.ptr, y.nb, y.ne, rms_eps(node), b->stream);
 }
 
-int compute_mul_mat(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
+// ---- mul_mat -> add(bias) -> silu fusion --------------------------------
+// A mul_mat whose output is read only by a bias add (the other operand a
+// vector of M floats broadcast over the N columns) and/or a SiLU, each
+// intermediate read by nothing else, not a graph output and computed by the
+// very next node, runs as one kernel: the chain's last tensor is written by
+// the mul_mat's epilogue and the add / silu nodes are skipped (the
+// compile-time fusion of the reference's roadmap, docs/DESIGN.md:251).
+struct ActChain {
+    int64_t add = -1, silu = -1;  // fused nodes (tensor indices)
+    int64_t bias = -1;            // the bias vector
+    int64_t out = -1;             // the tensor the mul_mat kernel writes
+};
+
+// The only tensor that reads tensor `ti` (-1 when none or several do).
+int64_t sole_reader(const fb_plan *plan, int64_t ti) {
+    int64_t r = -1, n = 0;
+    for (int64_t i = 0; i < plan->n_tensors; i++) {
+        const fb_plan_tensor &t = plan->tensors[i];
+        for (int k = 0; k < t.n_srcs && k < FB_MAX_SRC; k++)
+            if (t.srcs[k] == ti) {
+                r = i;
+                n++;
+            }
+    }
+    return n == 1 ? r : -1;
+}
+
+bool f32_2d(const fb_plan_tensor &t, int64_t M, int64_t N) {
+    return t.dtype == FB_F32 && t.ne[0] == M && t.ne[1] == N && t.ne[2] == 1 && t.ne[3] == 1 && t.nb[0] == 4;
+}
+
+// The chain starting at the mul_mat at node position `pos`, or none.
+ActChain act_chain(const fb_plan *plan, int64_t pos) {
+    ActChain c;
+    const int64_t mi = plan->nodes[pos];
+    const fb_plan_tensor &mm = plan->tensors[mi];
+    const int64_t M = mm.ne[0], N = mm.ne[1];
+    if (mm.op != FB_OP_MUL_MAT || (mm.flags & FB_FLAG_OUTPUT) || !f32_2d(mm, M, N)) return c;
+    auto next_is = [&](int64_t p, int64_t t) { return p < plan->n_nodes && plan->nodes[p] == t; };
+    const int64_t r1 = sole_reader(plan, mi);
+    if (r1 < 0 || !next_is(pos + 1, r1)) return c;
+    const fb_plan_tensor &t1 = plan->tensors[r1];
+    ActChain found;
+    if (t1.op == FB_OP_ADD && t1.n_srcs == 2 && f32_2d(t1, M, N)) {
+        const int64_t bi = t1.srcs[0] == mi ? t1.srcs[1] : t1.srcs[0];
+        if (bi < 0 || bi >= plan->n_tensors || bi == mi || (t1.srcs[0] != mi && t1.srcs[1] != mi)) return c;
+        const fb_plan_tensor &bt = plan->tensors[bi];
+        if (bt.dtype != FB_F32 || bt.ne[0] != M || bt.ne[1] != 1 || bt.ne[2] != 1 || bt.ne[3] != 1 || bt.nb[0] != 4)
+            return c;
+        found.add = r1;
+        found.bias = bi;
+        found.out = r1;
+        const int64_t r2 = (t1.flags & FB_FLAG_OUTPUT) ? -1 : sole_reader(plan, r1);
+        if (r2 >= 0 && next_is(pos + 2, r2)) {
+            const fb_plan_tensor &t2 = plan->tensors[r2];
+            if (t2.op == FB_OP_SILU && t2.n_srcs == 1 && f32_2d(t2, M, N)) {
+                found.silu = r2;
+                found.out = r2;
+            }
+        }
+    } else if (t1.op == FB_OP_SILU && t1.n_srcs == 1 && f32_2d(t1, M, N)) {
+        found.silu = r1;
+        found.out = r1;
+    } else {
+        return c;
+    }
+    // the kernel writes `out` while reading the weights, the activations and
+    // the bias: none of them may share its bytes (the mul_mat's own output
+    // and the add's are never materialized, so `out` may reuse them)
+    const fb_plan_tensor &o = plan->tensors[found.out];
+    const int64_t reads[3] = {mm.srcs[0], mm.srcs[1], found.bias};
+    for (int64_t ri : reads)
+        if (ri >= 0 && ri < plan->n_tensors && ranges_overlap(plan, plan->tensors[ri], o)) return c;
+    return found;
+}
+
+int compute_mul_mat(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node, const ActChain *chain = nullptr) {
     if (node.n_srcs != 2) return set_error(FB_ERR_INVALID, "mul_mat: expected 2 sources");
     DevTensor A, B, C;
     int rc;
@@ -453,7 +536,17 @@ int compute_mul_mat(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &no
     if ((rc = resolve(b, plan, node.srcs[0], &A)) ||
         (rc = resolve(b, plan, fused_norm ? plan->tensors[act].srcs[0] : act, &B)))
         return rc;
-    if ((rc = resolve(b, plan, &node - plan->tensors, &C))) return rc;
+    if ((rc = resolve(b, plan, chain ? chain->out : &node - plan->tensors, &C))) return rc;
+    fbk::EpiAct epi{nullptr, 0};
+    if (chain) {
+        if (chain->bias >= 0) {
+            DevTensor Bias;
+            if ((rc = resolve(b, plan, chain->bias, &Bias))) return rc;
+            if (overlap(Bias, C)) return set_error(FB_ERR_INVALID, "B200: fused mul_mat dst aliases the bias");
+            epi.bias = reinterpret_cast<const float *>(Bias.ptr);
+        }
+        epi.silu = chain->silu >= 0 ? 1 : 0;
+    }
     if (overlap(A, C) || overlap(B, C)) return set_error(FB_ERR_INVALID, "B200: mul_mat dst aliases a source");
     const fb_plan_tensor &a = *A.t, &x = *B.t, &y = *C.t;
     if (!is_mul_mat_dtype(a.dtype) || x.dtype != FB_F32 || y.dtype != FB_F32)
@@ -467,7 +560,37 @@ int compute_mul_mat(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &no
     if (a.nb[0] != (uint64_t)fb::dtype_traits(a.dtype)->type_size || x.nb[0] != 4 || y.nb[0] != 4)
         return set_error(FB_ERR_UNSUPPORTED, "B200: mul_mat needs contiguous rows");
     return do_mul_mat(a.dtype, A.ptr, a.nb[1], B.ptr, x.nb[1], C.ptr, y.nb[1], K, M, N, b->scratch, b->scratch_bytes,
-                      b->status_dev, b->stream, fused_norm ? &eps : nullptr);
+                      b->status_dev, b->stream, fused_norm ? &eps : nullptr, chain ? &epi : nullptr);
+}
+
+// Standalone add (feml-cpu/src/ops/elementwise.rs semantics: ggml
+// broadcasting; dst may alias a source exactly, any partial overlap is
+// rejected, as in feml-cpu/src/backend.rs:193-204).
+int compute_add(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
+    if (node.n_srcs != 2) return set_error(FB_ERR_INVALID, "add: expected 2 sources");
+    DevTensor X, Y, Z;
+    int rc;
+    if ((rc = resolve(b, plan, node.srcs[0], &X)) || (rc = resolve(b, plan, node.srcs[1], &Y)) ||
+        (rc = resolve(b, plan, &node - plan->tensors, &Z)))
+        return rc;
+    if (X.t->dtype != FB_F32 || Y.t->dtype != FB_F32 || Z.t->dtype != FB_F32)
+        return set_error(FB_ERR_UNSUPPORTED, "B200: add needs f32");
+    for (const DevTensor *S : {&X, &Y})
+        if (overlap(*S, Z) && (S->ptr != Z.ptr || S->nbytes != Z.nbytes))
+            return set_error(FB_ERR_INVALID, "B200: partial-overlap alias not supported");
+    return fbk::launch_add_f32(X.ptr, X.t->ne, X.t->nb, Y.ptr, Y.t->ne, Y.t->nb, Z.ptr, Z.t->ne, Z.t->nb, b->stream);
+}
+
+int compute_silu(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
+    if (node.n_srcs != 1) return set_error(FB_ERR_INVALID, "silu: expected 1 source");
+    DevTensor X, Y;
+    int rc;
+    if ((rc = resolve(b, plan, node.srcs[0], &X)) || (rc = resolve(b, plan, &node - plan->tensors, &Y))) return rc;
+    if (X.t->dtype != FB_F32 || Y.t->dtype != FB_F32) return set_error(FB_ERR_UNSUPPORTED, "B200: silu needs f32");
+    for (int d = 0; d < 4; d++)
+        if (X.t->ne[d] != Y.t->ne[d]) return set_error(FB_ERR_SHAPE, "shape error: silu: dst shape differs from src");
+    if (overlap(X, Y) && X.ptr != Y.ptr) return set_error(FB_ERR_INVALID, "B200: silu dst partly aliases src");
+    return fbk::launch_silu_f32(X.ptr, X.t->nb, Y.ptr, Y.t->nb, Y.t->ne, b->stream);
 }
 
 int compute_mul_mat_id(fb_backend *b, const fb_plan *plan, const fb_plan_tensor &node) {
@@ -765,7 +888,10 @@ int feml_b200_supports_op(fb_backend *, int32_t op, const int32_t *dt, int32_t n
     case FB_OP_MUL_MAT_ID:
         return n == 3 && dt && is_weight_dtype(dt[0]) && dt[1] == FB_F32 && dt[2] == FB_I32;
     case FB_OP_RMS_NORM:
+    case FB_OP_SILU:
         return n == 1 && dt && dt[0] == FB_F32;
+    case FB_OP_ADD:
+        return n == 2 && dt && dt[0] == FB_F32 && dt[1] == FB_F32;
     default:
         return 0;
     }
@@ -844,16 +970,34 @@ bool plan_matches(const std::vector<uint64_t> &key, const fb_plan *plan) {
 constexpr size_t kMaxPlanGraphs = 256;
 
 int run_nodes(fb_backend *b, const fb_plan *plan) {
+    // add / silu nodes computed by the epilogue of the mul_mat before them
+    std::vector<char> fused((size_t)plan->n_tensors, 0);
+    std::vector<ActChain> chains((size_t)plan->n_nodes);
+    for (int64_t i = 0; i < plan->n_nodes; i++) {
+        const int64_t ti = plan->nodes[i];
+        if (ti < 0 || ti >= plan->n_tensors) return set_error(FB_ERR_INVALID, "graph_compute: bad node index");
+        if (plan->tensors[ti].op != FB_OP_MUL_MAT || fused[ti]) continue;
+        chains[i] = act_chain(plan, i);
+        if (chains[i].add >= 0) fused[chains[i].add] = 1;
+        if (chains[i].silu >= 0) fused[chains[i].silu] = 1;
+    }
     for (int64_t i = 0; i < plan->n_nodes; i++) {
         const int64_t ti = plan->nodes[i];
         const fb_plan_tensor &node = plan->tensors[ti];
+        if (fused[ti]) continue;
         int rc;
         switch (node.op) {
         case FB_OP_VIEW:
             rc = FB_OK;
             break;
         case FB_OP_MUL_MAT:
-            rc = compute_mul_mat(b, plan, node);
+            rc = compute_mul_mat(b, plan, node, chains[i].out >= 0 ? &chains[i] : nullptr);
+            break;
+        case FB_OP_ADD:
+            rc = compute_add(b, plan, node);
+            break;
+        case FB_OP_SILU:
+            rc = compute_silu(b, plan, node);
             break;
         case FB_OP_MUL_MAT_ID:
             rc = compute_mul_mat_id(b, plan, node);
@@ -963,6 +1107,27 @@ int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan) {
     rc = run_nodes(b, plan);
     if (rc || !b->use_graphs || b->graphs.count(h)) return rc;  // (a hash collision keeps the first plan's graph)
     return capture_plan(b, plan, h, true);
+}
+
+int feml_b200_plan_fused_nodes(fb_backend *b, const fb_plan *plan, int64_t *count) {
+    if (!b || !plan || !count) return set_error(FB_ERR_INVALID, "plan_fused_nodes: null argument");
+    int64_t n = 0;
+    std::vector<char> fused((size_t)plan->n_tensors, 0);
+    for (int64_t i = 0; i < plan->n_nodes; i++) {
+        const int64_t ti = plan->nodes[i];
+        if (ti < 0 || ti >= plan->n_tensors) return set_error(FB_ERR_INVALID, "plan_fused_nodes: bad node index");
+        const fb_plan_tensor &t = plan->tensors[ti];
+        if (t.op == FB_OP_RMS_NORM && rms_fused(plan, ti)) n++;
+        if (t.op != FB_OP_MUL_MAT || fused[ti]) continue;
+        const ActChain c = act_chain(plan, i);
+        for (int64_t f : {c.add, c.silu})
+            if (f >= 0) {
+                fused[f] = 1;
+                n++;
+            }
+    }
+    *count = n;
+    return FB_OK;
 }
 
 int feml_b200_set_plan_graphs(fb_backend *b, int32_t enable) {

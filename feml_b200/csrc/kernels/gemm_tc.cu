@@ -113,6 +113,7 @@ struct TcParams {
     int split_pairs;      // split-K: pairs per CTA along blockIdx.z (0: none)
     float *partial;       // [splits][N][M] when split
     PeerOut peer;         // peer.n > 0 (grouped): outputs into every rank's buffer, then a signal
+    EpiAct epi;           // fused bias / SiLU (ungrouped, not split)
 };
 
 // Peer mode: count this CTA done; the grid's last CTA raises every rank's
@@ -729,7 +730,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                 off = (uint64_t)r * p.y_nb1;
                             }
                             if constexpr (!PEER) {
-                                reinterpret_cast<float *>(p.y + off)[m] = acc[i];
+                                reinterpret_cast<float *>(p.y + off)[m] = apply_act(acc[i], p.epi, m);
                             } else {  // NVLink stores into the owner's buffer, or every rank's
                                 const int b = (int)((*p.peer.epoch + 1u) & 1u);
                                 if (owner >= 0) {
@@ -801,15 +802,16 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
     }
 }
 
-// y[n][m] = sum over z in order of partial[z][n][m] (deterministic).
+// y[n][m] = sum over z in order of partial[z][n][m] (deterministic), then
+// the fused epilogue.
 __global__ void tc_split_reduce_kernel(const float *__restrict__ partial, int splits, int M, int N, uint8_t *y,
-                                       uint64_t y_nb1) {
+                                       uint64_t y_nb1, const EpiAct epi) {
     const int64_t total = (int64_t)M * N;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         float acc = partial[i];
         for (int z = 1; z < splits; z++) acc += partial[(int64_t)z * total + i];
         const int n = (int)(i / M), m = (int)(i % M);
-        reinterpret_cast<float *>(y + (uint64_t)n * y_nb1)[m] = acc;
+        reinterpret_cast<float *>(y + (uint64_t)n * y_nb1)[m] = apply_act(acc, epi, m);
     }
 }
 
@@ -849,7 +851,7 @@ int encode_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint6
 template <int WT>
 int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_planes, const XQ16 &xa, int64_t K,
                     int64_t M, int64_t rows, void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status,
-                    int splits, cudaStream_t s, const PeerOut *peer) {
+                    int splits, cudaStream_t s, const PeerOut *peer, const EpiAct &epi) {
     using C = TcCfg<WT>;
     using L = TcLayout<WT>;
     static_assert(L::BYTES <= 232448, "gemm_tc shared memory");
@@ -884,6 +886,7 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     p.grouped = groups != nullptr;
     if (groups) p.g = *groups;
     if (peer) p.peer = *peer;
+    p.epi = epi;
     const int total_pairs = (int)(K / (2 * QK));
     if (splits > 1) {
         const int per_chunks = (int)((K / QKK + splits - 1) / splits);
@@ -902,7 +905,7 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
         const int64_t total = M * rows;
         const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
         tc_split_reduce_kernel<<<blocks, 256, 0, s>>>(p.partial, splits, (int)M, (int)rows, static_cast<uint8_t *>(y),
-                                                      y_nb1);
+                                                      y_nb1, epi);
         e = cudaGetLastError();
         if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc split reduce launch: %s", cudaGetErrorString(e));
     }
@@ -988,7 +991,9 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
 
 int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa, int64_t K, int64_t M, int64_t N,
                    void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s,
-                   const PeerOut *peer) {
+                   const PeerOut *peer, const EpiAct *epi) {
+    if (epi_active(epi) && groups) return fb::set_error(FB_ERR_INVALID, "gemm_tc: fused epilogue needs the ungrouped mode");
+    const EpiAct ep = epi ? *epi : EpiAct{nullptr, 0};
     if (peer && (!groups || peer->n < 1 || peer->n > kMaxPeers || !peer->count || !peer->epoch))
         return fb::set_error(FB_ERR_INVALID, "gemm_tc: peer outputs need the grouped mode and a full peer set");
     const int64_t rows = groups ? N * groups->n_selected : N;
@@ -1003,13 +1008,13 @@ int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa,
     switch (wtype) {
     case WT_Q8_0:
         return launch_tc_typed<WT_Q8_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
-                                        peer);
+                                        peer, ep);
     case WT_Q4_0:
         return launch_tc_typed<WT_Q4_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
-                                        peer);
+                                        peer, ep);
     default:
         return launch_tc_typed<WT_Q4_K>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
-                                        peer);
+                                        peer, ep);
     }
 }
 

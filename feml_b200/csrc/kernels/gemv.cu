@@ -102,6 +102,7 @@ struct GemvParams {
     bool norm;        // rms-normalize each activation column before quantizing it
     float norm_eps;
     PeerOut peer;     // peer.n > 0: outputs go to every peer's buffer, then a signal
+    EpiAct epi;       // fused bias / SiLU on every output
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t v) { return (v + 15u) & ~15u; }
@@ -427,6 +428,7 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
 
     // output row `row`, column n: this rank's buffer or every peer's
     auto store_row = [&](int n, int row, float v) {
+        v = apply_act(v, p.epi, row);
         if (p.peer.n == 0) {
             reinterpret_cast<float *>(p.y + (uint64_t)n * p.y_nb1)[row] = v;
         } else {
@@ -666,6 +668,7 @@ struct KsParams {
     int32_t *status;
     bool x_vec16;
     PeerOut peer;        // peer.n > 0: outputs go to every peer's buffer, then a signal
+    EpiAct epi;          // fused bias / SiLU on every output
 };
 
 // One 32-element activation block quantized by a single lane: the operations
@@ -816,6 +819,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_ks_kernel(const __grid_c
         float v = part[t * kGemvWarps];
 #pragma unroll
         for (int w = 1; w < kGemvWarps; w++) v += part[t * kGemvWarps + w];
+        v = apply_act(v, p.epi, r_begin + t);
         if (p.peer.n == 0) {
             reinterpret_cast<float *>(p.y)[r_begin + t] = v;
         } else {
@@ -862,6 +866,7 @@ struct KsColsParams {
     uint32_t ring_off;
     uint32_t xs_off;  // shared-memory offset of the staged activations
     int32_t *status;
+    EpiAct epi;       // fused bias / SiLU on every output
 };
 
 template <int NC>
@@ -982,7 +987,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ks_cols_kernel(const __g
 #pragma unroll
         for (int w = 1; w < kGemvWarps; w++) sum += part[t * kGemvWarps + w];
         const int row = t / NC, n = t % NC;
-        reinterpret_cast<float *>(p.y + (uint64_t)n * p.y_nb1)[r_begin + row] = sum;
+        reinterpret_cast<float *>(p.y + (uint64_t)n * p.y_nb1)[r_begin + row] = apply_act(sum, p.epi, r_begin + row);
     }
 }
 
@@ -1089,7 +1094,7 @@ uint32_t chunk_bytes_of(int32_t wtype, uint32_t units) {
 // The K-split path for one column of wide Q4_K rows; returns -1 (nothing
 // launched) when the shape does not fit it.
 int launch_gemv_ks(const void *w, uint64_t w_nb1, const void *x, void *y, int64_t K, int64_t M, int32_t *status,
-                   cudaStream_t s, bool pdl, const PeerOut *peer) {
+                   cudaStream_t s, bool pdl, const PeerOut *peer, const EpiAct &epi) {
     const int nsb = (int)(K / QKK);
     const int widest = (nsb + kGemvWarps - 1) / kGemvWarps;  // super-blocks in the widest slice
     const uint32_t box_bytes = (uint32_t)widest * Q4_K_BYTES;
@@ -1117,6 +1122,7 @@ int launch_gemv_ks(const void *w, uint64_t w_nb1, const void *x, void *y, int64_
     p.status = status;
     p.x_vec16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     p.peer = peer ? *peer : PeerOut{};
+    p.epi = epi;
     auto kern = gemv_ks_kernel<1>;
     static DeviceFlags smem_set;
     rc = raise_smem_limit((const void *)kern, (int)kCoResidentCta, smem_set, "gemv");
@@ -1161,7 +1167,7 @@ int launch_ks_cols_typed(const CUtensorMap &tm, const KsColsParams &p, int grid,
 }
 
 int launch_gemv_ks_cols(const void *w, uint64_t w_nb1, const Q8Planar &xq, void *y, uint64_t y_nb1, int64_t K,
-                        int64_t M, int64_t N, int32_t *status, cudaStream_t s, bool pdl) {
+                        int64_t M, int64_t N, int32_t *status, cudaStream_t s, bool pdl, const EpiAct &epi) {
     const int nsb = (int)(K / QKK);
     const int widest = (nsb + kGemvWarps - 1) / kGemvWarps;
     const uint32_t box_bytes = (uint32_t)widest * Q4_K_BYTES;
@@ -1192,6 +1198,7 @@ int launch_gemv_ks_cols(const void *w, uint64_t w_nb1, const Q8Planar &xq, void 
     p.ring_off = ring_off;
     p.xs_off = (uint32_t)xs_off;
     p.status = status;
+    p.epi = epi;
     switch (N) {
     case 2: return launch_ks_cols_typed<2>(tm, p, grid, (uint32_t)smem, s, pdl);
     case 3: return launch_ks_cols_typed<3>(tm, p, grid, (uint32_t)smem, s, pdl);
@@ -1243,7 +1250,8 @@ int launch_peer_wait(const uint32_t *flag, uint32_t *epoch, int32_t n_ranks, int
 
 int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y, uint64_t y_nb1,
                 int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status, cudaStream_t s, bool pdl,
-                const PeerOut *peer, const float *norm_eps) {
+                const PeerOut *peer, const float *norm_eps, const EpiAct *epi) {
+    const EpiAct ep = epi ? *epi : EpiAct{nullptr, 0};
     if (!gemv_supported(wtype, K, N)) return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: unsupported shape");
     if (norm_eps && (xq || peer || K < 512 || !gemv_fused_ok(K, N)))
         return fb::set_error(FB_ERR_UNSUPPORTED, "gemv: fused rms_norm needs in-kernel activation quantization and K >= 512");
@@ -1269,11 +1277,11 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
 
     const bool rows16 = ((reinterpret_cast<uintptr_t>(w) | w_nb1) & 15) == 0;
     if (wtype == WT_Q4_K && N == 1 && !xq && rows16 && !norm_eps) {
-        const int rc = launch_gemv_ks(w, w_nb1, x, y, K, M, status, s, pdl, peer);
+        const int rc = launch_gemv_ks(w, w_nb1, x, y, K, M, status, s, pdl, peer, ep);
         if (rc >= 0) return rc;  // launched, or an error; -1: not this path
     }
     if (wtype == WT_Q4_K && N > 1 && xq && !peer && rows16) {
-        const int rc = launch_gemv_ks_cols(w, w_nb1, *xq, y, y_nb1, K, M, N, status, s, pdl);
+        const int rc = launch_gemv_ks_cols(w, w_nb1, *xq, y, y_nb1, K, M, N, status, s, pdl, ep);
         if (rc >= 0) return rc;
     }
 
@@ -1321,6 +1329,7 @@ int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uin
     p.copy_rows = ((reinterpret_cast<uintptr_t>(w) | w_nb1) % align) != 0;
     p.norm = norm_eps != nullptr;
     p.norm_eps = norm_eps ? *norm_eps : 0.0f;
+    p.epi = ep;
     // whole rows per chunk and at most two pairs per lane: activations in registers
     const int xr = (N == 1 && nchunks == 1 && rows16) ? (nunits <= 64 ? 1 : (nunits <= 128 ? 2 : 0)) : 0;
     switch (wtype) {

@@ -30,6 +30,24 @@ inline int raise_smem_limit(const void *func, int bytes, DeviceFlags &done, cons
     return FB_OK;
 }
 
+// Fused output epilogue of a mul_mat (a plan's mul_mat -> add(bias) -> silu
+// chain computed by the mul_mat's kernel): out[n][m] = act(y[n][m] + bias[m]).
+// The standalone add and silu kernels use the same expressions, so a fused
+// chain gives the bits of the node-by-node one.
+struct EpiAct {
+    const float *bias;  // M floats, or nullptr
+    int silu;           // apply SiLU, x / (1 + exp(-x)), after the bias
+};
+inline bool epi_active(const EpiAct *e) { return e && (e->bias || e->silu); }
+#ifdef __CUDACC__
+__device__ __forceinline__ float silu_f32(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
+__device__ __forceinline__ float apply_act(float v, const EpiAct &e, int m) {
+    if (e.bias) v = __fadd_rn(v, e.bias[m]);
+    if (e.silu) v = silu_f32(v);
+    return v;
+}
+#endif
+
 // Planar Q8_0 activations: the device-internal form the quantized kernels
 // read. Column n of an activation matrix [K, N] becomes qs[n*K .. n*K+K)
 // (int8), d[n*(K/32) + b] (the f16-rounded block scale as f32) and
@@ -79,9 +97,11 @@ struct PeerOut {
 };
 // With `norm_eps` (in-kernel quantization only: xq and peer null) every
 // activation column is rms-normalized with that eps before it is quantized.
+// With `epi` the outputs go through the fused bias / SiLU epilogue.
 int launch_gemv(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *y,
                 uint64_t y_nb1, int64_t K, int64_t M, int64_t N, const Q8Planar *xq, int32_t *status,
-                cudaStream_t s, bool pdl, const PeerOut *peer = nullptr, const float *norm_eps = nullptr);
+                cudaStream_t s, bool pdl, const PeerOut *peer = nullptr, const float *norm_eps = nullptr,
+                const EpiAct *epi = nullptr);
 // Wait until this rank's flag reaches (epoch + 1) * n_ranks, then advance
 // the epoch (bounded by timeout_us; STATUS_TIMEOUT on expiry).
 constexpr uint64_t kPeerWaitTimeoutUs = 1000000;  // default bound: one second
@@ -149,9 +169,11 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
 // With `peer` (grouped mode only): each output value is stored into every
 // rank's buffer of this step instead of y (see PeerOut), then every rank's
 // flag is raised once by the grid's last CTA.
+// With `epi` (ungrouped only) the outputs go through the fused bias / SiLU
+// epilogue.
 int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa, int64_t K, int64_t M, int64_t N,
                    void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s,
-                   const PeerOut *peer = nullptr);
+                   const PeerOut *peer = nullptr, const EpiAct *epi = nullptr);
 int gemm_tc_block_n();
 
 // Per-block int32 sums (bit-exactness probe); xq in ggml Q8_0 layout.
@@ -176,6 +198,16 @@ int launch_moe_route(const int32_t *ids, uint64_t ids_nb1, int64_t n_selected, i
                      int32_t *tile_start, int32_t block_n, int32_t *status, void *dst, uint64_t dst_nb1,
                      uint64_t dst_nb2, int64_t M, cudaStream_t s, void *dst_alt = nullptr,
                      const uint32_t *epoch = nullptr, int64_t owner_tokens = 0);
+
+// elementwise.cu: the reference's broadcasting add (feml-cpu/src/ops/
+// elementwise.rs), SiLU, and the bias / SiLU epilogue applied in place to a
+// finished mul_mat output y [N][M] (row n at y + n*y_nb1). ne[4] and byte
+// strides nb[4] as in feml-core layouts; c may alias a or b exactly.
+int launch_add_f32(const void *a, const int64_t *ane, const uint64_t *anb, const void *b, const int64_t *bne,
+                   const uint64_t *bnb, void *c, const int64_t *cne, const uint64_t *cnb, cudaStream_t s);
+int launch_silu_f32(const void *x, const uint64_t *xnb, void *y, const uint64_t *ynb, const int64_t *ne,
+                    cudaStream_t s);
+int launch_bias_act(void *y, uint64_t y_nb1, int64_t M, int64_t N, const EpiAct &epi, cudaStream_t s);
 
 int sm_count();
 

@@ -179,6 +179,15 @@ int feml_b200_supports_op(fb_backend *b, int32_t op, const int32_t *src_dtypes, 
  * feml_b200_set_plan_graphs); later calls of the same plan allocate nothing
  * and do not synchronize. */
 int feml_b200_graph_compute(fb_backend *b, const fb_plan *plan);
+/* Nodes of `plan` that graph_compute folds into a neighbouring kernel
+ * instead of running them: an rms_norm feeding only decode mul_mats (inside
+ * their activation quantization), and the bias add / SiLU after a mul_mat
+ * (inside its epilogue: a mul_mat whose output is read only by an add with
+ * an M-float bias vector and/or a silu, each intermediate read once, not an
+ * output and computed by the next node). The reference plans both fusions
+ * for compile time (docs/DESIGN.md:250-251). */
+int feml_b200_plan_fused_nodes(fb_backend *b, const fb_plan *plan, int64_t *count);
+
 /* Fill a vtable bound to `b` (for compile() and other generic callers). */
 int feml_b200_backend_vtable(fb_backend *b, fb_backend_vtable *vt);
 

@@ -146,3 +146,17 @@ def mul_mat_id_ref(dtype, wq_experts, x, ids, K, quantize_act=True, nthreads=Non
         y = mul_mat_quant_ref(dtype, wq_experts[e], x[toks], K, quantize_act, nthreads)
         out.reshape(N * n_sel, M)[sl] = y
     return out
+
+
+def silu_f32(x):
+    """SiLU as the plans define it (x / (1 + exp(-x))), in f32 -- the
+    reference op (feml-core/src/op.rs:32) has no kernel to follow, so this is
+    ggml's definition restated."""
+    x = np.asarray(x, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        return (x / (np.float32(1) + np.exp(-x))).astype(np.float32)
+
+
+def add_f32(a, b):
+    """The reference's broadcasting f32 add (feml-cpu/src/ops/elementwise.rs:30-96)."""
+    return (np.asarray(a, dtype=np.float32) + np.asarray(b, dtype=np.float32)).astype(np.float32)
