@@ -89,7 +89,8 @@ int mul_mat_launches(int32_t wtype, int64_t K, int64_t M, int64_t N) {
     if (M <= 0 || N <= 0) return 0;
     if (wtype == FB_F32) return 1;
     if (mul_mat_ws(wtype, K, M, N) == 0) return 1;  // fused decode GEMV
-    if (tc_shape(wtype, K, M, N)) return fbk::gemm_tc_splits(K, M, N) > 1 ? 3 : 2;
+    if (tc_shape(wtype, K, M, N))
+        return fbk::gemm_tc_splits(K, M, N) > 1 || fbk::gemm_tc_tail(K, M, N, nullptr) ? 3 : 2;
     if (fbk::gemv_supported(wtype, K, N)) return 2;
     const int64_t rb = fb::row_size(wtype, K);
     if (rb > 0 && fbk::gemm_q_supported(wtype, K, nullptr, (uint64_t)rb))

@@ -112,6 +112,13 @@ struct TcParams {
     GroupMap g;
     int split_pairs;      // split-K: pairs per CTA along blockIdx.z (0: none)
     float *partial;       // [splits][N][M] when split
+    // Tail split (ungrouped, 1D grid): work items [0, tail_full) are whole
+    // tiles in (m-tile, n-tile) order; the rest split the last tail_rows
+    // m-tile rows (every n-tile of them) tail_S ways in K, item
+    // tail_full + t * tail_S + s being split s of tail tile t, written to
+    // tail_partial[s][t][128 columns][128 rows]. tail_full < 0: off.
+    int tail_full, tail_S, tail_tiles_n, tail_m0, tail_n, tail_split_pairs;
+    float *tail_partial;
     PeerOut peer;         // peer.n > 0 (grouped): outputs into every rank's buffer, then a signal
     EpiAct epi;           // fused bias / SiLU (ungrouped, not split)
 };
@@ -403,9 +410,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *gbase = smem_raw + (sbase - smem_u32(smem_raw));
 
-    const int m0 = blockIdx.x * TC_BM;
+    int m0 = blockIdx.x * TC_BM;
     // activation rows [xrow0, xrow0 + ncols) of this tile, weight plane `expert`
     int xrow0 = blockIdx.y * TC_BN, ncols = min(TC_BN, p.N - xrow0), expert = 0;
+    int tsplit = -1, ttile = 0;  // tail split: this CTA's split and tail tile
+    if (p.tail_full >= 0) {
+        const int w = (int)blockIdx.x;
+        int mt, nt;
+        if (w < p.tail_full) {
+            mt = w / p.tail_tiles_n;
+            nt = w % p.tail_tiles_n;
+        } else {
+            tsplit = (w - p.tail_full) % p.tail_S;
+            ttile = (w - p.tail_full) / p.tail_S;
+            mt = p.tail_m0 + ttile / p.tail_tiles_n;
+            nt = ttile % p.tail_tiles_n;
+        }
+        m0 = mt * TC_BM;
+        xrow0 = nt * TC_BN;
+        ncols = min(TC_BN, p.N - xrow0);
+    }
     if (p.grouped) {
         const int t = blockIdx.y;
         if (t >= p.g.tile_start[p.g.n_groups]) {  // unused tile (uniform, before any set-up)
@@ -419,8 +443,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     // K range in block pairs (split-K: a slice per blockIdx.z); chunks of 4 pairs
     const int total_pairs = p.K / (2 * QK);
-    const int pair0 = p.split_pairs ? (int)blockIdx.z * p.split_pairs : 0;
-    const int npairs = p.split_pairs ? min(p.split_pairs, total_pairs - pair0) : total_pairs;
+    const int pair0 = tsplit >= 0 ? tsplit * p.tail_split_pairs : (p.split_pairs ? (int)blockIdx.z * p.split_pairs : 0);
+    const int npairs = tsplit >= 0      ? min(p.tail_split_pairs, total_pairs - pair0)
+                       : p.split_pairs ? min(p.split_pairs, total_pairs - pair0)
+                                       : total_pairs;
     const int chunk0 = pair0 / CHUNK_PAIRS, nchunks = npairs / CHUNK_PAIRS;
 
     // Barriers. tcgen05.commit arrivals complete one after another (a few
@@ -713,7 +739,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const int c = 32 * qc + i;
                     if (c < ncols) {
                         const int r = xrow0 + c;
-                        if (p.partial) {
+                        if (tsplit >= 0) {
+                            p.tail_partial[(((uint64_t)tsplit * p.tail_n + ttile) * TC_BN + c) * TC_BM + row] = acc[i];
+                        } else if (p.partial) {
                             p.partial[((uint64_t)blockIdx.z * p.N + r) * p.M + m] = acc[i];
                         } else {
                             uint64_t off;
@@ -815,6 +843,22 @@ __global__ void tc_split_reduce_kernel(const float *__restrict__ partial, int sp
     }
 }
 
+// Tail tiles: y = sum over s in order of the S partial tiles (deterministic),
+// then the fused epilogue.
+__global__ void tc_tail_reduce_kernel(const float *__restrict__ partial, int S, int n_tail, int tiles_n, int m0_tile,
+                                      int M, int N, uint8_t *y, uint64_t y_nb1, const EpiAct epi) {
+    const int64_t per = (int64_t)n_tail * TC_BN * TC_BM;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
+        const int tt = (int)(i / (TC_BN * TC_BM)), rem = (int)(i % (TC_BN * TC_BM));
+        const int c = rem / TC_BM, rr = rem % TC_BM;
+        const int m = (m0_tile + tt / tiles_n) * TC_BM + rr, n = (tt % tiles_n) * TC_BN + c;
+        if (m >= M || n >= N) continue;
+        float acc = partial[i];
+        for (int sp = 1; sp < S; sp++) acc += partial[(int64_t)sp * per + i];
+        reinterpret_cast<float *>(y + (uint64_t)n * y_nb1)[m] = apply_act(acc, epi, m);
+    }
+}
+
 // ---- host side ---------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static std::once_flag once;
@@ -898,9 +942,30 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     if (tiles_n == 0 || M == 0) return FB_OK;
     if (tiles_n > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_tc: too many column tiles");
     dim3 grid((unsigned)((M + TC_BM - 1) / TC_BM), tiles_n, (unsigned)std::max(splits, 1));
+    p.tail_full = -1;
+    TailPlan tp{};
+    if (!groups && splits <= 1 && gemm_tc_tail(K, M, rows, &tp)) {
+        const int tiles_m = (int)((M + TC_BM - 1) / TC_BM);
+        p.tail_tiles_n = (int)tiles_n;
+        p.tail_m0 = tiles_m - tp.rows;
+        p.tail_full = p.tail_m0 * (int)tiles_n;
+        p.tail_S = tp.splits;
+        p.tail_n = tp.rows * (int)tiles_n;
+        p.tail_split_pairs = tp.split_pairs;
+        p.tail_partial = xa.partial;
+        grid = dim3((unsigned)(p.tail_full + p.tail_n * p.tail_S), 1, 1);
+    }
     kern<<<grid, TC_THREADS, L::BYTES, s>>>(tw, tx, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc launch: %s", cudaGetErrorString(e));
+    if (p.tail_full >= 0) {
+        const int64_t total = (int64_t)p.tail_n * TC_BN * TC_BM;
+        const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
+        tc_tail_reduce_kernel<<<blocks, 256, 0, s>>>(p.tail_partial, p.tail_S, p.tail_n, p.tail_tiles_n, p.tail_m0,
+                                                     (int)M, (int)rows, static_cast<uint8_t *>(y), y_nb1, epi);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc tail reduce launch: %s", cudaGetErrorString(e));
+    }
     if (p.partial) {
         const int64_t total = M * rows;
         const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
@@ -947,12 +1012,45 @@ int gemm_tc_splits(int64_t K, int64_t M, int64_t N) {
     return (int)((nchunks + per - 1) / per);
 }
 
+// Tail split of an ungrouped GEMM whose tiles overflow the last of several
+// waves (C3: 344 tiles on 148 SMs = 2.32 waves): the last m-tile rows that
+// hold the overflow (every n-tile of them, so every column of those rows is
+// treated alike) are split in K so their CTAs fill one wave, each doing
+// 1/splits of the work; the other tiles run whole. A partial wave of
+// full-length tiles becomes a short one.
+bool gemm_tc_tail(int64_t K, int64_t M, int64_t N, TailPlan *tp) {
+    const int64_t tiles_m = (M + TC_BM - 1) / TC_BM, tiles_n = (N + TC_BN - 1) / TC_BN;
+    const int64_t tiles = tiles_m * tiles_n, sms = sm_count(), nchunks = K / QKK;
+    if (tiles <= sms || tiles * 2 <= sms || nchunks < 4) return false;
+    const int64_t over = tiles % sms;
+    if (over == 0) return false;
+    const int64_t r = (over + tiles_n - 1) / tiles_n, n_tail = r * tiles_n;
+    if (r >= tiles_m) return false;
+    const int64_t S = std::min<int64_t>({sms / n_tail, nchunks / 2, 4});
+    if (S < 2) return false;
+    // waves of whole tiles before and after (split CTAs take 1/S of a wave)
+    const double before = (double)((tiles + sms - 1) / sms);
+    const double after = (double)((tiles - n_tail + sms - 1) / sms) + 1.0 / (double)S;
+    if (after > before - 0.15) return false;
+    const int64_t per_chunks = (nchunks + S - 1) / S;
+    if (tp) {
+        tp->rows = (int)r;
+        tp->splits = (int)((nchunks + per_chunks - 1) / per_chunks);
+        tp->split_pairs = (int)(per_chunks * CHUNK_PAIRS);
+    }
+    return (nchunks + per_chunks - 1) / per_chunks >= 2;
+}
+
 uint64_t xq16_bytes(int64_t K, int64_t rows, int64_t M, bool grouped) {
     const uint64_t nblk = (uint64_t)K / QK;
     uint64_t b = pad256((uint64_t)rows * (uint64_t)K * 2) + 2 * pad256(nblk * (uint64_t)rows * 4);
     if (!grouped) {
         const int sp = gemm_tc_splits(K, M, rows);
-        if (sp > 1) b += pad256((uint64_t)sp * (uint64_t)M * (uint64_t)rows * 4);
+        TailPlan tp{};
+        if (sp > 1)
+            b += pad256((uint64_t)sp * (uint64_t)M * (uint64_t)rows * 4);
+        else if (gemm_tc_tail(K, M, rows, &tp))
+            b += pad256((uint64_t)tp.splits * tp.rows * ((rows + TC_BN - 1) / TC_BN) * TC_BN * TC_BM * 4);
     }
     return b;
 }

@@ -159,6 +159,13 @@ uint64_t xq16_bytes(int64_t K, int64_t rows, int64_t M, bool grouped);
 XQ16 xq16_carve(void *base, int64_t K, int64_t rows);
 bool gemm_tc_supported(int32_t wtype, int64_t K, int64_t M, int64_t N, const void *w, uint64_t w_nb1);
 int gemm_tc_splits(int64_t K, int64_t M, int64_t N);
+// Tail split of a multi-wave ungrouped GEMM: the last `rows` m-tile rows
+// split `splits` ways in K (split_pairs block pairs each) and summed by a
+// reduction kernel; false when the grid gains nothing from it.
+struct TailPlan {
+    int rows, splits, split_pairs;
+};
+bool gemm_tc_tail(int64_t K, int64_t M, int64_t N, TailPlan *tp);
 // With `routed` (mul_mat_id), the N * n_selected operand rows are the routed
 // slots in expert order (row r from token routed->rows[r] / n_selected).
 int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, const XQ16 &out,

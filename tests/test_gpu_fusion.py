@@ -130,3 +130,21 @@ def test_standalone_add_broadcasts_and_silu(b200):
     want_s = O.add_f32(O.add_f32(a, b), c)
     assert np.array_equal(got_s, want_s)
     assert np.max(np.abs(got_y - O.silu_f32(want_s))) <= 1e-6
+
+
+def test_fused_chain_on_the_tail_split_gemm(b200):
+    """The C3 shape (Q4_0 11008 x 4096 x 512: 344 tiles, more than two waves)
+    runs its last tile rows split in K with a reduction kernel; the fused
+    bias + SiLU epilogue lives in that reduction for those rows."""
+    rng = np.random.default_rng(31)
+    K, M, N = 4096, 11008, 512
+    wq = O.quantize(O.DT_Q4_0, (rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    bias = (rng.standard_normal(M) * 0.5).astype(np.float32)
+    got, n_fused = _run(b200, DType.Q4_0, wq, x, bias, K, M, "bias+silu", keep_apart=False)
+    apart, _ = _run(b200, DType.Q4_0, wq, x, bias, K, M, "bias+silu", keep_apart=True)
+    assert n_fused == 2
+    assert np.array_equal(got.view(np.uint32), apart.view(np.uint32))
+    want = O.silu_f32(O.add_f32(O.mul_mat_quant_ref(O.DT_Q4_0, wq, x, K), bias[None, :]))
+    ok, err = tol_ok(got, want)
+    assert ok, err
