@@ -439,14 +439,27 @@ def mul_mat_kernels_per_step(cfg, N):
 def dominant_kernel(cfg, N):
     wt = cfg["wtype"]
     if "E" in cfg:
-        return "gemm_tc_kernel (grouped, tcgen05)"
+        return "gemm_tc3_kernel (grouped, tcgen05 split-f16)" if wt in ("Q8_0", "Q4_0") else \
+            "gemm_tc_kernel (grouped, tcgen05)"
     if wt == "F32":
         return "gemm_f32_pipe_kernel"
     if N <= 8:
         if wt == "Q4_K" and 12288 <= cfg["K"] <= 16384:
             return "gemv_ks_kernel" if N == 1 else "gemv_ks_cols_kernel"
         return "gemv_kernel"
-    return "gemm_tc_kernel (tcgen05)"
+    return "gemm_tc3_kernel (tcgen05 split-f16)" if wt in ("Q8_0", "Q4_0") else "gemm_tc_kernel (tcgen05)"
+
+
+def compute_dtype(cfg, N):
+    """The arithmetic the dominant kernel computes in."""
+    wt = cfg["wtype"]
+    if wt == "F32":
+        return "f32"
+    if N <= 8:
+        return "int8 dot / f32 scale"
+    if wt in ("Q8_0", "Q4_0"):
+        return "f16 hi+lo operands (exact), f32 accumulate"
+    return "f16 integer dot / f32 scale"
 
 
 def mul_mat_id_case(cfg, N, timer, steps, warmup):
@@ -825,7 +838,7 @@ def run_b200(args, cfg_name, cfg, N):
     result = {
         "metric": metric_name(cfg_name, cfg), "value": value, "unit": unit, "n_gpus": ws, "steps": steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
-        "vs_baseline": None, "dtype": "int8 dot / f32 scale" if cfg["wtype"] != "F32" else "f32",
+        "vs_baseline": None, "dtype": compute_dtype(cfg, N),
         "data": "synthetic (seeded numpy draws, quantized on device by the library's quantizer)",
         "config": config_dict(cfg_name, cfg, N, ws),
         "l2": f"{copies} rotating weight copies per rank" if copies > 1 else "weights larger than 2x L2 per rank",

@@ -80,7 +80,7 @@ uint64_t mul_mat_ws(int32_t wtype, int64_t K, int64_t M, int64_t N) {
     // planar activations + split-K partials for the mma.sync GEMM; the
     // tcgen05 path needs the hi/lo activations instead
     const uint64_t planar = fbk::q8_planar_bytes(K, N) + fbk::gemm_q_split_bytes(K, M, N);
-    return tc_shape(wtype, K, M, N) ? std::max<uint64_t>(planar, fbk::xq16_bytes(K, N, M, false)) : planar;
+    return tc_shape(wtype, K, M, N) ? std::max<uint64_t>(planar, fbk::xq16_bytes(wtype, K, N, M, false)) : planar;
 }
 
 // Kernel launches one do_mul_mat of this shape enqueues (16-byte aligned
@@ -90,7 +90,7 @@ int mul_mat_launches(int32_t wtype, int64_t K, int64_t M, int64_t N) {
     if (wtype == FB_F32) return 1;
     if (mul_mat_ws(wtype, K, M, N) == 0) return 1;  // fused decode GEMV
     if (tc_shape(wtype, K, M, N))
-        return fbk::gemm_tc_splits(K, M, N) > 1 || fbk::gemm_tc_tail(K, M, N, nullptr) ? 3 : 2;
+        return fbk::gemm_tc_splits(wtype, K, M, N) > 1 || fbk::gemm_tc_tail(wtype, K, M, N, nullptr) ? 3 : 2;
     if (fbk::gemv_supported(wtype, K, N)) return 2;
     const int64_t rb = fb::row_size(wtype, K);
     if (rb > 0 && fbk::gemm_q_supported(wtype, K, nullptr, (uint64_t)rb))
@@ -128,8 +128,8 @@ int do_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint
     if (norm_eps) return set_error(FB_ERR_UNSUPPORTED, "mul_mat: fused rms_norm needs the decode GEMV");
     if (tc_shape(wtype, K, M, N) && fbk::gemm_tc_supported(wtype, K, M, N, w, w_nb1) &&
         ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0) {
-        const fbk::XQ16 xa = fbk::xq16_carve(ws, K, N);
-        int rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, nullptr, s);
+        const fbk::XQ16 xa = fbk::xq16_carve(wtype, ws, K, N);
+        int rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, nullptr, s, wtype);
         if (rc) return rc;
         return fbk::launch_gemm_tc(wtype, w, w_nb1, xa, K, M, N, y, y_nb1, nullptr, status, s, nullptr, epi);
     }
@@ -182,7 +182,7 @@ IdWorkspace id_ws_layout(void *base, int32_t wtype, int64_t K, int64_t N, int64_
     L.tile_start = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
     L.rows = reinterpret_cast<int32_t *>(take(4 * n_sel * N));
     uint64_t xq_bytes = fbk::q8_planar_bytes(K, N);
-    if (id_tc_shape(wtype, K, N, n_sel)) xq_bytes = std::max<uint64_t>(xq_bytes, fbk::xq16_bytes(K, N * n_sel, 0, true));
+    if (id_tc_shape(wtype, K, N, n_sel)) xq_bytes = std::max<uint64_t>(xq_bytes, fbk::xq16_bytes(wtype, K, N * n_sel, 0, true));
     L.xq = wtype == FB_F32 ? nullptr : take(xq_bytes);
     L.total = off;
     return L;
@@ -213,7 +213,7 @@ int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, 
                         fbk::gemm_tc_supported(wtype, K, M, N * n_sel, w, w_nb1) && (w_nb2 & 15) == 0 &&
                         ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0;
     const int block_n = wtype == FB_F32 ? fbk::gemm_f32_block_n()
-                        : use_tc        ? fbk::gemm_tc_block_n()
+                        : use_tc        ? fbk::gemm_tc_block_n(wtype)
                                         : fbk::gemm_q_block_n();
     if (wtype != FB_F32 && !use_tc && !fbk::gemm_q_supported(wtype, K, w, w_nb1))
         return set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: quantized experts need K %% 256 == 0 and 16-byte aligned rows");
@@ -234,8 +234,8 @@ int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, 
     if (n_local == 0) return FB_OK;
     if (wtype == FB_F32) return fbk::launch_gemm_f32_grouped(w, w_nb1, x, x_nb1, K, M, dst, g, s);
     if (use_tc) {
-        const fbk::XQ16 xa = fbk::xq16_carve(L.xq, K, N * n_sel);
-        rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, &g, s);
+        const fbk::XQ16 xa = fbk::xq16_carve(wtype, L.xq, K, N * n_sel);
+        rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, &g, s, wtype);
         if (rc) return rc;
         return fbk::launch_gemm_tc(wtype, w, w_nb1, xa, K, M, N, dst, 0, &g, status, s);
     }
@@ -1322,7 +1322,7 @@ int feml_b200_mul_mat_id_peer_owned(int32_t wtype, const void *w_local, uint64_t
     }
     // invalid ids: every rank zeroes the slot in its own buffer of this step
     int rc = fbk::launch_moe_route(ids, ids_nb1, n_selected, N, n_experts, shard, n_shards, L.counts, L.offsets,
-                                   L.rows, L.tile_start, fbk::gemm_tc_block_n(), status, po.y[0][shard], dst_nb1,
+                                   L.rows, L.tile_start, fbk::gemm_tc_block_n(wtype), status, po.y[0][shard], dst_nb1,
                                    dst_nb2, M, s, po.y[1][shard], epoch, owner_tokens);
     if (rc) return rc;
     fbk::GroupMap g{};
@@ -1335,9 +1335,9 @@ int feml_b200_mul_mat_id_peer_owned(int32_t wtype, const void *w_local, uint64_t
     g.w_group_stride = w_nb2;
     g.dst_nb1 = dst_nb1;
     g.dst_nb2 = dst_nb2;
-    g.max_tiles = (int32_t)((n_selected * N + fbk::gemm_tc_block_n() - 1) / fbk::gemm_tc_block_n() + n_local);
-    const fbk::XQ16 xa = fbk::xq16_carve(L.xq, K, N * n_selected);
-    rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, &g, s);
+    g.max_tiles = (int32_t)((n_selected * N + fbk::gemm_tc_block_n(wtype) - 1) / fbk::gemm_tc_block_n(wtype) + n_local);
+    const fbk::XQ16 xa = fbk::xq16_carve(wtype, L.xq, K, N * n_selected);
+    rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, &g, s, wtype);
     if (rc) return rc;
     return fbk::launch_gemm_tc(wtype, w_local, w_nb1, xa, K, M, N, nullptr, 0, &g, status, s, &po);
 }

@@ -24,6 +24,7 @@ constexpr int WT_F32 = 5, WT_Q4_0 = 7, WT_Q8_0 = 11, WT_Q4_K = 15, WT_Q5_K = 16,
 constexpr int STATUS_TIMEOUT = 1 << 0;    // a bounded wait gave up
 constexpr int STATUS_BAD_ID = 1 << 1;     // mul_mat_id id outside [0, n_experts)
 constexpr int STATUS_BAD_ARGS = 1 << 2;   // launch arguments failed a device-side check
+constexpr int STATUS_RANGE = 1 << 3;      // a dequantized weight left the f16 range of the split-f16 GEMM
 
 // Bound on mbarrier polls before a wait is declared failed (each try_wait
 // suspends for a hardware-defined slice, so this is seconds, not forever).

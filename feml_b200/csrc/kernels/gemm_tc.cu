@@ -1,9 +1,16 @@
 // Quantized mul_mat on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
-// Arithmetic. The reference result is the F32 mul_mat of the dequantized
-// weights and the dequantized Q8_0 activations X[n,k] = dx[n,b] * qx[n,k]
-// (b = k / 32; feml-cpu/src/ops/mul_mat.rs:36-57 on dequantized operands).
-// Per 32-element block b the tensor core computes the integer dot product
+// The reference result is the F32 mul_mat of the dequantized weights and the
+// dequantized Q8_0 activations X[n,k] = dx[n,b] * qx[n,k] (b = k / 32;
+// feml-cpu/src/ops/mul_mat.rs:36-57 on dequantized operands). Two kernels:
+//
+// gemm_tc3_kernel (Q8_0, Q4_0; further below): the dequantized weights and
+// activations as exact hi + lo pairs of f16, three MMAs per K step, the f32
+// accumulator in TMEM over the whole K range, read once per tile.
+//
+// gemm_tc_kernel (Q4_K, whose dequantized values d*sc*q - dmin*m do not fit
+// two f16): per 32-element block b the tensor core computes the integer dot
+// product
 //     T_b[m,n] = sum_{k in b} qw[m,k] * qx[n,k]
 // with f16 operands holding exact integers (qx in [-127, 127]; qw in
 // [-128, 127] for Q8_0, [-8, 7] for Q4_0, [0, 15] for Q4_K) and an f32
@@ -107,6 +114,7 @@ struct TcParams {
     uint64_t y_nb1;
     const float *dxT;     // [K/32][N] activation block scales
     const float *xsdT;    // [K/32][N] dx * sum(qx) (Q4_K)
+    const float *xscale;  // [N] power of two per activation row (split-f16 kernel)
     int32_t *status;
     bool grouped;         // mul_mat_id: column tiles through the group map
     GroupMap g;
@@ -163,6 +171,31 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
         : "memory");
 }
+
+// D[tmem] (+)= A[tmem] * B[smem]^T: A read from tensor memory (lane = row,
+// two f16 of K per 32-bit column), f16 operands, f32 accumulator.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+
+// Store 32 consecutive 32-bit TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 32 consecutive 32-bit TMEM columns of this warp's 32 lanes.
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -326,6 +359,25 @@ __device__ __forceinline__ void load_pair_words(const uint8_t *row, int p, uint3
     }
 }
 
+// The same words through 16-byte loads (Q8_0 / Q4_0): rows of 272 / 144
+// bytes are odd multiples of 16, so the 16-byte loads of 8 consecutive rows
+// fall in 8 different bank groups (the 4-byte loads of 32 rows 272 bytes
+// apart hit only 8 banks). Pair p starts p words into its first 16 bytes.
+template <int WT>
+__device__ __forceinline__ void load_pair_words_v(const uint8_t *row, int p, uint32_t (&w)[PairWords<WT>::N]) {
+    static_assert(WT == WT_Q8_0 || WT == WT_Q4_0, "Q8_0 / Q4_0 rows");
+    constexpr int PB = WT == WT_Q8_0 ? 68 : 36, NV = WT == WT_Q8_0 ? 5 : 3;
+    const uint4 *src = reinterpret_cast<const uint4 *>(row + ((PB * p) & ~15));
+    uint32_t u[4 * NV];
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        const uint4 v = src[i];
+        u[4 * i] = v.x, u[4 * i + 1] = v.y, u[4 * i + 2] = v.z, u[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < PairWords<WT>::N; i++) w[i] = u[p + i];
+}
+
 // Convert one block pair (its words w; for Q4_K also the super-block header
 // hdr and the pair index p) into f16 integers. Returns the pair's row scales
 // (sc0, sc1) and, for Q4_K, the min scales (mn0, mn1).
@@ -400,6 +452,113 @@ __device__ __forceinline__ void convert_pair(const uint32_t *w, const uint32_t *
     }
 }
 
+// One CTA's work: output rows [m0, m0 + 128) x activation rows [xrow0,
+// xrow0 + ncols) (ncols <= bn, the kernel's tile width) of weight plane `expert`, over block pairs [pair0, pair0 +
+// npairs) (chunks [chunk0, chunk0 + nchunks) of 4 pairs). tsplit >= 0: a
+// tail-split CTA (split tsplit of tail tile ttile). unused: a grouped grid's
+// spare tile (no work).
+struct TileWork {
+    int m0, xrow0, ncols, expert, tsplit, ttile, pair0, npairs, chunk0, nchunks;
+    bool unused;
+};
+
+__device__ __forceinline__ TileWork decode_tile(const TcParams &p, int bn) {
+    TileWork t;
+    t.m0 = blockIdx.x * TC_BM;
+    t.xrow0 = blockIdx.y * bn;
+    t.ncols = min(bn, p.N - t.xrow0);
+    t.expert = 0;
+    t.tsplit = -1;
+    t.ttile = 0;
+    t.unused = false;
+    if (p.tail_full >= 0) {
+        const int w = (int)blockIdx.x;
+        int mt, nt;
+        if (w < p.tail_full) {
+            mt = w / p.tail_tiles_n;
+            nt = w % p.tail_tiles_n;
+        } else {
+            t.tsplit = (w - p.tail_full) % p.tail_S;
+            t.ttile = (w - p.tail_full) / p.tail_S;
+            mt = p.tail_m0 + t.ttile / p.tail_tiles_n;
+            nt = t.ttile % p.tail_tiles_n;
+        }
+        t.m0 = mt * TC_BM;
+        t.xrow0 = nt * bn;
+        t.ncols = min(bn, p.N - t.xrow0);
+    }
+    if (p.grouped) {
+        const int tt = blockIdx.y;
+        if (tt >= p.g.tile_start[p.g.n_groups]) {
+            t.unused = true;
+            t.npairs = t.nchunks = 0;
+            return t;
+        }
+        while (p.g.tile_start[t.expert + 1] <= tt) t.expert++;
+        const int jt = tt - p.g.tile_start[t.expert];
+        t.xrow0 = p.g.offsets[t.expert] + jt * bn;
+        t.ncols = min(bn, p.g.counts[t.expert] - jt * bn);
+    }
+    // K range in block pairs (split-K: a slice per blockIdx.z); chunks of 4 pairs
+    const int total_pairs = p.K / (2 * QK);
+    t.pair0 = t.tsplit >= 0 ? t.tsplit * p.tail_split_pairs : (p.split_pairs ? (int)blockIdx.z * p.split_pairs : 0);
+    t.npairs = t.tsplit >= 0    ? min(p.tail_split_pairs, total_pairs - t.pair0)
+               : p.split_pairs ? min(p.split_pairs, total_pairs - t.pair0)
+                               : total_pairs;
+    t.chunk0 = t.pair0 / CHUNK_PAIRS;
+    t.nchunks = t.npairs / CHUNK_PAIRS;
+    return t;
+}
+
+// Store one epilogue thread's 32 outputs: weight row `row` of the tile,
+// columns 32*qc .. 32*qc+31. Destinations: the tail or split-K partial
+// buffers, the grouped map (optionally into a peer's buffer), or y through
+// the fused epilogue.
+template <bool PEER, int BN>
+__device__ __forceinline__ void store_tile_row(const TcParams &p, const TileWork &t, int row, int qc,
+                                               const float (&acc)[32]) {
+    const int m = t.m0 + row;
+    if (m >= p.M) return;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        const int c = 32 * qc + i;
+        const float v = acc[i];
+        if (c < t.ncols) {
+            const int r = t.xrow0 + c;
+            if (t.tsplit >= 0) {
+                p.tail_partial[(((uint64_t)t.tsplit * p.tail_n + t.ttile) * BN + c) * TC_BM + row] = v;
+            } else if (p.partial) {
+                p.partial[((uint64_t)blockIdx.z * p.N + r) * p.M + m] = v;
+            } else {
+                uint64_t off;
+                int owner = -1;  // peer owner mode: the one rank that receives this slot
+                if (p.grouped) {
+                    const int slot = p.g.rows[r];
+                    int tok = slot / p.g.n_selected;
+                    if (PEER && p.peer.owner_tokens > 0) {
+                        owner = tok / p.peer.owner_tokens;
+                        tok -= owner * p.peer.owner_tokens;
+                    }
+                    off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 + (uint64_t)tok * p.g.dst_nb2;
+                } else {
+                    off = (uint64_t)r * p.y_nb1;
+                }
+                if constexpr (!PEER) {
+                    reinterpret_cast<float *>(p.y + off)[m] = apply_act(v, p.epi, m);
+                } else {  // NVLink stores into the owner's buffer, or every rank's
+                    const int b = (int)((*p.peer.epoch + 1u) & 1u);
+                    if (owner >= 0) {
+                        reinterpret_cast<float *>(p.peer.y[b][owner] + off)[m] = v;
+                    } else {
+                        for (int pr = 0; pr < p.peer.n; pr++)
+                            reinterpret_cast<float *>(p.peer.y[b][pr] + off)[m] = v;
+                    }
+                }
+            }
+        }
+    }
+}
+
 template <int WT, bool PEER>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
@@ -410,44 +569,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *gbase = smem_raw + (sbase - smem_u32(smem_raw));
 
-    int m0 = blockIdx.x * TC_BM;
-    // activation rows [xrow0, xrow0 + ncols) of this tile, weight plane `expert`
-    int xrow0 = blockIdx.y * TC_BN, ncols = min(TC_BN, p.N - xrow0), expert = 0;
-    int tsplit = -1, ttile = 0;  // tail split: this CTA's split and tail tile
-    if (p.tail_full >= 0) {
-        const int w = (int)blockIdx.x;
-        int mt, nt;
-        if (w < p.tail_full) {
-            mt = w / p.tail_tiles_n;
-            nt = w % p.tail_tiles_n;
-        } else {
-            tsplit = (w - p.tail_full) % p.tail_S;
-            ttile = (w - p.tail_full) / p.tail_S;
-            mt = p.tail_m0 + ttile / p.tail_tiles_n;
-            nt = ttile % p.tail_tiles_n;
-        }
-        m0 = mt * TC_BM;
-        xrow0 = nt * TC_BN;
-        ncols = min(TC_BN, p.N - xrow0);
+    const TileWork tw = decode_tile(p, TC_BN);
+    if (tw.unused) {  // unused tile (uniform, before any set-up)
+        if (PEER && threadIdx.x == 0) peer_cta_done(p.peer);
+        return;
     }
-    if (p.grouped) {
-        const int t = blockIdx.y;
-        if (t >= p.g.tile_start[p.g.n_groups]) {  // unused tile (uniform, before any set-up)
-            if (PEER && threadIdx.x == 0) peer_cta_done(p.peer);
-            return;
-        }
-        while (p.g.tile_start[expert + 1] <= t) expert++;
-        const int jt = t - p.g.tile_start[expert];
-        xrow0 = p.g.offsets[expert] + jt * TC_BN;
-        ncols = min(TC_BN, p.g.counts[expert] - jt * TC_BN);
-    }
-    // K range in block pairs (split-K: a slice per blockIdx.z); chunks of 4 pairs
-    const int total_pairs = p.K / (2 * QK);
-    const int pair0 = tsplit >= 0 ? tsplit * p.tail_split_pairs : (p.split_pairs ? (int)blockIdx.z * p.split_pairs : 0);
-    const int npairs = tsplit >= 0      ? min(p.tail_split_pairs, total_pairs - pair0)
-                       : p.split_pairs ? min(p.split_pairs, total_pairs - pair0)
-                                       : total_pairs;
-    const int chunk0 = pair0 / CHUNK_PAIRS, nchunks = npairs / CHUNK_PAIRS;
+    const int m0 = tw.m0, xrow0 = tw.xrow0, ncols = tw.ncols, expert = tw.expert;
+    const int pair0 = tw.pair0, npairs = tw.npairs, chunk0 = tw.chunk0, nchunks = tw.nchunks;
 
     // Barriers. tcgen05.commit arrivals complete one after another (a few
     // hundred cycles each), so the MMA thread commits once per block pair:
@@ -732,46 +860,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             float acc[32];
 #pragma unroll
             for (int i = 0; i < 16; i++) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
-            const int m = m0 + row;
-            if (m < p.M) {
-#pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const int c = 32 * qc + i;
-                    if (c < ncols) {
-                        const int r = xrow0 + c;
-                        if (tsplit >= 0) {
-                            p.tail_partial[(((uint64_t)tsplit * p.tail_n + ttile) * TC_BN + c) * TC_BM + row] = acc[i];
-                        } else if (p.partial) {
-                            p.partial[((uint64_t)blockIdx.z * p.N + r) * p.M + m] = acc[i];
-                        } else {
-                            uint64_t off;
-                            int owner = -1;  // peer owner mode: the one rank that receives this slot
-                            if (p.grouped) {
-                                const int slot = p.g.rows[r];
-                                int t = slot / p.g.n_selected;
-                                if (PEER && p.peer.owner_tokens > 0) {
-                                    owner = t / p.peer.owner_tokens;
-                                    t -= owner * p.peer.owner_tokens;
-                                }
-                                off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 + (uint64_t)t * p.g.dst_nb2;
-                            } else {
-                                off = (uint64_t)r * p.y_nb1;
-                            }
-                            if constexpr (!PEER) {
-                                reinterpret_cast<float *>(p.y + off)[m] = apply_act(acc[i], p.epi, m);
-                            } else {  // NVLink stores into the owner's buffer, or every rank's
-                                const int b = (int)((*p.peer.epoch + 1u) & 1u);
-                                if (owner >= 0) {
-                                    reinterpret_cast<float *>(p.peer.y[b][owner] + off)[m] = acc[i];
-                                } else {
-                                    for (int pr = 0; pr < p.peer.n; pr++)
-                                        reinterpret_cast<float *>(p.peer.y[b][pr] + off)[m] = acc[i];
-                                }
-                            }
-                        }
-                    }
-                }
-            }
+            store_tile_row<PEER, TC_BN>(p, tw, row, qc, acc);
         }
     }
 
@@ -787,16 +876,329 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
-// ---- activations: Q8_0 quantize into exact f16 integers + block scales -------
+// ---- split-f16 dequantizing GEMM (Q8_0, Q4_0) ---------------------------------
+// Every dequantized operand value is an f16 block scale times a small
+// integer: weights d*q (q in [-128, 127] for Q8_0, [-8, 7] for Q4_0), the
+// Q8_0-rounded activations dx*qx (qx in [-127, 127]). Such a product has at
+// most 11 + 8 significant bits, so it is exactly hi + lo with hi = rn16(d*q)
+// and lo = d*q - hi (both f16; the f16 fma computes the remainder exactly).
+// The tensor core then accumulates
+//     D += Ahi*Bhi + Ahi*Blo + Alo*Bhi       (Alo*Blo < 2^-22 of each product)
+// in f32 over the tile's whole K range: three MMAs per K step and no
+// per-block epilogue; the accumulator is read once, at the end of the tile.
+// Range: activation row t is scaled by a power of two 2^-e_t (exact) that
+// puts its largest value below 2^15, and the epilogue multiplies by 2^e_t.
+// Weights are used unscaled; a block scale whose products leave the f16
+// range (Q8_0 |d| > 511.75, Q4_0 |d| > 8188) raises STATUS_RANGE.
+//
+// Operands: the weight tile (A) lives in tensor memory, written there by
+// the converters (tcgen05.st, one TMEM lane per weight row), so the MMAs read
+// only the activations from shared memory: three 128 x 128 x 16 MMAs with
+// both operands in shared memory would need 96 KB of operand reads per block
+// pair, as much shared-memory bandwidth as they have time for.
+// Tiles are 128 weight rows x 192 activation rows: each converted weight
+// tile feeds up to 192 columns, the MMAs (N up to 192) stay ahead of their
+// issue, three activation stages fit beside the raw weight ring, and a
+// mul_mat_id expert group of up to 192 routed rows is one tile.
+// TMEM columns: [0, 192) the f32 accumulator; then T3Cfg::NA slots of 64
+// columns, one block pair each (hi plane: 32 columns of two f16, lo plane:
+// the next 32).
+// Roles (512 threads):
+//   warp 0      TMA: raw weight chunks (8 blocks x 128 rows), as gemm_tc_kernel.
+//   warp 1      TMA: activation stages (192 rows x 64 f16, the hi and lo
+//               planes) into a ring of T3Cfg::NBP block pairs.
+//   warp 2      TMEM (512 columns) and the MMAs (one thread, one commit per
+//               block pair, which frees its A slot and its B stage).
+//   warp 3      gate: waits for a pair's A slot and B stage and raises the
+//               pair's `ready` barrier, so the MMA thread waits once per
+//               pair (barrier waits are slow while the tensor core streams
+//               operands from shared memory).
+//   warps 4-7   converters: one weight row (= TMEM lane) each; hi and lo of
+//               a pair into an A slot.
+//   warps 8-15  epilogue: lane quarter warp % 4, 96 columns each.
+constexpr int T3_THREADS = 512;
+constexpr int T3_BN = 192;
+constexpr int T3_TMEM_COLS = 512;
+constexpr int T3_HALF = T3_BN * 128;  // one plane of a block pair: 192 rows x 64 f16
+
+template <int WT>
+struct T3Cfg;
+template <>
+struct T3Cfg<WT_Q8_0> {
+    static constexpr int NR = 2, NA = 4, NBP = 3;
+    static constexpr float kMaxScale = 65504.0f / 128.0f;
+};
+template <>
+struct T3Cfg<WT_Q4_0> {
+    static constexpr int NR = 4, NA = 4, NBP = 3;
+    static constexpr float kMaxScale = 65504.0f / 8.0f;
+};
+
+template <int WT>
+struct T3Layout {
+    using C = T3Cfg<WT>;
+    static_assert(T3_BN + 64 * C::NA <= T3_TMEM_COLS, "TMEM: accumulator + A slots");
+    static constexpr int RAW_STAGE = TC_BM * TcCfg<WT>::RAWB;
+    static constexpr int B_STAGE3 = 2 * T3_HALF;  // [hi plane][lo plane]
+    static constexpr int OFF_B = 0;
+    static constexpr int OFF_RAW = OFF_B + C::NBP * B_STAGE3;
+    static constexpr int OFF_BAR = OFF_RAW + ((C::NR * RAW_STAGE + 1023) / 1024) * 1024;
+    static constexpr int N_BARS = 2 * C::NR + C::NA + 2 * C::NBP + TC_ND + 1;
+    static constexpr int OFF_MISC = OFF_BAR + N_BARS * 8;
+    static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+};
+
+// One block's 16 words of exact f16 integers (element order) times the
+// block scale d, split into the hi and lo planes (16 words each).
+__device__ __forceinline__ void split_block(const uint32_t (&v)[16], __half2 d2, uint32_t *hi, uint32_t *lo) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        const __half2 h = __hmul2(bits_h2(v[i]), d2);
+        hi[i] = h2_bits(h);
+        lo[i] = h2_bits(__hfma2(bits_h2(v[i]), d2, __hneg2(h)));
+    }
+}
+
+template <int WT, bool PEER>
+__global__ void __launch_bounds__(T3_THREADS, 1)
+    gemm_tc3_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                    const TcParams p) {
+    using C = T3Cfg<WT>;
+    using L = T3Layout<WT>;
+    using RC = TcCfg<WT>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *gbase = smem_raw + (sbase - smem_u32(smem_raw));
+
+    const TileWork tw = decode_tile(p, T3_BN);
+    if (tw.unused) {  // unused tile (uniform, before any set-up)
+        if (PEER && threadIdx.x == 0) peer_cta_done(p.peer);
+        return;
+    }
+    const int m0 = tw.m0, xrow0 = tw.xrow0, ncols = tw.ncols, expert = tw.expert;
+    const int pair0 = tw.pair0, npairs = tw.npairs, chunk0 = tw.chunk0, nchunks = tw.nchunks;
+
+    uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + L::OFF_BAR);
+    uint64_t *raw_full = bars;
+    uint64_t *raw_empty = raw_full + C::NR;
+    uint64_t *a_full = raw_empty + C::NR;
+    uint64_t *b_full = a_full + C::NA;
+    uint64_t *ready = b_full + C::NBP;
+    uint64_t *pair_done = ready + C::NBP;
+    uint64_t *mma_done = pair_done + TC_ND;
+    auto done_parity = [](int q) { return (uint32_t)((q / TC_ND) & 1); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + L::OFF_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + L::OFF_MISC + 4);
+    int *range_flag = reinterpret_cast<int *>(gbase + L::OFF_MISC + 8);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        for (int i = 0; i < C::NR; i++) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], 128);
+        }
+        for (int i = 0; i < C::NA; i++) mbar_init(&a_full[i], 128);
+        for (int i = 0; i < C::NBP; i++) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&ready[i], 1);
+        }
+        for (int i = 0; i < TC_ND; i++) mbar_init(&pair_done[i], 1);
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        *range_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 2) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(T3_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- raw weight chunks ------------------------------------------------
+        if (lane == 0) {
+            int armed[C::NR];
+            for (int i = 0; i < C::NR; i++) armed[i] = -1;
+            for (int c = 0; c < nchunks; c++) {
+                const int s = c % C::NR;
+                if (!tc_wait(&raw_empty[s], ((c / C::NR) & 1) ^ 1, abort_flag, 64)) break;
+                mbar_arrive_expect_tx(&raw_full[s], L::RAW_STAGE);
+                const int gc = chunk0 + c;
+                const int x0 = WT == WT_Q8_0 ? gc * (RC::RAWB / 2) : gc * RC::RAWB;
+                tma_load_3d(sbase + L::OFF_RAW + s * L::RAW_STAGE, &tm_w, x0, m0, expert, smem_u32(&raw_full[s]));
+                armed[s] = (c / C::NR) & 1;
+            }
+            if (*abort_flag)  // let the copies in flight land before the CTA exits
+                for (int i = 0; i < C::NR; i++)
+                    if (armed[i] >= 0) mbar_wait_bounded(&raw_full[i], (uint32_t)armed[i]);
+        }
+    } else if (warp == 1) {
+        // ---- activation stages: both planes of a pair on one barrier ------------------
+        if (lane == 0) {
+            int armed[C::NBP];
+            for (int i = 0; i < C::NBP; i++) armed[i] = -1;
+            for (int q = 0; q < npairs; q++) {
+                const int s = q % C::NBP;
+                if (q >= C::NBP && !tc_wait(&pair_done[(q - C::NBP) % TC_ND], done_parity(q - C::NBP), abort_flag, 16))
+                    break;
+                mbar_arrive_expect_tx(&b_full[s], L::B_STAGE3);
+                const uint32_t dst = sbase + L::OFF_B + s * L::B_STAGE3;
+                tma_load_3d(dst, &tm_x, (pair0 + q) * 64, xrow0, 0, smem_u32(&b_full[s]));
+                tma_load_3d(dst + T3_HALF, &tm_x, (pair0 + q) * 64, xrow0, 1, smem_u32(&b_full[s]));
+                armed[s] = (q / C::NBP) & 1;
+            }
+            if (*abort_flag)
+                for (int i = 0; i < C::NBP; i++)
+                    if (armed[i] >= 0) mbar_wait_bounded(&b_full[i], (uint32_t)armed[i]);
+        }
+    } else if (warp == 3) {
+        // ---- gate: A slot + B stage of pair q -> ready[q] -------------------------
+        // (ready[q % NBP] cannot be raised for pair q + NBP before the MMAs
+        // of pair q have completed: its B stage is loaded only after that)
+        if (lane == 0) {
+            for (int q = 0; q < npairs; q++) {
+                if (!tc_wait(&a_full[q % C::NA], (q / C::NA) & 1, abort_flag) ||
+                    !tc_wait(&b_full[q % C::NBP], (q / C::NBP) & 1, abort_flag))
+                    break;
+                mbar_arrive(&ready[q % C::NBP]);
+            }
+        }
+    } else if (warp == 2) {
+        // ---- MMA issue: the whole warp waits, one thread issues ------------------
+        {
+            // a narrow tile multiplies only its columns, rounded up to the
+            // MMA's N granularity of 16 (M = 128: N = 16..256, N % 16 == 0)
+            const int nmma = min(T3_BN, (ncols + 15) & ~15);
+            const uint32_t idesc = f16_idesc(TC_BM, nmma);
+            for (int q = 0; q < npairs; q++) {
+                const int sa = q % C::NA, sb = q % C::NBP;
+                // every lane polls (the verdict is the same for all: a lane
+                // gives up only when the bound runs out or another role aborted)
+                const bool okw = tc_wait(&ready[sb], (q / C::NBP) & 1, abort_flag);
+                if (!__all_sync(0xffffffffu, okw)) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a_hi = tmem + (uint32_t)(T3_BN + 64 * sa), a_lo = a_hi + 32u;
+                    const uint32_t b_hi = sbase + L::OFF_B + sb * L::B_STAGE3, b_lo = b_hi + T3_HALF;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        // K step of 16: 8 TMEM columns of A; 32 bytes in the swizzled B rows
+                        const uint32_t ka = 8u * k, kb = 64u * (k >> 1) + 32u * (k & 1);
+                        tc_mma_f16_ts(tmem, a_hi + ka, sw128_desc(b_hi + kb), idesc, (q | k) ? 1u : 0u);
+                        tc_mma_f16_ts(tmem, a_hi + ka, sw128_desc(b_lo + kb), idesc, 1u);
+                        tc_mma_f16_ts(tmem, a_lo + ka, sw128_desc(b_hi + kb), idesc, 1u);
+                    }
+                    tc_commit(smem_u32(&pair_done[q % TC_ND]));
+                }
+                __syncwarp();
+            }
+            // the accumulator is complete when every issued MMA has finished
+            if (lane == 0) tc_commit(smem_u32(mma_done));
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---- converters: one weight row per thread, one block pair at a time ----
+        const int row = tid - 128;
+        bool range_ok = true;
+        for (int c = 0; c < nchunks; c++) {
+            const int s = c % C::NR;
+            if (!tc_wait_warp(&raw_full[s], (c / C::NR) & 1, abort_flag, lane)) break;
+            const uint8_t *rrow = gbase + L::OFF_RAW + s * L::RAW_STAGE + row * RC::RAWB;
+            bool ok = true;
+#pragma unroll
+            for (int pp = 0; pp < CHUNK_PAIRS; pp++) {
+                const int q = CHUNK_PAIRS * c + pp;
+                const int sa = q % C::NA;
+                uint32_t w[PairWords<WT>::N];
+                load_pair_words_v<WT>(rrow, pp, w);
+                if (pp == CHUNK_PAIRS - 1) mbar_arrive(&raw_empty[s]);  // the chunk is in registers
+                uint32_t v0[16], v1[16];
+                float sc0, sc1, mn0, mn1;
+                convert_pair<WT>(w, nullptr, pp, v0, v1, sc0, sc1, mn0, mn1);
+                range_ok = range_ok && fabsf(sc0) <= C::kMaxScale && fabsf(sc1) <= C::kMaxScale;
+                uint32_t h[32], l[32];  // the pair's 64 elements, hi and lo
+                split_block(v0, __float2half2_rn(sc0), h, l);
+                split_block(v1, __float2half2_rn(sc1), h + 16, l + 16);
+                // the slot was last read by the MMAs of pair q - NA
+                if (q >= C::NA &&
+                    !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(T3_BN + 64 * sa);
+                tc_st32(ta, h);
+                tc_st32(ta + 32u, l);
+                tc_wait_st();
+                tc_fence_before();
+                mbar_arrive(&a_full[sa]);
+            }
+            if (!ok) break;
+        }
+        if (!range_ok) *range_flag = 1;
+    } else if (warp >= 8) {
+        // ---- epilogue: lane quarter warp % 4, columns 96*half .. +95 --------------
+        const int sub = warp & 3, half = (warp - 8) >> 2;
+        const int row = 32 * sub + lane;
+        if (96 * half < ncols && tc_wait_warp(mma_done, 0, abort_flag, lane, 256) && !*abort_flag) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int cc = 0; cc < 3; cc++) {
+                const int qc = 3 * half + cc;
+                if (32 * qc >= ncols) break;
+                uint32_t r[32];
+                tc_ld32(tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(32 * qc), r);
+                tc_wait_ld();
+                // activation row scales 2^e_t of these 32 columns
+                const int c = 32 * qc + lane;
+                const float sc = c < ncols ? p.xscale[xrow0 + c] : 1.0f;
+                float acc[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    acc[i] = npairs > 0 ? __uint_as_float(r[i]) * __shfl_sync(0xffffffffu, sc, i) : 0.0f;
+                store_tile_row<PEER, T3_BN>(p, tw, row, qc, acc);
+            }
+        }
+    }
+
+    if (PEER) __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        if (*abort_flag) report_status(p.status, STATUS_TIMEOUT);
+        if (*range_flag) report_status(p.status, STATUS_RANGE);
+    }
+    if (PEER && tid == 0) peer_cta_done(p.peer);
+    if (warp == 2) {
+        // every issued MMA has completed before the columns are released
+        if (lane == 0) mbar_wait_bounded(mma_done, 0);
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T3_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---- activations: Q8_0 quantize into f16 operands -----------------------------
 // One CTA per activation row r (with `routed`, the activation of routed slot
-// r: token g.rows[r] / n_selected, for r < sum(counts)). Writes q16[r][k]
-// (f16 integer), dxT[b][r] = dx (the f16 block scale as f32) and
-// xsdT[b][r] = dx * sum(qx) (both [K/32][rows]).
+// r: token g.rows[r] / n_selected, for r < sum(counts)).
+// hilo == false (the per-block kernel): q16[r][k] = qx as an f16 integer,
+// dxT[b][r] = dx (the f16 block scale as f32), xsdT[b][r] = dx * sum(qx).
+// hilo == true (the split-f16 kernel): the row's scale exponent e is chosen
+// from its largest block scale D (D * 128 < 2^(e + 15)), then
+// v = dx*qx * 2^-e (exact) is written as hi = rn16(v) to plane 0
+// (q16[r][k]) and lo = v - hi to plane 1 (q16[rows + r][k]); xscale[r] = 2^e.
 constexpr int QF_THREADS = 256;
 
 __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8_t *__restrict__ x, uint64_t x_nb1,
                                                                     int K, int rows, __half *__restrict__ q16,
                                                                     float *__restrict__ dxT, float *__restrict__ xsdT,
+                                                                    float *__restrict__ xscale, bool hilo,
                                                                     bool routed, GroupMap g) {
     const int r = blockIdx.x, tid = threadIdx.x;
     int src = r;
@@ -807,6 +1209,35 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
     const float *xr = reinterpret_cast<const float *>(x + (uint64_t)src * x_nb1);
     const int nblk = K / QK;
     __half *orow = q16 + (uint64_t)r * K;
+    __half *orow_lo = q16 + ((uint64_t)rows + r) * K;
+    float down = 1.0f;  // 2^-e
+    if (hilo) {
+        __shared__ float wmax[QF_THREADS / 32];
+        float amax = 0.0f;
+        for (int k = 4 * tid; k < K; k += 4 * QF_THREADS) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + k);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if ((tid & 31) == 0) wmax[tid >> 5] = amax;
+        __syncthreads();
+        amax = wmax[0];
+#pragma unroll
+        for (int w = 1; w < QF_THREADS / 32; w++) amax = fmaxf(amax, wmax[w]);
+        // the largest block scale: the quantizer's d of the row maximum
+        // (division and f16 rounding are monotonic)
+        const float dmax = __half2float(__float2half_rn(__fdiv_rn(amax, 127.0f)));
+        const float bound = dmax * 128.0f;
+        int e = 0;
+        if (bound > 0.0f && isfinite(bound)) {
+            int ex;
+            frexpf(bound, &ex);  // bound < 2^ex
+            e = ex - 15;
+        }
+        down = ldexpf(1.0f, -e);
+        if (tid == 0) xscale[r] = ldexpf(1.0f, e);
+    }
     // 8 lanes per block, 4 elements per lane; every lane of the warp calls the
     // quantize routine (uniform trip count)
     for (int base = 0; base < nblk; base += QF_THREADS / 8) {
@@ -818,15 +1249,26 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
         int qsum;
         const uint32_t q = quantize_q8_0_quad(v, dbits, qsum);
         if (!valid) continue;
+        const float d = f16_bits_to_f32(dbits);
         __half hq[4];
+        if (hilo) {
+            __half lq[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) hq[i] = __int2half_rn((int)(int8_t)((q >> (8 * i)) & 0xFFu));
-        *reinterpret_cast<uint2 *>(orow + k) = *reinterpret_cast<const uint2 *>(hq);
-        if ((tid & 7) == 0) {
-            const float d = f16_bits_to_f32(dbits);
-            dxT[(uint64_t)b * rows + r] = d;
-            xsdT[(uint64_t)b * rows + r] = d * (float)qsum;
+            for (int i = 0; i < 4; i++) {
+                const float val = (d * (float)(int8_t)((q >> (8 * i)) & 0xFFu)) * down;  // exact
+                hq[i] = __float2half_rn(val);
+                lq[i] = __float2half_rn(val - __half2float(hq[i]));
+            }
+            *reinterpret_cast<uint2 *>(orow_lo + k) = *reinterpret_cast<const uint2 *>(lq);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) hq[i] = __int2half_rn((int)(int8_t)((q >> (8 * i)) & 0xFFu));
+            if ((tid & 7) == 0) {
+                dxT[(uint64_t)b * rows + r] = d;
+                xsdT[(uint64_t)b * rows + r] = d * (float)qsum;
+            }
         }
+        *reinterpret_cast<uint2 *>(orow + k) = *reinterpret_cast<const uint2 *>(hq);
     }
 }
 
@@ -846,12 +1288,12 @@ __global__ void tc_split_reduce_kernel(const float *__restrict__ partial, int sp
 // Tail tiles: y = sum over s in order of the S partial tiles (deterministic),
 // then the fused epilogue.
 __global__ void tc_tail_reduce_kernel(const float *__restrict__ partial, int S, int n_tail, int tiles_n, int m0_tile,
-                                      int M, int N, uint8_t *y, uint64_t y_nb1, const EpiAct epi) {
-    const int64_t per = (int64_t)n_tail * TC_BN * TC_BM;
+                                      int M, int N, int bn, uint8_t *y, uint64_t y_nb1, const EpiAct epi) {
+    const int64_t per = (int64_t)n_tail * bn * TC_BM;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
-        const int tt = (int)(i / (TC_BN * TC_BM)), rem = (int)(i % (TC_BN * TC_BM));
+        const int tt = (int)(i / (bn * TC_BM)), rem = (int)(i % (bn * TC_BM));
         const int c = rem / TC_BM, rr = rem % TC_BM;
-        const int m = (m0_tile + tt / tiles_n) * TC_BM + rr, n = (tt % tiles_n) * TC_BN + c;
+        const int m = (m0_tile + tt / tiles_n) * TC_BM + rr, n = (tt % tiles_n) * bn + c;
         if (m >= M || n >= N) continue;
         float acc = partial[i];
         for (int sp = 1; sp < S; sp++) acc += partial[(int64_t)sp * per + i];
@@ -890,6 +1332,14 @@ int encode_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint6
     return FB_OK;
 }
 
+template <int WT>
+constexpr int smem_bytes_of() {
+    if constexpr (WT == WT_Q4_K)
+        return TcLayout<WT>::BYTES;
+    else
+        return T3Layout<WT>::BYTES;
+}
+
 // rows: activation rows in the operand buffer; n_planes / w_nb2: weight
 // planes (experts) of the grouped mode (1 / unused otherwise).
 template <int WT>
@@ -899,6 +1349,12 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     using C = TcCfg<WT>;
     using L = TcLayout<WT>;
     static_assert(L::BYTES <= 232448, "gemm_tc shared memory");
+    // Q8_0 / Q4_0: the split-f16 kernel over the hi / lo activation planes;
+    // Q4_K: the per-block kernel over exact f16 integers
+    constexpr bool kSplit = WT != WT_Q4_K;
+    constexpr int BN = kSplit ? T3_BN : TC_BN;
+    constexpr int kBytes = smem_bytes_of<WT>();
+    static_assert(kBytes <= 232448, "gemm_tc3 shared memory");
     CUtensorMap tw, tx;
     const uint64_t planes = (uint64_t)n_planes, pstride = n_planes > 1 ? w_nb2 : w_nb1 * (uint64_t)M;
     int rc;
@@ -909,14 +1365,21 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
         rc = encode_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, w_nb1, (uint64_t)M, planes, w_nb1, pstride, C::RAWB,
                         TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    rc = encode_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xa.q16, (uint64_t)K, (uint64_t)rows, 0, (uint64_t)K * 2, 0,
-                    64, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    // activations: [rows][K] f16 (Q4_K), or planes [2][rows][K] (hi, lo)
+    rc = encode_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xa.q16, (uint64_t)K, (uint64_t)rows, kSplit ? 2 : 0,
+                    (uint64_t)K * 2, kSplit ? (uint64_t)rows * (uint64_t)K * 2 : 0, 64, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     // the peer-store variant is a separate instantiation, so the plain kernel
     // carries none of its registers
-    const auto kern = peer ? gemm_tc_kernel<WT, true> : gemm_tc_kernel<WT, false>;
+    using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const TcParams);
+    KernFn kern;
+    if constexpr (kSplit)
+        kern = peer ? gemm_tc3_kernel<WT, true> : gemm_tc3_kernel<WT, false>;
+    else
+        kern = peer ? gemm_tc_kernel<WT, true> : gemm_tc_kernel<WT, false>;
     static DeviceFlags configured[2];
-    rc = raise_smem_limit((const void *)kern, L::BYTES, configured[peer ? 1 : 0], "gemm_tc");
+    rc = raise_smem_limit((const void *)kern, kBytes, configured[peer ? 1 : 0], "gemm_tc");
     if (rc) return rc;
     TcParams p{};
     p.M = (int)M;
@@ -926,6 +1389,7 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     p.y_nb1 = y_nb1;
     p.dxT = xa.dxT;
     p.xsdT = xa.xsdT;
+    p.xscale = xa.xscale;
     p.status = status;
     p.grouped = groups != nullptr;
     if (groups) p.g = *groups;
@@ -938,13 +1402,13 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
         splits = (total_pairs + p.split_pairs - 1) / p.split_pairs;
         p.partial = xa.partial;
     }
-    const unsigned tiles_n = groups ? (unsigned)groups->max_tiles : (unsigned)((rows + TC_BN - 1) / TC_BN);
+    const unsigned tiles_n = groups ? (unsigned)groups->max_tiles : (unsigned)((rows + BN - 1) / BN);
     if (tiles_n == 0 || M == 0) return FB_OK;
     if (tiles_n > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_tc: too many column tiles");
     dim3 grid((unsigned)((M + TC_BM - 1) / TC_BM), tiles_n, (unsigned)std::max(splits, 1));
     p.tail_full = -1;
     TailPlan tp{};
-    if (!groups && splits <= 1 && gemm_tc_tail(K, M, rows, &tp)) {
+    if (!groups && splits <= 1 && gemm_tc_tail(WT, K, M, rows, &tp)) {
         const int tiles_m = (int)((M + TC_BM - 1) / TC_BM);
         p.tail_tiles_n = (int)tiles_n;
         p.tail_m0 = tiles_m - tp.rows;
@@ -955,14 +1419,14 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
         p.tail_partial = xa.partial;
         grid = dim3((unsigned)(p.tail_full + p.tail_n * p.tail_S), 1, 1);
     }
-    kern<<<grid, TC_THREADS, L::BYTES, s>>>(tw, tx, p);
+    kern<<<grid, kSplit ? T3_THREADS : TC_THREADS, kBytes, s>>>(tw, tx, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc launch: %s", cudaGetErrorString(e));
     if (p.tail_full >= 0) {
-        const int64_t total = (int64_t)p.tail_n * TC_BN * TC_BM;
+        const int64_t total = (int64_t)p.tail_n * BN * TC_BM;
         const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
         tc_tail_reduce_kernel<<<blocks, 256, 0, s>>>(p.tail_partial, p.tail_S, p.tail_n, p.tail_tiles_n, p.tail_m0,
-                                                     (int)M, (int)rows, static_cast<uint8_t *>(y), y_nb1, epi);
+                                                     (int)M, (int)rows, BN, static_cast<uint8_t *>(y), y_nb1, epi);
         e = cudaGetLastError();
         if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc tail reduce launch: %s", cudaGetErrorString(e));
     }
@@ -995,15 +1459,16 @@ bool gemm_tc_supported(int32_t wtype, int64_t K, int64_t M, int64_t N, const voi
     if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K) return false;
     if (K <= 0 || K % QKK || K > (1 << 24) || M <= 0 || N <= 0 || M > INT32_MAX || N > INT32_MAX / 64) return false;
     if (((reinterpret_cast<uintptr_t>(w) | w_nb1) & 15) != 0) return false;
-    return (N + TC_BN - 1) / TC_BN <= 65535;
+    return (N + gemm_tc_block_n(wtype) - 1) / gemm_tc_block_n(wtype) <= 65535;
 }
 
-int gemm_tc_block_n() { return TC_BN; }
+int gemm_tc_block_n(int32_t wtype) { return wtype == WT_Q4_K ? TC_BN : T3_BN; }
 
 // Split-K when the tile grid leaves most SMs idle (ungrouped only): one CTA
 // per SM in a single wave, every split at least two weight chunks.
-int gemm_tc_splits(int64_t K, int64_t M, int64_t N) {
-    const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+int gemm_tc_splits(int32_t wtype, int64_t K, int64_t M, int64_t N) {
+    const int64_t bn = gemm_tc_block_n(wtype);
+    const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn);
     const int64_t nchunks = K / QKK, sms = sm_count();
     if (tiles * 2 > sms || nchunks < 4) return 1;
     const int64_t splits = std::min<int64_t>({sms / tiles, nchunks / 2, 16});
@@ -1013,20 +1478,21 @@ int gemm_tc_splits(int64_t K, int64_t M, int64_t N) {
 }
 
 // Tail split of an ungrouped GEMM whose tiles overflow the last of several
-// waves (C3: 344 tiles on 148 SMs = 2.32 waves): the last m-tile rows that
-// hold the overflow (every n-tile of them, so every column of those rows is
+// waves by a little (a few rows of tiles past a whole number of waves): the
+// last m-tile rows that hold the overflow (every n-tile of them, so every column of those rows is
 // treated alike) are split in K so their CTAs fill one wave, each doing
 // 1/splits of the work; the other tiles run whole. A partial wave of
 // full-length tiles becomes a short one.
-bool gemm_tc_tail(int64_t K, int64_t M, int64_t N, TailPlan *tp) {
-    const int64_t tiles_m = (M + TC_BM - 1) / TC_BM, tiles_n = (N + TC_BN - 1) / TC_BN;
+bool gemm_tc_tail(int32_t wtype, int64_t K, int64_t M, int64_t N, TailPlan *tp) {
+    const int64_t bn = gemm_tc_block_n(wtype);
+    const int64_t tiles_m = (M + TC_BM - 1) / TC_BM, tiles_n = (N + bn - 1) / bn;
     const int64_t tiles = tiles_m * tiles_n, sms = sm_count(), nchunks = K / QKK;
     if (tiles <= sms || tiles * 2 <= sms || nchunks < 4) return false;
     const int64_t over = tiles % sms;
     if (over == 0) return false;
     const int64_t r = (over + tiles_n - 1) / tiles_n, n_tail = r * tiles_n;
     if (r >= tiles_m) return false;
-    const int64_t S = std::min<int64_t>({sms / n_tail, nchunks / 2, 4});
+    const int64_t S = std::min<int64_t>({sms / n_tail, nchunks / 2, 8});
     if (S < 2) return false;
     // waves of whole tiles before and after (split CTAs take 1/S of a wave)
     const double before = (double)((tiles + sms - 1) / sms);
@@ -1041,36 +1507,47 @@ bool gemm_tc_tail(int64_t K, int64_t M, int64_t N, TailPlan *tp) {
     return (nchunks + per_chunks - 1) / per_chunks >= 2;
 }
 
-uint64_t xq16_bytes(int64_t K, int64_t rows, int64_t M, bool grouped) {
+// Split-f16 (Q8_0 / Q4_0): the hi and lo planes and the row scales.
+// Per-block (Q4_K): the f16 integers and the two block-scale arrays.
+uint64_t xq16_bytes(int32_t wtype, int64_t K, int64_t rows, int64_t M, bool grouped) {
     const uint64_t nblk = (uint64_t)K / QK;
-    uint64_t b = pad256((uint64_t)rows * (uint64_t)K * 2) + 2 * pad256(nblk * (uint64_t)rows * 4);
+    uint64_t b = wtype == WT_Q4_K ? pad256((uint64_t)rows * (uint64_t)K * 2) + 2 * pad256(nblk * (uint64_t)rows * 4)
+                                  : pad256(2 * (uint64_t)rows * (uint64_t)K * 2) + pad256((uint64_t)rows * 4);
     if (!grouped) {
-        const int sp = gemm_tc_splits(K, M, rows);
+        const int sp = gemm_tc_splits(wtype, K, M, rows);
         TailPlan tp{};
         if (sp > 1)
             b += pad256((uint64_t)sp * (uint64_t)M * (uint64_t)rows * 4);
-        else if (gemm_tc_tail(K, M, rows, &tp))
-            b += pad256((uint64_t)tp.splits * tp.rows * ((rows + TC_BN - 1) / TC_BN) * TC_BN * TC_BM * 4);
+        else if (gemm_tc_tail(wtype, K, M, rows, &tp)) {
+            const int64_t bn = gemm_tc_block_n(wtype);
+            b += pad256((uint64_t)tp.splits * tp.rows * ((rows + bn - 1) / bn) * bn * TC_BM * 4);
+        }
     }
     return b;
 }
 
-XQ16 xq16_carve(void *base, int64_t K, int64_t rows) {
+XQ16 xq16_carve(int32_t wtype, void *base, int64_t K, int64_t rows) {
     const uint64_t nblk = (uint64_t)K / QK;
     uint8_t *p = static_cast<uint8_t *>(base);
-    XQ16 r;
+    XQ16 r{};
     r.q16 = p;
-    p += pad256((uint64_t)rows * (uint64_t)K * 2);
-    r.dxT = reinterpret_cast<float *>(p);
-    p += pad256(nblk * (uint64_t)rows * 4);
-    r.xsdT = reinterpret_cast<float *>(p);
-    p += pad256(nblk * (uint64_t)rows * 4);
+    if (wtype == WT_Q4_K) {
+        p += pad256((uint64_t)rows * (uint64_t)K * 2);
+        r.dxT = reinterpret_cast<float *>(p);
+        p += pad256(nblk * (uint64_t)rows * 4);
+        r.xsdT = reinterpret_cast<float *>(p);
+        p += pad256(nblk * (uint64_t)rows * 4);
+    } else {
+        p += pad256(2 * (uint64_t)rows * (uint64_t)K * 2);
+        r.xscale = reinterpret_cast<float *>(p);
+        p += pad256((uint64_t)rows * 4);
+    }
     r.partial = reinterpret_cast<float *>(p);
     return r;
 }
 
 int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, const XQ16 &out,
-                           const GroupMap *routed, cudaStream_t s) {
+                           const GroupMap *routed, cudaStream_t s, int32_t wtype) {
     const int64_t rows = routed ? N * routed->n_selected : N;
     if (rows == 0) return FB_OK;
     if (K % QK || K <= 0 || K > INT32_MAX / 4 || rows > INT32_MAX)
@@ -1081,7 +1558,7 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
     if (routed) g = *routed;
     quantize_q8_f16_kernel<<<(unsigned)rows, QF_THREADS, 0, s>>>(
         static_cast<const uint8_t *>(x), x_nb1, (int)K, (int)rows, static_cast<__half *>(out.q16), out.dxT, out.xsdT,
-        routed != nullptr, g);
+        out.xscale, wtype != WT_Q4_K, routed != nullptr, g);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "quantize_q8_f16 launch: %s", cudaGetErrorString(e));
     return FB_OK;
@@ -1102,7 +1579,7 @@ int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa,
     if (groups && (groups->n_groups < 1 || (w_nb2 & 15) || ((groups->dst_nb1 | groups->dst_nb2) & 3)))
         return fb::set_error(FB_ERR_INVALID, "gemm_tc: grouped strides");
     if ((reinterpret_cast<uintptr_t>(y) | y_nb1) & 3) return fb::set_error(FB_ERR_INVALID, "gemm_tc: output alignment");
-    const int splits = groups ? 1 : gemm_tc_splits(K, M, rows);
+    const int splits = groups ? 1 : gemm_tc_splits(wtype, K, M, rows);
     switch (wtype) {
     case WT_Q8_0:
         return launch_tc_typed<WT_Q8_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,

@@ -18,7 +18,7 @@ SHAPES = [
     (DType.Q8_0, 4096, 4096, 8),    # quantized activations in scratch, GEMV on 8 columns
     (DType.Q4_0, 1024, 300, 33),    # tiled GEMM over the scratch activations
     (DType.Q4_K, 2048, 256, 1),     # fused GEMV: no scratch used
-    (DType.Q8_0, 4096, 512, 600),   # large scratch (about 9.8 MB)
+    (DType.Q8_0, 4096, 512, 400),   # large scratch (about 13 MB: operand planes + split-K partials)
 ]
 
 
