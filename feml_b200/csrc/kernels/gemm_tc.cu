@@ -944,8 +944,19 @@ struct T3Layout {
     static constexpr int OFF_RAW = OFF_B + C::NBP * B_STAGE3;
     static constexpr int OFF_BAR = OFF_RAW + ((C::NR * RAW_STAGE + 1023) / 1024) * 1024;
     static constexpr int N_BARS = 2 * C::NR + C::NA + 2 * C::NBP + TC_ND + 1;
-    static constexpr int OFF_MISC = OFF_BAR + N_BARS * 8;
+    // epilogue column table: destination (8 bytes), scale, owner rank
+    static constexpr int OFF_COLS = OFF_BAR + ((N_BARS * 8 + 15) / 16) * 16;
+    static constexpr int OFF_MISC = OFF_COLS + T3_BN * 16;
     static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+    static_assert(C::NBP * B_STAGE3 >= T3_BN * TC_BM * 4, "the output tile is staged in the activation ring");
+};
+
+// The tile's output column c (row 0 of the tile): where it goes, its
+// activation row scale, and (peer mode) the rank that receives it (-1: all).
+struct T3Col {
+    uint64_t dst;  // byte address (peer mode: byte offset in a rank's buffer)
+    float scale;
+    int owner;
 };
 
 // One block's 16 words of exact f16 integers (element order) times the
@@ -990,6 +1001,7 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + L::OFF_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + L::OFF_MISC + 4);
     int *range_flag = reinterpret_cast<int *>(gbase + L::OFF_MISC + 8);
+    T3Col *cols = reinterpret_cast<T3Col *>(gbase + L::OFF_COLS);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -1142,11 +1154,48 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
         }
         if (!range_ok) *range_flag = 1;
     } else if (warp >= 8) {
-        // ---- epilogue: lane quarter warp % 4, columns 96*half .. +95 --------------
+        // ---- epilogue ------------------------------------------------------------
+        // (1) while the main loop runs: the column table (destinations of the
+        //     tile's columns, their activation row scales);
+        // (2) after the last MMA: TMEM -> the output tile staged in shared
+        //     memory as [column][128 rows] (the activation ring is free);
+        // (3) each column's 128 rows leave as one 512-byte store per warp.
+        const int et = tid - 256;  // 0..255
         const int sub = warp & 3, half = (warp - 8) >> 2;
         const int row = 32 * sub + lane;
-        if (96 * half < ncols && tc_wait_warp(mma_done, 0, abort_flag, lane, 256) && !*abort_flag) {
+        for (int c = et; c < ncols; c += 256) {
+            const int r = xrow0 + c;
+            T3Col d;
+            d.scale = p.xscale[r];
+            d.owner = -1;
+            if (tw.tsplit >= 0) {
+                d.dst = reinterpret_cast<uint64_t>(p.tail_partial +
+                                                   (((uint64_t)tw.tsplit * p.tail_n + tw.ttile) * T3_BN + c) * TC_BM);
+            } else if (p.partial) {
+                d.dst = reinterpret_cast<uint64_t>(p.partial + ((uint64_t)blockIdx.z * p.N + r) * p.M + m0);
+            } else {
+                uint64_t off;
+                if (p.grouped) {
+                    const int slot = p.g.rows[r];
+                    int tok = slot / p.g.n_selected;
+                    if (PEER && p.peer.owner_tokens > 0) {
+                        d.owner = tok / p.peer.owner_tokens;
+                        tok -= d.owner * p.peer.owner_tokens;
+                    }
+                    off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 + (uint64_t)tok * p.g.dst_nb2;
+                } else {
+                    off = (uint64_t)r * p.y_nb1;
+                }
+                off += (uint64_t)m0 * 4;
+                d.dst = PEER ? off : reinterpret_cast<uint64_t>(p.y) + off;
+            }
+            cols[c] = d;
+        }
+        float *stage = reinterpret_cast<float *>(gbase + L::OFF_B);
+        const bool live = tc_wait_warp(mma_done, 0, abort_flag, lane, 256) && !*abort_flag;
+        if (live && 96 * half < ncols) {
             tc_fence_after();
+            fence_proxy_async_smem();  // the ring was last written by TMA and read by the tensor core
 #pragma unroll 1
             for (int cc = 0; cc < 3; cc++) {
                 const int qc = 3 * half + cc;
@@ -1154,19 +1203,56 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
                 uint32_t r[32];
                 tc_ld32(tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(32 * qc), r);
                 tc_wait_ld();
-                // activation row scales 2^e_t of these 32 columns
-                const int c = 32 * qc + lane;
-                const float sc = c < ncols ? p.xscale[xrow0 + c] : 1.0f;
-                float acc[32];
 #pragma unroll
                 for (int i = 0; i < 32; i++)
-                    acc[i] = npairs > 0 ? __uint_as_float(r[i]) * __shfl_sync(0xffffffffu, sc, i) : 0.0f;
-                store_tile_row<PEER, T3_BN>(p, tw, row, qc, acc);
+                    stage[(32 * qc + i) * TC_BM + row] = npairs > 0 ? __uint_as_float(r[i]) : 0.0f;
+            }
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
+        if (live) {
+            const int rows_valid = min(TC_BM, p.M - m0);
+            const int r0 = 4 * lane;  // this lane's 4 rows
+            const int ep = (warp - 8);
+            const int pb = PEER ? (int)((*p.peer.epoch + 1u) & 1u) : 0;  // this step's peer buffer
+            for (int c = ep; c < ncols; c += 8) {
+                const T3Col d = cols[c];
+                float4 v = *reinterpret_cast<const float4 *>(stage + c * TC_BM + r0);
+                v.x *= d.scale, v.y *= d.scale, v.z *= d.scale, v.w *= d.scale;
+                if (!PEER && tw.tsplit < 0 && !p.partial && (p.epi.bias || p.epi.silu)) {  // fused bias / SiLU on y
+                    if (r0 < rows_valid) v.x = apply_act(v.x, p.epi, m0 + r0);
+                    if (r0 + 1 < rows_valid) v.y = apply_act(v.y, p.epi, m0 + r0 + 1);
+                    if (r0 + 2 < rows_valid) v.z = apply_act(v.z, p.epi, m0 + r0 + 2);
+                    if (r0 + 3 < rows_valid) v.w = apply_act(v.w, p.epi, m0 + r0 + 3);
+                }
+                auto put = [&](uint8_t *base) {
+                    float *o = reinterpret_cast<float *>(base) + r0;
+                    if (r0 + 4 <= rows_valid && (reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+                        *reinterpret_cast<float4 *>(o) = v;
+                    } else {
+                        if (r0 < rows_valid) o[0] = v.x;
+                        if (r0 + 1 < rows_valid) o[1] = v.y;
+                        if (r0 + 2 < rows_valid) o[2] = v.z;
+                        if (r0 + 3 < rows_valid) o[3] = v.w;
+                    }
+                };
+                if constexpr (PEER) {
+                    if (tw.tsplit >= 0 || p.partial) {
+                        put(reinterpret_cast<uint8_t *>(d.dst));
+                    } else {  // NVLink stores into the owner's buffer, or every rank's
+                        if (d.owner >= 0)
+                            put(p.peer.y[pb][d.owner] + d.dst);
+                        else
+                            for (int pr = 0; pr < p.peer.n; pr++) put(p.peer.y[pb][pr] + d.dst);
+                    }
+                } else {
+                    put(reinterpret_cast<uint8_t *>(d.dst));
+                }
             }
         }
     }
 
-    if (PEER) __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
+    // the epilogue threads' peer stores, before the CTA counts itself done
+    if (PEER && warp >= 8) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
