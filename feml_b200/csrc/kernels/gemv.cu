@@ -767,6 +767,63 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_ks_kernel(const __grid_c
         }
     }
 
+    // Up to kKsDefer boxes (all of a CTA's rows when it has at most 32): the
+    // lane keeps its partial sum of every row in registers and the warp
+    // reduces them once at the end with a transposing butterfly (31 shuffles,
+    // lane l ends with row l), instead of a 5-level reduction after each box.
+    constexpr int kKsDefer = 32 / kKsRows;
+    if (n_items <= kKsDefer) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kKsDefer; i++) {
+            if (i >= n_items) break;
+            const int stage = i % kKsStages;
+            const bool ok = mbar_wait_bounded(&bars[stage], (uint32_t)(i / kKsStages) & 1u);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0) {
+                    report_status(p.status, STATUS_TIMEOUT);
+                    for (int j = i; j < issued; j++)
+                        mbar_wait_bounded(&bars[j % kKsStages], (uint32_t)(j / kKsStages) & 1u);
+                }
+                break;
+            }
+            const uint8_t *st = ring + (uint32_t)stage * stage_bytes;
+#pragma unroll
+            for (int r = 0; r < kKsRows; r++) {
+#pragma unroll
+                for (int j = 0; j < XP; j++) {
+                    const int q = lane + 32 * j;
+                    if (q < npairs) {
+                        int s0, s1;
+                        float dsc0, dmm0, dsc1, dmm1;
+                        q4k_pair_dot_x(st + r * p.box_bytes + (q / 4) * Q4_K_BYTES, q % 4, xa0[j], xa1[j], xb0[j],
+                                       xb1[j], s0, s1, dsc0, dmm0, dsc1, dmm1);
+                        v[i * kKsRows + r] += dxa[j] * (dsc0 * (float)s0 - dmm0 * (float)sxa[j]) +
+                                              dxb[j] * (dsc1 * (float)s1 - dmm1 * (float)sxb[j]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && issued < n_items) {
+                fence_proxy_async_smem();
+                issue(issued);
+            }
+            issued = min(issued + 1, n_items);
+        }
+#pragma unroll
+        for (int o = 16, cnt = 16; o >= 1; o >>= 1, cnt >>= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int j = 0; j < cnt; j++) {
+                const float send = upper ? v[j] : v[j + cnt];
+                const float keep = upper ? v[j + cnt] : v[j];
+                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+        if (lane < rows) part[lane * kGemvWarps + warp] = v[0];
+    } else
     for (int i = 0; i < n_items; i++) {
         const int stage = i % kKsStages;
         const bool ok = mbar_wait_bounded(&bars[stage], (uint32_t)(i / kKsStages) & 1u);
