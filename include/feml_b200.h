@@ -318,8 +318,16 @@ int feml_b200_mul_mat_workspace(int32_t wtype, int64_t K, int64_t M, int64_t N, 
 /* mul_mat, ggml semantics (feml-cpu/src/ops/mul_mat.rs:14-58):
  *   dst[m*4 + n*dst_nb1] = sum_k W[k, m] * X[k, n]
  * W: wtype blocks, row m at w + m*w_nb1; X: f32, column n at x + n*x_nb1;
- * quantized weights are multiplied against the Q8_0-quantized activations
- * with int32 per-block sums. dst must not overlap w or x. */
+ * quantized weights are multiplied against the Q8_0-quantized activations:
+ * int32 per-block sums on the decode GEMVs (N <= 8) and the Q4_K GEMM; the
+ * Q8_0 / Q4_0 GEMM (N > 8) multiplies the dequantized values, each split
+ * exactly into two f16, with f32 accumulation. That GEMM needs every
+ * dequantized weight within the f16 range (|d| <= 511.75 for Q8_0,
+ * <= 8188 for Q4_0; quantized model weights have d = amax/127). Under
+ * graph_compute a larger block scale sets bit 3 of the backend's status
+ * word, which synchronize reports as FB_ERR_DEVICE; this entry point has no
+ * status word, and such a scale shows as non-finite outputs. dst must not
+ * overlap w or x. */
 int feml_b200_mul_mat(int32_t wtype, const void *w, uint64_t w_nb1, const void *x, uint64_t x_nb1, void *dst,
                       uint64_t dst_nb1, int64_t K, int64_t M, int64_t N, void *workspace, uint64_t workspace_bytes,
                       void *stream);

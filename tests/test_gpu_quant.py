@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 import torch
 
+import feml_b200 as F
 from feml_b200 import DType
 from feml_b200 import ops
 from oracle import oracle as O
@@ -316,3 +317,26 @@ def test_large_activations_stay_in_tolerance(b200, dt):
     bound = 1e-3 + 2e-5 * (xd @ wd.T)
     err = np.abs(got.astype(np.float64) - want)
     assert (err <= bound).all(), f"max err/bound {float((err / bound).max())}"
+
+
+@pytest.mark.parametrize("d,ok", [(500.0, True), (600.0, False)])
+def test_gemm_reports_weights_beyond_the_f16_range(b200, d, ok):
+    """The Q8_0 GEMM splits every dequantized weight into two f16. A block
+    scale whose products stay within the f16 range (500 * 127 = 63500) is
+    exact; one that leaves it (600 * 127 = 76200) must fail loudly through
+    the status word, not return infinities."""
+    rng = np.random.default_rng(5)
+    K, M, N = 512, 128, 16
+    wq = O.quantize(O.DT_Q8_0, weights(rng, M, K)).copy()
+    wq[5, 0:2] = np.frombuffer(np.float16(d).tobytes(), dtype=np.uint8)  # block 0 of row 5
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    if ok:
+        got = run_mul_mat(b200, DType.Q8_0, wq, x, K, M)
+        good, err = tol_ok(got, O.mul_mat_quant_ref(O.DT_Q8_0, wq, x, K))
+        assert good, f"max abs err {err}"
+    else:
+        with pytest.raises(F.FemlError):
+            run_mul_mat(b200, DType.Q8_0, wq, x, K, M)
+        # the error was reported and cleared: the backend keeps working
+        got = run_mul_mat(b200, DType.Q8_0, O.quantize(O.DT_Q8_0, weights(rng, M, K)), x, K, M)
+        assert np.isfinite(got).all()
