@@ -856,15 +856,85 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 mbar_arrive(&s_empty[ss]);
             }
         }
+        // The tile leaves through shared memory: staged as [column][128 rows]
+        // in the A stages (free once every pair's MMAs have completed), then
+        // each column's rows go out as one 512-byte store per warp (per-lane
+        // scalar stores to 32 output rows were as slow as the main loop in
+        // the split-f16 kernel).
+        float *stage = reinterpret_cast<float *>(gbase + L::OFF_A);
+        static_assert(C::NA * A_STAGE >= TC_BN * TC_BM * 4, "the output tile is staged in the A stages");
         if (ok) {
             float acc[32];
 #pragma unroll
             for (int i = 0; i < 16; i++) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
-            store_tile_row<PEER, TC_BN>(p, tw, row, qc, acc);
+#pragma unroll
+            for (int i = 0; i < 32; i++) stage[(32 * qc + i) * TC_BM + row] = acc[i];
+        }
+        asm volatile("bar.sync 1, 512;" ::: "memory");  // the 16 epilogue warps
+        if (!*abort_flag) {
+            const int rows_valid = min(TC_BM, p.M - m0);
+            const int r0 = 4 * lane;
+            const int pb = PEER ? (int)((*p.peer.epoch + 1u) & 1u) : 0;
+            for (int c = warp - 8; c < ncols; c += TC_EPI_WARPS) {
+                const int r = xrow0 + c;
+                float4 v = *reinterpret_cast<const float4 *>(stage + c * TC_BM + r0);
+                uint8_t *dst;
+                int owner = -1;
+                bool plain = false;
+                if (tw.tsplit >= 0) {
+                    dst = reinterpret_cast<uint8_t *>(p.tail_partial +
+                                                      (((uint64_t)tw.tsplit * p.tail_n + tw.ttile) * TC_BN + c) * TC_BM);
+                } else if (p.partial) {
+                    dst = reinterpret_cast<uint8_t *>(p.partial + ((uint64_t)blockIdx.z * p.N + r) * p.M + m0);
+                } else {
+                    uint64_t off;
+                    if (p.grouped) {
+                        const int slot = p.g.rows[r];
+                        int tok = slot / p.g.n_selected;
+                        if (PEER && p.peer.owner_tokens > 0) {
+                            owner = tok / p.peer.owner_tokens;
+                            tok -= owner * p.peer.owner_tokens;
+                        }
+                        off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 + (uint64_t)tok * p.g.dst_nb2;
+                    } else {
+                        off = (uint64_t)r * p.y_nb1;
+                    }
+                    off += (uint64_t)m0 * 4;
+                    dst = PEER ? reinterpret_cast<uint8_t *>(off) : p.y + off;
+                    plain = !PEER;
+                }
+                if (plain && (p.epi.bias || p.epi.silu)) {  // fused bias / SiLU on y
+                    if (r0 < rows_valid) v.x = apply_act(v.x, p.epi, m0 + r0);
+                    if (r0 + 1 < rows_valid) v.y = apply_act(v.y, p.epi, m0 + r0 + 1);
+                    if (r0 + 2 < rows_valid) v.z = apply_act(v.z, p.epi, m0 + r0 + 2);
+                    if (r0 + 3 < rows_valid) v.w = apply_act(v.w, p.epi, m0 + r0 + 3);
+                }
+                auto put = [&](uint8_t *base) {
+                    float *o = reinterpret_cast<float *>(base) + r0;
+                    if (r0 + 4 <= rows_valid && (reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+                        *reinterpret_cast<float4 *>(o) = v;
+                    } else {
+                        if (r0 < rows_valid) o[0] = v.x;
+                        if (r0 + 1 < rows_valid) o[1] = v.y;
+                        if (r0 + 2 < rows_valid) o[2] = v.z;
+                        if (r0 + 3 < rows_valid) o[3] = v.w;
+                    }
+                };
+                if (PEER && tw.tsplit < 0 && !p.partial) {  // NVLink stores into the owner's buffer, or every rank's
+                    const uint64_t off = reinterpret_cast<uint64_t>(dst);
+                    if (owner >= 0)
+                        put(p.peer.y[pb][owner] + off);
+                    else
+                        for (int pr = 0; pr < p.peer.n; pr++) put(p.peer.y[pb][pr] + off);
+                } else {
+                    put(dst);
+                }
+            }
         }
     }
 
-    if (PEER) __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
+    // the epilogue threads' peer stores, before the CTA counts itself done
+    if (PEER && warp >= 8) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     if (*abort_flag && tid == 0) report_status(p.status, STATUS_TIMEOUT);

@@ -136,3 +136,21 @@ def test_mul_mat_id_repeated_calls_are_deterministic(b200, dt):
     outs = [ops.mul_mat_id(dt, wt, xt, it, K) for _ in range(3)]
     torch.cuda.synchronize()
     assert all(torch.equal(outs[0], o) for o in outs[1:])
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0])
+def test_mul_mat_id_expert_group_wider_than_a_tile(b200, dt):
+    """One expert receives more routed slots than a column tile holds (the
+    Q8_0 / Q4_0 GEMM's grouped tiles are 192 wide): its group spans a full
+    tile and a narrow one; the weight rows end inside an m-tile."""
+    rng = np.random.default_rng(41)
+    E, M, K, N = 3, 200, 512, 260
+    wb = _expert_weights(rng, dt, E, M, K)
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    ids = np.zeros((N, 1), np.int32)
+    ids[230:245] = 1
+    ids[245:] = 2
+    got = run_mul_mat_id(b200, dt, wb, x, ids, K, M)
+    want = O.mul_mat_id_ref(QT[dt], wb, x, ids, K, quantize_act=True)
+    ok, err = tol_ok(got, want)
+    assert ok, err
