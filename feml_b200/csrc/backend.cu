@@ -213,7 +213,7 @@ int do_mul_mat_id(int32_t wtype, const void *w, uint64_t w_nb1, uint64_t w_nb2, 
                         fbk::gemm_tc_supported(wtype, K, M, N * n_sel, w, w_nb1) && (w_nb2 & 15) == 0 &&
                         ((reinterpret_cast<uintptr_t>(x) | x_nb1) & 15) == 0;
     const int block_n = wtype == FB_F32 ? fbk::gemm_f32_block_n()
-                        : use_tc        ? fbk::gemm_tc_block_n(wtype)
+                        : use_tc        ? fbk::gemm_tc_block_n(wtype, K)
                                         : fbk::gemm_q_block_n();
     if (wtype != FB_F32 && !use_tc && !fbk::gemm_q_supported(wtype, K, w, w_nb1))
         return set_error(FB_ERR_UNSUPPORTED, "mul_mat_id: quantized experts need K %% 256 == 0 and 16-byte aligned rows");
@@ -1322,7 +1322,7 @@ int feml_b200_mul_mat_id_peer_owned(int32_t wtype, const void *w_local, uint64_t
     }
     // invalid ids: every rank zeroes the slot in its own buffer of this step
     int rc = fbk::launch_moe_route(ids, ids_nb1, n_selected, N, n_experts, shard, n_shards, L.counts, L.offsets,
-                                   L.rows, L.tile_start, fbk::gemm_tc_block_n(wtype), status, po.y[0][shard], dst_nb1,
+                                   L.rows, L.tile_start, fbk::gemm_tc_block_n(wtype, K), status, po.y[0][shard], dst_nb1,
                                    dst_nb2, M, s, po.y[1][shard], epoch, owner_tokens);
     if (rc) return rc;
     fbk::GroupMap g{};
@@ -1335,7 +1335,7 @@ int feml_b200_mul_mat_id_peer_owned(int32_t wtype, const void *w_local, uint64_t
     g.w_group_stride = w_nb2;
     g.dst_nb1 = dst_nb1;
     g.dst_nb2 = dst_nb2;
-    g.max_tiles = (int32_t)((n_selected * N + fbk::gemm_tc_block_n(wtype) - 1) / fbk::gemm_tc_block_n(wtype) + n_local);
+    g.max_tiles = (int32_t)((n_selected * N + fbk::gemm_tc_block_n(wtype, K) - 1) / fbk::gemm_tc_block_n(wtype, K) + n_local);
     const fbk::XQ16 xa = fbk::xq16_carve(wtype, L.xq, K, N * n_selected);
     rc = fbk::launch_quantize_q8_f16(x, x_nb1, K, N, xa, &g, s, wtype);
     if (rc) return rc;

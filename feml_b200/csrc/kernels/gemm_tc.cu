@@ -197,6 +197,13 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32])
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Store 8 consecutive 32-bit TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
 // 32 consecutive 32-bit TMEM columns of this warp's 32 lanes.
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
@@ -335,6 +342,20 @@ __device__ __forceinline__ void store_a_block(uint32_t a_stage, int row, int j, 
 }
 
 __device__ __forceinline__ uint32_t byte_of(const uint32_t *w, int k) { return (w[k >> 2] >> (8 * (k & 3))) & 0xFFu; }
+
+// Q4_K super-block header (4 words: d, dmin as f16, then the 12 bytes of
+// 6-bit scales and mins): the scale and min of sub-block j (0..7), in the
+// ggml k-quant packing (j < 4: low 6 bits of bytes j and j + 4; j >= 4: a
+// nibble of byte j + 4 with the top 2 bits of bytes j - 4 / j).
+__device__ __forceinline__ void q4k_scale_min(const uint32_t *hdr, int j, int &sc, int &mn) {
+    if (j < 4) {
+        sc = (int)(byte_of(hdr, 4 + j) & 63u);
+        mn = (int)(byte_of(hdr, 8 + j) & 63u);
+    } else {
+        sc = (int)((byte_of(hdr, 8 + j) & 0x0Fu) | ((byte_of(hdr, j) >> 6) << 4));
+        mn = (int)((byte_of(hdr, 8 + j) >> 4) | ((byte_of(hdr, j + 4) >> 6) << 4));
+    }
+}
 
 // Words of block pair p of a raw chunk row: Q8_0 17 (68 bytes at 68p, 4-byte
 // aligned), Q4_0 9 (36 bytes at 36p), Q4_K 8 (the 32 nibble bytes at
@@ -1003,6 +1024,16 @@ struct T3Cfg<WT_Q4_0> {
     static constexpr int NR = 4, NA = 4, NBP = 3;
     static constexpr float kMaxScale = 65504.0f / 8.0f;
 };
+// Q4_K: w = d*(sc*q) - dmin*m. sc*q <= 63*15 = 945 is an exact f16 integer, so
+// d*(sc*q) splits into hi + lo exactly as the other types do; the min term is
+// carried as extra contraction positions (below). Limits: d*945 and dmin*63
+// within the f16 range.
+template <>
+struct T3Cfg<WT_Q4_K> {
+    static constexpr int NR = 4, NA = 4, NBP = 3;
+    static constexpr float kMaxScale = 65504.0f / 945.0f;
+    static constexpr float kMaxMin = 65504.0f / 63.0f;
+};
 
 template <int WT>
 struct T3Layout {
@@ -1057,7 +1088,15 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
         return;
     }
     const int m0 = tw.m0, xrow0 = tw.xrow0, ncols = tw.ncols, expert = tw.expert;
-    const int pair0 = tw.pair0, npairs = tw.npairs, chunk0 = tw.chunk0, nchunks = tw.nchunks;
+    const int chunk0 = tw.chunk0, nchunks = tw.nchunks;
+    // Contraction steps ("pairs", 64 positions each). Q4_K: every two
+    // super-blocks (8 pairs) are followed by one extra pair whose first 16
+    // positions hold the 16 sub-blocks' -dmin*m against the activation block
+    // sums (the rest of it is not multiplied); the activation planes are laid
+    // out the same way (576 positions per 512 elements). Tiles and splits
+    // cover whole super-block pairs, so chunk0 and nchunks are even.
+    const int pair0 = WT == WT_Q4_K ? chunk0 / 2 * 9 : tw.pair0;
+    const int npairs = WT == WT_Q4_K ? nchunks / 2 * 9 : tw.npairs;
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + L::OFF_BAR);
     uint64_t *raw_full = bars;
@@ -1168,8 +1207,11 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
                 if (lane == 0) {
                     const uint32_t a_hi = tmem + (uint32_t)(T3_BN + 64 * sa), a_lo = a_hi + 32u;
                     const uint32_t b_hi = sbase + L::OFF_B + sb * L::B_STAGE3, b_lo = b_hi + T3_HALF;
+                    // a Q4_K min-term pair uses its first K step only
+                    const int nk = (WT == WT_Q4_K && q % 9 == 8) ? 1 : 4;
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
+                        if (k >= nk) break;
                         // K step of 16: 8 TMEM columns of A; 32 bytes in the swizzled B rows
                         const uint32_t ka = 8u * k, kb = 64u * (k >> 1) + 32u * (k & 1);
                         tc_mma_f16_ts(tmem, a_hi + ka, sw128_desc(b_hi + kb), idesc, (q | k) ? 1u : 0u);
@@ -1185,6 +1227,101 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
         }
     } else if (warp >= 4 && warp < 8) {
         // ---- converters: one weight row per thread, one block pair at a time ----
+        if constexpr (WT == WT_Q4_K) {
+            // Q4_K: a chunk is one super-block (4 pairs); after every second
+            // one, the min-term pair of both (see the pair numbering above).
+            const int row = tid - 128;
+            bool range_ok = true;
+            float mins[8];  // -dmin*m of the previous (even) super-block, exact in f32
+            for (int c = 0; c < nchunks; c++) {
+                const int s = c % C::NR;
+                if (!tc_wait_warp(&raw_full[s], (c / C::NR) & 1, abort_flag, lane)) break;
+                const uint8_t *rrow = gbase + L::OFF_RAW + s * L::RAW_STAGE + row * RC::RAWB;
+                const uint4 hv = *reinterpret_cast<const uint4 *>(rrow);
+                const uint32_t hdr[4] = {hv.x, hv.y, hv.z, hv.w};
+                uint32_t w[CHUNK_PAIRS][8];
+#pragma unroll
+                for (int pp = 0; pp < CHUNK_PAIRS; pp++) load_pair_words<WT>(rrow, pp, w[pp]);
+                mbar_arrive(&raw_empty[s]);  // the super-block is in registers
+                const float d = f16_bits_to_f32((uint16_t)(hdr[0] & 0xFFFFu));
+                const float dmin = f16_bits_to_f32((uint16_t)(hdr[0] >> 16));
+                range_ok = range_ok && fabsf(d) <= C::kMaxScale && fabsf(dmin) <= C::kMaxMin;
+                const __half2 d2 = __half2half2(__ushort_as_half((uint16_t)(hdr[0] & 0xFFFFu)));
+                bool ok = true;
+#pragma unroll
+                for (int pp = 0; pp < CHUNK_PAIRS; pp++) {
+                    const int q = (c >> 1) * 9 + (c & 1) * CHUNK_PAIRS + pp;
+                    const int sa = q % C::NA;
+                    int sc0, mn0, sc1, mn1;
+                    q4k_scale_min(hdr, 2 * pp, sc0, mn0);
+                    q4k_scale_min(hdr, 2 * pp + 1, sc1, mn1);
+                    const __half2 s0 = __float2half2_rn((float)sc0), s1 = __float2half2_rn((float)sc1);
+                    uint32_t v0[16], v1[16];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        uint32_t lo[2], hi[2];
+                        nib_word_to_f16<0>(w[pp][i], lo, hi);
+                        // sc * q: exact f16 integers (<= 945)
+                        v0[2 * i] = h2_bits(__hmul2(bits_h2(lo[0]), s0));
+                        v0[2 * i + 1] = h2_bits(__hmul2(bits_h2(lo[1]), s0));
+                        v1[2 * i] = h2_bits(__hmul2(bits_h2(hi[0]), s1));
+                        v1[2 * i + 1] = h2_bits(__hmul2(bits_h2(hi[1]), s1));
+                    }
+                    uint32_t h[32], l[32];
+                    split_block(v0, d2, h, l);
+                    split_block(v1, d2, h + 16, l + 16);
+                    if (q >= C::NA &&
+                        !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(T3_BN + 64 * sa);
+                    tc_st32(ta, h);
+                    tc_st32(ta + 32u, l);
+                    tc_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&a_full[sa]);
+                }
+                if (!ok) break;
+                float cur[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    int scj, mnj;
+                    q4k_scale_min(hdr, j, scj, mnj);
+                    cur[j] = -(dmin * (float)mnj);  // exact: 11 + 6 significant bits
+                }
+                if ((c & 1) == 0) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) mins[j] = cur[j];
+                    continue;
+                }
+                // the min-term pair: 16 values (sub-blocks of super-blocks c-1, c)
+                const int q = (c >> 1) * 9 + 8;
+                const int sa = q % C::NA;
+                uint32_t h8[8], l8[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float a = i < 4 ? mins[2 * i] : cur[2 * i - 8];
+                    const float b = i < 4 ? mins[2 * i + 1] : cur[2 * i - 7];
+                    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+                    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+                    h8[i] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+                    l8[i] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+                }
+                if (q >= C::NA &&
+                    !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane))
+                    break;
+                tc_fence_after();
+                const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(T3_BN + 64 * sa);
+                tc_st8(ta, h8);
+                tc_st8(ta + 32u, l8);
+                tc_wait_st();
+                tc_fence_before();
+                mbar_arrive(&a_full[sa]);
+            }
+            if (!range_ok) *range_flag = 1;
+        } else {
         const int row = tid - 128;
         bool range_ok = true;
         for (int c = 0; c < nchunks; c++) {
@@ -1223,6 +1360,7 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
             if (!ok) break;
         }
         if (!range_ok) *range_flag = 1;
+        }
     } else if (warp >= 8) {
         // ---- epilogue ------------------------------------------------------------
         // (1) while the main loop runs: the column table (destinations of the
@@ -1354,7 +1492,7 @@ constexpr int QF_THREADS = 256;
 __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8_t *__restrict__ x, uint64_t x_nb1,
                                                                     int K, int rows, __half *__restrict__ q16,
                                                                     float *__restrict__ dxT, float *__restrict__ xsdT,
-                                                                    float *__restrict__ xscale, bool hilo,
+                                                                    float *__restrict__ xscale, bool hilo, bool ext,
                                                                     bool routed, GroupMap g) {
     const int r = blockIdx.x, tid = threadIdx.x;
     int src = r;
@@ -1364,8 +1502,11 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
     }
     const float *xr = reinterpret_cast<const float *>(x + (uint64_t)src * x_nb1);
     const int nblk = K / QK;
-    __half *orow = q16 + (uint64_t)r * K;
-    __half *orow_lo = q16 + ((uint64_t)rows + r) * K;
+    // ext (Q4_K): 576 positions per 512 elements, the 64 after each 512
+    // starting with the 16 blocks' sums (the min-term pair of the GEMM)
+    const int KE = ext ? K / 512 * 576 : K;
+    __half *orow = q16 + (uint64_t)r * KE;
+    __half *orow_lo = q16 + ((uint64_t)rows + r) * KE;
     float down = 1.0f;  // 2^-e
     if (hilo) {
         __shared__ float wmax[QF_THREADS / 32];
@@ -1384,7 +1525,7 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
         // the largest block scale: the quantizer's d of the row maximum
         // (division and f16 rounding are monotonic)
         const float dmax = __half2float(__float2half_rn(__fdiv_rn(amax, 127.0f)));
-        const float bound = dmax * 128.0f;
+        const float bound = dmax * (ext ? 4096.0f : 128.0f);  // ext: block sums up to 32 * 127 * d
         int e = 0;
         if (bound > 0.0f && isfinite(bound)) {
             int ex;
@@ -1406,7 +1547,15 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
         const uint32_t q = quantize_q8_0_quad(v, dbits, qsum);
         if (!valid) continue;
         const float d = f16_bits_to_f32(dbits);
+        const int kp = ext ? k + (k >> 9) * 64 : k;  // position in the operand row
         __half hq[4];
+        if (hilo && ext && (tid & 7) == 0) {  // the block sum, as hi + lo (24 significant bits: lo rounds)
+            const float xs = (d * (float)qsum) * down;
+            const __half h = __float2half_rn(xs);
+            const int pe = (b >> 4) * 576 + 512 + (b & 15);
+            orow[pe] = h;
+            orow_lo[pe] = __float2half_rn(xs - __half2float(h));
+        }
         if (hilo) {
             __half lq[4];
 #pragma unroll
@@ -1415,7 +1564,7 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
                 hq[i] = __float2half_rn(val);
                 lq[i] = __float2half_rn(val - __half2float(hq[i]));
             }
-            *reinterpret_cast<uint2 *>(orow_lo + k) = *reinterpret_cast<const uint2 *>(lq);
+            *reinterpret_cast<uint2 *>(orow_lo + kp) = *reinterpret_cast<const uint2 *>(lq);
         } else {
 #pragma unroll
             for (int i = 0; i < 4; i++) hq[i] = __int2half_rn((int)(int8_t)((q >> (8 * i)) & 0xFFu));
@@ -1424,7 +1573,7 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
                 xsdT[(uint64_t)b * rows + r] = d * (float)qsum;
             }
         }
-        *reinterpret_cast<uint2 *>(orow + k) = *reinterpret_cast<const uint2 *>(hq);
+        *reinterpret_cast<uint2 *>(orow + kp) = *reinterpret_cast<const uint2 *>(hq);
     }
 }
 
@@ -1488,28 +1637,41 @@ int encode_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint6
     return FB_OK;
 }
 
-template <int WT>
+// The split-f16 kernel runs Q8_0 and Q4_0, and Q4_K when K is a multiple of
+// 512 (every min-term pair covers two whole super-blocks).
+bool split_kernel(int32_t wtype, int64_t K) { return wtype != WT_Q4_K || K % 512 == 0; }
+// Length of an activation operand row: K, or for the split-f16 Q4_K 576
+// positions per 512 elements.
+int64_t operand_k(int32_t wtype, int64_t K) { return wtype == WT_Q4_K && K % 512 == 0 ? K / 512 * 576 : K; }
+// Q4_K K ranges (splits) cover whole super-block pairs.
+int chunk_round(int32_t wtype, int chunks) { return wtype == WT_Q4_K ? (chunks + 1) / 2 * 2 : chunks; }
+
+template <int WT, bool SPLIT>
 constexpr int smem_bytes_of() {
-    if constexpr (WT == WT_Q4_K)
-        return TcLayout<WT>::BYTES;
-    else
+    if constexpr (SPLIT)
         return T3Layout<WT>::BYTES;
+    else
+        return TcLayout<WT>::BYTES;
 }
 
 // rows: activation rows in the operand buffer; n_planes / w_nb2: weight
-// planes (experts) of the grouped mode (1 / unused otherwise).
-template <int WT>
+// planes (experts) of the grouped mode (1 / unused otherwise). SPLIT: the
+// split-f16 kernel (Q8_0, Q4_0, Q4_K with K % 512 == 0), else the per-block
+// kernel (Q4_K).
+template <int WT, bool SPLIT>
 int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_planes, const XQ16 &xa, int64_t K,
                     int64_t M, int64_t rows, void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status,
                     int splits, cudaStream_t s, const PeerOut *peer, const EpiAct &epi) {
     using C = TcCfg<WT>;
     using L = TcLayout<WT>;
     static_assert(L::BYTES <= 232448, "gemm_tc shared memory");
-    // Q8_0 / Q4_0: the split-f16 kernel over the hi / lo activation planes;
-    // Q4_K: the per-block kernel over exact f16 integers
-    constexpr bool kSplit = WT != WT_Q4_K;
+    // the split-f16 kernel over the hi / lo activation planes (Q4_K: the
+    // extended rows with the block sums), or the per-block kernel over exact
+    // f16 integers
+    constexpr bool kSplit = SPLIT;
     constexpr int BN = kSplit ? T3_BN : TC_BN;
-    constexpr int kBytes = smem_bytes_of<WT>();
+    constexpr int kBytes = smem_bytes_of<WT, SPLIT>();
+    const int64_t KE = operand_k(WT, K);
     static_assert(kBytes <= 232448, "gemm_tc3 shared memory");
     CUtensorMap tw, tx;
     const uint64_t planes = (uint64_t)n_planes, pstride = n_planes > 1 ? w_nb2 : w_nb1 * (uint64_t)M;
@@ -1522,8 +1684,8 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
                         TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     // activations: [rows][K] f16 (Q4_K), or planes [2][rows][K] (hi, lo)
-    rc = encode_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xa.q16, (uint64_t)K, (uint64_t)rows, kSplit ? 2 : 0,
-                    (uint64_t)K * 2, kSplit ? (uint64_t)rows * (uint64_t)K * 2 : 0, 64, BN,
+    rc = encode_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xa.q16, (uint64_t)KE, (uint64_t)rows, kSplit ? 2 : 0,
+                    (uint64_t)KE * 2, kSplit ? (uint64_t)rows * (uint64_t)KE * 2 : 0, 64, BN,
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     // the peer-store variant is a separate instantiation, so the plain kernel
@@ -1553,7 +1715,7 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     p.epi = epi;
     const int total_pairs = (int)(K / (2 * QK));
     if (splits > 1) {
-        const int per_chunks = (int)((K / QKK + splits - 1) / splits);
+        const int per_chunks = chunk_round(WT, (int)((K / QKK + splits - 1) / splits));
         p.split_pairs = per_chunks * CHUNK_PAIRS;
         splits = (total_pairs + p.split_pairs - 1) / p.split_pairs;
         p.partial = xa.partial;
@@ -1615,21 +1777,21 @@ bool gemm_tc_supported(int32_t wtype, int64_t K, int64_t M, int64_t N, const voi
     if (wtype != WT_Q8_0 && wtype != WT_Q4_0 && wtype != WT_Q4_K) return false;
     if (K <= 0 || K % QKK || K > (1 << 24) || M <= 0 || N <= 0 || M > INT32_MAX || N > INT32_MAX / 64) return false;
     if (((reinterpret_cast<uintptr_t>(w) | w_nb1) & 15) != 0) return false;
-    return (N + gemm_tc_block_n(wtype) - 1) / gemm_tc_block_n(wtype) <= 65535;
+    return (N + gemm_tc_block_n(wtype, K) - 1) / gemm_tc_block_n(wtype, K) <= 65535;
 }
 
-int gemm_tc_block_n(int32_t wtype) { return wtype == WT_Q4_K ? TC_BN : T3_BN; }
+int gemm_tc_block_n(int32_t wtype, int64_t K) { return split_kernel(wtype, K) ? T3_BN : TC_BN; }
 
 // Split-K when the tile grid leaves most SMs idle (ungrouped only): one CTA
 // per SM in a single wave, every split at least two weight chunks.
 int gemm_tc_splits(int32_t wtype, int64_t K, int64_t M, int64_t N) {
-    const int64_t bn = gemm_tc_block_n(wtype);
+    const int64_t bn = gemm_tc_block_n(wtype, K);
     const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn);
     const int64_t nchunks = K / QKK, sms = sm_count();
     if (tiles * 2 > sms || nchunks < 4) return 1;
     const int64_t splits = std::min<int64_t>({sms / tiles, nchunks / 2, 16});
     if (splits < 2) return 1;
-    const int64_t per = (nchunks + splits - 1) / splits;
+    const int64_t per = chunk_round(wtype, (int)((nchunks + splits - 1) / splits));
     return (int)((nchunks + per - 1) / per);
 }
 
@@ -1640,7 +1802,7 @@ int gemm_tc_splits(int32_t wtype, int64_t K, int64_t M, int64_t N) {
 // 1/splits of the work; the other tiles run whole. A partial wave of
 // full-length tiles becomes a short one.
 bool gemm_tc_tail(int32_t wtype, int64_t K, int64_t M, int64_t N, TailPlan *tp) {
-    const int64_t bn = gemm_tc_block_n(wtype);
+    const int64_t bn = gemm_tc_block_n(wtype, K);
     const int64_t tiles_m = (M + TC_BM - 1) / TC_BM, tiles_n = (N + bn - 1) / bn;
     const int64_t tiles = tiles_m * tiles_n, sms = sm_count(), nchunks = K / QKK;
     if (tiles <= sms || tiles * 2 <= sms || nchunks < 4) return false;
@@ -1654,7 +1816,7 @@ bool gemm_tc_tail(int32_t wtype, int64_t K, int64_t M, int64_t N, TailPlan *tp) 
     const double before = (double)((tiles + sms - 1) / sms);
     const double after = (double)((tiles - n_tail + sms - 1) / sms) + 1.0 / (double)S;
     if (after > before - 0.15) return false;
-    const int64_t per_chunks = (nchunks + S - 1) / S;
+    const int64_t per_chunks = chunk_round(wtype, (int)((nchunks + S - 1) / S));
     if (tp) {
         tp->rows = (int)r;
         tp->splits = (int)((nchunks + per_chunks - 1) / per_chunks);
@@ -1663,19 +1825,21 @@ bool gemm_tc_tail(int32_t wtype, int64_t K, int64_t M, int64_t N, TailPlan *tp) 
     return (nchunks + per_chunks - 1) / per_chunks >= 2;
 }
 
-// Split-f16 (Q8_0 / Q4_0): the hi and lo planes and the row scales.
-// Per-block (Q4_K): the f16 integers and the two block-scale arrays.
+// Split-f16 (Q8_0, Q4_0, Q4_K with K % 512 == 0): the hi and lo planes and
+// the row scales. Per-block (other Q4_K): the f16 integers and the two
+// block-scale arrays.
 uint64_t xq16_bytes(int32_t wtype, int64_t K, int64_t rows, int64_t M, bool grouped) {
-    const uint64_t nblk = (uint64_t)K / QK;
-    uint64_t b = wtype == WT_Q4_K ? pad256((uint64_t)rows * (uint64_t)K * 2) + 2 * pad256(nblk * (uint64_t)rows * 4)
-                                  : pad256(2 * (uint64_t)rows * (uint64_t)K * 2) + pad256((uint64_t)rows * 4);
+    const uint64_t nblk = (uint64_t)K / QK, KE = (uint64_t)operand_k(wtype, K);
+    uint64_t b = !split_kernel(wtype, K)
+                     ? pad256((uint64_t)rows * (uint64_t)K * 2) + 2 * pad256(nblk * (uint64_t)rows * 4)
+                     : pad256(2 * (uint64_t)rows * KE * 2) + pad256((uint64_t)rows * 4);
     if (!grouped) {
         const int sp = gemm_tc_splits(wtype, K, M, rows);
         TailPlan tp{};
         if (sp > 1)
             b += pad256((uint64_t)sp * (uint64_t)M * (uint64_t)rows * 4);
         else if (gemm_tc_tail(wtype, K, M, rows, &tp)) {
-            const int64_t bn = gemm_tc_block_n(wtype);
+            const int64_t bn = gemm_tc_block_n(wtype, K);
             b += pad256((uint64_t)tp.splits * tp.rows * ((rows + bn - 1) / bn) * bn * TC_BM * 4);
         }
     }
@@ -1687,14 +1851,14 @@ XQ16 xq16_carve(int32_t wtype, void *base, int64_t K, int64_t rows) {
     uint8_t *p = static_cast<uint8_t *>(base);
     XQ16 r{};
     r.q16 = p;
-    if (wtype == WT_Q4_K) {
+    if (!split_kernel(wtype, K)) {
         p += pad256((uint64_t)rows * (uint64_t)K * 2);
         r.dxT = reinterpret_cast<float *>(p);
         p += pad256(nblk * (uint64_t)rows * 4);
         r.xsdT = reinterpret_cast<float *>(p);
         p += pad256(nblk * (uint64_t)rows * 4);
     } else {
-        p += pad256(2 * (uint64_t)rows * (uint64_t)K * 2);
+        p += pad256(2 * (uint64_t)rows * (uint64_t)operand_k(wtype, K) * 2);
         r.xscale = reinterpret_cast<float *>(p);
         p += pad256((uint64_t)rows * 4);
     }
@@ -1714,7 +1878,7 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
     if (routed) g = *routed;
     quantize_q8_f16_kernel<<<(unsigned)rows, QF_THREADS, 0, s>>>(
         static_cast<const uint8_t *>(x), x_nb1, (int)K, (int)rows, static_cast<__half *>(out.q16), out.dxT, out.xsdT,
-        out.xscale, wtype != WT_Q4_K, routed != nullptr, g);
+        out.xscale, split_kernel(wtype, K), wtype == WT_Q4_K && split_kernel(wtype, K), routed != nullptr, g);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "quantize_q8_f16 launch: %s", cudaGetErrorString(e));
     return FB_OK;
@@ -1738,14 +1902,17 @@ int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa,
     const int splits = groups ? 1 : gemm_tc_splits(wtype, K, M, rows);
     switch (wtype) {
     case WT_Q8_0:
-        return launch_tc_typed<WT_Q8_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
-                                        peer, ep);
+        return launch_tc_typed<WT_Q8_0, true>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status,
+                                              splits, s, peer, ep);
     case WT_Q4_0:
-        return launch_tc_typed<WT_Q4_0>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
-                                        peer, ep);
+        return launch_tc_typed<WT_Q4_0, true>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status,
+                                              splits, s, peer, ep);
     default:
-        return launch_tc_typed<WT_Q4_K>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status, splits, s,
-                                        peer, ep);
+        if (split_kernel(wtype, K))
+            return launch_tc_typed<WT_Q4_K, true>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status,
+                                                  splits, s, peer, ep);
+        return launch_tc_typed<WT_Q4_K, false>(w, w_nb1, w_nb2, planes, xa, K, M, rows, y, y_nb1, groups, status,
+                                               splits, s, peer, ep);
     }
 }
 

@@ -144,12 +144,13 @@ int gemm_q_splits(int64_t K, int64_t M, int64_t N);
 uint64_t gemm_q_split_bytes(int64_t K, int64_t M, int64_t N);
 
 // gemm_tc.cu: tcgen05/TMEM GEMM for Q8_0 / Q4_0 / Q4_K weights (K % 256 == 0,
-// 16-byte aligned rows). Activations come quantized to Q8_0 as XQ16. For
-// Q8_0 / Q4_0 (the split-f16 kernel): q16 holds two planes [2][rows][K] of
-// f16, hi and lo of the dequantized activation times 2^-e_row, and xscale
-// [rows] = 2^e_row. For Q4_K (the per-block kernel): q16 [rows][K] exact f16
-// integers, dxT / xsdT [K/32][rows] (block scale and scale * integer sum).
-// Both leave room for split-K partial tiles.
+// 16-byte aligned rows). Activations come quantized to Q8_0 as XQ16. For the
+// split-f16 kernel (Q8_0, Q4_0, and Q4_K with K % 512 == 0): q16 holds two
+// planes [2][rows][KE] of f16, hi and lo of the dequantized activation times
+// 2^-e_row (Q4_K: KE = 576 per 512 elements, the block sums after each 512),
+// and xscale [rows] = 2^e_row. For the per-block kernel (other Q4_K): q16
+// [rows][K] exact f16 integers, dxT / xsdT [K/32][rows] (block scale and
+// scale * integer sum). Both leave room for split-K partial tiles.
 struct XQ16 {
     void *q16;
     float *dxT;
@@ -178,7 +179,7 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
                            const GroupMap *routed, cudaStream_t s, int32_t wtype);
 // With `groups` (mul_mat_id): expert planes w + e*groups->w_group_stride,
 // activation rows = routed slots (N tokens x n_selected), outputs through
-// the group map. Column tiles of groups->tile_start use gemm_tc_block_n(wtype).
+// the group map. Column tiles of groups->tile_start use gemm_tc_block_n(wtype, K).
 // With `peer` (grouped mode only): each output value is stored into every
 // rank's buffer of this step instead of y (see PeerOut), then every rank's
 // flag is raised once by the grid's last CTA.
@@ -187,8 +188,9 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
 int launch_gemm_tc(int32_t wtype, const void *w, uint64_t w_nb1, const XQ16 &xa, int64_t K, int64_t M, int64_t N,
                    void *y, uint64_t y_nb1, const GroupMap *groups, int32_t *status, cudaStream_t s,
                    const PeerOut *peer = nullptr, const EpiAct *epi = nullptr);
-// Column-tile width of the kernel that runs `wtype` (256 split-f16, 128 Q4_K).
-int gemm_tc_block_n(int32_t wtype);
+// Column-tile width of the kernel that runs `wtype` at this K (192 split-f16,
+// 128 per-block).
+int gemm_tc_block_n(int32_t wtype, int64_t K);
 
 // Per-block int32 sums (bit-exactness probe); xq in ggml Q8_0 layout.
 int launch_block_dots(int32_t wtype, const void *w, uint64_t w_nb1, const void *xq, int64_t K, int64_t M, int64_t N,

@@ -340,3 +340,25 @@ def test_gemm_reports_weights_beyond_the_f16_range(b200, d, ok):
         # the error was reported and cleared: the backend keeps working
         got = run_mul_mat(b200, DType.Q8_0, O.quantize(O.DT_Q8_0, weights(rng, M, K)), x, K, M)
         assert np.isfinite(got).all()
+
+
+@pytest.mark.parametrize("off,v,ok", [(0, 60.0, True), (0, 80.0, False), (2, 1000.0, True), (2, 1100.0, False)])
+def test_q4_k_gemm_reports_scales_beyond_the_f16_range(b200, off, v, ok):
+    """The Q4_K GEMM (K % 512 == 0) splits d * (sc * q) into two f16, with
+    sc * q <= 945, and carries -dmin * m (m <= 63) as f16 too: d up to
+    65504 / 945 and dmin up to 65504 / 63 are exact, larger ones must fail
+    loudly through the status word."""
+    rng = np.random.default_rng(6)
+    K, M, N = 1024, 128, 16
+    wq = O.quantize(O.DT_Q4_K, weights(rng, M, K)).copy()
+    wq[5, off:off + 2] = np.frombuffer(np.float16(v).tobytes(), dtype=np.uint8)  # super-block 0 of row 5
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    if ok:
+        got = run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
+        good, err = tol_ok(got, O.mul_mat_quant_ref(O.DT_Q4_K, wq, x, K))
+        assert good, f"max abs err {err}"
+    else:
+        with pytest.raises(F.FemlError):
+            run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
+        got = run_mul_mat(b200, DType.Q4_K, O.quantize(O.DT_Q4_K, weights(rng, M, K)), x, K, M)
+        assert np.isfinite(got).all()
