@@ -447,7 +447,8 @@ def dominant_kernel(cfg, N):
         if wt == "Q4_K" and 12288 <= cfg["K"] <= 16384:
             return "gemv_ks_kernel" if N == 1 else "gemv_ks_cols_kernel"
         return "gemv_kernel"
-    return "gemm_tc3_kernel (tcgen05 split-f16)" if wt in ("Q8_0", "Q4_0") else "gemm_tc_kernel (tcgen05)"
+    split = wt in ("Q8_0", "Q4_0") or (wt == "Q4_K" and cfg["K"] % 512 == 0)
+    return "gemm_tc3_kernel (tcgen05 split-f16)" if split else "gemm_tc_kernel (tcgen05)"
 
 
 def compute_dtype(cfg, N):
@@ -457,7 +458,7 @@ def compute_dtype(cfg, N):
         return "f32"
     if N <= 8:
         return "int8 dot / f32 scale"
-    if wt in ("Q8_0", "Q4_0"):
+    if wt in ("Q8_0", "Q4_0") or (wt == "Q4_K" and cfg["K"] % 512 == 0):
         return "f16 hi+lo operands (exact), f32 accumulate"
     return "f16 integer dot / f32 scale"
 
