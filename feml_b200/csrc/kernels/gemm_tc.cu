@@ -127,6 +127,11 @@ struct TcParams {
     // tail_partial[s][t][128 columns][128 rows]. tail_full < 0: off.
     int tail_full, tail_S, tail_tiles_n, tail_m0, tail_n, tail_split_pairs;
     float *tail_partial;
+    // Grouped tail (mul_mat_id, 1D grid; gtail_sms > 0): the same split,
+    // planned in the kernel from the routed column tile count (tail_plan);
+    // partials in tail_partial as above.
+    int gtail_sms;
+    bool gtail_even;
     PeerOut peer;         // peer.n > 0 (grouped): outputs into every rank's buffer, then a signal
     EpiAct epi;           // fused bias / SiLU (ungrouped, not split)
 };
@@ -480,8 +485,40 @@ __device__ __forceinline__ void convert_pair(const uint32_t *w, const uint32_t *
 // spare tile (no work).
 struct TileWork {
     int m0, xrow0, ncols, expert, tsplit, ttile, pair0, npairs, chunk0, nchunks;
+    int tail_n;  // tail tiles (partial buffer index: split * tail_n + tile)
     bool unused;
 };
+
+// Tail split of a grid of tiles_m x tiles_n tiles over `nchunks` weight
+// chunks, one CTA per SM on `sms` SMs: when the last wave is a few rows of
+// tiles past a whole number of waves, the last `rows` m-tile rows (every
+// n-tile of them, so every column of those rows is treated alike) are split
+// `splits` ways in K so that their CTAs fill one wave, each doing 1/splits of
+// the work, and the launch takes at least one wave less. `even`: slices of
+// whole chunk pairs (Q4_K on the split-f16 kernel). Evaluated on the host
+// for mul_mat and in the kernels for mul_mat_id, whose column tile count is
+// known only on the device.
+__host__ __device__ inline bool tail_plan(int64_t tiles_m, int64_t tiles_n, int64_t nchunks, int64_t sms, bool even,
+                                          TailPlan *tp) {
+    const int64_t tiles = tiles_m * tiles_n;
+    if (tiles_n <= 0 || tiles <= sms || nchunks < 4) return false;
+    const int64_t over = tiles % sms;
+    if (over == 0) return false;
+    const int64_t r = (over + tiles_n - 1) / tiles_n, n_tail = r * tiles_n;
+    if (r >= tiles_m) return false;
+    int64_t S = sms / n_tail;
+    if (S > nchunks / 2) S = nchunks / 2;
+    if (S > 8) S = 8;
+    if (S < 2) return false;
+    // whole waves before and after: the split CTAs add 1/S of a wave
+    if ((tiles - n_tail + sms - 1) / sms >= (tiles + sms - 1) / sms) return false;
+    int64_t per = (nchunks + S - 1) / S;
+    if (even) per = (per + 1) / 2 * 2;
+    tp->rows = (int)r;
+    tp->splits = (int)((nchunks + per - 1) / per);
+    tp->split_pairs = (int)(per * CHUNK_PAIRS);
+    return tp->splits >= 2;
+}
 
 __device__ __forceinline__ TileWork decode_tile(const TcParams &p, int bn) {
     TileWork t;
@@ -491,8 +528,38 @@ __device__ __forceinline__ TileWork decode_tile(const TcParams &p, int bn) {
     t.expert = 0;
     t.tsplit = -1;
     t.ttile = 0;
+    t.tail_n = p.tail_n;
     t.unused = false;
-    if (p.tail_full >= 0) {
+    int tail_pairs = p.tail_split_pairs;
+    int tt = blockIdx.y;  // grouped: column tile over the experts' groups
+    if (p.grouped && p.gtail_sms > 0) {
+        // 1D grid: tiles in (m-tile, column tile) order over the column tile
+        // count the routing wrote, then the tail split's work items; the
+        // grid is sized for the largest count, the rest exit
+        const int T = p.g.tile_start[p.g.n_groups];
+        const int tiles_m = (p.M + TC_BM - 1) / TC_BM;
+        TailPlan tp{};
+        const bool on = tail_plan(tiles_m, T, p.K / QKK, p.gtail_sms, p.gtail_even, &tp);
+        const int n_tail = on ? tp.rows * T : 0, full = tiles_m * T - n_tail;
+        const int w = (int)blockIdx.x;
+        int mt;
+        if (w < full) {
+            mt = w / T;
+            tt = w % T;
+        } else if (on && w < full + n_tail * tp.splits) {
+            t.tsplit = (w - full) % tp.splits;
+            t.ttile = (w - full) / tp.splits;
+            mt = tiles_m - tp.rows + t.ttile / T;
+            tt = t.ttile % T;
+            t.tail_n = n_tail;
+            tail_pairs = tp.split_pairs;
+        } else {
+            t.unused = true;
+            t.npairs = t.nchunks = 0;
+            return t;
+        }
+        t.m0 = mt * TC_BM;
+    } else if (p.tail_full >= 0) {
         const int w = (int)blockIdx.x;
         int mt, nt;
         if (w < p.tail_full) {
@@ -509,7 +576,6 @@ __device__ __forceinline__ TileWork decode_tile(const TcParams &p, int bn) {
         t.ncols = min(bn, p.N - t.xrow0);
     }
     if (p.grouped) {
-        const int tt = blockIdx.y;
         if (tt >= p.g.tile_start[p.g.n_groups]) {
             t.unused = true;
             t.npairs = t.nchunks = 0;
@@ -522,62 +588,13 @@ __device__ __forceinline__ TileWork decode_tile(const TcParams &p, int bn) {
     }
     // K range in block pairs (split-K: a slice per blockIdx.z); chunks of 4 pairs
     const int total_pairs = p.K / (2 * QK);
-    t.pair0 = t.tsplit >= 0 ? t.tsplit * p.tail_split_pairs : (p.split_pairs ? (int)blockIdx.z * p.split_pairs : 0);
-    t.npairs = t.tsplit >= 0    ? min(p.tail_split_pairs, total_pairs - t.pair0)
+    t.pair0 = t.tsplit >= 0 ? t.tsplit * tail_pairs : (p.split_pairs ? (int)blockIdx.z * p.split_pairs : 0);
+    t.npairs = t.tsplit >= 0    ? min(tail_pairs, total_pairs - t.pair0)
                : p.split_pairs ? min(p.split_pairs, total_pairs - t.pair0)
                                : total_pairs;
     t.chunk0 = t.pair0 / CHUNK_PAIRS;
     t.nchunks = t.npairs / CHUNK_PAIRS;
     return t;
-}
-
-// Store one epilogue thread's 32 outputs: weight row `row` of the tile,
-// columns 32*qc .. 32*qc+31. Destinations: the tail or split-K partial
-// buffers, the grouped map (optionally into a peer's buffer), or y through
-// the fused epilogue.
-template <bool PEER, int BN>
-__device__ __forceinline__ void store_tile_row(const TcParams &p, const TileWork &t, int row, int qc,
-                                               const float (&acc)[32]) {
-    const int m = t.m0 + row;
-    if (m >= p.M) return;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-        const int c = 32 * qc + i;
-        const float v = acc[i];
-        if (c < t.ncols) {
-            const int r = t.xrow0 + c;
-            if (t.tsplit >= 0) {
-                p.tail_partial[(((uint64_t)t.tsplit * p.tail_n + t.ttile) * BN + c) * TC_BM + row] = v;
-            } else if (p.partial) {
-                p.partial[((uint64_t)blockIdx.z * p.N + r) * p.M + m] = v;
-            } else {
-                uint64_t off;
-                int owner = -1;  // peer owner mode: the one rank that receives this slot
-                if (p.grouped) {
-                    const int slot = p.g.rows[r];
-                    int tok = slot / p.g.n_selected;
-                    if (PEER && p.peer.owner_tokens > 0) {
-                        owner = tok / p.peer.owner_tokens;
-                        tok -= owner * p.peer.owner_tokens;
-                    }
-                    off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 + (uint64_t)tok * p.g.dst_nb2;
-                } else {
-                    off = (uint64_t)r * p.y_nb1;
-                }
-                if constexpr (!PEER) {
-                    reinterpret_cast<float *>(p.y + off)[m] = apply_act(v, p.epi, m);
-                } else {  // NVLink stores into the owner's buffer, or every rank's
-                    const int b = (int)((*p.peer.epoch + 1u) & 1u);
-                    if (owner >= 0) {
-                        reinterpret_cast<float *>(p.peer.y[b][owner] + off)[m] = v;
-                    } else {
-                        for (int pr = 0; pr < p.peer.n; pr++)
-                            reinterpret_cast<float *>(p.peer.y[b][pr] + off)[m] = v;
-                    }
-                }
-            }
-        }
-    }
 }
 
 template <int WT, bool PEER>
@@ -904,7 +921,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 bool plain = false;
                 if (tw.tsplit >= 0) {
                     dst = reinterpret_cast<uint8_t *>(p.tail_partial +
-                                                      (((uint64_t)tw.tsplit * p.tail_n + tw.ttile) * TC_BN + c) * TC_BM);
+                                                      (((uint64_t)tw.tsplit * tw.tail_n + tw.ttile) * TC_BN + c) * TC_BM);
                 } else if (p.partial) {
                     dst = reinterpret_cast<uint8_t *>(p.partial + ((uint64_t)blockIdx.z * p.N + r) * p.M + m0);
                 } else {
@@ -1378,7 +1395,7 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
             d.owner = -1;
             if (tw.tsplit >= 0) {
                 d.dst = reinterpret_cast<uint64_t>(p.tail_partial +
-                                                   (((uint64_t)tw.tsplit * p.tail_n + tw.ttile) * T3_BN + c) * TC_BM);
+                                                   (((uint64_t)tw.tsplit * tw.tail_n + tw.ttile) * T3_BN + c) * TC_BM);
             } else if (p.partial) {
                 d.dst = reinterpret_cast<uint64_t>(p.partial + ((uint64_t)blockIdx.z * p.N + r) * p.M + m0);
             } else {
@@ -1606,6 +1623,34 @@ __global__ void tc_tail_reduce_kernel(const float *__restrict__ partial, int S, 
     }
 }
 
+// Grouped tail (mul_mat_id): each split tile's columns are summed over the
+// splits in order (deterministic) and stored through the group map; the
+// plan is recomputed from the routed column tile count (none: no work).
+__global__ void tc_gtail_reduce_kernel(const TcParams p, int bn) {
+    const int T = p.g.tile_start[p.g.n_groups];
+    const int tiles_m = (p.M + TC_BM - 1) / TC_BM;
+    TailPlan tp{};
+    if (!tail_plan(tiles_m, T, p.K / QKK, p.gtail_sms, p.gtail_even, &tp)) return;
+    const int n_tail = tp.rows * T;
+    const int64_t per = (int64_t)n_tail * bn * TC_BM;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / (bn * TC_BM)), rem = (int)(i % (bn * TC_BM));
+        const int c = rem / TC_BM, row = rem % TC_BM;
+        const int m = (tiles_m - tp.rows + t / T) * TC_BM + row, tt = t % T;
+        if (m >= p.M) continue;
+        int e = 0;
+        while (p.g.tile_start[e + 1] <= tt) e++;
+        const int jt = tt - p.g.tile_start[e];
+        if (c >= min(bn, p.g.counts[e] - jt * bn)) continue;
+        float acc = p.tail_partial[((int64_t)t * bn + c) * TC_BM + row];
+        for (int sp = 1; sp < tp.splits; sp++) acc += p.tail_partial[(((int64_t)sp * n_tail + t) * bn + c) * TC_BM + row];
+        const int slot = p.g.rows[p.g.offsets[e] + jt * bn + c];
+        const uint64_t off = (uint64_t)(slot % p.g.n_selected) * p.g.dst_nb1 +
+                             (uint64_t)(slot / p.g.n_selected) * p.g.dst_nb2 + (uint64_t)m * 4;
+        *reinterpret_cast<float *>(p.y + off) = apply_act(acc, p.epi, m);
+    }
+}
+
 // ---- host side ---------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static std::once_flag once;
@@ -1736,6 +1781,15 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
         p.tail_split_pairs = tp.split_pairs;
         p.tail_partial = xa.partial;
         grid = dim3((unsigned)(p.tail_full + p.tail_n * p.tail_S), 1, 1);
+    } else if (groups && !peer && splits <= 1 && ((M + TC_BM - 1) / TC_BM) * (int64_t)tiles_n > sm_count()) {
+        // mul_mat_id whose largest tile count overflows one wave: the tail
+        // split is planned in the kernel from the routed column tile count;
+        // the grid covers the largest count plus one wave of split work
+        // items (tail_plan: at most one per SM)
+        p.gtail_sms = sm_count();
+        p.gtail_even = WT == WT_Q4_K;
+        p.tail_partial = xa.partial;
+        grid = dim3((unsigned)(((M + TC_BM - 1) / TC_BM) * (int64_t)tiles_n + p.gtail_sms), 1, 1);
     }
     kern<<<grid, kSplit ? T3_THREADS : TC_THREADS, kBytes, s>>>(tw, tx, p);
     cudaError_t e = cudaGetLastError();
@@ -1745,6 +1799,13 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
         const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
         tc_tail_reduce_kernel<<<blocks, 256, 0, s>>>(p.tail_partial, p.tail_S, p.tail_n, p.tail_tiles_n, p.tail_m0,
                                                      (int)M, (int)rows, BN, static_cast<uint8_t *>(y), y_nb1, epi);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc tail reduce launch: %s", cudaGetErrorString(e));
+    }
+    if (p.gtail_sms > 0) {
+        const int64_t total = (int64_t)p.gtail_sms * BN * TC_BM;  // the largest tail
+        const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
+        tc_gtail_reduce_kernel<<<blocks, 256, 0, s>>>(p, BN);
         e = cudaGetLastError();
         if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc tail reduce launch: %s", cudaGetErrorString(e));
     }
@@ -1795,34 +1856,13 @@ int gemm_tc_splits(int32_t wtype, int64_t K, int64_t M, int64_t N) {
     return (int)((nchunks + per - 1) / per);
 }
 
-// Tail split of an ungrouped GEMM whose tiles overflow the last of several
-// waves by a little (a few rows of tiles past a whole number of waves): the
-// last m-tile rows that hold the overflow (every n-tile of them, so every column of those rows is
-// treated alike) are split in K so their CTAs fill one wave, each doing
-// 1/splits of the work; the other tiles run whole. A partial wave of
-// full-length tiles becomes a short one.
+// Tail split of an ungrouped GEMM (tail_plan).
 bool gemm_tc_tail(int32_t wtype, int64_t K, int64_t M, int64_t N, TailPlan *tp) {
     const int64_t bn = gemm_tc_block_n(wtype, K);
-    const int64_t tiles_m = (M + TC_BM - 1) / TC_BM, tiles_n = (N + bn - 1) / bn;
-    const int64_t tiles = tiles_m * tiles_n, sms = sm_count(), nchunks = K / QKK;
-    if (tiles <= sms || tiles * 2 <= sms || nchunks < 4) return false;
-    const int64_t over = tiles % sms;
-    if (over == 0) return false;
-    const int64_t r = (over + tiles_n - 1) / tiles_n, n_tail = r * tiles_n;
-    if (r >= tiles_m) return false;
-    const int64_t S = std::min<int64_t>({sms / n_tail, nchunks / 2, 8});
-    if (S < 2) return false;
-    // waves of whole tiles before and after (split CTAs take 1/S of a wave)
-    const double before = (double)((tiles + sms - 1) / sms);
-    const double after = (double)((tiles - n_tail + sms - 1) / sms) + 1.0 / (double)S;
-    if (after > before - 0.15) return false;
-    const int64_t per_chunks = chunk_round(wtype, (int)((nchunks + S - 1) / S));
-    if (tp) {
-        tp->rows = (int)r;
-        tp->splits = (int)((nchunks + per_chunks - 1) / per_chunks);
-        tp->split_pairs = (int)(per_chunks * CHUNK_PAIRS);
-    }
-    return (nchunks + per_chunks - 1) / per_chunks >= 2;
+    TailPlan t{};
+    const bool on = tail_plan((M + TC_BM - 1) / TC_BM, (N + bn - 1) / bn, K / QKK, sm_count(), wtype == WT_Q4_K, &t);
+    if (on && tp) *tp = t;
+    return on;
 }
 
 // Split-f16 (Q8_0, Q4_0, Q4_K with K % 512 == 0): the hi and lo planes and
@@ -1833,7 +1873,9 @@ uint64_t xq16_bytes(int32_t wtype, int64_t K, int64_t rows, int64_t M, bool grou
     uint64_t b = !split_kernel(wtype, K)
                      ? pad256((uint64_t)rows * (uint64_t)K * 2) + 2 * pad256(nblk * (uint64_t)rows * 4)
                      : pad256(2 * (uint64_t)rows * KE * 2) + pad256((uint64_t)rows * 4);
-    if (!grouped) {
+    if (grouped) {  // the tail split's partial tiles: at most one per SM
+        b += pad256((uint64_t)sm_count() * gemm_tc_block_n(wtype, K) * TC_BM * 4);
+    } else {
         const int sp = gemm_tc_splits(wtype, K, M, rows);
         TailPlan tp{};
         if (sp > 1)

@@ -154,3 +154,27 @@ def test_mul_mat_id_expert_group_wider_than_a_tile(b200, dt):
     want = O.mul_mat_id_ref(QT[dt], wb, x, ids, K, quantize_act=True)
     ok, err = tol_ok(got, want)
     assert ok, err
+
+
+@pytest.mark.parametrize("dt,K", [(DType.Q8_0, 2048), (DType.Q4_0, 2048), (DType.Q4_K, 2048), (DType.Q4_K, 1280)])
+def test_mul_mat_id_tail_split(b200, dt, K):
+    """38 weight-row tiles x 4 expert column tiles = 152 tiles on 148 SMs:
+    the grouped GEMM splits the last weight-row tile of every expert in K
+    (planned in the kernel from the routed tile count) and a reduce kernel
+    writes those outputs through the group map. M ends inside that tile.
+    K = 1280 (Q4_K) runs the per-block kernel's 128-column tiles."""
+    rng = np.random.default_rng(43)
+    E, M, N, n_sel = 4, 4800, 100, 2
+    wb = _expert_weights(rng, dt, E, M, K)
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    ids = topk_ids(rng, N, n_sel, E)
+    got = run_mul_mat_id(b200, dt, wb, x, ids, K, M)
+    want = O.mul_mat_id_ref(QT[dt], wb, x, ids, K, quantize_act=True)
+    ok, err = tol_ok(got, want)
+    assert ok, err
+    wt = torch.from_numpy(wb).cuda()
+    xt = torch.from_numpy(x).cuda()
+    it = torch.from_numpy(ids).cuda()
+    outs = [ops.mul_mat_id(dt, wt, xt, it, K) for _ in range(2)]
+    assert torch.equal(outs[0], outs[1])
+    assert np.array_equal(outs[0].cpu().numpy().reshape(got.shape), got)
