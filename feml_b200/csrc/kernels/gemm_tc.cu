@@ -261,6 +261,22 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
     return false;
 }
 
+// Named barrier `id` of `nthreads` threads (whole warps) with an OR vote:
+// every participant gets the OR of all votes. It orders memory among the
+// participants like __syncthreads (no shared-memory traffic).
+__device__ __forceinline__ bool named_bar_red_or(int id, int nthreads, bool vote) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pv, pr;\n\t"
+        "setp.ne.u32 pv, %1, 0;\n\t"
+        "bar.red.or.pred pr, %2, %3, pv;\n\t"
+        "selp.u32 %0, 1, 0, pr;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)vote), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 // Warp-uniform form for roles that then run .sync.aligned instructions or
 // read what the barrier guards: lane 0 polls, the verdict is broadcast, and
 // every lane re-reads the completed phase (acquire).
@@ -1017,14 +1033,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 //               planes) into a ring of T3Cfg::NBP block pairs.
 //   warp 2      TMEM (512 columns) and the MMAs (one thread, one commit per
 //               block pair, which frees its A slot and its B stage).
-//   warp 3      gate: waits for a pair's A slot and B stage and raises the
-//               pair's `ready` barrier, so the MMA thread waits once per
-//               pair (barrier waits are slow while the tensor core streams
-//               operands from shared memory).
+//   warp 3      gate: waits for a pair's A slot and B stage, then meets the
+//               MMA warp at named barrier T3_GATE_BAR with its verdict, so
+//               the MMA warp never polls a shared-memory barrier (those
+//               polls are slow while the tensor core streams operands from
+//               shared memory; a named barrier does not touch it).
 //   warps 4-7   converters: one weight row (= TMEM lane) each; hi and lo of
 //               a pair into an A slot.
 //   warps 8-15  epilogue: lane quarter warp % 4, 96 columns each.
 constexpr int T3_THREADS = 512;
+constexpr int T3_GATE_BAR = 2;  // named barrier of warps 2 and 3 (0: __syncthreads, 1: epilogue)
 constexpr int T3_BN = 192;
 constexpr int T3_TMEM_COLS = 512;
 constexpr int T3_HALF = T3_BN * 128;  // one plane of a block pair: 192 rows x 64 f16
@@ -1061,7 +1079,7 @@ struct T3Layout {
     static constexpr int OFF_B = 0;
     static constexpr int OFF_RAW = OFF_B + C::NBP * B_STAGE3;
     static constexpr int OFF_BAR = OFF_RAW + ((C::NR * RAW_STAGE + 1023) / 1024) * 1024;
-    static constexpr int N_BARS = 2 * C::NR + C::NA + 2 * C::NBP + TC_ND + 1;
+    static constexpr int N_BARS = 2 * C::NR + C::NA + C::NBP + TC_ND + 1;
     // epilogue column table: destination (8 bytes), scale, owner rank
     static constexpr int OFF_COLS = OFF_BAR + ((N_BARS * 8 + 15) / 16) * 16;
     static constexpr int OFF_MISC = OFF_COLS + T3_BN * 16;
@@ -1120,8 +1138,7 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
     uint64_t *raw_empty = raw_full + C::NR;
     uint64_t *a_full = raw_empty + C::NR;
     uint64_t *b_full = a_full + C::NA;
-    uint64_t *ready = b_full + C::NBP;
-    uint64_t *pair_done = ready + C::NBP;
+    uint64_t *pair_done = b_full + C::NBP;
     uint64_t *mma_done = pair_done + TC_ND;
     auto done_parity = [](int q) { return (uint32_t)((q / TC_ND) & 1); };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + L::OFF_MISC);
@@ -1139,7 +1156,6 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
         for (int i = 0; i < C::NA; i++) mbar_init(&a_full[i], 128);
         for (int i = 0; i < C::NBP; i++) {
             mbar_init(&b_full[i], 1);
-            mbar_init(&ready[i], 1);
         }
         for (int i = 0; i < TC_ND; i++) mbar_init(&pair_done[i], 1);
         mbar_init(mma_done, 1);
@@ -1196,16 +1212,18 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
                     if (armed[i] >= 0) mbar_wait_bounded(&b_full[i], (uint32_t)armed[i]);
         }
     } else if (warp == 3) {
-        // ---- gate: A slot + B stage of pair q -> ready[q] -------------------------
-        // (ready[q % NBP] cannot be raised for pair q + NBP before the MMAs
-        // of pair q have completed: its B stage is loaded only after that)
-        if (lane == 0) {
-            for (int q = 0; q < npairs; q++) {
-                if (!tc_wait(&a_full[q % C::NA], (q / C::NA) & 1, abort_flag) ||
-                    !tc_wait(&b_full[q % C::NBP], (q / C::NBP) & 1, abort_flag))
-                    break;
-                mbar_arrive(&ready[q % C::NBP]);
-            }
+        // ---- gate: A slot + B stage of pair q, then the rendezvous --------------
+        // Both warps take exactly one barrier step per pair until the OR of
+        // their votes is set (this warp's bounded waits gave up), and leave
+        // the loop at the same pair: the waits are bounded, so the MMA warp
+        // is never left alone at the barrier.
+        for (int q = 0; q < npairs; q++) {
+            int ok = 0;
+            if (lane == 0)
+                ok = tc_wait(&a_full[q % C::NA], (q / C::NA) & 1, abort_flag) &&
+                     tc_wait(&b_full[q % C::NBP], (q / C::NBP) & 1, abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (named_bar_red_or(T3_GATE_BAR, 64, !ok)) break;
         }
     } else if (warp == 2) {
         // ---- MMA issue: the whole warp waits, one thread issues ------------------
@@ -1216,10 +1234,8 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
             const uint32_t idesc = f16_idesc(TC_BM, nmma);
             for (int q = 0; q < npairs; q++) {
                 const int sa = q % C::NA, sb = q % C::NBP;
-                // every lane polls (the verdict is the same for all: a lane
-                // gives up only when the bound runs out or another role aborted)
-                const bool okw = tc_wait(&ready[sb], (q / C::NBP) & 1, abort_flag);
-                if (!__all_sync(0xffffffffu, okw)) break;
+                // the gate's verdict for pair q (uniform over the warp)
+                if (named_bar_red_or(T3_GATE_BAR, 64, false)) break;
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t a_hi = tmem + (uint32_t)(T3_BN + 64 * sa), a_lo = a_hi + 32u;
