@@ -1046,6 +1046,8 @@ constexpr int T3_GATE_BAR = 2;  // named barrier of warps 2 and 3 (0: __syncthre
 constexpr int T3_BN = 192;
 constexpr int T3_TMEM_COLS = 512;
 constexpr int T3_HALF = T3_BN * 128;  // one plane of a block pair: 192 rows x 64 f16
+constexpr int T3_XB = 64;              // activation rows per TMA box (T3_BN % T3_XB == 0, 8-row swizzle groups)
+static_assert(T3_BN % T3_XB == 0 && T3_XB % 8 == 0, "activation boxes");
 
 template <int WT>
 struct T3Cfg;
@@ -1194,17 +1196,23 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
         }
     } else if (warp == 1) {
         // ---- activation stages: both planes of a pair on one barrier ------------------
+        // (boxes of T3_XB rows, only as many as the tile's live columns need:
+        // a narrow tile's stages are written with fewer shared-memory bytes)
         if (lane == 0) {
             int armed[C::NBP];
             for (int i = 0; i < C::NBP; i++) armed[i] = -1;
+            const int nbox = (ncols + T3_XB - 1) / T3_XB;
             for (int q = 0; q < npairs; q++) {
                 const int s = q % C::NBP;
                 if (q >= C::NBP && !tc_wait(&pair_done[(q - C::NBP) % TC_ND], done_parity(q - C::NBP), abort_flag, 16))
                     break;
-                mbar_arrive_expect_tx(&b_full[s], L::B_STAGE3);
+                mbar_arrive_expect_tx(&b_full[s], (uint32_t)(2 * nbox * T3_XB * 128));
                 const uint32_t dst = sbase + L::OFF_B + s * L::B_STAGE3;
-                tma_load_3d(dst, &tm_x, (pair0 + q) * 64, xrow0, 0, smem_u32(&b_full[s]));
-                tma_load_3d(dst + T3_HALF, &tm_x, (pair0 + q) * 64, xrow0, 1, smem_u32(&b_full[s]));
+                for (int b = 0; b < nbox; b++) {
+                    const uint32_t o = (uint32_t)(b * T3_XB * 128);
+                    tma_load_3d(dst + o, &tm_x, (pair0 + q) * 64, xrow0 + b * T3_XB, 0, smem_u32(&b_full[s]));
+                    tma_load_3d(dst + T3_HALF + o, &tm_x, (pair0 + q) * 64, xrow0 + b * T3_XB, 1, smem_u32(&b_full[s]));
+                }
                 armed[s] = (q / C::NBP) & 1;
             }
             if (*abort_flag)
@@ -1746,7 +1754,7 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     if (rc) return rc;
     // activations: [rows][K] f16 (Q4_K), or planes [2][rows][K] (hi, lo)
     rc = encode_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xa.q16, (uint64_t)KE, (uint64_t)rows, kSplit ? 2 : 0,
-                    (uint64_t)KE * 2, kSplit ? (uint64_t)rows * (uint64_t)KE * 2 : 0, 64, BN,
+                    (uint64_t)KE * 2, kSplit ? (uint64_t)rows * (uint64_t)KE * 2 : 0, 64, kSplit ? T3_XB : BN,
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     // the peer-store variant is a separate instantiation, so the plain kernel
