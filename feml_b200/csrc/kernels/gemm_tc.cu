@@ -45,6 +45,7 @@
 // lets the copies and MMAs it issued land and frees its TMEM before it
 // returns.
 #include <cuda.h>
+#include <type_traits>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
@@ -1024,9 +1025,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // tile feeds up to 192 columns, the MMAs (N up to 192) stay ahead of their
 // issue, three activation stages fit beside the raw weight ring, and a
 // mul_mat_id expert group of up to 192 routed rows is one tile.
-// TMEM columns: [0, 192) the f32 accumulator; then T3Cfg::NA slots of 64
+// TMEM columns: [0, 192) the f32 accumulator ([0, 256) stacked); then T3Cfg::NA slots of 64
 // columns, one block pair each (hi plane: 32 columns of two f16, lo plane:
 // the next 32).
+// An ungrouped product of at most 128 columns (one tile) stacks the
+// activation planes (the STACK instantiation): the stage holds the hi rows, then the lo rows right
+// after them (W = 64 * ceil(ncols / 64) rows each), and a K step is two
+// MMAs instead of three: Ahi x [Bhi; Blo]
+// (N = 2W, columns [0, W) += Ahi.Bhi and [W, 2W) += Ahi.Blo) and Alo x Bhi
+// (N = W, into [0, W)); the epilogue adds the two halves. An MMA's cost has
+// a floor well above its N / 2 cycles at small N, so fewer, wider MMAs win.
 // Roles (512 threads):
 //   warp 0      TMA: raw weight chunks (8 blocks x 128 rows), as gemm_tc_kernel.
 //   warp 1      TMA: activation stages (192 rows x 64 f16, the hi and lo
@@ -1045,6 +1053,7 @@ constexpr int T3_THREADS = 512;
 constexpr int T3_GATE_BAR = 2;  // named barrier of warps 2 and 3 (0: __syncthreads, 1: epilogue)
 constexpr int T3_BN = 192;
 constexpr int T3_TMEM_COLS = 512;
+constexpr int T3_ACC_COLS = 256;  // accumulator region; the A slots follow
 constexpr int T3_HALF = T3_BN * 128;  // one plane of a block pair: 192 rows x 64 f16
 constexpr int T3_XB = 64;              // activation rows per TMA box (T3_BN % T3_XB == 0, 8-row swizzle groups)
 static_assert(T3_BN % T3_XB == 0 && T3_XB % 8 == 0, "activation boxes");
@@ -1075,7 +1084,7 @@ struct T3Cfg<WT_Q4_K> {
 template <int WT>
 struct T3Layout {
     using C = T3Cfg<WT>;
-    static_assert(T3_BN + 64 * C::NA <= T3_TMEM_COLS, "TMEM: accumulator + A slots");
+    static_assert(T3_BN <= T3_ACC_COLS && T3_ACC_COLS + 64 * C::NA <= T3_TMEM_COLS, "TMEM: accumulator + A slots");
     static constexpr int RAW_STAGE = TC_BM * TcCfg<WT>::RAWB;
     static constexpr int B_STAGE3 = 2 * T3_HALF;  // [hi plane][lo plane]
     static constexpr int OFF_B = 0;
@@ -1108,7 +1117,7 @@ __device__ __forceinline__ void split_block(const uint32_t (&v)[16], __half2 d2,
     }
 }
 
-template <int WT, bool PEER>
+template <int WT, bool PEER, bool STACK>
 __global__ void __launch_bounds__(T3_THREADS, 1)
     gemm_tc3_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                     const TcParams p) {
@@ -1134,6 +1143,13 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
     // cover whole super-block pairs, so chunk0 and nchunks are even.
     const int pair0 = WT == WT_Q4_K ? chunk0 / 2 * 9 : tw.pair0;
     const int npairs = WT == WT_Q4_K ? nchunks / 2 * 9 : tw.npairs;
+    // STACK (an ungrouped product of at most 128 columns, one tile): the
+    // activation planes are stacked, W rows each. Its rounding differs from
+    // the three-MMA form's, and every column of the product is treated
+    // alike, so permuting the columns permutes the output bits.
+    static_assert(T3_XB == 64, "stacked planes use 64-row boxes");
+    const int stack_w = STACK ? T3_XB * ((ncols + T3_XB - 1) / T3_XB) : 0;
+    constexpr int acol0 = STACK ? T3_ACC_COLS : T3_BN;  // TMEM column of the first A slot
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + L::OFF_BAR);
     uint64_t *raw_full = bars;
@@ -1153,7 +1169,7 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
     if (tid == 0) {
         for (int i = 0; i < C::NR; i++) {
             mbar_init(&raw_full[i], 1);
-            mbar_init(&raw_empty[i], 128);
+            mbar_init(&raw_empty[i], WT == WT_Q4_K ? 256 : 128);  // Q4_K: both converter groups
         }
         for (int i = 0; i < C::NA; i++) mbar_init(&a_full[i], 128);
         for (int i = 0; i < C::NBP; i++) {
@@ -1175,6 +1191,112 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+
+    // Q4_K converters: group 0 is warps 4-7, group 1 warps 8-11 (which then
+    // run the epilogue); warp w writes TMEM lanes 32*(w % 4) .. +31.
+    auto convert_q4k = [&](auto grp_c) {
+        constexpr int grp = decltype(grp_c)::value;
+        if constexpr (WT == WT_Q4_K) {
+            // Q4_K: a chunk is one super-block (4 pairs); after every second
+            // one, the min-term pair of both (see the pair numbering above).
+            // Group grp converts pairs 2grp and 2grp+1 of every super-block;
+            // group 1 also the min-term pairs.
+            const int row = 32 * (warp & 3) + lane;
+            bool range_ok = true;
+            float mins[8];  // -dmin*m of the previous (even) super-block, exact in f32
+            for (int c = 0; c < nchunks; c++) {
+                const int s = c % C::NR;
+                if (!tc_wait_warp(&raw_full[s], (c / C::NR) & 1, abort_flag, lane)) break;
+                const uint8_t *rrow = gbase + L::OFF_RAW + s * L::RAW_STAGE + row * RC::RAWB;
+                const uint4 hv = *reinterpret_cast<const uint4 *>(rrow);
+                const uint32_t hdr[4] = {hv.x, hv.y, hv.z, hv.w};
+                uint32_t w[2][8];
+#pragma unroll
+                for (int j = 0; j < 2; j++) load_pair_words<WT>(rrow, 2 * grp + j, w[j]);
+                mbar_arrive(&raw_empty[s]);  // the super-block is in registers
+                const float d = f16_bits_to_f32((uint16_t)(hdr[0] & 0xFFFFu));
+                const float dmin = f16_bits_to_f32((uint16_t)(hdr[0] >> 16));
+                range_ok = range_ok && fabsf(d) <= C::kMaxScale && fabsf(dmin) <= C::kMaxMin;
+                const __half2 d2 = __half2half2(__ushort_as_half((uint16_t)(hdr[0] & 0xFFFFu)));
+                bool ok = true;
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int pp = 2 * grp + j;
+                    const int q = (c >> 1) * 9 + (c & 1) * CHUNK_PAIRS + pp;
+                    const int sa = q % C::NA;
+                    int sc0, mn0, sc1, mn1;
+                    q4k_scale_min(hdr, 2 * pp, sc0, mn0);
+                    q4k_scale_min(hdr, 2 * pp + 1, sc1, mn1);
+                    const __half2 s0 = __float2half2_rn((float)sc0), s1 = __float2half2_rn((float)sc1);
+                    uint32_t v0[16], v1[16];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        uint32_t lo[2], hi[2];
+                        nib_word_to_f16<0>(w[j][i], lo, hi);
+                        // sc * q: exact f16 integers (<= 945)
+                        v0[2 * i] = h2_bits(__hmul2(bits_h2(lo[0]), s0));
+                        v0[2 * i + 1] = h2_bits(__hmul2(bits_h2(lo[1]), s0));
+                        v1[2 * i] = h2_bits(__hmul2(bits_h2(hi[0]), s1));
+                        v1[2 * i + 1] = h2_bits(__hmul2(bits_h2(hi[1]), s1));
+                    }
+                    uint32_t h[32], l[32];
+                    split_block(v0, d2, h, l);
+                    split_block(v1, d2, h + 16, l + 16);
+                    if (q >= C::NA &&
+                        !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(acol0 + 64 * sa);
+                    tc_st32(ta, h);
+                    tc_st32(ta + 32u, l);
+                    tc_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&a_full[sa]);
+                }
+                if (!ok) break;
+                if constexpr (grp == 1) {
+                    float cur[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        int scj, mnj;
+                        q4k_scale_min(hdr, j, scj, mnj);
+                        cur[j] = -(dmin * (float)mnj);  // exact: 11 + 6 significant bits
+                    }
+                    if ((c & 1) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++) mins[j] = cur[j];
+                        continue;
+                    }
+                    // the min-term pair: 16 values (sub-blocks of super-blocks c-1, c)
+                    const int q = (c >> 1) * 9 + 8;
+                    const int sa = q % C::NA;
+                    uint32_t h8[8], l8[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const float a = i < 4 ? mins[2 * i] : cur[2 * i - 8];
+                        const float b = i < 4 ? mins[2 * i + 1] : cur[2 * i - 7];
+                        const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+                        const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+                        h8[i] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+                        l8[i] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+                    }
+                    if (q >= C::NA &&
+                        !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane))
+                        break;
+                    tc_fence_after();
+                    const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(acol0 + 64 * sa);
+                    tc_st8(ta, h8);
+                    tc_st8(ta + 32u, l8);
+                    tc_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&a_full[sa]);
+                }
+            }
+            if (!range_ok) *range_flag = 1;
+        }
+    };
 
     if (warp == 0) {
         // ---- raw weight chunks ------------------------------------------------
@@ -1211,7 +1333,8 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
                 for (int b = 0; b < nbox; b++) {
                     const uint32_t o = (uint32_t)(b * T3_XB * 128);
                     tma_load_3d(dst + o, &tm_x, (pair0 + q) * 64, xrow0 + b * T3_XB, 0, smem_u32(&b_full[s]));
-                    tma_load_3d(dst + T3_HALF + o, &tm_x, (pair0 + q) * 64, xrow0 + b * T3_XB, 1, smem_u32(&b_full[s]));
+                    tma_load_3d(dst + (STACK ? (uint32_t)stack_w * 128u : (uint32_t)T3_HALF) + o, &tm_x,
+                                (pair0 + q) * 64, xrow0 + b * T3_XB, 1, smem_u32(&b_full[s]));
                 }
                 armed[s] = (q / C::NBP) & 1;
             }
@@ -1240,13 +1363,14 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
             // MMA's N granularity of 16 (M = 128: N = 16..256, N % 16 == 0)
             const int nmma = min(T3_BN, (ncols + 15) & ~15);
             const uint32_t idesc = f16_idesc(TC_BM, nmma);
+            const uint32_t idesc_w = f16_idesc(TC_BM, STACK ? 2 * stack_w : 16), idesc_n = f16_idesc(TC_BM, STACK ? stack_w : 16);
             for (int q = 0; q < npairs; q++) {
                 const int sa = q % C::NA, sb = q % C::NBP;
                 // the gate's verdict for pair q (uniform over the warp)
                 if (named_bar_red_or(T3_GATE_BAR, 64, false)) break;
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint32_t a_hi = tmem + (uint32_t)(T3_BN + 64 * sa), a_lo = a_hi + 32u;
+                    const uint32_t a_hi = tmem + (uint32_t)(acol0 + 64 * sa), a_lo = a_hi + 32u;
                     const uint32_t b_hi = sbase + L::OFF_B + sb * L::B_STAGE3, b_lo = b_hi + T3_HALF;
                     // a Q4_K min-term pair uses its first K step only
                     const int nk = (WT == WT_Q4_K && q % 9 == 8) ? 1 : 4;
@@ -1255,9 +1379,14 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
                         if (k >= nk) break;
                         // K step of 16: 8 TMEM columns of A; 32 bytes in the swizzled B rows
                         const uint32_t ka = 8u * k, kb = 64u * (k >> 1) + 32u * (k & 1);
-                        tc_mma_f16_ts(tmem, a_hi + ka, sw128_desc(b_hi + kb), idesc, (q | k) ? 1u : 0u);
-                        tc_mma_f16_ts(tmem, a_hi + ka, sw128_desc(b_lo + kb), idesc, 1u);
-                        tc_mma_f16_ts(tmem, a_lo + ka, sw128_desc(b_hi + kb), idesc, 1u);
+                        if constexpr (STACK) {  // [Bhi; Blo] in one operand of 2W rows
+                            tc_mma_f16_ts(tmem, a_hi + ka, sw128_desc(b_hi + kb), idesc_w, (q | k) ? 1u : 0u);
+                            tc_mma_f16_ts(tmem, a_lo + ka, sw128_desc(b_hi + kb), idesc_n, 1u);
+                        } else {
+                            tc_mma_f16_ts(tmem, a_hi + ka, sw128_desc(b_hi + kb), idesc, (q | k) ? 1u : 0u);
+                            tc_mma_f16_ts(tmem, a_hi + ka, sw128_desc(b_lo + kb), idesc, 1u);
+                            tc_mma_f16_ts(tmem, a_lo + ka, sw128_desc(b_hi + kb), idesc, 1u);
+                        }
                     }
                     tc_commit(smem_u32(&pair_done[q % TC_ND]));
                 }
@@ -1269,99 +1398,7 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
     } else if (warp >= 4 && warp < 8) {
         // ---- converters: one weight row per thread, one block pair at a time ----
         if constexpr (WT == WT_Q4_K) {
-            // Q4_K: a chunk is one super-block (4 pairs); after every second
-            // one, the min-term pair of both (see the pair numbering above).
-            const int row = tid - 128;
-            bool range_ok = true;
-            float mins[8];  // -dmin*m of the previous (even) super-block, exact in f32
-            for (int c = 0; c < nchunks; c++) {
-                const int s = c % C::NR;
-                if (!tc_wait_warp(&raw_full[s], (c / C::NR) & 1, abort_flag, lane)) break;
-                const uint8_t *rrow = gbase + L::OFF_RAW + s * L::RAW_STAGE + row * RC::RAWB;
-                const uint4 hv = *reinterpret_cast<const uint4 *>(rrow);
-                const uint32_t hdr[4] = {hv.x, hv.y, hv.z, hv.w};
-                uint32_t w[CHUNK_PAIRS][8];
-#pragma unroll
-                for (int pp = 0; pp < CHUNK_PAIRS; pp++) load_pair_words<WT>(rrow, pp, w[pp]);
-                mbar_arrive(&raw_empty[s]);  // the super-block is in registers
-                const float d = f16_bits_to_f32((uint16_t)(hdr[0] & 0xFFFFu));
-                const float dmin = f16_bits_to_f32((uint16_t)(hdr[0] >> 16));
-                range_ok = range_ok && fabsf(d) <= C::kMaxScale && fabsf(dmin) <= C::kMaxMin;
-                const __half2 d2 = __half2half2(__ushort_as_half((uint16_t)(hdr[0] & 0xFFFFu)));
-                bool ok = true;
-#pragma unroll
-                for (int pp = 0; pp < CHUNK_PAIRS; pp++) {
-                    const int q = (c >> 1) * 9 + (c & 1) * CHUNK_PAIRS + pp;
-                    const int sa = q % C::NA;
-                    int sc0, mn0, sc1, mn1;
-                    q4k_scale_min(hdr, 2 * pp, sc0, mn0);
-                    q4k_scale_min(hdr, 2 * pp + 1, sc1, mn1);
-                    const __half2 s0 = __float2half2_rn((float)sc0), s1 = __float2half2_rn((float)sc1);
-                    uint32_t v0[16], v1[16];
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        uint32_t lo[2], hi[2];
-                        nib_word_to_f16<0>(w[pp][i], lo, hi);
-                        // sc * q: exact f16 integers (<= 945)
-                        v0[2 * i] = h2_bits(__hmul2(bits_h2(lo[0]), s0));
-                        v0[2 * i + 1] = h2_bits(__hmul2(bits_h2(lo[1]), s0));
-                        v1[2 * i] = h2_bits(__hmul2(bits_h2(hi[0]), s1));
-                        v1[2 * i + 1] = h2_bits(__hmul2(bits_h2(hi[1]), s1));
-                    }
-                    uint32_t h[32], l[32];
-                    split_block(v0, d2, h, l);
-                    split_block(v1, d2, h + 16, l + 16);
-                    if (q >= C::NA &&
-                        !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(T3_BN + 64 * sa);
-                    tc_st32(ta, h);
-                    tc_st32(ta + 32u, l);
-                    tc_wait_st();
-                    tc_fence_before();
-                    mbar_arrive(&a_full[sa]);
-                }
-                if (!ok) break;
-                float cur[8];
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    int scj, mnj;
-                    q4k_scale_min(hdr, j, scj, mnj);
-                    cur[j] = -(dmin * (float)mnj);  // exact: 11 + 6 significant bits
-                }
-                if ((c & 1) == 0) {
-#pragma unroll
-                    for (int j = 0; j < 8; j++) mins[j] = cur[j];
-                    continue;
-                }
-                // the min-term pair: 16 values (sub-blocks of super-blocks c-1, c)
-                const int q = (c >> 1) * 9 + 8;
-                const int sa = q % C::NA;
-                uint32_t h8[8], l8[8];
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const float a = i < 4 ? mins[2 * i] : cur[2 * i - 8];
-                    const float b = i < 4 ? mins[2 * i + 1] : cur[2 * i - 7];
-                    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-                    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
-                    h8[i] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
-                    l8[i] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
-                }
-                if (q >= C::NA &&
-                    !tc_wait_warp(&pair_done[(q - C::NA) % TC_ND], done_parity(q - C::NA), abort_flag, lane))
-                    break;
-                tc_fence_after();
-                const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(T3_BN + 64 * sa);
-                tc_st8(ta, h8);
-                tc_st8(ta + 32u, l8);
-                tc_wait_st();
-                tc_fence_before();
-                mbar_arrive(&a_full[sa]);
-            }
-            if (!range_ok) *range_flag = 1;
+            convert_q4k(std::integral_constant<int, 0>{});
         } else {
         const int row = tid - 128;
         bool range_ok = true;
@@ -1391,7 +1428,7 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(T3_BN + 64 * sa);
+                const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(acol0 + 64 * sa);
                 tc_st32(ta, h);
                 tc_st32(ta + 32u, l);
                 tc_wait_st();
@@ -1403,6 +1440,9 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
         if (!range_ok) *range_flag = 1;
         }
     } else if (warp >= 8) {
+        if constexpr (WT == WT_Q4_K) {
+            if (warp < 12) convert_q4k(std::integral_constant<int, 1>{});
+        }
         // ---- epilogue ------------------------------------------------------------
         // (1) while the main loop runs: the column table (destinations of the
         //     tile's columns, their activation row scales);
@@ -1452,6 +1492,13 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
                 uint32_t r[32];
                 tc_ld32(tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(32 * qc), r);
                 tc_wait_ld();
+                if constexpr (STACK) {  // + the Ahi.Blo half
+                    uint32_t r2[32];
+                    tc_ld32(tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(stack_w + 32 * qc), r2);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(r2[i]));
+                }
 #pragma unroll
                 for (int i = 0; i < 32; i++)
                     stage[(32 * qc + i) * TC_BM + row] = npairs > 0 ? __uint_as_float(r[i]) : 0.0f;
@@ -1758,15 +1805,18 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     // the peer-store variant is a separate instantiation, so the plain kernel
-    // carries none of its registers
+    // carries none of its registers; so is the stacked one (an ungrouped
+    // product of at most 128 columns)
+    const bool stack = kSplit && !groups && rows <= 128;
     using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const TcParams);
     KernFn kern;
     if constexpr (kSplit)
-        kern = peer ? gemm_tc3_kernel<WT, true> : gemm_tc3_kernel<WT, false>;
+        kern = peer ? (stack ? gemm_tc3_kernel<WT, true, true> : gemm_tc3_kernel<WT, true, false>)
+                    : (stack ? gemm_tc3_kernel<WT, false, true> : gemm_tc3_kernel<WT, false, false>);
     else
         kern = peer ? gemm_tc_kernel<WT, true> : gemm_tc_kernel<WT, false>;
-    static DeviceFlags configured[2];
-    rc = raise_smem_limit((const void *)kern, kBytes, configured[peer ? 1 : 0], "gemm_tc");
+    static DeviceFlags configured[4];
+    rc = raise_smem_limit((const void *)kern, kBytes, configured[(peer ? 2 : 0) + (stack ? 1 : 0)], "gemm_tc");
     if (rc) return rc;
     TcParams p{};
     p.M = (int)M;
