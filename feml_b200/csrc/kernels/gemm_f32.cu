@@ -13,18 +13,18 @@
 //    4-stage shared-memory ring as 2D TMA boxes (32 k x the CTA's rows, 32 k
 //    x its 32 columns; 128-byte swizzle), 8 tensor copies per chunk: with
 //    one bulk copy per 512-byte row segment (64 per chunk) the copies, not
-//    the arithmetic, set the pace (110 us against 88 us for C1). A compute
+//    the arithmetic, set the pace (110 us against 88 us for 4096 x 4096 weights x 32 columns). A compute
 //    warp owns 4 rows x 32 columns; each lane a 2-row x 2-column micro-tile
 //    (4 chains), reading 4 k values of each of its rows and columns with
 //    16-byte shared loads two steps ahead of the arithmetic: 4 loads per 16
 //    multiply-adds, conflict-free through the swizzle. Two warps per SM
 //    sub-partition hide each other's latencies better than one warp with
-//    twice the chains (84 against 88 us for C1, identical outputs). The sequential chains
+//    twice the chains (84 against 88 us at that size, identical outputs). The sequential chains
 //    leave the kernel bound by FP32 issue, not by HBM: a lane's two columns
 //    of a row take their adds in one packed f32x2 instruction (two
 //    independent round-to-nearest adds, so the bits are unchanged), three
-//    FP32 instructions per two multiply-adds instead of four (C1 82.9 ->
-//    76.7 us).
+//    FP32 instructions per two multiply-adds instead of four (82.9 -> 76.7 us
+//    at that size).
 //  - gemm_f32_exact_kernel (everything else, and mul_mat_id with F32
 //    experts): a CTA owns a 32x32 output tile; each of its 128 threads owns a
 //    4 (rows) x 2 (columns) micro-tile, i.e. 8 independent chains. K is walked

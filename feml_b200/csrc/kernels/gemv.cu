@@ -656,7 +656,7 @@ __global__ void __launch_bounds__(kGemvThreads, XR > 0 ? 2 : 1) gemv_kernel(cons
 // ring; the eight slices' partial sums of a row meet in shared memory and are
 // added in warp order.
 constexpr int kKsRows = 4;    // rows per TMA box
-constexpr int kKsStages = 3;  // ring stages per warp
+constexpr int kKsStages = 2;  // ring stages per warp (Q4_K 14336 x 4096, one column: 3 stages 11.9 us, 2 stages 11.4 us)
 
 struct KsParams {
     const float *x;
