@@ -362,3 +362,27 @@ def test_q4_k_gemm_reports_scales_beyond_the_f16_range(b200, off, v, ok):
             run_mul_mat(b200, DType.Q4_K, wq, x, K, M)
         got = run_mul_mat(b200, DType.Q4_K, O.quantize(O.DT_Q4_K, weights(rng, M, K)), x, K, M)
         assert np.isfinite(got).all()
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_0, DType.Q4_K])
+@pytest.mark.parametrize("N", [100, 160])
+def test_gemm_one_tile_properties(b200, dt, N):
+    """A product of one column tile: at most 128 columns run the stacked
+    two-MMA form, 129..192 the three-MMA form. Either way every column gets
+    the same arithmetic (permuting the columns permutes the output bits) and
+    scaling the activations by 8 scales the outputs by 8 exactly."""
+    rng = np.random.default_rng(N)
+    K, M = 1024, 384
+    wq = O.quantize(QT[dt], weights(rng, M, K))
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    wt = torch.from_numpy(wq).cuda()
+    xt = torch.from_numpy(x).cuda()
+    y = ops.mul_mat(dt, wt, xt, K)
+    y8 = ops.mul_mat(dt, wt, xt * 8.0, K)
+    perm = torch.from_numpy(rng.permutation(N)).cuda()
+    yp = ops.mul_mat(dt, wt, xt[perm].contiguous(), K)
+    torch.cuda.synchronize()
+    assert torch.equal(y8, y * 8.0)
+    assert torch.equal(yp, y[perm])
+    ok, err = tol_ok(y.cpu().numpy(), O.mul_mat_quant_ref(QT[dt], wq, x, K))
+    assert ok, f"max abs err {err}"
