@@ -436,6 +436,17 @@ def mul_mat_kernels_per_step(cfg, N):
     return ops.mul_mat_launches(DType[cfg["wtype"]], cfg["K"], cfg["M"], N)
 
 
+def mul_mat_id_kernels_per_step(cfg, N):
+    """Routing, activation quantization and the grouped GEMM, plus the tail
+    reduction when the GEMM's largest tile grid (weight-row tiles x the
+    column-tile bound) overflows one wave of CTAs (one per SM)."""
+    import torch
+    bn = 192 if cfg["wtype"] in ("Q8_0", "Q4_0") or (cfg["wtype"] == "Q4_K" and cfg["K"] % 512 == 0) else 128
+    max_tiles = -(-N * cfg["n_sel"] // bn) + cfg["E"]
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return 3 + (1 if -(-cfg["M"] // 128) * max_tiles > sms else 0)
+
+
 def dominant_kernel(cfg, N):
     wt = cfg["wtype"]
     if "E" in cfg:
@@ -573,7 +584,8 @@ def run_extras_single(args, timer):
             e2e = e2e_c_abi(cfg, N, w0, None, args.warmup, torch.cuda.current_device())
         key = f"{name}_n{N}" if name == "c4" else name
         out[key] = extra_line(name, cfg, N, ms, steps, copies, e2e=e2e)
-        launches += steps * mul_mat_kernels_per_step(cfg, N)
+        out[key]["gpu_launches"] = steps * mul_mat_kernels_per_step(cfg, N)
+        launches += out[key]["gpu_launches"]
         del w0
         torch.cuda.empty_cache()
     return out, launches
@@ -637,7 +649,9 @@ def experts_sharded_case(cfg, N, timer, steps, warmup, combine, e2e_steps):
     torch.cuda.synchronize()
     barrier()
     mod.close()
-    kernels = 3 + (1 if fused else 0)  # route + quantize + grouped GEMM (+ flag wait)
+    # route + quantize + grouped GEMM, then the flag wait (peer-store
+    # combines) or the tail reduction when the tile grid overflows a wave
+    kernels = 3 + (1 if fused else mul_mat_id_kernels_per_step(dict(cfg, E=len(mine)), N) - 3)
     return ms, steps, copies, e2e, kernels
 
 
@@ -804,7 +818,7 @@ def run_b200(args, cfg_name, cfg, N):
     if ws == 1:
         if is_moe:
             ms, steps, copies, w0 = mul_mat_id_case(cfg, N, timer, args.steps, args.warmup)
-            launches = steps * 3
+            launches = steps * mul_mat_id_kernels_per_step(cfg, N)
         else:
             ms, steps, copies, w0, _ = mul_mat_case(cfg, N, timer, args.steps, args.warmup)
             launches = steps * mul_mat_kernels_per_step(cfg, N)
@@ -812,8 +826,7 @@ def run_b200(args, cfg_name, cfg, N):
         del w0
         torch.cuda.empty_cache()
         if not args.no_extras:
-            extras, extra_launches = run_extras_single(args, timer)
-            launches += extra_launches
+            extras, _ = run_extras_single(args, timer)  # each extra line carries its own count
         scaling = "strong"
     else:
         if not is_moe:
@@ -826,11 +839,11 @@ def run_b200(args, cfg_name, cfg, N):
                 ms_c, st_c, cp_c, _, k_c = experts_sharded_case(cfg, N, timer, None, args.warmup, comb, 0)
                 extras[f"c5_{comb}"] = extra_line("c5", cfg, N, ms_c, st_c, cp_c, world=ws)
                 extras[f"c5_{comb}"]["combine"] = comb
-                launches += st_c * k_c
+                extras[f"c5_{comb}"]["gpu_launches"] = st_c * k_c
             c4 = CONFIGS["c4"]
             ms_r, st_r, cp_r = rows_sharded_case(c4, 1, timer, args.warmup, fused=True)
             extras["c4_rows_fused_n1"] = extra_line("c4", c4, 1, ms_r, st_r, cp_r, world=ws)
-            launches += st_r * 2
+            extras["c4_rows_fused_n1"]["gpu_launches"] = st_r * 2
         scaling = "strong"
     time.sleep(0.25)
     sampler.stop()
