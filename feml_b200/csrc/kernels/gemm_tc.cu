@@ -1807,11 +1807,11 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     // the peer-store variant is a separate instantiation, so the plain kernel
     // carries none of its registers; so is the stacked one (an ungrouped
     // product of at most 128 columns)
-    const bool stack = kSplit && !groups && rows <= 128;
+    const bool stack = kSplit && !groups && !peer && rows <= 128;
     using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const TcParams);
     KernFn kern;
     if constexpr (kSplit)
-        kern = peer ? (stack ? gemm_tc3_kernel<WT, true, true> : gemm_tc3_kernel<WT, true, false>)
+        kern = peer ? gemm_tc3_kernel<WT, true, false>  // peer stores: grouped only
                     : (stack ? gemm_tc3_kernel<WT, false, true> : gemm_tc3_kernel<WT, false, false>);
     else
         kern = peer ? gemm_tc_kernel<WT, true> : gemm_tc_kernel<WT, false>;
