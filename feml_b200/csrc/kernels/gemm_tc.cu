@@ -111,6 +111,7 @@ struct TcLayout {
 
 struct TcParams {
     int M, N, K;          // N: activation rows of the operand buffer
+    int bw;               // ungrouped column-tile width (<= the kernel's tile width)
     uint8_t *y;
     uint64_t y_nb1;
     const float *dxT;     // [K/32][N] activation block scales
@@ -540,8 +541,8 @@ __host__ __device__ inline bool tail_plan(int64_t tiles_m, int64_t tiles_n, int6
 __device__ __forceinline__ TileWork decode_tile(const TcParams &p, int bn) {
     TileWork t;
     t.m0 = blockIdx.x * TC_BM;
-    t.xrow0 = blockIdx.y * bn;
-    t.ncols = min(bn, p.N - t.xrow0);
+    t.xrow0 = blockIdx.y * p.bw;
+    t.ncols = min(p.bw, p.N - t.xrow0);
     t.expert = 0;
     t.tsplit = -1;
     t.ttile = 0;
@@ -589,8 +590,8 @@ __device__ __forceinline__ TileWork decode_tile(const TcParams &p, int bn) {
             nt = t.ttile % p.tail_tiles_n;
         }
         t.m0 = mt * TC_BM;
-        t.xrow0 = nt * bn;
-        t.ncols = min(bn, p.N - t.xrow0);
+        t.xrow0 = nt * p.bw;
+        t.ncols = min(p.bw, p.N - t.xrow0);
     }
     if (p.grouped) {
         if (tt >= p.g.tile_start[p.g.n_groups]) {
@@ -1681,13 +1682,13 @@ __global__ void tc_split_reduce_kernel(const float *__restrict__ partial, int sp
 // Tail tiles: y = sum over s in order of the S partial tiles (deterministic),
 // then the fused epilogue.
 __global__ void tc_tail_reduce_kernel(const float *__restrict__ partial, int S, int n_tail, int tiles_n, int m0_tile,
-                                      int M, int N, int bn, uint8_t *y, uint64_t y_nb1, const EpiAct epi) {
+                                      int M, int N, int bn, int bw, uint8_t *y, uint64_t y_nb1, const EpiAct epi) {
     const int64_t per = (int64_t)n_tail * bn * TC_BM;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
         const int tt = (int)(i / (bn * TC_BM)), rem = (int)(i % (bn * TC_BM));
         const int c = rem / TC_BM, rr = rem % TC_BM;
-        const int m = (m0_tile + tt / tiles_n) * TC_BM + rr, n = (tt % tiles_n) * bn + c;
-        if (m >= M || n >= N) continue;
+        const int m = (m0_tile + tt / tiles_n) * TC_BM + rr, n = (tt % tiles_n) * bw + c;
+        if (c >= bw || m >= M || n >= N) continue;
         float acc = partial[i];
         for (int sp = 1; sp < S; sp++) acc += partial[(int64_t)sp * per + i];
         reinterpret_cast<float *>(y + (uint64_t)n * y_nb1)[m] = apply_act(acc, epi, m);
@@ -1822,6 +1823,15 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
     p.M = (int)M;
     p.N = (int)rows;
     p.K = (int)K;
+    // Ungrouped split-f16 tiles share the columns evenly (rounded to the
+    // MMA's N step of 16): an MMA costs a floor of cycles well above N / 2 at
+    // small N, so 176 + 176 + 160 columns beat 192 + 192 + 128.
+    p.bw = BN;
+    if (kSplit && !groups && rows > 0) {
+        const int64_t nt = (rows + BN - 1) / BN;
+        p.bw = (int)std::min<int64_t>(BN, ((rows + nt - 1) / nt + 15) / 16 * 16);
+        if ((rows + p.bw - 1) / p.bw != nt) p.bw = BN;  // the same tile count as the planners assume
+    }
     p.y = static_cast<uint8_t *>(y);
     p.y_nb1 = y_nb1;
     p.dxT = xa.dxT;
@@ -1872,7 +1882,7 @@ int launch_tc_typed(const void *w, uint64_t w_nb1, uint64_t w_nb2, int64_t n_pla
         const int64_t total = (int64_t)p.tail_n * BN * TC_BM;
         const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sm_count());
         tc_tail_reduce_kernel<<<blocks, 256, 0, s>>>(p.tail_partial, p.tail_S, p.tail_n, p.tail_tiles_n, p.tail_m0,
-                                                     (int)M, (int)rows, BN, static_cast<uint8_t *>(y), y_nb1, epi);
+                                                     (int)M, (int)rows, BN, p.bw, static_cast<uint8_t *>(y), y_nb1, epi);
         e = cudaGetLastError();
         if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "gemm_tc tail reduce launch: %s", cudaGetErrorString(e));
     }
