@@ -390,7 +390,7 @@ def roofline(cfg, N, ms, world, kernel, prof):
         a = ops_ / sec / 1e12
         r = {"bound": "tensor", "achieved": a, "peak": peaks["bf16_tflops"] * world, "unit": "TFLOP/s",
              "peak_note": f"dense bf16 TFLOP/s x {world} GPU(s), {peaks['source']} burst figure (the kernel "
-                          f"issues f16 tcgen05 MMAs; f16 dense measured within 3% of bf16 on this pool)",
+                          f"issues f16 tcgen05 MMAs; f16 dense measured within 3% of bf16 on B200)",
              "frac_of_sustained": a / (peaks["bf16_tflops_sustained"] * world)}
     else:
         a = alg / sec / 1e9
