@@ -319,11 +319,14 @@ int feml_b200_mul_mat_workspace(int32_t wtype, int64_t K, int64_t M, int64_t N, 
  *   dst[m*4 + n*dst_nb1] = sum_k W[k, m] * X[k, n]
  * W: wtype blocks, row m at w + m*w_nb1; X: f32, column n at x + n*x_nb1;
  * quantized weights are multiplied against the Q8_0-quantized activations:
- * int32 per-block sums on the decode GEMVs (N <= 8) and the Q4_K GEMM; the
- * Q8_0 / Q4_0 GEMM (N > 8) multiplies the dequantized values, each split
- * exactly into two f16, with f32 accumulation. That GEMM needs every
- * dequantized weight within the f16 range (|d| <= 511.75 for Q8_0,
- * <= 8188 for Q4_0; quantized model weights have d = amax/127). Under
+ * int32 per-block sums on the decode GEMVs (N <= 8) and on the Q4_K GEMM
+ * when K % 512 != 0; the Q8_0 / Q4_0 / Q4_K (K % 512 == 0) GEMM (N > 8)
+ * multiplies the dequantized values, each split exactly into two f16, with
+ * f32 accumulation (Q4_K: d * (sc * q) split, and -dmin * m against the
+ * activation block sums). That GEMM needs every dequantized weight within
+ * the f16 range (|d| <= 511.75 for Q8_0, <= 8188 for Q4_0; for Q4_K
+ * |d| <= 65504/945 and |dmin| <= 65504/63; quantized model weights stay far
+ * below). Under
  * graph_compute a larger block scale sets bit 3 of the backend's status
  * word, which synchronize reports as FB_ERR_DEVICE; this entry point has no
  * status word, and such a scale shows as non-finite outputs. dst must not
