@@ -1576,14 +1576,28 @@ __global__ void __launch_bounds__(T3_THREADS, 1)
 // from its largest block scale D (D * 128 < 2^(e + 15)), then
 // v = dx*qx * 2^-e (exact) is written as hi = rn16(v) to plane 0
 // (q16[r][k]) and lo = v - hi to plane 1 (q16[rows + r][k]); xscale[r] = 2^e.
+// With `chunks` > 1 (few rows: a cluster of `chunks` CTAs per row) each CTA
+// takes a contiguous run of the row's blocks and the CTAs of the cluster
+// exchange their maxima through distributed shared memory.
 constexpr int QF_THREADS = 256;
+
+__device__ __forceinline__ float ld_cluster_f32(const float *p, uint32_t rank) {
+    uint32_t ra;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8_t *__restrict__ x, uint64_t x_nb1,
                                                                     int K, int rows, __half *__restrict__ q16,
                                                                     float *__restrict__ dxT, float *__restrict__ xsdT,
                                                                     float *__restrict__ xscale, bool hilo, bool ext,
-                                                                    bool routed, GroupMap g) {
-    const int r = blockIdx.x, tid = threadIdx.x;
+                                                                    bool routed, GroupMap g, int chunks) {
+    const int r = (int)blockIdx.x / chunks, part = (int)blockIdx.x % chunks, tid = threadIdx.x;
     int src = r;
     if (routed) {
         if (g.n_groups == 0 || r >= g.offsets[g.n_groups - 1] + g.counts[g.n_groups - 1]) return;
@@ -1591,6 +1605,9 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
     }
     const float *xr = reinterpret_cast<const float *>(x + (uint64_t)src * x_nb1);
     const int nblk = K / QK;
+    // this CTA's blocks [b_lo, b_hi) of the row
+    // (32-bit: part < 8 and nblk < 2^26)
+    const int b_lo = chunks == 1 ? 0 : part * nblk / chunks, b_hi = chunks == 1 ? nblk : (part + 1) * nblk / chunks;
     // ext (Q4_K): 576 positions per 512 elements, the 64 after each 512
     // starting with the 16 blocks' sums (the min-term pair of the GEMM)
     const int KE = ext ? K / 512 * 576 : K;
@@ -1600,7 +1617,7 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
     if (hilo) {
         __shared__ float wmax[QF_THREADS / 32];
         float amax = 0.0f;
-        for (int k = 4 * tid; k < K; k += 4 * QF_THREADS) {
+        for (int k = b_lo * QK + 4 * tid; k < b_hi * QK; k += 4 * QF_THREADS) {
             const float4 v = *reinterpret_cast<const float4 *>(xr + k);
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         }
@@ -1611,6 +1628,13 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
         amax = wmax[0];
 #pragma unroll
         for (int w = 1; w < QF_THREADS / 32; w++) amax = fmaxf(amax, wmax[w]);
+        if (chunks > 1) {  // the row's maximum over the cluster's CTAs
+            __shared__ float part_max;
+            if (tid == 0) part_max = amax;
+            cluster_sync_all();
+            for (int j = 0; j < chunks; j++) amax = fmaxf(amax, ld_cluster_f32(&part_max, (uint32_t)j));
+            cluster_sync_all();  // every CTA has read before any leaves
+        }
         // the largest block scale: the quantizer's d of the row maximum
         // (division and f16 rounding are monotonic)
         const float dmax = __half2float(__float2half_rn(__fdiv_rn(amax, 127.0f)));
@@ -1622,14 +1646,14 @@ __global__ void __launch_bounds__(QF_THREADS) quantize_q8_f16_kernel(const uint8
             e = ex - 15;
         }
         down = ldexpf(1.0f, -e);
-        if (tid == 0) xscale[r] = ldexpf(1.0f, e);
+        if (tid == 0 && part == 0) xscale[r] = ldexpf(1.0f, e);
     }
     // 8 lanes per block, 4 elements per lane; every lane of the warp calls the
     // quantize routine (uniform trip count)
-    for (int base = 0; base < nblk; base += QF_THREADS / 8) {
+    for (int base = b_lo; base < b_hi; base += QF_THREADS / 8) {
         const int b = base + (tid >> 3);
         const int k = b * QK + (tid & 7) * 4;
-        const bool valid = b < nblk;
+        const bool valid = b < b_hi;
         const float4 v = valid ? *reinterpret_cast<const float4 *>(xr + k) : make_float4(0.f, 0.f, 0.f, 0.f);
         uint16_t dbits;
         int qsum;
@@ -2002,10 +2026,36 @@ int launch_quantize_q8_f16(const void *x, uint64_t x_nb1, int64_t K, int64_t N, 
         return fb::set_error(FB_ERR_INVALID, "quantize_q8_f16: activations must be 16-byte aligned");
     GroupMap g{};
     if (routed) g = *routed;
-    quantize_q8_f16_kernel<<<(unsigned)rows, QF_THREADS, 0, s>>>(
-        static_cast<const uint8_t *>(x), x_nb1, (int)K, (int)rows, static_cast<__half *>(out.q16), out.dxT, out.xsdT,
-        out.xscale, split_kernel(wtype, K), wtype == WT_Q4_K && split_kernel(wtype, K), routed != nullptr, g);
-    cudaError_t e = cudaGetLastError();
+    const bool hilo = split_kernel(wtype, K), ext = wtype == WT_Q4_K && hilo;
+    // Few long rows (K >= 8192): a cluster of CTAs per row, up to two waves
+    // of CTAs, at least 32 blocks per CTA, a power of two up to 8. (Rows of
+    // 4096 were measured faster as one CTA each: the cluster barriers cost
+    // more than the split saves.)
+    int chunks = 1;
+    if (hilo && K / QK >= 256)
+        while (chunks < 8 && rows * chunks < 2 * (int64_t)sm_count() && K / QK >= 64 * chunks) chunks *= 2;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(rows * chunks));
+    cfg.blockDim = dim3(QF_THREADS);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)chunks;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaSuccess;
+    if (chunks == 1)
+        quantize_q8_f16_kernel<<<(unsigned)rows, QF_THREADS, 0, s>>>(static_cast<const uint8_t *>(x), x_nb1, (int)K,
+                                                                      (int)rows, static_cast<__half *>(out.q16), out.dxT,
+                                                                      out.xsdT, out.xscale, hilo, ext, routed != nullptr,
+                                                                      g, 1);
+    else
+        e = cudaLaunchKernelEx(&cfg, quantize_q8_f16_kernel, static_cast<const uint8_t *>(x), x_nb1, (int)K, (int)rows,
+                               static_cast<__half *>(out.q16), out.dxT, out.xsdT, out.xscale, hilo, ext,
+                               routed != nullptr, g, chunks);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fb::set_error(FB_ERR_CUDA, "quantize_q8_f16 launch: %s", cudaGetErrorString(e));
     return FB_OK;
 }
