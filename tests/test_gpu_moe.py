@@ -180,3 +180,24 @@ def test_mul_mat_id_tail_split(b200, dt, K):
     outs = [ops.mul_mat_id(dt, wt, xt, it, K) for _ in range(2)]
     assert torch.equal(outs[0], outs[1])
     assert np.array_equal(outs[0].cpu().numpy().reshape(got.shape), got)
+
+
+@pytest.mark.parametrize("dt", [DType.Q8_0, DType.Q4_K])
+def test_mul_mat_id_long_rows_few_slots(b200, dt):
+    """K = 8192 with 39 routed slots: the activation quantizer splits each
+    slot's row over a cluster of CTAs; an invalid id leaves its slot out of
+    the routed rows (those clusters return at once) and zero."""
+    rng = np.random.default_rng(44)
+    E, M, K, N, n_sel = 4, 256, 8192, 20, 2
+    wb = _expert_weights(rng, dt, E, M, K)
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    ids = topk_ids(rng, N, n_sel, E)
+    ids[7, 1] = E  # invalid: reported, its slot zero
+    out, err = run_mul_mat_id(b200, dt, wb, x, ids, K, M, check_sync=False)
+    assert isinstance(err, F.FemlError)
+    assert not out[7, 1].any()
+    want = O.mul_mat_id_ref(QT[dt], wb, x, ids, K, quantize_act=True)
+    ok, e2 = tol_ok(out, want)
+    assert ok, e2
+    b200.synchronize()
+

@@ -80,6 +80,7 @@ SHAPES = [
     (8192, 40, 4), (4096, 300, 6),                                  # GEMV with a pre-quantized activation buffer
     (256, 300, 16), (2048, 200, 64),                                # GEMM path
     (768, 150, 33), (256, 1, 100), (4096, 257, 128), (512, 130, 300),
+    (8192, 70, 20), (14336, 40, 9),                                 # long rows: cluster-split activation quantizer
 ]
 
 
