@@ -387,3 +387,19 @@ def test_gemm_one_tile_properties(b200, dt, N):
     assert torch.equal(yp, y[perm])
     ok, err = tol_ok(y.cpu().numpy(), O.mul_mat_quant_ref(QT[dt], wq, x, K))
     assert ok, f"max abs err {err}"
+
+
+def test_gemm_tail_split_with_balanced_tiles(b200):
+    """300 columns run as two balanced tiles of 160 + 140; 9600 weight rows
+    give 75 x 2 = 150 tiles, 2 past one wave of 148, so the last weight-row
+    tile row is split 4 ways in K and a reduction writes it (its column map
+    follows the 160-column tiles). Every output against the oracle."""
+    rng = np.random.default_rng(45)
+    K, M, N = 2048, 9600, 300
+    from feml_b200 import ops as _ops
+    assert _ops.mul_mat_launches(DType.Q8_0, K, M, N) == 3  # quantizer, GEMM, tail reduction
+    wq = O.quantize(O.DT_Q8_0, weights(rng, M, K))
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    got = run_mul_mat(b200, DType.Q8_0, wq, x, K, M)
+    ok, err = tol_ok(got, O.mul_mat_quant_ref(O.DT_Q8_0, wq, x, K))
+    assert ok, f"max abs err {err}"

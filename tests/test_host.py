@@ -464,3 +464,17 @@ def test_library_hides_internal_symbols():
     out = os.popen(f"nm -D --defined-only {F._L.LIB_PATH}").read()
     exported = [line.split()[-1] for line in out.splitlines() if " T " in line]
     assert all(s.startswith(("feml_b200_", "fb_")) for s in exported), exported
+
+
+def test_mul_mat_launch_plans():
+    """The host planner's launch counts (no GPU needed: 148 SMs assumed):
+    the decode GEMV quantizes inside its one kernel; a GEMM is the activation
+    quantizer plus the GEMM, plus a reduction when K is split (a tile grid
+    that leaves most SMs idle) or when the last wave's overflow is split in K
+    (19200 rows = 150 weight-row tiles: 2 past one wave); 258 tiles (11008 x
+    512) take no tail split (the overflow is too wide to split)."""
+    from feml_b200 import DType, ops
+    assert ops.mul_mat_launches(DType.Q8_0, 4096, 4096, 1) == 1
+    assert ops.mul_mat_launches(DType.Q4_0, 4096, 11008, 512) == 2
+    assert ops.mul_mat_launches(DType.Q4_K, 14336, 4096, 64) == 3
+    assert ops.mul_mat_launches(DType.Q8_0, 4096, 19200, 100) == 3
